@@ -1,0 +1,501 @@
+#!/usr/bin/env python
+"""Benchmark of the fgm-kernels quantised GEMM path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (BASELINE config 1 at the metric's M = 8): the decode GEMM sweep
+shapes q 2048x2048, kv 2048x512, o 2048x2048, fused gate/up 2048x16384 and
+down 8192x2048 (K x N), int4 weights in the .fgm q4g layout with f16 group-64
+scales, over 12 distinct layer copies (~383 MB of weights + scales, larger
+than 2x the 126 MB L2, so every step streams its weights from HBM).  A step
+is one decode pass through that stack: per layer four activation preps
+(attention input, attention output, FFN input, down input; f32 X[8, K] ->
+rotate-free quantise + pack) and five GEMMs, i.e. fastgemma's Gemm::run
+(forward.rs:128-158) for each projection.  The step is captured once in a
+CUDA graph and replayed.
+
+``value`` = weight+scale bytes streamed per step / device time per step
+(GB/s).  ``e2e`` = the same metric through the host-pointer C ABI
+(fgm_linear_q4g_cuda: pinned host X in, pinned host C out, every call).
+``prefill`` = BASELINE config 2 (W8A8, M = 256) in int8 TOPS.
+``cpu_baseline`` = the reference's own CPU kernels (AMX, else VNNI) on the
+host cores over a bounded sample of the same workload.
+
+For N > 1 (torchrun), every rank runs its own copy of the stack (the decode
+projections are replicated, not sharded: BASELINE runs them on one GPU), so
+the scaling is weak and the step has no collective.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+DECODE_SHAPES = [("q", 2048, 2048), ("kv", 2048, 512), ("o", 2048, 2048),
+                 ("gate_up", 2048, 16384), ("down", 8192, 2048)]  # (name, K, N)
+# which activation feeds each projection: q and kv share the attention input
+DECODE_INPUT = {"q": 0, "kv": 0, "o": 1, "gate_up": 2, "down": 3}
+PREFILL_SHAPES = [("gate_up", 2048, 16384), ("down", 8192, 2048)]
+M_DECODE, GROUP, M_PREFILL = 8, 64, 256
+
+
+def q4g_bytes(k, n, group=GROUP):
+    return n * k // 2, (k // group) * n * 2
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=12)
+    ap.add_argument("--prefill-copies", type=int, default=8)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    HW = 0x8          # HW slowdown
+    HW_THERMAL = 0x40
+    SW_THERMAL = 0x20
+    SW_POWER = 0x4
+
+    def __init__(self, cuda_index: int, period: float = 0.005):
+        self.period = period
+        self.samples, self.reasons = [], set()
+        self._stop = threading.Event()
+        self.max_mhz = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            pr = torch.cuda.get_device_properties(cuda_index)
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        except Exception:  # NVML missing: report no samples rather than guess
+            self.nv = None
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = self.get_reasons(self.h)
+                for bit, name in ((self.HW, "hw_slowdown"), (self.HW_THERMAL, "hw_thermal_slowdown"),
+                                  (self.SW_THERMAL, "sw_thermal_slowdown"),
+                                  (self.SW_POWER, "sw_power_cap")):
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.nv:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.nv:
+            self.t.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------- distributed
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------- CPU reference
+def cpu_reference_run(layers: int, seconds: float | None, steps: int | None, warmup: int,
+                      seed: int = 7):
+    """Time the reference's CPU kernels on this host over the decode workload.
+
+    Returns (GB/s, info).  One sample = one layer of the stack (4 preps +
+    5 GEMMs) on layer copy (i % layers), driven by a persistent pool over all
+    host cores exactly as fgm-core's Pool does (pool.rs:285-311).
+    """
+    from oracle.oracle import Oracle, load_reference
+    from fastgemma_b200 import fgm_format as F
+    import ctypes as C
+    impl = load_reference()
+    kind = "reference"
+    if impl is None:
+        impl, kind = Oracle(), "port"
+    backend = getattr(impl, "backend", "scalar-port")
+    cores = os.cpu_count() or 1
+    L = impl.lib
+    L.cpu_pool_start(cores, impl.init_fn() if kind == "reference" else None)
+    rng = np.random.default_rng(seed)
+    xs = {K: rng.standard_normal((M_DECODE, K), dtype=np.float32) for K in (2048, 8192)}
+    prep = {}
+    for K in (2048, 8192):
+        prep[K] = (np.zeros((M_DECODE, K), np.float32), np.zeros((M_DECODE, K), np.int8),
+                   np.zeros(M_DECODE, np.float32), np.zeros(16 * K, np.int8))
+    ws = []
+    for _ in range(layers):
+        lw = {}
+        for name, K, N in DECODE_SHAPES:
+            lw[name] = F.synth_q4g(N, K, GROUP, int(rng.integers(1 << 30)), structured=False)
+        ws.append(lw)
+    cs = {name: np.zeros((M_DECODE, N), np.float32) for name, K, N in DECODE_SHAPES}
+    f_q4g, f_prep = impl.fn("q4g"), impl.fn("prep")
+    P = lambda a: a.ctypes.data  # noqa: E731
+    per_layer = sum(sum(q4g_bytes(K, N)) for _, K, N in DECODE_SHAPES)
+
+    def one_layer(i):
+        lw = ws[i % layers]
+        done_inputs = set()
+        for name, K, N in DECODE_SHAPES:
+            inp = DECODE_INPUT[name]
+            rot, qa, qs, pa = prep[K]
+            if inp not in done_inputs:
+                L.cpu_pool_prep(f_prep, P(xs[K]), K, P(rot), P(qa), P(qs), P(pa), M_DECODE, K, 0)
+                done_inputs.add(inp)
+            bq, s = lw[name]
+            L.cpu_pool_gemm_q4g(f_q4g, M_DECODE, N, K, P(pa), P(qs), P(bq), P(s.view(np.uint16)),
+                                GROUP, P(cs[name]), N)
+
+    for i in range(warmup):
+        one_layer(i)
+    t0 = L.cpu_pool_now()
+    n = 0
+    while True:
+        one_layer(n)
+        n += 1
+        el = L.cpu_pool_now() - t0
+        if (steps is not None and n >= steps) or (steps is None and el >= seconds):
+            break
+    L.cpu_pool_stop()
+    gbs = per_layer * n / el / 1e9
+    info = {"kind": kind, "cores": cores, "backend": backend,
+            "sample": f"{n} single-layer samples (4 preps + 5 int4 GEMMs, M=8, "
+                      f"{per_layer / 1e6:.1f} MB of weights each) rotating over {layers} "
+                      f"layer copies, {el:.2f} s"}
+    return gbs, el / n, info
+
+
+def run_reference_arm(args, world, rank):
+    if rank != 0:
+        return
+    gbs, sec, info = cpu_reference_run(args.layers, None, args.steps, args.warmup)
+    line = {
+        "metric": "decode W4A8 GEMM weight GB/s (M=8); prefill W8A8 GEMM int8 TOPS at M=256",
+        "impl": "reference", "value": gbs, "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic",
+        "config": {"workload": "BASELINE config 1 at M=8 (decode projections q/kv/o/gate_up/"
+                               "down, int4 g64), one layer per step, reference CPU kernels",
+                   "l2": "12 layer copies rotated (383 MB) > host last-level cache"},
+        "cpu_baseline": dict(info, value=gbs, unit="GB/s"),
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------- GPU arm
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        run_reference_arm(args, world, rank)
+        return
+    import torch
+    import torch.distributed as dist
+    from fastgemma_b200 import device as D
+    from fastgemma_b200 import _lib
+    lib = _lib.lib()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    if not lib.fgm_cuda_available():
+        raise SystemExit("no sm_100 device")
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    L = args.layers
+    # ---- decode stack: weights streamed from HBM every step
+    layers = []
+    for _ in range(L):
+        lw = {}
+        for name, K, N in DECODE_SHAPES:
+            wb, sb = q4g_bytes(K, N)
+            w = torch.randint(0, 256, (wb,), dtype=torch.uint8, device=dev, generator=gen)
+            s = torch.empty((K // GROUP, N), dtype=torch.float32, device=dev).uniform_(
+                0.005, 0.02, generator=gen).half()
+            lw[name] = (w, s)
+        layers.append(lw)
+    xs = [torch.randn((M_DECODE, K), dtype=torch.float32, device=dev, generator=gen)
+          for K in (2048, 2048, 2048, 8192)]
+    pas = [D.packed_a(M_DECODE, x.shape[1], dev) for x in xs]
+    qss = [torch.empty(M_DECODE, dtype=torch.float32, device=dev) for _ in xs]
+    cs = {name: torch.empty((M_DECODE, N), dtype=torch.float32, device=dev)
+          for name, K, N in DECODE_SHAPES}
+    wbytes_step = L * sum(sum(q4g_bytes(K, N)) for _, K, N in DECODE_SHAPES)
+
+    def step(events=None):
+        for l in range(L):
+            for i, x in enumerate(xs):
+                D.prep_rows(x, x.shape[1], qss[i], pas[i], M_DECODE, x.shape[1], 0)
+            for name, K, N in DECODE_SHAPES:
+                w, s = layers[l][name]
+                i = DECODE_INPUT[name]
+                if events is not None and name == "gate_up":
+                    events[l][0].record()
+                D.gemm_q4g(M_DECODE, N, K, pas[i], qss[i], w, s, GROUP, cs[name])
+                if events is not None and name == "gate_up":
+                    events[l][1].record()
+
+    side = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.synchronize()
+    c0 = lib.fgm_cuda_launch_count()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        step()
+    launches_per_step = lib.fgm_cuda_launch_count() - c0
+    # a twin graph with event-record nodes around the dominant kernel
+    kev = [(torch.cuda.Event(enable_timing=True, external=True),
+            torch.cuda.Event(enable_timing=True, external=True)) for _ in range(L)]
+    tgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(tgraph, stream=side):
+        step(kev)
+
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        time.sleep(0.02)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / args.steps
+    value = world * wbytes_step / (ms * 1e-3) / 1e9
+
+    # ---- roofline of the dominant kernel (gate/up q4g GEMM), CUDA events
+    kdur = []
+    for _ in range(5):
+        tgraph.replay()
+        torch.cuda.synchronize()
+        kdur += [a.elapsed_time(b) * 1e-3 for a, b in kev]
+    K_, N_ = 2048, 16384
+    alg = sum(q4g_bytes(K_, N_)) + M_DECODE * K_ + M_DECODE * 4 + M_DECODE * N_ * 4
+    kmean = statistics.mean(kdur)
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    hbm = peaks.get("hbm_gbs")
+    peak_src = "measured" if hbm else "fallback"
+    hbm = hbm or 6650.0
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get("gemv_q4g_gate_up_M8")
+    achieved = alg / kmean / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "traffic": traffic, "peak_source": peak_src,
+                "kernel": "gemv_kernel<q4g, M<=8> gate/up 2048x16384",
+                "algorithmic_bytes_per_launch": alg, "mean_launch_us": kmean * 1e6,
+                "launches_timed": len(kdur)}
+
+    # ---- prefill: W8A8, M = 256
+    prefill = None
+    if not args.no_prefill:
+        prefill = bench_prefill(args, dev, gen, world)
+
+    # ---- e2e through the host-pointer C ABI
+    e2e = None
+    if not args.no_e2e:
+        e2e = bench_e2e(args, world, dev)
+
+    cpu = None
+    if not args.no_cpu and rank == 0 and world == 1:
+        gbs, _, info = cpu_reference_run(L, args.cpu_seconds, None, 2)
+        cpu = dict(info, value=gbs, unit="GB/s")
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": "decode W4A8 GEMM weight GB/s (M=8); prefill W8A8 GEMM int8 TOPS at M=256",
+            "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seeded uniform int4 codes, f16 scales U(0.005,0.02), X~N(0,1))",
+            "config": {
+                "workload": "BASELINE config 1 at M=8: q 2048x2048, kv 2048x512, o 2048x2048, "
+                            "gate_up 2048x16384, down 8192x2048 (KxN), int4 q4g group 64 f16 "
+                            f"scales, {L} distinct layer copies, 4 preps + 5 GEMMs per layer",
+                "weight_bytes_per_step": wbytes_step, "l2": "inputs larger than L2 "
+                f"({wbytes_step / 1e6:.0f} MB of weights per step > 2 x 126 MB)",
+                "graph": "one CUDA graph per step", "parallelism": f"replicas x{world}"},
+            "roofline": roofline,
+            "gpu_launches": int(launches_per_step * args.steps),
+            "clocks": clk.summary(),
+            "e2e": e2e, "prefill": prefill, "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        del graph, tgraph
+        dist.destroy_process_group()
+
+
+def bench_prefill(args, dev, gen, world):
+    import torch
+    from fastgemma_b200 import device as D
+    copies = args.prefill_copies
+    ws = []
+    for _ in range(copies):
+        lw = {}
+        for name, K, N in PREFILL_SHAPES:
+            w = torch.randint(-127, 128, (N * K,), dtype=torch.int8, device=dev, generator=gen)
+            s = torch.empty(N, dtype=torch.float32, device=dev).uniform_(0.001, 0.01, generator=gen)
+            lw[name] = (w, s)
+        ws.append(lw)
+    xs = {K: torch.randn((M_PREFILL, K), dtype=torch.float32, device=dev, generator=gen)
+          for _, K, _ in PREFILL_SHAPES}
+    pas = {K: D.packed_a(M_PREFILL, K, dev) for K in xs}
+    qss = {K: torch.empty(M_PREFILL, dtype=torch.float32, device=dev) for K in xs}
+    cs = {name: torch.empty((M_PREFILL, N), dtype=torch.float32, device=dev)
+          for name, K, N in PREFILL_SHAPES}
+
+    def step():
+        for c in range(copies):
+            for name, K, N in PREFILL_SHAPES:
+                D.prep_rows(xs[K], K, qss[K], pas[K], M_PREFILL, K, 0)
+                w, s = ws[c][name]
+                D.gemm_q8c(M_PREFILL, N, K, pas[K], qss[K], w, s, cs[name])
+
+    side = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        step()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    steps = max(5, args.steps // 10)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
+    ops = copies * sum(2 * M_PREFILL * N * K for _, K, N in PREFILL_SHAPES)
+    return {"value": world * ops / (ms * 1e-3) / 1e12, "unit": "TOPS", "ms_per_step": ms,
+            "steps": steps, "workload": f"BASELINE config 2: M=256 prep + W8A8 GEMM at "
+            f"2048x16384 and 8192x2048 (KxN), {copies} weight copies per step"}
+
+
+def bench_e2e(args, world, dev):
+    """Same decode stack through fgm_linear_q4g_cuda with pinned host buffers."""
+    import torch
+    from fastgemma_b200 import _lib
+    from fastgemma_b200 import fgm_format as F
+    lib = _lib.lib()
+    rng = np.random.default_rng(99)
+    L = args.layers
+    hw = []
+    for _ in range(L):
+        lw = {}
+        for name, K, N in DECODE_SHAPES:
+            bq, s = F.synth_q4g(N, K, GROUP, int(rng.integers(1 << 30)), structured=False)
+            _lib.call("fgm_cuda_register", bq.ctypes.data, bq.nbytes)
+            _lib.call("fgm_cuda_register", s.ctypes.data, s.nbytes)
+            lw[name] = (bq, s)
+        hw.append(lw)
+    xs = {K: torch.randn((M_DECODE, K), dtype=torch.float32).pin_memory() for K in (2048, 8192)}
+    cs = {name: torch.empty((M_DECODE, N), dtype=torch.float32).pin_memory()
+          for name, K, N in DECODE_SHAPES}
+    h2d = d2h = 0
+    for name, K, N in DECODE_SHAPES:
+        h2d += L * M_DECODE * K * 4
+        d2h += L * M_DECODE * N * 4
+
+    def step():
+        for l in range(L):
+            for name, K, N in DECODE_SHAPES:
+                bq, s = hw[l][name]
+                _lib.check(lib.fgm_linear_q4g_cuda(
+                    xs[K].data_ptr(), K, 0, M_DECODE, N, K, bq.ctypes.data, s.ctypes.data, GROUP,
+                    cs[name].data_ptr(), N))
+
+    for _ in range(max(3, args.warmup // 4)):
+        step()
+    steps = max(5, args.steps // 10)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    sec = max_over_ranks(time.perf_counter() - t0, world, dev) / steps
+    wbytes = L * sum(sum(q4g_bytes(K, N)) for _, K, N in DECODE_SHAPES)
+    for l in range(L):
+        for bq, s in hw[l].values():
+            _lib.call("fgm_cuda_unregister", bq.ctypes.data)
+            _lib.call("fgm_cuda_unregister", s.ctypes.data)
+    return {"value": world * wbytes / sec / 1e9, "unit": "GB/s", "ms_per_step": sec * 1e3,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
+            "path": "fgm_linear_q4g_cuda per projection (host X in, host C out, synchronous), "
+                    "host wall clock"}
+
+
+if __name__ == "__main__":
+    main()

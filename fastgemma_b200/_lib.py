@@ -1,0 +1,76 @@
+"""ctypes binding of libfgm_cuda.so (include/fgm_cuda.h).
+
+The library is the product; this module only loads it and turns negative
+status codes into exceptions.  Loading fails loudly when the shared object is
+missing -- there is no CPU fallback behind these functions.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libfgm_cuda.so")
+
+_p, _i, _sz = C.c_void_p, C.c_int, C.c_size_t
+
+# symbol -> (argtypes, restype); every symbol include/fgm_cuda.h declares
+SIGNATURES = {
+    "fgm_cuda_available": ([], _i),
+    "fgm_cuda_init": ([_i], _i),
+    "fgm_cuda_last_error": ([], C.c_char_p),
+    "fgm_cuda_launch_count": ([], C.c_uint64),
+    "fgm_cuda_device_status": ([], _i),
+    "fgm_gemm_q4g_cuda": ([_i, _i, _i, _p, _p, _p, _p, _i, _p, _i, _i, _i], _i),
+    "fgm_gemm_q8c_cuda": ([_i, _i, _i, _p, _p, _p, _p, _p, _i, _i, _i], _i),
+    "fgm_linear_q4g_cuda": ([_p, _i, _i, _i, _i, _i, _p, _p, _i, _p, _i], _i),
+    "fgm_linear_q8c_cuda": ([_p, _i, _i, _i, _i, _i, _p, _p, _p, _i], _i),
+    "fgm_prep_rows_cuda": ([_p, _i, _p, _p, _p, _p, _i, _i, _i, _i, _i], _i),
+    "fgm_quant_act_cuda": ([_p, _i, _i, _p, _p], _i),
+    "fgm_fwht_cuda": ([_p, _i, _i], _i),
+    "fgm_pack_a_cuda": ([_i, _i, _p, _p], _i),
+    "fgm_cuda_register": ([_p, _sz], _i),
+    "fgm_cuda_unregister": ([_p], _i),
+    "fgm_cuda_lookup": ([_p], _p),
+    "fgm_cuda_registry_bytes": ([], _sz),
+    "fgm_cuda_gemm_q4g": ([_i, _i, _i, _p, _p, _p, _p, _i, _p, _i, _i, _i, _p], _i),
+    "fgm_cuda_gemm_q8c": ([_i, _i, _i, _p, _p, _p, _p, _p, _i, _i, _i, _p], _i),
+    "fgm_cuda_prep_rows": ([_p, _i, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p], _i),
+    "fgm_cuda_gemm_q4g_acc": ([_i, _i, _i, _p, _p, _i, _p, _i, _i, _p], _i),
+    "fgm_cuda_gemm_q8c_acc": ([_i, _i, _i, _p, _p, _p, _i, _i, _p], _i),
+}
+
+
+class FgmCudaError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"fgm_cuda error {code}: {msg}")
+        self.code = code
+
+
+_lib = None
+
+
+def lib():
+    """The loaded library (loaded once; raises if it was never built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(
+                f"{LIB_PATH} is missing: build it with `python -m fastgemma_b200.build`")
+        L = C.CDLL(LIB_PATH)
+        for name, (args, res) in SIGNATURES.items():
+            f = getattr(L, name)
+            f.argtypes = args
+            f.restype = res
+        _lib = L
+    return _lib
+
+
+def check(rc: int) -> int:
+    if rc < 0:
+        raise FgmCudaError(rc, lib().fgm_cuda_last_error().decode())
+    return rc
+
+
+def call(name: str, *args) -> int:
+    return check(getattr(lib(), name)(*args))

@@ -1,0 +1,656 @@
+// C ABI of the sm_100a backend (include/fgm_cuda.h): argument contracts,
+// device selection, the weight registry, host-pointer drop-ins and the
+// device-pointer entry points.
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "fgm_cuda.h"
+#include "fgm_internal.h"
+
+namespace fgm {
+
+static std::atomic<uint64_t> g_launches{0};
+void count_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+
+static thread_local std::string t_err;
+
+static int fail(int code, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_err = buf;
+  return code;
+}
+
+static int cuda_fail(cudaError_t e, const char *what) {
+  return fail(FGM_CUDA_ERUNTIME, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define FGM_TRY(call)                                            \
+  do {                                                           \
+    cudaError_t e_ = (call);                                     \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call);          \
+  } while (0)
+
+// ------------------------------------------------------------------ contracts
+static int check_gemm(int M, int N, int K, int ldc, int n0, int n1, int group, bool q4) {
+  if (M < 0) return fail(FGM_CUDA_EINVAL, "M=%d < 0", M);
+  if (K <= 0 || K % 64 != 0 || K > 65536)
+    return fail(FGM_CUDA_EINVAL, "K=%d: need 0 < K <= 65536 and K %% 64 == 0", K);
+  if (N <= 0 || N % 16 != 0) return fail(FGM_CUDA_EINVAL, "N=%d: need N > 0 and N %% 16 == 0", N);
+  if (n0 < 0 || n1 < n0 || n1 > N / 16)
+    return fail(FGM_CUDA_EINVAL, "n-block range [%d, %d) outside [0, %d]", n0, n1, N / 16);
+  if ((n1 - n0) % 4 != 0)
+    return fail(FGM_CUDA_EINVAL, "n-block range [%d, %d) is not a multiple of 4", n0, n1);
+  if (ldc < N) return fail(FGM_CUDA_EINVAL, "ldc=%d < N=%d", ldc, N);
+  if (q4 && (group <= 0 || group % 64 != 0 || K % group != 0))
+    return fail(FGM_CUDA_EINVAL, "group=%d: need group > 0, group %% 64 == 0, K %% group == 0",
+                group);
+  return FGM_CUDA_OK;
+}
+
+static int check_prep(int lda, int m, int k, int hsz, int r0, int r1, bool have_qa) {
+  if (m < 0) return fail(FGM_CUDA_EINVAL, "m=%d < 0", m);
+  if (k <= 0 || k % 64 != 0 || k > 65536)
+    return fail(FGM_CUDA_EINVAL, "k=%d: need 0 < k <= 65536 and k %% 64 == 0", k);
+  if (lda < k) return fail(FGM_CUDA_EINVAL, "lda=%d < k=%d", lda, k);
+  if (hsz < 0 || (hsz > 0 && ((hsz & (hsz - 1)) != 0 || k % hsz != 0)))
+    return fail(FGM_CUDA_EINVAL, "hsz=%d: need 0 or a power of two dividing k=%d", hsz, k);
+  if (r0 < 0 || r0 % 16 != 0 || r1 > m || (r1 < r0))
+    return fail(FGM_CUDA_EINVAL, "rows [%d, %d) of m=%d: need r0 %% 16 == 0, r0 <= r1 <= m", r0,
+                r1, m);
+  if (r1 < m && r1 % 16 != 0 && !have_qa)
+    return fail(FGM_CUDA_EINVAL, "a row range ending inside a tile block needs qa");
+  return FGM_CUDA_OK;
+}
+
+static size_t packed_len(int m, int k) { return (size_t)((m + 15) / 16) * 16 * (size_t)k; }
+
+// ------------------------------------------------------------------- device
+static std::mutex g_dev_mu;
+static int g_dev = -1;
+static cudaStream_t g_stream = nullptr;
+
+static int pick_device(int want) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return fail(FGM_CUDA_ENODEV, "no CUDA device visible");
+  }
+  int dev = want;
+  if (dev < 0) {
+    const char *e = getenv("FGM_CUDA_DEVICE");
+    if (e && *e) dev = atoi(e);
+    else if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  }
+  if (dev < 0 || dev >= n) return fail(FGM_CUDA_ENODEV, "device %d of %d", dev, n);
+  cudaDeviceProp prop;
+  FGM_TRY(cudaGetDeviceProperties(&prop, dev));
+  if (prop.major != 10)
+    return fail(FGM_CUDA_ENODEV, "device %d is sm_%d%d; this build targets sm_100a", dev,
+                prop.major, prop.minor);
+  return dev;
+}
+
+static int ensure_device() {
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (g_dev < 0) {
+    int dev = pick_device(-1);
+    if (dev < 0) return dev;
+    FGM_TRY(cudaSetDevice(dev));
+    FGM_TRY(cudaStreamCreateWithFlags(&g_stream, cudaStreamNonBlocking));
+    g_dev = dev;
+  } else {
+    FGM_TRY(cudaSetDevice(g_dev));
+  }
+  return FGM_CUDA_OK;
+}
+
+// ----------------------------------------------------------------- registry
+struct RegEntry {
+  void *dev;
+  size_t bytes;
+};
+static std::mutex g_reg_mu;
+static std::unordered_map<const void *, RegEntry> g_reg;
+static size_t g_reg_bytes = 0;
+
+static int reg_upload(const void *host, size_t bytes, const void **dev) {
+  std::lock_guard<std::mutex> lk(g_reg_mu);
+  auto it = g_reg.find(host);
+  if (it != g_reg.end()) {
+    if (it->second.bytes != bytes)
+      return fail(FGM_CUDA_EINVAL, "weight %p registered with %zu bytes, now %zu", host,
+                  it->second.bytes, bytes);
+    *dev = it->second.dev;
+    return FGM_CUDA_OK;
+  }
+  void *d = nullptr;
+  if (cudaMalloc(&d, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(FGM_CUDA_ENOMEM, "cudaMalloc(%zu) for weight %p", bytes, host);
+  }
+  cudaError_t e = cudaMemcpy(d, host, bytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    return cuda_fail(e, "weight upload");
+  }
+  g_reg[host] = RegEntry{d, bytes};
+  g_reg_bytes += bytes;
+  *dev = d;
+  return FGM_CUDA_OK;
+}
+
+// Device copy of a registered blob, or nullptr.  A registered blob must span
+// at least `bytes`; an unregistered one is the caller's to upload per call.
+static int reg_find(const void *host, size_t bytes, const void **dev) {
+  std::lock_guard<std::mutex> lk(g_reg_mu);
+  auto it = g_reg.find(host);
+  *dev = nullptr;
+  if (it == g_reg.end()) return FGM_CUDA_OK;
+  if (it->second.bytes < bytes)
+    return fail(FGM_CUDA_EINVAL, "weight %p registered with %zu bytes, call needs %zu", host,
+                it->second.bytes, bytes);
+  *dev = it->second.dev;
+  return FGM_CUDA_OK;
+}
+
+// ------------------------------------------------------------ host staging
+// One pinned host buffer and one device buffer, grown geometrically and kept:
+// after the first call of a given size the host path allocates nothing.
+struct Staging {
+  char *h = nullptr;
+  size_t hcap = 0;
+  char *d = nullptr;
+  size_t dcap = 0;
+};
+static std::mutex g_host_mu;  // serialises the host-pointer entry points
+static Staging g_stage;
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+static int stage_reserve(size_t bytes) {
+  if (bytes > g_stage.hcap) {
+    size_t cap = std::max(bytes, g_stage.hcap * 2);
+    if (g_stage.h) cudaFreeHost(g_stage.h);
+    g_stage.h = nullptr;
+    g_stage.hcap = 0;
+    if (cudaMallocHost(&g_stage.h, cap) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(FGM_CUDA_ENOMEM, "cudaMallocHost(%zu)", cap);
+    }
+    g_stage.hcap = cap;
+  }
+  if (bytes > g_stage.dcap) {
+    size_t cap = std::max(bytes, g_stage.dcap * 2);
+    if (g_stage.d) cudaFree(g_stage.d);
+    g_stage.d = nullptr;
+    g_stage.dcap = 0;
+    if (cudaMalloc(&g_stage.d, cap) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(FGM_CUDA_ENOMEM, "cudaMalloc(%zu)", cap);
+    }
+    g_stage.dcap = cap;
+  }
+  return FGM_CUDA_OK;
+}
+
+static bool is_pinned(const void *p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeHost;
+}
+
+// Copy `bytes` from host `src` to device `dst` (through staging at `hoff`
+// unless src is pinned).
+static int h2d(void *dst, const void *src, size_t bytes, size_t hoff) {
+  if (!bytes) return FGM_CUDA_OK;
+  if (is_pinned(src)) {
+    FGM_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, g_stream));
+  } else {
+    memcpy(g_stage.h + hoff, src, bytes);
+    FGM_TRY(cudaMemcpyAsync(dst, g_stage.h + hoff, bytes, cudaMemcpyHostToDevice, g_stream));
+  }
+  return FGM_CUDA_OK;
+}
+
+// Rows [0, rows) x `width` bytes of a compact device matrix into host memory
+// with pitch `hpitch`, then wait.
+static int d2h_rows_sync(void *dst, size_t hpitch, const void *dsrc, size_t width, int rows,
+                         size_t hoff) {
+  if (rows <= 0 || width == 0) {
+    FGM_TRY(cudaStreamSynchronize(g_stream));
+    return FGM_CUDA_OK;
+  }
+  if (is_pinned(dst)) {
+    FGM_TRY(cudaMemcpy2DAsync(dst, hpitch, dsrc, width, width, rows, cudaMemcpyDeviceToHost,
+                              g_stream));
+    FGM_TRY(cudaStreamSynchronize(g_stream));
+  } else {
+    FGM_TRY(cudaMemcpyAsync(g_stage.h + hoff, dsrc, width * rows, cudaMemcpyDeviceToHost,
+                            g_stream));
+    FGM_TRY(cudaStreamSynchronize(g_stream));
+    for (int r = 0; r < rows; r++)
+      memcpy((char *)dst + (size_t)r * hpitch, g_stage.h + hoff + (size_t)r * width, width);
+  }
+  return FGM_CUDA_OK;
+}
+
+// ------------------------------------------------- per-device launch facts
+struct DevInfo {
+  int sms = 0;
+  size_t smem_optin = 0;
+  int *err = nullptr;  // bounded-wait failure flag, cleared by fgm_cuda_device_status
+};
+static std::mutex g_info_mu;
+static DevInfo g_info[64];
+
+static int dev_info(DevInfo **out) {
+  int dev = 0;
+  FGM_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(FGM_CUDA_ENODEV, "device index %d", dev);
+  std::lock_guard<std::mutex> lk(g_info_mu);
+  DevInfo &d = g_info[dev];
+  if (!d.sms) {
+    int v = 0;
+    FGM_TRY(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev));
+    int sm = 0;
+    FGM_TRY(cudaDeviceGetAttribute(&sm, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    void *e = nullptr;
+    FGM_TRY(cudaMalloc(&e, 256));
+    FGM_TRY(cudaMemset(e, 0, 256));
+    d.err = static_cast<int *>(e);
+    d.smem_optin = (size_t)sm - 1024;  // headroom for the kernels' static shared memory
+    d.sms = v;
+  }
+  *out = &d;
+  return FGM_CUDA_OK;
+}
+
+// PDL (programmatic dependent launch) lets a kernel's weight prefetch overlap
+// the tail of the kernel before it.  FGM_CUDA_PDL=0 turns it off.
+static bool use_pdl() {
+  static int v = -1;
+  if (v < 0) {
+    const char *e = getenv("FGM_CUDA_PDL");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+static bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
+// ------------------------------------------------------------- launchers
+static int run_gemm(bool q4, int M, int N, int K, const int8_t *A, const float *a_scale,
+                    const void *B, const void *b_scale, int group, float *C, int ldc, int c_col0,
+                    int32_t *acc, int n0, int n1, cudaStream_t st) {
+  if (M == 0 || n0 == n1) return FGM_CUDA_OK;
+  if (!aligned16(B) || (q4 && b_scale && !aligned16(b_scale)))
+    return fail(FGM_CUDA_EINVAL, "weights and int4 scales must be 16-byte aligned");
+  DevInfo *di = nullptr;
+  int rc = dev_info(&di);
+  if (rc) return rc;
+  GemvParams p{};
+  p.err = di->err;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.group = q4 ? group : 0;
+  p.A = A;
+  p.a_scale = a_scale;
+  p.B = static_cast<const uint8_t *>(B);
+  p.b_scale = b_scale;
+  p.C = C;
+  p.ldc = ldc;
+  p.c_col0 = c_col0;
+  p.acc = acc;
+  p.nb0 = n0;
+  cudaError_t e = launch_gemv(p, n1 - n0, q4, use_pdl(), di->sms, di->smem_optin, st);
+  if (e != cudaSuccess) return cuda_fail(e, q4 ? "gemm_q4g launch" : "gemm_q8c launch");
+  count_launch();
+  return FGM_CUDA_OK;
+}
+
+static int run_prep(const float *src, int lda, float *rot, int8_t *qa, float *qs, int8_t *pa,
+                    int m, int k, int hsz, int r0, int r1, cudaStream_t st) {
+  if (r0 >= r1) return FGM_CUDA_OK;
+  PrepParams p{src, lda, rot, qa, qs, pa, m, k, hsz, r0, r1};
+  cudaError_t e = launch_prep(p, use_pdl(), st);
+  if (e != cudaSuccess) return cuda_fail(e, "prep launch");
+  count_launch();
+  return FGM_CUDA_OK;
+}
+
+// Host-pointer GEMM: stage A and a_scale, resolve weights, run, bring back C.
+static int host_gemm(bool q4, int M, int N, int K, const int8_t *A, const float *a_scale,
+                     const void *B, const void *b_scale, int group, float *C, int ldc, int n0,
+                     int n1) {
+  int rc = check_gemm(M, N, K, ldc, n0, n1, group, q4);
+  if (rc) return rc;
+  if (M == 0 || n0 == n1) return FGM_CUDA_OK;
+  if (!A || !a_scale || !B || !b_scale || !C) return fail(FGM_CUDA_EINVAL, "null pointer");
+  std::lock_guard<std::mutex> lk(g_host_mu);
+  if ((rc = ensure_device())) return rc;
+  const void *dB = nullptr, *dS = nullptr;
+  const size_t wbytes = q4 ? (size_t)N * K / 2 : (size_t)N * K;
+  const size_t sbytes = q4 ? (size_t)(K / group) * N * 2 : (size_t)N * 4;
+  if ((rc = reg_find(B, wbytes, &dB))) return rc;
+  if ((rc = reg_find(b_scale, sbytes, &dS))) return rc;
+  const int cols = (n1 - n0) * 16;
+  const size_t a_len = packed_len(M, K), s_len = (size_t)M * 4, c_len = (size_t)M * cols * 4;
+  const size_t o_s = align256(a_len), o_c = o_s + align256(s_len), o_w = o_c + align256(c_len);
+  const size_t o_ws = o_w + (dB ? 0 : align256(wbytes));
+  const size_t total = o_ws + (dS ? 0 : align256(sbytes));
+  if ((rc = stage_reserve(total))) return rc;
+  char *d = g_stage.d;
+  if ((rc = h2d(d, A, a_len, 0))) return rc;
+  if ((rc = h2d(d + o_s, a_scale, s_len, o_s))) return rc;
+  if (!dB) {  // unregistered weights: this call's own upload
+    if ((rc = h2d(d + o_w, B, wbytes, o_w))) return rc;
+    dB = d + o_w;
+  }
+  if (!dS) {
+    if ((rc = h2d(d + o_ws, b_scale, sbytes, o_ws))) return rc;
+    dS = d + o_ws;
+  }
+  rc = run_gemm(q4, M, N, K, (const int8_t *)d, (const float *)(d + o_s), dB, dS, group,
+                (float *)(d + o_c), cols, n0 * 16, nullptr, n0, n1, g_stream);
+  if (rc) return rc;
+  return d2h_rows_sync(C + (size_t)n0 * 16, (size_t)ldc * 4, d + o_c, (size_t)cols * 4, M, o_c);
+}
+
+// Host-pointer Gemm::run (forward.rs:128-158): prep on the device, then GEMM.
+static int host_linear(bool q4, const float *src, int lda, int hsz, int M, int N, int K,
+                       const void *B, const void *b_scale, int group, float *C, int ldc) {
+  int rc = check_gemm(M, N, K, ldc, 0, N / 16 / 4 * 4, group, q4);
+  if (rc) return rc;
+  if (N % 64 != 0) return fail(FGM_CUDA_EINVAL, "N=%d: linear needs N %% 64 == 0", N);
+  if ((rc = check_prep(lda, M, K, hsz, 0, M, false))) return rc;
+  if (M == 0) return FGM_CUDA_OK;
+  if (!src || !B || !b_scale || !C) return fail(FGM_CUDA_EINVAL, "null pointer");
+  std::lock_guard<std::mutex> lk(g_host_mu);
+  if ((rc = ensure_device())) return rc;
+  const void *dB = nullptr, *dS = nullptr;
+  const size_t wbytes = q4 ? (size_t)N * K / 2 : (size_t)N * K;
+  const size_t sbytes = q4 ? (size_t)(K / group) * N * 2 : (size_t)N * 4;
+  if ((rc = reg_find(B, wbytes, &dB))) return rc;
+  if ((rc = reg_find(b_scale, sbytes, &dS))) return rc;
+  const size_t x_len = ((size_t)(M - 1) * lda + K) * 4;
+  const size_t a_len = packed_len(M, K), s_len = (size_t)M * 4, c_len = (size_t)M * N * 4;
+  const size_t o_a = align256(x_len), o_s = o_a + align256(a_len), o_c = o_s + align256(s_len);
+  const size_t o_w = o_c + align256(c_len), o_ws = o_w + (dB ? 0 : align256(wbytes));
+  const size_t total = o_ws + (dS ? 0 : align256(sbytes));
+  if ((rc = stage_reserve(total))) return rc;
+  char *d = g_stage.d;
+  if ((rc = h2d(d, src, x_len, 0))) return rc;
+  if (!dB) {
+    if ((rc = h2d(d + o_w, B, wbytes, o_w))) return rc;
+    dB = d + o_w;
+  }
+  if (!dS) {
+    if ((rc = h2d(d + o_ws, b_scale, sbytes, o_ws))) return rc;
+    dS = d + o_ws;
+  }
+  rc = run_prep((const float *)d, lda, nullptr, nullptr, (float *)(d + o_s), (int8_t *)(d + o_a),
+                M, K, hsz, 0, M, g_stream);
+  if (rc) return rc;
+  rc = run_gemm(q4, M, N, K, (const int8_t *)(d + o_a), (const float *)(d + o_s), dB, dS, group,
+                (float *)(d + o_c), N, 0, nullptr, 0, N / 16, g_stream);
+  if (rc) return rc;
+  return d2h_rows_sync(C, (size_t)ldc * 4, d + o_c, (size_t)N * 4, M, o_c);
+}
+
+}  // namespace fgm
+
+using namespace fgm;
+
+// ===================================================================== C ABI
+extern "C" {
+
+int fgm_cuda_available(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  for (int i = 0; i < n; i++) {
+    cudaDeviceProp p;
+    if (cudaGetDeviceProperties(&p, i) == cudaSuccess && p.major == 10) return 1;
+  }
+  return 0;
+}
+
+int fgm_cuda_init(int device) {
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  int dev = pick_device(device);
+  if (dev < 0) return dev;
+  FGM_TRY(cudaSetDevice(dev));
+  if (g_dev != dev) {
+    if (g_stream) cudaStreamDestroy(g_stream);
+    FGM_TRY(cudaStreamCreateWithFlags(&g_stream, cudaStreamNonBlocking));
+    g_dev = dev;
+  }
+  return FGM_CUDA_OK;
+}
+
+const char *fgm_cuda_last_error(void) { return t_err.c_str(); }
+
+int fgm_cuda_device_status(void) {
+  DevInfo *di = nullptr;
+  int rc = dev_info(&di);
+  if (rc) return rc;
+  FGM_TRY(cudaDeviceSynchronize());
+  int v = 0;
+  FGM_TRY(cudaMemcpy(&v, di->err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (v) {
+    FGM_TRY(cudaMemset(di->err, 0, sizeof(int)));
+    return fail(FGM_CUDA_ETIMEOUT, "a kernel gave up on a bounded wait (code %d)", v);
+  }
+  return FGM_CUDA_OK;
+}
+
+uint64_t fgm_cuda_launch_count(void) { return g_launches.load(); }
+
+int fgm_gemm_q4g_cuda(int M, int N, int K, const int8_t *A, const float *a_scale,
+                      const uint8_t *Bq, const uint16_t *b_scale, int group, float *C, int ldc,
+                      int n0, int n1) {
+  return host_gemm(true, M, N, K, A, a_scale, Bq, b_scale, group, C, ldc, n0, n1);
+}
+
+int fgm_gemm_q8c_cuda(int M, int N, int K, const int8_t *A, const float *a_scale,
+                      const int8_t *B, const float *b_scale, float *C, int ldc, int n0, int n1) {
+  return host_gemm(false, M, N, K, A, a_scale, B, b_scale, 64, C, ldc, n0, n1);
+}
+
+int fgm_linear_q4g_cuda(const float *src, int lda, int hsz, int M, int N, int K,
+                        const uint8_t *Bq, const uint16_t *b_scale, int group, float *C,
+                        int ldc) {
+  return host_linear(true, src, lda, hsz, M, N, K, Bq, b_scale, group, C, ldc);
+}
+
+int fgm_linear_q8c_cuda(const float *src, int lda, int hsz, int M, int N, int K,
+                        const int8_t *B, const float *b_scale, float *C, int ldc) {
+  return host_linear(false, src, lda, hsz, M, N, K, B, b_scale, 64, C, ldc);
+}
+
+int fgm_prep_rows_cuda(const float *src, int lda, float *rot, int8_t *qa, float *qs, int8_t *pa,
+                       int m, int k, int hsz, int r0, int r1) {
+  int rc = check_prep(lda, m, k, hsz, r0, r1, qa != nullptr);
+  if (rc) return rc;
+  if (r0 >= r1) return FGM_CUDA_OK;
+  if (!src || !qs || !pa) return fail(FGM_CUDA_EINVAL, "null pointer");
+  std::lock_guard<std::mutex> lk(g_host_mu);
+  if ((rc = ensure_device())) return rc;
+  const int rend = (r1 + 15) / 16 * 16;
+  // device images cover rows [0, rend) so row indices stay absolute
+  const size_t x_len = ((size_t)(r1 - 1) * lda + k) * 4, rot_len = (size_t)m * k * 4;
+  const size_t qa_len = (size_t)m * k, qs_len = (size_t)m * 4, pa_len = packed_len(rend, k);
+  const size_t o_rot = align256(x_len), o_qa = o_rot + align256(rot_len);
+  const size_t o_qs = o_qa + align256(qa_len), o_pa = o_qs + align256(qs_len);
+  const size_t total = o_pa + align256(pa_len);
+  if ((rc = stage_reserve(total))) return rc;
+  char *d = g_stage.d;
+  // only rows [r0, r1) of src are read
+  if ((rc = h2d(d + (size_t)r0 * lda * 4, src + (size_t)r0 * lda,
+                ((size_t)(r1 - 1 - r0) * lda + k) * 4, 0)))
+    return rc;
+  if (qa && r1 < m && r1 % 16 != 0) {  // tail rows of the last block come from qa
+    const size_t off = (size_t)r1 * k, len = (size_t)(std::min(m, rend) - r1) * k;
+    if ((rc = h2d(d + o_qa + off, qa + off, len, o_qa + off))) return rc;
+  }
+  rc = run_prep((const float *)d, lda, rot ? (float *)(d + o_rot) : nullptr,
+                qa ? (int8_t *)(d + o_qa) : nullptr, (float *)(d + o_qs), (int8_t *)(d + o_pa),
+                m, k, hsz, r0, r1, g_stream);
+  if (rc) return rc;
+  if (rot)
+    FGM_TRY(cudaMemcpyAsync(g_stage.h + o_rot + (size_t)r0 * k * 4, d + o_rot + (size_t)r0 * k * 4,
+                            (size_t)(r1 - r0) * k * 4, cudaMemcpyDeviceToHost, g_stream));
+  if (qa)
+    FGM_TRY(cudaMemcpyAsync(g_stage.h + o_qa + (size_t)r0 * k, d + o_qa + (size_t)r0 * k,
+                            (size_t)(r1 - r0) * k, cudaMemcpyDeviceToHost, g_stream));
+  FGM_TRY(cudaMemcpyAsync(g_stage.h + o_qs + (size_t)r0 * 4, d + o_qs + (size_t)r0 * 4,
+                          (size_t)(r1 - r0) * 4, cudaMemcpyDeviceToHost, g_stream));
+  const size_t pa0 = (size_t)(r0 / 16) * 16 * k, pan = packed_len(rend, k) - pa0;
+  FGM_TRY(cudaMemcpyAsync(g_stage.h + o_pa + pa0, d + o_pa + pa0, pan, cudaMemcpyDeviceToHost,
+                          g_stream));
+  FGM_TRY(cudaStreamSynchronize(g_stream));
+  if (rot) memcpy(rot + (size_t)r0 * k, g_stage.h + o_rot + (size_t)r0 * k * 4,
+                  (size_t)(r1 - r0) * k * 4);
+  if (qa) memcpy(qa + (size_t)r0 * k, g_stage.h + o_qa + (size_t)r0 * k, (size_t)(r1 - r0) * k);
+  memcpy(qs + r0, g_stage.h + o_qs + (size_t)r0 * 4, (size_t)(r1 - r0) * 4);
+  memcpy(pa + pa0, g_stage.h + o_pa + pa0, pan);
+  return FGM_CUDA_OK;
+}
+
+int fgm_quant_act_cuda(const float *x, int rows, int k, int8_t *q, float *scale) {
+  if (rows < 0 || k <= 0 || k % 64 != 0)
+    return fail(FGM_CUDA_EINVAL, "quant_act needs rows >= 0 and k %% 64 == 0 (k=%d)", k);
+  if (rows == 0) return FGM_CUDA_OK;
+  // quantisation alone is prep with no rotation; the packed copy is discarded
+  std::vector<int8_t> pa(packed_len(rows, k));
+  return fgm_prep_rows_cuda(x, k, nullptr, q, scale, pa.data(), rows, k, 0, 0, rows);
+}
+
+int fgm_fwht_cuda(float *x, int n, int hsz) {
+  if (hsz <= 0 || (hsz & (hsz - 1)) != 0 || n < 0 || n % hsz != 0)
+    return fail(FGM_CUDA_EINVAL, "fwht needs hsz a power of two dividing n (n=%d, hsz=%d)", n,
+                hsz);
+  if (n == 0) return FGM_CUDA_OK;
+  // rows of hsz values (padded to a multiple of 64 for the prep kernel's tiles)
+  int k = hsz < 64 ? 64 : hsz;
+  if (n % k != 0) k = hsz;  // cannot happen for hsz >= 64; small hsz uses k = 64 when it divides n
+  if (k % 64 != 0) return fail(FGM_CUDA_EINVAL, "fwht with n=%d, hsz=%d unsupported", n, hsz);
+  const int rows = n / k;
+  std::vector<int8_t> qa((size_t)n), pa(packed_len(rows, k));
+  std::vector<float> qs((size_t)rows);
+  return fgm_prep_rows_cuda(x, k, x, qa.data(), qs.data(), pa.data(), rows, k, hsz, 0, rows);
+}
+
+int fgm_pack_a_cuda(int M, int K, const int8_t *A, int8_t *Ap) {
+  if (M < 0 || K <= 0 || K % 64 != 0) return fail(FGM_CUDA_EINVAL, "pack_a: K %% 64 != 0");
+  // pure data movement with no arithmetic: done on the host, like ops.c:279
+  const int KB = K / 64, MB = (M + 15) / 16;
+  for (int mb = 0; mb < MB; mb++)
+    for (int kb = 0; kb < KB; kb++) {
+      int8_t *d = Ap + ((size_t)mb * KB + kb) * 1024;
+      for (int r = 0; r < 16; r++) {
+        const int m = mb * 16 + r;
+        if (m < M) memcpy(d + r * 64, A + (size_t)m * K + kb * 64, 64);
+        else memset(d + r * 64, 0, 64);
+      }
+    }
+  return FGM_CUDA_OK;
+}
+
+int fgm_cuda_register(const void *host, size_t bytes) {
+  if (!host || !bytes) return fail(FGM_CUDA_EINVAL, "register: null pointer or zero size");
+  int rc = ensure_device();
+  if (rc) return rc;
+  const void *d;
+  return reg_upload(host, bytes, &d);
+}
+
+int fgm_cuda_unregister(const void *host) {
+  std::lock_guard<std::mutex> lk(g_reg_mu);
+  auto it = g_reg.find(host);
+  if (it == g_reg.end()) return fail(FGM_CUDA_EINVAL, "unregister: %p not registered", host);
+  cudaFree(it->second.dev);
+  g_reg_bytes -= it->second.bytes;
+  g_reg.erase(it);
+  return FGM_CUDA_OK;
+}
+
+const void *fgm_cuda_lookup(const void *host) {
+  std::lock_guard<std::mutex> lk(g_reg_mu);
+  auto it = g_reg.find(host);
+  return it == g_reg.end() ? nullptr : it->second.dev;
+}
+
+size_t fgm_cuda_registry_bytes(void) {
+  std::lock_guard<std::mutex> lk(g_reg_mu);
+  return g_reg_bytes;
+}
+
+int fgm_cuda_gemm_q4g(int M, int N, int K, const int8_t *A, const float *a_scale,
+                      const uint8_t *Bq, const uint16_t *b_scale, int group, float *C, int ldc,
+                      int n0, int n1, void *stream) {
+  int rc = check_gemm(M, N, K, ldc, n0, n1, group, true);
+  if (rc) return rc;
+  if (M > 0 && n0 < n1 && (!A || !a_scale || !Bq || !b_scale || !C))
+    return fail(FGM_CUDA_EINVAL, "null pointer");
+  return run_gemm(true, M, N, K, A, a_scale, Bq, b_scale, group, C, ldc, 0, nullptr, n0, n1,
+                  (cudaStream_t)stream);
+}
+
+int fgm_cuda_gemm_q8c(int M, int N, int K, const int8_t *A, const float *a_scale,
+                      const int8_t *B, const float *b_scale, float *C, int ldc, int n0, int n1,
+                      void *stream) {
+  int rc = check_gemm(M, N, K, ldc, n0, n1, 64, false);
+  if (rc) return rc;
+  if (M > 0 && n0 < n1 && (!A || !a_scale || !B || !b_scale || !C))
+    return fail(FGM_CUDA_EINVAL, "null pointer");
+  return run_gemm(false, M, N, K, A, a_scale, B, b_scale, 64, C, ldc, 0, nullptr, n0, n1,
+                  (cudaStream_t)stream);
+}
+
+int fgm_cuda_prep_rows(const float *src, int lda, float *rot, int8_t *qa, float *qs, int8_t *pa,
+                       int m, int k, int hsz, int r0, int r1, void *stream) {
+  int rc = check_prep(lda, m, k, hsz, r0, r1, qa != nullptr);
+  if (rc) return rc;
+  if (r0 < r1 && (!src || !qs || !pa)) return fail(FGM_CUDA_EINVAL, "null pointer");
+  return run_prep(src, lda, rot, qa, qs, pa, m, k, hsz, r0, r1, (cudaStream_t)stream);
+}
+
+int fgm_cuda_gemm_q4g_acc(int M, int N, int K, const int8_t *A, const uint8_t *Bq, int group,
+                          int32_t *acc, int n0, int n1, void *stream) {
+  int rc = check_gemm(M, N, K, N, n0, n1, group, true);
+  if (rc) return rc;
+  if (M > 0 && n0 < n1 && (!A || !Bq || !acc)) return fail(FGM_CUDA_EINVAL, "null pointer");
+  return run_gemm(true, M, N, K, A, nullptr, Bq, nullptr, group, nullptr, N, 0, acc, n0, n1,
+                  (cudaStream_t)stream);
+}
+
+int fgm_cuda_gemm_q8c_acc(int M, int N, int K, const int8_t *A, const int8_t *B, int32_t *acc,
+                          int n0, int n1, void *stream) {
+  int rc = check_gemm(M, N, K, N, n0, n1, 64, false);
+  if (rc) return rc;
+  if (M > 0 && n0 < n1 && (!A || !B || !acc)) return fail(FGM_CUDA_EINVAL, "null pointer");
+  return run_gemm(false, M, N, K, A, nullptr, B, nullptr, 64, nullptr, N, 0, acc, n0, n1,
+                  (cudaStream_t)stream);
+}
+
+}  // extern "C"

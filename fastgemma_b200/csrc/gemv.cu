@@ -1,0 +1,738 @@
+// Decode-shaped quantised GEMM: C[M, N] for M <= 16 rows per CTA row block,
+// reading the .fgm weight tiles exactly as the converter wrote them.
+//
+// Reference: fgm_gemm_q4g / fgm_gemm_q8c (amx_gemm.c:333-475, small-M path
+// INNER_Q4_1x4 :300-331) and their VNNI twins (vnni_gemm.c:224-322).
+//
+// Why the tile layout needs no repack for the tensor cores
+// --------------------------------------------------------
+// mma.sync.m16n8k32 (s8) takes its A operand as four 32-bit registers per
+// thread; thread (g, t) of a warp (g = lane/4, t = lane%4) holds rows g and
+// g+8, k-quads t and 4+t.  With the weights as A (16 output channels x 32 k)
+// and the activations as B (32 k x 8 batch rows):
+//  * int8 tile row r (64 bytes) holds, at byte 4n, the four k = 4r..4r+3 of
+//    channel n (convert/quant.py:96-107), so the word (r, n) is one register;
+//  * int4 tile row r (32 bytes) holds, at byte 4q, channel q in the low
+//    nibbles and channel q+8 in the high nibbles of the same four k
+//    (quant.py:76-82), so ONE 32-bit word yields a row-g and a row-g+8
+//    register after a mask: (w << 4) & 0xF0F0F0F0 and w & 0xF0F0F0F0.
+// The int4 registers carry 16 * value (nibble in the high half of its byte,
+// two's complement), so the int32 sums are 16x the true ones; the factor is
+// taken out of the scale (s * 2^-4, exact) or shifted out exactly.
+//
+// Memory pipeline
+// ---------------
+// The kernel is persistent.  The work unit is one n-block (16 output columns)
+// over all of K; a "team" of P warps shares a unit, warp p taking the p-th
+// group-aligned slice of K (P = 1 for wide N, more when N has too few
+// n-blocks to occupy every warp).  Each warp streams its slices through a
+// private ring of shared-memory stages, one cp.async.bulk per stage (a
+// unit's tiles are contiguous in the [N/16][K/64] order, so a stage of 8
+// int4 tiles is one 4 KB copy), refilled as soon as a stage is consumed,
+// across unit boundaries.  The f16 scale rows do not go through the copy
+// engine: each lane loads one 32-bit word of the rows a stage needs, two
+// stages ahead, and the values reach their users by warp shuffles.  Weight
+// prefetch does not depend on earlier kernels: under programmatic dependent
+// launch the ring fills before griddepcontrol.wait, which guards only
+// activation reads and output writes.  The activations of the CTA's row
+// block are staged once in shared memory in the order the B fragments want
+// (k-quads t, 4+t, 8+t, 12+t adjacent): one 128-bit load per tile and 8 rows.
+//
+// Reduction order and bit-exactness
+// ---------------------------------
+// Tiles are summed per scale group in int32 (exact).  With P = 1 the warp
+// folds each completed group into its f32 outputs right away:
+// c = fmaf((float)acc_g, s_g, c), ascending g, then c * a_scale -- the drain
+// of amx_gemm.c:103-113 and the final scaling of :365-371.  With P > 1 the
+// parts publish their int32 group sums in shared memory and the team folds
+// all groups of a unit in ascending order once every part is done.  int8:
+// acc * (b_scale * a_scale) (amx_gemm.c:399); parts add int32 partials.
+// Every f32 operation is an explicit _rn intrinsic.
+
+#include "fgm_common.cuh"
+#include "fgm_internal.h"
+#include "tc_ptx.cuh"
+
+namespace fgm {
+
+namespace {
+
+constexpr int kMaxWarps = 16;
+
+template <bool Q4>
+struct Geo {
+  static constexpr int TB = Q4 ? kQ4Tile : kQ8Tile;  // bytes per weight tile
+  static constexpr int T = Q4 ? 8 : 4;               // tiles per ring stage
+};
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes,
+                                         uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(dst),
+      "l"(src), "r"(bytes), "r"(tc::smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void team_sync(int team, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(team + 1), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(a));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t ldg_stream_u32(const void *p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ float f16_to_f32(uint32_t bits16) {
+  return __half2float(__ushort_as_half((unsigned short)bits16));
+}
+
+// The scale pair (columns g and g+8 of a group row) of thread (g, .), from the
+// 8-word row held one word per lane at lanes base..base+7 of register v.
+__device__ __forceinline__ void scale_pair(uint32_t v, int base, int g8, float &s0, float &s1) {
+  const uint32_t w0 = __shfl_sync(0xffffffffu, v, base + (g8 >> 1));
+  const uint32_t w1 = __shfl_sync(0xffffffffu, v, base + 4 + (g8 >> 1));
+  const int sh = (g8 & 1) * 16;
+  s0 = f16_to_f32(w0 >> sh);
+  s1 = f16_to_f32(w1 >> sh);
+}
+
+// Per-lane constants shared by the stage routines.
+struct Lane {
+  int g8, tig, lane;
+  uint32_t w_off;  // weight word (row tig, column g8) inside a tile
+  uint32_t a_off;  // activation row g8, k-quads t..12+t, inside a tile's 8 rows
+};
+
+// One ring stage of NT tiles, NT a compile-time count (no per-tile guards, so
+// all of the stage's loads are issued before its MMAs).  MODE 0: fold each
+// completed scale group into cf (int4, P = 1).  MODE 1: publish each
+// completed group's int32 sum to pub[g][row][col] (int4 split K or int32
+// output).  MODE 2: accumulate into gacc (int8).  Stages start on a group
+// boundary (GK divides NT).
+template <bool Q4, int MT, int GK, int NT, int MODE>
+__device__ __forceinline__ void stage_full(uint32_t st, uint32_t ab, const Lane &L, int g0,
+                                           uint32_t sc0, uint32_t sc1, float (&cf)[MT][4],
+                                           int32_t (&gacc)[MT][4], int32_t *pub,
+                                           uint32_t *pub_sc) {
+  constexpr int TB = Geo<Q4>::TB;
+  uint32_t w[NT][Q4 ? 4 : 8];
+  uint32_t b[NT][MT][4];
+#pragma unroll
+  for (int t = 0; t < NT; t++) {
+#pragma unroll
+    for (int q = 0; q < 4; q++) {  // tile rows q*4 + tig
+      if (Q4) {
+        w[t][q] = lds32(st + t * TB + L.w_off + q * 128);
+      } else {
+        w[t][2 * q] = lds32(st + t * TB + L.w_off + q * 256);
+        w[t][2 * q + 1] = lds32(st + t * TB + L.w_off + q * 256 + 32);
+      }
+    }
+#pragma unroll
+    for (int mt = 0; mt < MT; mt++) {
+      const uint4 v = lds128(ab + (t * MT + mt) * 512 + L.a_off);
+      b[t][mt][0] = v.x;
+      b[t][mt][1] = v.y;
+      b[t][mt][2] = v.z;
+      b[t][mt][3] = v.w;
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < NT; t++) {
+    int32_t ta[MT][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; mt++) {
+      if (Q4) {
+        mma_s8_m16n8k32_c(ta[mt], nib_lo_x16(w[t][0]), nib_hi_x16(w[t][0]), nib_lo_x16(w[t][1]),
+                          nib_hi_x16(w[t][1]), b[t][mt][0], b[t][mt][1], 0, 0, 0, 0);
+        mma_s8_m16n8k32_c(ta[mt], nib_lo_x16(w[t][2]), nib_hi_x16(w[t][2]), nib_lo_x16(w[t][3]),
+                          nib_hi_x16(w[t][3]), b[t][mt][2], b[t][mt][3], ta[mt][0], ta[mt][1],
+                          ta[mt][2], ta[mt][3]);
+      } else {
+        mma_s8_m16n8k32_c(ta[mt], w[t][0], w[t][1], w[t][2], w[t][3], b[t][mt][0], b[t][mt][1], 0,
+                          0, 0, 0);
+        mma_s8_m16n8k32_c(ta[mt], w[t][4], w[t][5], w[t][6], w[t][7], b[t][mt][2], b[t][mt][3],
+                          ta[mt][0], ta[mt][1], ta[mt][2], ta[mt][3]);
+      }
+    }
+    if (MODE == 2) {
+#pragma unroll
+      for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) gacc[mt][i] += ta[mt][i];
+      continue;
+    }
+#pragma unroll
+    for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) gacc[mt][i] = (t % GK == 0) ? ta[mt][i] : gacc[mt][i] + ta[mt][i];
+    if ((t + 1) % GK != 0) continue;  // group not complete yet
+    const int lg = t / GK;            // group index inside the stage
+    if (MODE == 0) {
+      float s0, s1;
+      scale_pair(lg < 4 ? sc0 : sc1, (lg & 3) * 8, L.g8, s0, s1);
+      s0 = __fmul_rn(s0, 0.0625f);
+      s1 = __fmul_rn(s1, 0.0625f);
+#pragma unroll
+      for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+          cf[mt][i] = __fmaf_rn(__int2float_rn(gacc[mt][i]), i < 2 ? s0 : s1, cf[mt][i]);
+    } else {
+#pragma unroll
+      for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+          pub[((size_t)(g0 + lg) * MT * 8 + mt * 8 + 2 * L.tig + (i & 1)) * 16 + L.g8 +
+              (i >= 2 ? 8 : 0)] = gacc[mt][i] >> 4;
+      if (pub_sc && (L.lane >> 3) == (lg & 3))  // the 8 lanes holding this row
+        pub_sc[(size_t)(g0 + lg) * 8 + (L.lane & 7)] = lg < 4 ? sc0 : sc1;
+    }
+  }
+  if (MODE != 2)  // the stage ended on a group boundary: nothing carries over
+#pragma unroll
+    for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) gacc[mt][i] = 0;
+}
+
+// Any stage the fast path does not cover: a partial stage, activations read
+// from global memory, or scale groups that straddle stages.  Scales are read
+// from global memory here.  gacc carries a group across stage boundaries.
+template <bool Q4, int MT, int GK, int MODE>
+__device__ __forceinline__ void stage_generic(uint32_t st, uint32_t a_sm, const int8_t *abase,
+                                              bool a_in, const Lane &L, int gt0, int nt, int gk,
+                                              int nb, const GemvParams &p, uint32_t sc0,
+                                              uint32_t sc1, float (&cf)[MT][4],
+                                              int32_t (&gacc)[MT][4], int32_t *pub, int gbase,
+                                              uint32_t *pub_sc) {
+  constexpr int TB = Geo<Q4>::TB;
+  for (int t = 0; t < nt; t++) {
+    const int gt = gt0 + t;
+    uint32_t w[Q4 ? 4 : 8];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      if (Q4) {
+        w[q] = lds32(st + t * TB + L.w_off + q * 128);
+      } else {
+        w[2 * q] = lds32(st + t * TB + L.w_off + q * 256);
+        w[2 * q + 1] = lds32(st + t * TB + L.w_off + q * 256 + 32);
+      }
+    }
+    uint32_t b[MT][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; mt++) {
+      if (a_in) {
+        const uint4 v = lds128(a_sm + (gt * MT + mt) * 512 + L.a_off);
+        b[mt][0] = v.x;
+        b[mt][1] = v.y;
+        b[mt][2] = v.z;
+        b[mt][3] = v.w;
+      } else {
+        const int8_t *ar = abase + (size_t)gt * kATile + (mt * 8 + L.g8) * 64 + L.tig * 4;
+        b[mt][0] = ld_shared_ro_u32(ar);
+        b[mt][1] = ld_shared_ro_u32(ar + 16);
+        b[mt][2] = ld_shared_ro_u32(ar + 32);
+        b[mt][3] = ld_shared_ro_u32(ar + 48);
+      }
+    }
+    int32_t ta[MT][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; mt++) {
+      if (Q4) {
+        mma_s8_m16n8k32_c(ta[mt], nib_lo_x16(w[0]), nib_hi_x16(w[0]), nib_lo_x16(w[1]),
+                          nib_hi_x16(w[1]), b[mt][0], b[mt][1], 0, 0, 0, 0);
+        mma_s8_m16n8k32_c(ta[mt], nib_lo_x16(w[2]), nib_hi_x16(w[2]), nib_lo_x16(w[3]),
+                          nib_hi_x16(w[3]), b[mt][2], b[mt][3], ta[mt][0], ta[mt][1], ta[mt][2],
+                          ta[mt][3]);
+      } else {
+        mma_s8_m16n8k32_c(ta[mt], w[0], w[1], w[2], w[3], b[mt][0], b[mt][1], 0, 0, 0, 0);
+        mma_s8_m16n8k32_c(ta[mt], w[4], w[5], w[6], w[7], b[mt][2], b[mt][3], ta[mt][0],
+                          ta[mt][1], ta[mt][2], ta[mt][3]);
+      }
+    }
+#pragma unroll
+    for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) gacc[mt][i] += ta[mt][i];
+    if (MODE == 2) continue;
+    if ((gt + 1) % gk != 0) continue;
+    const int g = gt / gk;
+    const int lg = (gt - gt0) / gk;  // group index inside the stage (GK > 0 only)
+    if (MODE == 0) {
+      float s0, s1;
+      if (GK) {  // groups tile the stage: the prefetched rows hold this group
+        scale_pair(lg < 4 ? sc0 : sc1, (lg & 3) * 8, L.g8, s0, s1);
+      } else {
+        const __half *sr =
+            reinterpret_cast<const __half *>(p.b_scale) + (size_t)g * p.N + nb * 16;
+        s0 = __half2float(sr[L.g8]);
+        s1 = __half2float(sr[L.g8 + 8]);
+      }
+#pragma unroll
+      for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+          cf[mt][i] = __fmaf_rn(__int2float_rn(gacc[mt][i] >> 4), i < 2 ? s0 : s1, cf[mt][i]);
+    } else {
+#pragma unroll
+      for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+          pub[((size_t)(g - gbase) * MT * 8 + mt * 8 + 2 * L.tig + (i & 1)) * 16 + L.g8 +
+              (i >= 2 ? 8 : 0)] = gacc[mt][i] >> 4;
+      if (pub_sc) {
+        if (GK) {
+          if ((L.lane >> 3) == (lg & 3))
+            pub_sc[(size_t)(g - gbase) * 8 + (L.lane & 7)] = lg < 4 ? sc0 : sc1;
+        } else if (L.lane < 8) {
+          pub_sc[(size_t)(g - gbase) * 8 + L.lane] = *reinterpret_cast<const uint32_t *>(
+              reinterpret_cast<const uint8_t *>(p.b_scale) +
+              ((size_t)g * p.N + (size_t)nb * 16) * 2 + L.lane * 4);
+        }
+      }
+    }
+#pragma unroll
+    for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) gacc[mt][i] = 0;
+  }
+}
+
+template <bool Q4, int MT, int GK>
+__global__ void __launch_bounds__(kMaxWarps * 32, 1)
+    gemv_kernel(const GemvParams p, const GemvPlan pl) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int s_abort;
+  constexpr int TB = Geo<Q4>::TB;
+  constexpr int T = Geo<Q4>::T;
+  const bool raw = p.acc != nullptr;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, NW = blockDim.x >> 5;
+  const int P = pl.parts, team = warp / P, part = warp % P, teams = NW / P;
+  const int KB = p.K / kTileK;
+  const int gk = Q4 ? (GK ? GK : p.group / kTileK) : KB;
+  const int G = KB / gk;
+  const int ptiles = KB / P;
+  const int nch = (ptiles + T - 1) / T;
+  const int S = pl.stages;
+  // int4: part 0 of a team folds its groups in registers as they complete;
+  // the other parts publish int32 group sums to the team's shared area (as
+  // does every part for int32 output); int8: accumulate.
+  const bool fold = Q4 && !raw && part == 0;
+  const bool want_sc = Q4 && !raw;            // this warp needs its groups' scales
+  const int gpub = (Q4 && !raw) ? G / P : 0;  // first group held in the shared area
+  uint8_t *after_ring = smem + (size_t)NW * S * pl.stage_bytes;
+  int32_t *xsum = reinterpret_cast<int32_t *>(after_ring + (size_t)team * pl.xchg_bytes);
+  // part 0's running f32 outputs, handed to the team after the last group,
+  // then the published groups' f16 scale rows (8 words each)
+  float *cpart = reinterpret_cast<float *>(xsum + (size_t)(G - gpub) * MT * 128);
+  uint32_t *xscale = reinterpret_cast<uint32_t *>(cpart + MT * 128);
+  uint32_t *pub_sc = (Q4 && !raw && P > 1) ? xscale : nullptr;
+  uint32_t *a_sm = reinterpret_cast<uint32_t *>(after_ring + (size_t)teams * pl.xchg_bytes);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(a_sm) + pl.a_bytes) +
+                   warp * S;
+  const uint32_t ring = tc::smem_u32(smem) + (uint32_t)(warp * S * pl.stage_bytes);
+  const uint32_t a_sm_u = tc::smem_u32(a_sm);
+  const int mb = blockIdx.y;
+  const int8_t *abase = p.A + (size_t)mb * KB * kATile;
+
+  Lane L;
+  L.lane = lane;
+  L.g8 = lane >> 2;
+  L.tig = lane & 3;
+  L.w_off = Q4 ? (uint32_t)(L.tig * 32 + L.g8 * 4) : (uint32_t)(L.tig * 64 + L.g8 * 4);
+  L.a_off = (uint32_t)(L.g8 * 64 + L.tig * 16);
+
+  if (threadIdx.x == 0) s_abort = 0;
+  if (lane == 0) {
+    for (int s = 0; s < S; s++) tc::mbar_init(&bars[s], 1);
+    tc::fence_mbar_init();
+  }
+  if (P > 1 && !Q4)
+    for (int i = threadIdx.x; i < teams * MT * 128; i += blockDim.x)
+      reinterpret_cast<int32_t *>(after_ring + (size_t)(i / (MT * 128)) * pl.xchg_bytes)
+          [i % (MT * 128)] = 0;
+  __syncthreads();
+  pdl_launch_dependents();
+
+  const int tstride = gridDim.x * teams;
+  const int unit0 = blockIdx.x * teams + team;
+  const int my_units = unit0 < pl.units ? (pl.units - unit0 + tstride - 1) / tstride : 0;
+  const int items = my_units * nch;
+
+  // issue cursor: (unit index, stage) of the next stage to fetch and its slot
+  int iu = 0, ic = 0, islot = 0;
+  auto issue = [&]() {
+    const int nb = p.nb0 + unit0 + iu * tstride;
+    const int gt0 = part * ptiles + ic * T;
+    const int gt1 = min(gt0 + T, (part + 1) * ptiles);
+    const uint32_t wbytes = (uint32_t)(gt1 - gt0) * TB;
+    if (lane == 0) {
+      tc::mbar_expect_tx(&bars[islot], wbytes);
+      bulk_g2s(ring + islot * pl.stage_bytes, p.B + ((size_t)nb * KB + gt0) * TB, wbytes,
+               &bars[islot]);
+    }
+    if (++ic == nch) {
+      ic = 0;
+      iu++;
+    }
+    if (++islot == S) islot = 0;
+  };
+  // scale cursor (int4 fold): lane l holds word l%8 of the stage's group rows
+  // glo + l/8 and glo + 4 + l/8, fetched two stages ahead
+  int su = 0, sch = 0;
+  auto scale_fetch = [&](uint32_t &r0, uint32_t &r1) {
+    r0 = r1 = 0;
+    if (su >= my_units) return;
+    const int nb = p.nb0 + unit0 + su * tstride;
+    const int gt0 = part * ptiles + sch * T;
+    const int gt1 = min(gt0 + T, (part + 1) * ptiles);
+    const int glo = gt0 / gk, ng = gt1 / gk - glo;
+    const uint8_t *row = reinterpret_cast<const uint8_t *>(p.b_scale) +
+                         ((size_t)glo * p.N + (size_t)nb * 16) * 2 + (lane & 7) * 4;
+    const int r = lane >> 3;
+    if (r < ng) r0 = ldg_stream_u32(row + (size_t)r * p.N * 2);
+    if (r + 4 < ng) r1 = ldg_stream_u32(row + (size_t)(r + 4) * p.N * 2);
+    if (++sch == nch) {
+      sch = 0;
+      su++;
+    }
+  };
+
+  const int prologue = items < S ? items : S;
+  for (int it = 0; it < prologue; it++) issue();
+  uint32_t sc_a0 = 0, sc_a1 = 0, sc_b0 = 0, sc_b1 = 0;  // stages it and it+1
+  if (want_sc && GK) {
+    scale_fetch(sc_a0, sc_a1);
+    scale_fetch(sc_b0, sc_b1);
+  }
+  pdl_wait();  // activations and outputs are ordered after earlier kernels
+
+  if (pl.a_bytes) {  // stage this row block's activations, B-fragment order
+    // 16-byte pieces: piece c of a 64-byte row holds k-quads 4c..4c+3, which
+    // land at word positions j*4 + c.  Loads go out in independent batches.
+    constexpr int kBatchLd = 8;
+    const int pieces = KB * MT * 8 * 4;
+    for (int base = threadIdx.x; base < pieces; base += kBatchLd * blockDim.x) {
+      uint4 v[kBatchLd];
+#pragma unroll
+      for (int u = 0; u < kBatchLd; u++) {
+        const int i = base + u * blockDim.x;
+        if (i < pieces) {
+          const int c = i & 3, row = (i >> 2) % (MT * 8), tile = (i >> 2) / (MT * 8);
+          v[u] = *reinterpret_cast<const uint4 *>(abase + (size_t)tile * kATile + row * 64 + c * 16);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kBatchLd; u++) {
+        const int i = base + u * blockDim.x;
+        if (i < pieces) {
+          const int c = i & 3, rowg = i >> 2;  // rowg = tile * MT*8 + row
+          uint32_t *d = a_sm + (rowg << 4) + c;
+          d[0] = v[u].x;
+          d[4] = v[u].y;
+          d[8] = v[u].z;
+          d[12] = v[u].w;
+        }
+      }
+    }
+    __syncthreads();
+  }
+
+  float cf[MT][4];
+  int32_t gacc[MT][4];
+  int cu = 0, cc = 0, cslot = 0;
+  uint32_t cphase = 0;
+  for (int it = 0; it < items; it++) {
+    const int nb = p.nb0 + unit0 + cu * tstride;
+    const int gt0 = part * ptiles + cc * T;
+    const int nt = min(T, (part + 1) * ptiles - gt0);
+    if (cc == 0) {
+#pragma unroll
+      for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          cf[mt][i] = 0.0f;
+          gacc[mt][i] = 0;
+        }
+    }
+    const uint32_t sc0 = sc_a0, sc1 = sc_a1;
+    if (want_sc && GK) {  // rotate the two-ahead scale prefetch
+      sc_a0 = sc_b0;
+      sc_a1 = sc_b1;
+      scale_fetch(sc_b0, sc_b1);
+    }
+    bool ok = !*reinterpret_cast<volatile int *>(&s_abort) && tc::mbar_wait(&bars[cslot], cphase);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) {
+      s_abort = 1;
+      if (lane == 0 && p.err) atomicExch(p.err, 1);
+    }
+    const uint32_t st = ring + cslot * pl.stage_bytes;
+    if (ok) {
+      const bool fast = GK && pl.a_bytes && nt == T;
+      const uint32_t ab = a_sm_u + (uint32_t)(gt0 * MT * 512);
+      const bool a_in = pl.a_bytes != 0;
+      if (!Q4) {
+        if (fast) stage_full<Q4, MT, 1, T, 2>(st, ab, L, 0, 0, 0, cf, gacc, nullptr, nullptr);
+        else
+          stage_generic<Q4, MT, 0, 2>(st, a_sm_u, abase, a_in, L, gt0, nt, gk, nb, p, 0, 0, cf,
+                                      gacc, nullptr, 0, nullptr);
+      } else if (fold) {
+        if (fast)
+          stage_full<Q4, MT, GK ? GK : 1, T, 0>(st, ab, L, 0, sc0, sc1, cf, gacc, nullptr,
+                                                nullptr);
+        else
+          stage_generic<Q4, MT, GK, 0>(st, a_sm_u, abase, a_in, L, gt0, nt, gk, nb, p, sc0, sc1,
+                                       cf, gacc, nullptr, 0, nullptr);
+      } else {
+        if (fast)
+          stage_full<Q4, MT, GK ? GK : 1, T, 1>(st, ab, L, gt0 / gk - gpub, sc0, sc1, cf, gacc,
+                                                xsum, pub_sc);
+        else
+          stage_generic<Q4, MT, GK, 1>(st, a_sm_u, abase, a_in, L, gt0, nt, gk, nb, p, sc0, sc1,
+                                       cf, gacc, xsum, gpub, pub_sc);
+      }
+    }
+    __syncwarp();
+    fence_proxy_async_smem();
+    if (ok && it + S < items) issue();
+    if (++cslot == S) {
+      cslot = 0;
+      cphase ^= 1u;
+    }
+    const bool unit_done = (cc == nch - 1);
+    if (++cc == nch) {
+      cc = 0;
+      cu++;
+    }
+    if (!unit_done) continue;
+
+    // ---- this warp's part of unit nb is done
+    if (P == 1) {
+      if (!ok) continue;
+      if (Q4 && raw) {  // the warp's published group sums -> acc[m][g][n]
+        __syncwarp();
+        for (int o = lane; o < G * MT * 128; o += 32) {
+          const int g = o / (MT * 128), r = o % (MT * 128), ml = r >> 4, nl = r & 15;
+          const int m = mb * 16 + ml;
+          if (m < p.M) p.acc[((size_t)m * G + g) * p.N + nb * 16 + nl] = xsum[o];
+        }
+        __syncwarp();
+        continue;
+      }
+#pragma unroll
+      for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const int m = mb * 16 + mt * 8 + 2 * L.tig + (i & 1);
+          const int n = nb * 16 + L.g8 + (i >= 2 ? 8 : 0);
+          if (m >= p.M) continue;
+          if (raw) {
+            p.acc[(size_t)m * p.N + n] = gacc[mt][i];
+          } else if (Q4) {
+            p.C[(size_t)m * p.ldc + (n - p.c_col0)] = __fmul_rn(cf[mt][i], p.a_scale[m]);
+          } else {
+            const float bs = reinterpret_cast<const float *>(p.b_scale)[n];
+            p.C[(size_t)m * p.ldc + (n - p.c_col0)] =
+                __fmul_rn(__int2float_rn(gacc[mt][i]), __fmul_rn(bs, p.a_scale[m]));
+          }
+        }
+      continue;
+    }
+    if (!Q4) {  // int8 split K: add the int32 partials
+#pragma unroll
+      for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+          atomicAdd(&xsum[(mt * 8 + 2 * L.tig + (i & 1)) * 16 + L.g8 + (i >= 2 ? 8 : 0)],
+                    gacc[mt][i]);
+    }
+    if (Q4 && !raw && part == 0 && ok) {  // hand the chain over to the team
+#pragma unroll
+      for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+          cpart[(mt * 8 + 2 * L.tig + (i & 1)) * 16 + L.g8 + (i >= 2 ? 8 : 0)] = cf[mt][i];
+    }
+    team_sync(team, P * 32);
+    for (int o = part * 32 + lane; o < MT * 128; o += P * 32) {
+      const int ml = o >> 4, nl = o & 15;
+      const int m = mb * 16 + ml, n = nb * 16 + nl;
+      if (Q4) {
+        if (m >= p.M) continue;
+        if (raw) {
+          for (int g = 0; g < G; g++)
+            p.acc[((size_t)m * G + g) * p.N + n] = xsum[(g * MT * 8 + ml) * 16 + nl];
+          continue;
+        }
+        // continue part 0's chain through the published groups, in order
+        const __half *sc = reinterpret_cast<const __half *>(xscale) + nl;
+        float c = cpart[o];
+#pragma unroll 8
+        for (int g = gpub; g < G; g++)
+          c = __fmaf_rn(__int2float_rn(xsum[((g - gpub) * MT * 8 + ml) * 16 + nl]),
+                        __half2float(sc[(size_t)(g - gpub) * 16]), c);
+        p.C[(size_t)m * p.ldc + (n - p.c_col0)] = __fmul_rn(c, p.a_scale[m]);
+      } else {
+        const int32_t v = xsum[ml * 16 + nl];
+        xsum[ml * 16 + nl] = 0;
+        if (m >= p.M) continue;
+        if (raw) {
+          p.acc[(size_t)m * p.N + n] = v;
+        } else {
+          const float bs = reinterpret_cast<const float *>(p.b_scale)[n];
+          p.C[(size_t)m * p.ldc + (n - p.c_col0)] =
+              __fmul_rn(__int2float_rn(v), __fmul_rn(bs, p.a_scale[m]));
+        }
+      }
+    }
+    team_sync(team, P * 32);
+  }
+}
+
+template <bool Q4, int MT, int GK>
+cudaError_t launch_t(const GemvParams &p, const GemvPlan &pl, dim3 grid, bool pdl,
+                     cudaStream_t st) {
+  auto kern = gemv_kernel<Q4, MT, GK>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)pl.smem_bytes);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(pl.warps * 32);
+  cfg.dynamicSmemBytes = pl.smem_bytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, p, pl);
+}
+
+template <bool Q4, int MT>
+cudaError_t launch_gk(const GemvParams &p, const GemvPlan &pl, dim3 grid, bool pdl,
+                      cudaStream_t st) {
+  if (!Q4) return launch_t<Q4, MT, 1>(p, pl, grid, pdl, st);
+  switch (p.group / kTileK) {  // groups that tile a stage exactly
+    case 1: return launch_t<Q4, MT, 1>(p, pl, grid, pdl, st);
+    case 2: return launch_t<Q4, MT, 2>(p, pl, grid, pdl, st);
+    case 4: return launch_t<Q4, MT, 4>(p, pl, grid, pdl, st);
+    case 8: return launch_t<Q4, MT, 8>(p, pl, grid, pdl, st);
+    default: return launch_t<Q4, MT, 0>(p, pl, grid, pdl, st);  // groups spanning stages
+  }
+}
+
+}  // namespace
+
+// Pick the warp team size, warps per CTA, ring depth, activation staging and
+// grid for a launch.
+GemvPlan plan_gemv(const GemvParams &p, int nblocks, bool q4, int num_sms, size_t smem_limit) {
+  GemvPlan pl{};
+  const int MT = p.M <= 8 ? 1 : 2;
+  const int KB = p.K / kTileK, gk = q4 ? p.group / kTileK : KB, G = KB / gk;
+  const int TB = q4 ? kQ4Tile : kQ8Tile;
+  const int T = q4 ? Geo<true>::T : Geo<false>::T;
+  const bool raw = p.acc != nullptr;
+  pl.warps = kMaxWarps;
+  pl.units = nblocks;
+  pl.parts = 1;
+  pl.ctas_per_sm = 1;
+  pl.chunk_tiles = T;
+  // team size: enough (unit, part) pairs to give every warp of the grid work
+  int Pmax = 1;
+  const int want = num_sms * kMaxWarps;
+  while (Pmax < kMaxWarps && (long)nblocks * Pmax * 2 <= want) {
+    const int P2 = Pmax * 2;
+    const bool parts_ok = q4 ? (G % P2 == 0) : (KB % P2 == 0);
+    if (!parts_ok) break;
+    Pmax = P2;
+  }
+  pl.stage_bytes = (T * TB + 127) / 128 * 128;
+  const size_t a_bytes = (size_t)KB * MT * 8 * 64;
+  // Largest team size whose exchange area still leaves a useful ring.  Warps
+  // per CTA: enough to cover every (unit, part) pair across all SMs, at most
+  // kMaxWarps, a multiple of the team size.  Then the deepest ring that fits,
+  // preferring activations in shared memory.
+  bool found = false;
+  for (int P = Pmax; P >= 1 && !found; P /= 2) {
+    const long pairs = (long)nblocks * P;
+    int want_warps = (int)((pairs + num_sms - 1) / num_sms);
+    want_warps = (want_warps + P - 1) / P * P;
+    if (want_warps > kMaxWarps) want_warps = kMaxWarps;
+    if (want_warps < P) want_warps = P;
+    size_t xchg = 0;
+    if (q4 && raw) xchg = (size_t)G * MT * 128 * 4;  // every group's int32 sum
+    else if (q4 && P > 1)  // groups of parts 1..P-1 with their scale rows, part 0's chain
+      xchg = (size_t)(G - G / P) * (MT * 128 * 4 + 32) + (size_t)MT * 128 * 4;
+    else if (P > 1) xchg = (size_t)MT * 128 * 4;  // int8 partials
+    const int xchg_bytes = (int)((xchg + 127) / 128 * 128);
+    // fewer warps per CTA when the exchange areas would not fit otherwise
+    for (int warps = want_warps; warps >= P && !found; warps -= P) {
+      const int teams = warps / P;
+      const size_t bars_w = (size_t)warps * 8 * 8;
+      for (int with_a = 1; with_a >= 0 && !found; with_a--) {
+        const size_t fixed = (size_t)teams * xchg_bytes + (with_a ? a_bytes : 0) + bars_w;
+        for (int S = 6; S >= 2; S--) {
+          const size_t total = fixed + (size_t)warps * S * pl.stage_bytes;
+          if (total <= smem_limit) {
+            pl.warps = warps;
+            pl.parts = P;
+            pl.xchg_bytes = xchg_bytes;
+            pl.stages = S;
+            pl.a_bytes = with_a ? (int)a_bytes : 0;
+            pl.smem_bytes = total;
+            found = true;
+            break;
+          }
+        }
+      }
+    }
+  }
+  if (!found) pl.smem_bytes = smem_limit + 1;  // caller reports the failure
+  const int teams = pl.warps / pl.parts;
+  const int ctas_needed = (nblocks + teams - 1) / teams;
+  pl.grid_x = ctas_needed < num_sms ? ctas_needed : num_sms;
+  return pl;
+}
+
+cudaError_t launch_gemv(const GemvParams &p, int nblocks, bool q4, bool pdl, int num_sms,
+                        size_t smem_limit, cudaStream_t st) {
+  if (nblocks <= 0 || p.M <= 0) return cudaSuccess;
+  const GemvPlan pl = plan_gemv(p, nblocks, q4, num_sms, smem_limit);
+  if (pl.smem_bytes > smem_limit) return cudaErrorInvalidConfiguration;
+  const dim3 grid(pl.grid_x, (p.M + 15) / 16);
+  const bool mt1 = p.M <= 8;
+  if (q4)
+    return mt1 ? launch_gk<true, 1>(p, pl, grid, pdl, st) : launch_gk<true, 2>(p, pl, grid, pdl, st);
+  return mt1 ? launch_gk<false, 1>(p, pl, grid, pdl, st) : launch_gk<false, 2>(p, pl, grid, pdl, st);
+}
+
+}  // namespace fgm

@@ -1,0 +1,52 @@
+"""Device-resident entry points (include/fgm_cuda.h, "device pointers").
+
+Every buffer is a CUDA tensor on the current device; work is enqueued on the
+current torch stream (or ``stream=``) and nothing waits.  torch is used only
+for allocation and stream handles; the arithmetic is the library's.
+"""
+from __future__ import annotations
+
+import torch
+
+from ._lib import call
+
+
+def _s(stream):
+    return (stream or torch.cuda.current_stream()).cuda_stream
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def gemm_q4g(M, N, K, A, a_scale, Bq, b_scale, group, C, ldc=None, n0=0, n1=None, stream=None):
+    n1 = N // 16 if n1 is None else n1
+    call("fgm_cuda_gemm_q4g", M, N, K, _p(A), _p(a_scale), _p(Bq), _p(b_scale), group, _p(C),
+         N if ldc is None else ldc, n0, n1, _s(stream))
+
+
+def gemm_q8c(M, N, K, A, a_scale, B, b_scale, C, ldc=None, n0=0, n1=None, stream=None):
+    n1 = N // 16 if n1 is None else n1
+    call("fgm_cuda_gemm_q8c", M, N, K, _p(A), _p(a_scale), _p(B), _p(b_scale), _p(C),
+         N if ldc is None else ldc, n0, n1, _s(stream))
+
+
+def gemm_q4g_acc(M, N, K, A, Bq, group, acc, n0=0, n1=None, stream=None):
+    n1 = N // 16 if n1 is None else n1
+    call("fgm_cuda_gemm_q4g_acc", M, N, K, _p(A), _p(Bq), group, _p(acc), n0, n1, _s(stream))
+
+
+def gemm_q8c_acc(M, N, K, A, B, acc, n0=0, n1=None, stream=None):
+    n1 = N // 16 if n1 is None else n1
+    call("fgm_cuda_gemm_q8c_acc", M, N, K, _p(A), _p(B), _p(acc), n0, n1, _s(stream))
+
+
+def prep_rows(src, lda, qs, pa, m, k, hsz, rot=None, qa=None, r0=0, r1=None, stream=None):
+    r1 = m if r1 is None else r1
+    call("fgm_cuda_prep_rows", _p(src), lda, _p(rot), _p(qa), _p(qs), _p(pa), m, k, hsz, r0, r1,
+         _s(stream))
+
+
+def packed_a(m: int, k: int, device=None) -> torch.Tensor:
+    """An uninitialised packed-activation buffer of ``packed_a_len(m, k)`` bytes."""
+    return torch.empty((m + 15) // 16 * 16 * k, dtype=torch.int8, device=device or "cuda")

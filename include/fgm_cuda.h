@@ -1,0 +1,177 @@
+/*
+ * fgm_cuda.h -- C ABI of the B200 (sm_100a) backend for fastgemma's quantised
+ * GEMM hot path.  Implemented by libfgm_cuda.so (fastgemma_b200/csrc).
+ *
+ * The reference binds its CPU kernels through the `extern "C"` block of
+ * crates/fgm-kernels/src/lib.rs:13-80 and dispatches on `Backend`
+ * (lib.rs:86-138).  This header is what a third backend, `Backend::Cuda`,
+ * binds.  Reference paths are relative to the fastgemma project root.
+ *
+ * Conventions shared by every entry point:
+ *  - Return 0 on success, a negative FGM_CUDA_E* code on failure.  Nothing
+ *    aborts the process; fgm_cuda_last_error() describes the last failure on
+ *    the calling thread.  (The reference returns void and leaves misuse
+ *    undefined; lib.rs:177-178 / :203-204 only debug-assert the shapes.)
+ *  - Shape contract, checked on every call (EINVAL otherwise): K > 0,
+ *    K % 64 == 0, K <= 65536; N > 0, N % 16 == 0; M >= 0;
+ *    0 <= n0 <= n1 <= N/16 and (n1 - n0) % 4 == 0 (n-blocks of 16 columns,
+ *    stepped in fours as pool.rs:121-124 splits them); ldc >= N;
+ *    for int4: group > 0, group % 64 == 0, K % group == 0.
+ *  - A is tile-packed activations [ceil(M/16)][K/64][16][64] int8 with zero
+ *    padding rows (ops.c:279-290); a_scale is f32 [M].
+ *  - int4 weights: the .fgm q4g blob, N*K/2 bytes, tiles [N/16][K/64] of
+ *    512 bytes, nibble-packed (convert/quant.py:76-107); scales f16
+ *    [K/group][N] passed as raw uint16 (model.rs:182).
+ *  - int8 weights: the .fgm q8c blob, N*K bytes, tiles [N/16][K/64] of 1024
+ *    bytes [k/4][n][k%4]; scales f32 [N] (convert/quant.py:110-117).
+ *  - C is f32 row-major with leading dimension ldc; only rows [0, M) and
+ *    columns [n0*16, n1*16) are written (amx_gemm.c:333-372 contract).
+ *  - Arithmetic is bit-exact with the reference kernels: int32 accumulators
+ *    per scale group, then for int4 C = a_scale[m] * fold_g fma(acc_g, s_g, .)
+ *    in ascending group order, for int8 C = acc * (b_scale[n] * a_scale[m]).
+ */
+#ifndef FGM_CUDA_H
+#define FGM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  FGM_CUDA_OK = 0,
+  FGM_CUDA_EINVAL = -1,   /* argument outside the shape contract */
+  FGM_CUDA_ENODEV = -2,   /* no sm_100 device, or the device is unusable */
+  FGM_CUDA_ERUNTIME = -3, /* a CUDA runtime call or kernel launch failed */
+  FGM_CUDA_ENOMEM = -4,   /* device or pinned-host allocation failed */
+  FGM_CUDA_ETIMEOUT = -5  /* a bounded device-side wait gave up */
+};
+
+/* ------------------------------------------------------------ probe / setup */
+
+/* 1 if a compute-capability 10.x device is visible, else 0.  The CUDA analogue
+ * of fgm_cpu_has_amx / fgm_cpu_has_avx512_vnni (vnni_gemm.c:61-80), which
+ * backend() consults before choosing (lib.rs:112-138). */
+int fgm_cuda_available(void);
+
+/* Bind the library to `device` (-1: FGM_CUDA_DEVICE or the current device).
+ * Optional: every entry point initialises lazily.  No reference counterpart
+ * beyond fgm_amx_init (amx_gemm.c:40), the per-thread capability grant. */
+int fgm_cuda_init(int device);
+
+/* Text of the last failure on the calling thread ("" if none). */
+const char *fgm_cuda_last_error(void);
+
+/* Number of kernels this library has launched since load (instrumentation). */
+uint64_t fgm_cuda_launch_count(void);
+
+/* Wait for the current device, then report whether any kernel of this library
+ * gave up on a bounded wait since the last call (FGM_CUDA_ETIMEOUT, flag
+ * cleared) -- every device-side wait has a time limit instead of spinning
+ * forever.  No reference counterpart (the CPU kernels never wait). */
+int fgm_cuda_device_status(void);
+
+/* ---------------------------------------------- drop-ins, host pointers
+ * Same argument lists as the reference symbols, plus a status return.  All
+ * pointers are HOST pointers; the call is synchronous like the reference's.
+ * Weights (Bq/B and their scales) registered with fgm_cuda_register() are
+ * used from their resident device copy -- the intended mode, matching the
+ * reference's immutable mmap'd blobs (model.rs:98-103).  Unregistered weights
+ * are still correct: they are uploaded for that call alone, never cached, so
+ * a host buffer reused for other data can not be served stale.  Activations
+ * and C cross the bus on every call.  Serialised internally: concurrent
+ * callers are safe but do not overlap. */
+
+/* replaces fgm_gemm_q4g (amx_gemm.c:333) and fgm_gemm_q4g_vnni
+ * (vnni_gemm.c:291); Rust binding lib.rs:21-25 */
+int fgm_gemm_q4g_cuda(int M, int N, int K, const int8_t *A, const float *a_scale,
+                      const uint8_t *Bq, const uint16_t *b_scale, int group,
+                      float *C, int ldc, int n0, int n1);
+
+/* replaces fgm_gemm_q8c (amx_gemm.c:444) and fgm_gemm_q8c_vnni
+ * (vnni_gemm.c:224); Rust binding lib.rs:26-30 */
+int fgm_gemm_q8c_cuda(int M, int N, int K, const int8_t *A, const float *a_scale,
+                      const int8_t *B, const float *b_scale, float *C, int ldc,
+                      int n0, int n1);
+
+/* Gemm::run (crates/fgm-core/src/forward.rs:128-158) on this backend: the
+ * pair Pool::prep + Pool::gemm (pool.rs:285-311) that every linear layer
+ * issues, as one call.  src [M, lda] f32 host rows are rotated (hsz), quantised
+ * and packed on the device, multiplied over all N columns, and C [M, ldc]
+ * comes back to the host.  N % 64 == 0. */
+int fgm_linear_q4g_cuda(const float *src, int lda, int hsz, int M, int N, int K,
+                        const uint8_t *Bq, const uint16_t *b_scale, int group,
+                        float *C, int ldc);
+int fgm_linear_q8c_cuda(const float *src, int lda, int hsz, int M, int N, int K,
+                        const int8_t *B, const float *b_scale, float *C, int ldc);
+
+/* replaces fgm_prep_rows (ops.c:293-314); Rust binding lib.rs:17-20.
+ * src [m, lda] f32 rows -> rot [m, k] f32 (rotated copy), qa [m, k] int8,
+ * qs [m] f32 scales, pa tile-packed.  Rows [r0, r1), r0 % 16 == 0,
+ * k % 64 == 0, hsz 0 or a power of two dividing k.  rot and qa may be NULL. */
+int fgm_prep_rows_cuda(const float *src, int lda, float *rot, int8_t *qa,
+                       float *qs, int8_t *pa, int m, int k, int hsz, int r0,
+                       int r1);
+
+/* replaces fgm_quant_act (ops.c:181-204); Rust binding lib.rs:54 */
+int fgm_quant_act_cuda(const float *x, int rows, int k, int8_t *q, float *scale);
+
+/* replaces fgm_fwht (ops.c:153-175); Rust binding lib.rs:53.  n % hsz == 0. */
+int fgm_fwht_cuda(float *x, int n, int hsz);
+
+/* replaces fgm_pack_a (ops.c:279-290); Rust binding lib.rs:16 */
+int fgm_pack_a_cuda(int M, int K, const int8_t *A, int8_t *Ap);
+
+/* ---------------------------------------------------------- weight registry
+ * Device-resident copies of immutable host weight blobs, keyed by host
+ * address.  The reference needs none: its kernels read the mmap directly
+ * (model.rs:120-128). */
+
+/* Upload `bytes` at `host` once (no-op if already registered with the same
+ * size; EINVAL if registered with another size).  The blob must not change
+ * while registered: the host-pointer entry points serve the device copy. */
+int fgm_cuda_register(const void *host, size_t bytes);
+/* Drop the device copy (and any derived operand copy) of `host`. */
+int fgm_cuda_unregister(const void *host);
+/* Device address of a registered blob, or NULL. */
+const void *fgm_cuda_lookup(const void *host);
+/* Total device bytes held by the registry. */
+size_t fgm_cuda_registry_bytes(void);
+
+/* ------------------------------------- device pointers, asynchronous
+ * Same contracts with every buffer in device memory; work is enqueued on
+ * `stream` (a cudaStream_t; NULL = the legacy default stream) and the call
+ * returns without waiting.  These are the entry points a GPU-resident forward
+ * pass uses. */
+
+int fgm_cuda_gemm_q4g(int M, int N, int K, const int8_t *A, const float *a_scale,
+                      const uint8_t *Bq, const uint16_t *b_scale, int group,
+                      float *C, int ldc, int n0, int n1, void *stream);
+
+int fgm_cuda_gemm_q8c(int M, int N, int K, const int8_t *A, const float *a_scale,
+                      const int8_t *B, const float *b_scale, float *C, int ldc,
+                      int n0, int n1, void *stream);
+
+/* rot and qa may be NULL (not written). */
+int fgm_cuda_prep_rows(const float *src, int lda, float *rot, int8_t *qa,
+                       float *qs, int8_t *pa, int m, int k, int hsz, int r0,
+                       int r1, void *stream);
+
+/* int32 accumulators of the int4 product, acc [M][K/group][N]:
+ * acc[m][g][n] = sum over group g of A[m][k] * W[n][k], columns
+ * [n0*16, n1*16).  Same kernel as fgm_cuda_gemm_q4g with the f32 epilogue
+ * replaced by a raw store, for bit-exact accumulator checks.  No reference
+ * counterpart: the reference never exposes its int32 lanes. */
+int fgm_cuda_gemm_q4g_acc(int M, int N, int K, const int8_t *A, const uint8_t *Bq,
+                          int group, int32_t *acc, int n0, int n1, void *stream);
+
+/* int32 accumulators of the int8 product over all K, acc [M][N]. */
+int fgm_cuda_gemm_q8c_acc(int M, int N, int K, const int8_t *A, const int8_t *B,
+                          int32_t *acc, int n0, int n1, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FGM_CUDA_H */

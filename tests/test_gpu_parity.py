@@ -1,0 +1,331 @@
+"""Parity of the sm_100a kernels with the reference, through the C ABI.
+
+Bar: int32 accumulators bit-exact; f32 outputs bit-exact as well (the kernels
+reproduce the reference's rounding order), which implies the north-star
+tolerance of 1e-5 relative -- checked explicitly too (REL_TOL).
+"""
+import numpy as np
+import pytest
+
+import harness
+import fastgemma_b200 as fg
+import fastgemma_b200.device  # noqa: F401  (binds fg.device)
+from fastgemma_b200 import fgm_format as F
+
+pytestmark = pytest.mark.gpu
+REL_TOL = 1e-5  # f32 outputs vs the reference
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module", autouse=True)
+def cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    torch.cuda.set_device(0)
+    from fastgemma_b200 import _lib
+    assert _lib.lib().fgm_cuda_available() == 1
+
+
+def D(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def assert_bits(got, want, what=""):
+    got, want = np.asarray(got, np.float32), np.asarray(want, np.float32)
+    assert got.shape == want.shape, (got.shape, want.shape)
+    same = got.view(np.uint32) == want.view(np.uint32)
+    if not same.all():
+        idx = np.argwhere(~same)[:5]
+        raise AssertionError(f"{what}: {int((~same).sum())} elements differ, first {idx.tolist()}: "
+                             f"{got[tuple(idx[0])]} vs {want[tuple(idx[0])]}")
+    denom = np.maximum(np.abs(want), 1e-30)
+    assert float(np.max(np.abs(got - want) / denom, initial=0.0)) <= REL_TOL
+
+
+# ---------------------------------------------------------------- golden
+@pytest.mark.parametrize("idx", range(len(harness.VNNI_TEST_CASES)))
+def test_reference_harness_cases_host_abi(orc, golden, idx):
+    """bench/kernels/vnni_test.c's cases through the host-pointer drop-in."""
+    case, A, a_scale, B, b_scale = list(harness.vnni_test_inputs(orc))[idx]
+    kind, M, N, K, group, n0, n1 = case
+    tag = f"vnni_{idx:02d}_{kind}_M{M}_N{N}_K{K}" + (f"_g{group}" if group else "")
+    ap = F.pack_a(A)
+    c = np.zeros((M, N), np.float32)
+    if kind == "q8c":
+        fg.gemm_q8c(M, N, K, ap, a_scale, B, b_scale, c, N, n0, n1)
+    else:
+        fg.gemm_q4g(M, N, K, ap, a_scale, B, b_scale, group, c, N, n0, n1)
+    want = orc.gemm_q8c(M, N, K, ap, a_scale, B, b_scale, n0=n0, n1=n1) if kind == "q8c" else \
+        orc.gemm_q4g(M, N, K, ap, a_scale, B, b_scale, group, n0=n0, n1=n1)
+    assert_bits(c, want, tag)
+    import hashlib
+    assert hashlib.sha256(c.tobytes()).hexdigest() == str(golden[tag + "_C_sha"])
+
+
+def test_reference_gemm_test_case(golden, orc):
+    g = harness.gemm_test_inputs(orc)
+    M, N, K, group = g["M"], g["N"], g["K"], g["group"]
+    ap = F.pack_a(g["A"])
+    c4 = np.zeros((M, N), np.float32)
+    c8 = np.zeros((M, N), np.float32)
+    fg.gemm_q4g(M, N, K, ap, g["a_scale"], g["Bq"], g["bs4"], group, c4, N, 0, N // 16)
+    fg.gemm_q8c(M, N, K, ap, g["a_scale"], g["B8"], g["bs8"], c8, N, 0, N // 16)
+    assert_bits(c4, golden["gemmtest_q4g_C"], "q4g M=40")
+    assert_bits(c8, golden["gemmtest_q8c_C"], "q8c M=40")
+    c4d = np.zeros((8, N), np.float32)
+    fg.gemm_q4g(8, N, K, F.pack_a(g["A"][:8]), g["a_scale"], g["Bq"], g["bs4"], group, c4d, N,
+                0, N // 16)
+    assert_bits(c4d, golden["gemmtest_q4g_decode_C"], "q4g decode M=8")
+
+
+def test_int32_accumulators_golden(orc, golden):
+    st = np.array([0x51ED2701], np.uint64)
+    for (kind, M, N, K) in [("q8c", 16, 128, 2048), ("q8c", 8, 64, 8192),
+                            ("q4g", 16, 128, 2048), ("q4g", 5, 64, 8192)]:
+        A = orc.xorshift(st, -127, 127, M * K).astype(np.int8).reshape(M, K)
+        tag = f"acc_{kind}_M{M}_N{N}_K{K}"
+        ap = D(F.pack_a(A))
+        if kind == "q8c":
+            B = orc.xorshift(st, -127, 127, N * K).astype(np.int8)
+            acc = torch.zeros((M, N), dtype=torch.int32, device="cuda")
+            fg.device.gemm_q8c_acc(M, N, K, ap, D(B), acc)
+            got = acc.cpu().numpy()
+        else:
+            B = orc.xorshift(st, 0, 255, N * K // 2).astype(np.uint8)
+            acc = torch.zeros((M, 1, N), dtype=torch.int32, device="cuda")
+            fg.device.gemm_q4g_acc(M, N, K, ap, D(B), K, acc)
+            got = acc.cpu().numpy()[:, 0, :]
+        torch.cuda.synchronize()
+        assert np.array_equal(got, golden[tag + "_acc"]), tag
+
+
+@pytest.mark.parametrize("idx", range(8))
+def test_prep_rows_golden_host_abi(orc, golden, idx):
+    import hashlib
+    prep_cases = [(1, 2048, 2048, 0), (8, 2048, 2048, 128), (17, 2048, 2176, 128),
+                  (5, 512, 512, 8), (3, 256, 256, 16), (16, 8192, 8192, 128),
+                  (2, 1024, 1024, 1024), (33, 512, 520, 64)]
+    m, k, lda, hsz = prep_cases[idx]
+    x = harness.prep_input(orc, m, lda, seed=1000 + idx)
+    if idx == 1:
+        x[3, :] = 0.0
+    if idx == 0:
+        x[0, :] = 0.0
+        x[0, :8] = [127.0, 2.5, 3.5, -2.5, -3.5, 0.5, -0.5, 126.5]
+    tag = f"prep_{idx}_m{m}_k{k}_lda{lda}_h{hsz}"
+    rot = np.zeros((m, k), np.float32)
+    qa = np.zeros((m, k), np.int8)
+    qs = np.zeros(m, np.float32)
+    pa = np.zeros(F.packed_a_len(m, k), np.int8)
+    fg.prep_rows(x, lda, rot, qa, qs, pa, m, k, hsz, 0, m)
+    sha = lambda a: hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()  # noqa: E731
+    assert np.array_equal(qs.view(np.uint32), golden[tag + "_qs"].view(np.uint32))
+    assert sha(rot) == str(golden[tag + "_rot_sha"])
+    assert sha(qa) == str(golden[tag + "_qa_sha"])
+    assert sha(pa) == str(golden[tag + "_pa_sha"])
+
+
+# ------------------------------------------------- BASELINE decode shapes
+DECODE = [(2048, 2048), (2048, 512), (2048, 16384), (8192, 2048)]  # (K, N): q/o, kv, gate_up, down
+
+
+@pytest.mark.parametrize("M", [1, 2, 4, 8, 16])
+@pytest.mark.parametrize("K,N", DECODE)
+def test_decode_q4g_shapes_bit_exact(orc, M, K, N):
+    """BASELINE config 1 shapes: f32 outputs and int32 group accumulators."""
+    rng = np.random.default_rng(M * 100003 + K + N)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    bq, s = F.synth_q4g(N, K, 64, M + K + N, structured=False)
+    _, _, qs, pa = orc.prep_rows(x, M, K, 0)
+    xd, pad, qsd = D(x), torch.empty(pa.size, dtype=torch.int8, device="cuda"), \
+        torch.empty(M, dtype=torch.float32, device="cuda")
+    fg.device.prep_rows(xd, K, qsd, pad, M, K, 0)
+    c = torch.full((M, N), float("nan"), device="cuda")
+    bqd, sd = D(bq), D(s.view(np.uint16))
+    fg.device.gemm_q4g(M, N, K, pad, qsd, bqd, sd, 64, c)
+    acc = torch.zeros((M, K // 64, N), dtype=torch.int32, device="cuda")
+    fg.device.gemm_q4g_acc(M, N, K, pad, bqd, 64, acc)
+    torch.cuda.synchronize()
+    assert np.array_equal(pad.cpu().numpy(), pa)
+    assert np.array_equal(qsd.cpu().numpy().view(np.uint32), qs.view(np.uint32))
+    assert_bits(c.cpu().numpy(), orc.gemm_q4g(M, N, K, pa, qs, bq, s, 64), f"q4g M={M} {K}x{N}")
+    if N <= 2048:
+        assert np.array_equal(acc.cpu().numpy(), orc.gemm_q4g_acc(M, N, K, pa, bq, 64))
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 2048, 512), (8, 2048, 2048), (16, 8192, 256),
+                                   (17, 2048, 256), (64, 1024, 512), (256, 2048, 512),
+                                   (256, 8192, 256)])
+def test_q8c_shapes_bit_exact(orc, M, K, N):
+    rng = np.random.default_rng(M + K * 3 + N)
+    A = rng.integers(-127, 128, size=(M, K), dtype=np.int8)
+    b, s = F.synth_q8c(N, K, M + N)
+    a_s = rng.uniform(0.001, 0.05, size=M).astype(np.float32)
+    pa = F.pack_a(A)
+    c = torch.full((M, N), float("nan"), device="cuda")
+    pad, bd = D(pa), D(b)
+    fg.device.gemm_q8c(M, N, K, pad, D(a_s), bd, D(s), c)
+    acc = torch.zeros((M, N), dtype=torch.int32, device="cuda")
+    fg.device.gemm_q8c_acc(M, N, K, pad, bd, acc)
+    torch.cuda.synchronize()
+    assert_bits(c.cpu().numpy(), orc.gemm_q8c(M, N, K, pa, a_s, b, s), f"q8c M={M}")
+    assert np.array_equal(acc.cpu().numpy(), orc.gemm_q8c_acc(M, N, K, pa, b))
+
+
+@pytest.mark.parametrize("group", [128, 256, 512, 2048])
+@pytest.mark.parametrize("M", [3, 16, 33])
+def test_q4g_group_sizes_and_row_blocks(orc, group, M):
+    K, N = 2048, 256
+    rng = np.random.default_rng(group + M)
+    A = rng.integers(-128, 128, size=(M, K), dtype=np.int8)
+    bq, s = F.synth_q4g(N, K, group, group * 7 + M)
+    a_s = rng.uniform(0.001, 0.05, size=M).astype(np.float32)
+    pa = F.pack_a(A)
+    c = torch.zeros((M, N), device="cuda")
+    fg.device.gemm_q4g(M, N, K, D(pa), D(a_s), D(bq), D(s.view(np.uint16)), group, c)
+    torch.cuda.synchronize()
+    assert_bits(c.cpu().numpy(), orc.gemm_q4g(M, N, K, pa, a_s, bq, s, group))
+
+
+def test_partial_range_ldc_and_untouched(orc):
+    """Only rows < M and columns [n0*16, n1*16) are written (amx_gemm.c:333)."""
+    M, N, K, n0, n1, ldc = 5, 512, 1024, 8, 20, 600
+    rng = np.random.default_rng(5)
+    pa = F.pack_a(rng.integers(-128, 128, size=(M, K), dtype=np.int8))
+    bq, s = F.synth_q4g(N, K, 64, 5)
+    b8, s8 = F.synth_q8c(N, K, 6)
+    a_s = rng.uniform(0.001, 0.05, size=M).astype(np.float32)
+    for q4 in (True, False):
+        c = torch.full((M + 2, ldc), -7.0, device="cuda")
+        if q4:
+            fg.device.gemm_q4g(M, N, K, D(pa), D(a_s), D(bq), D(s.view(np.uint16)), 64, c, ldc,
+                               n0, n1)
+        else:
+            fg.device.gemm_q8c(M, N, K, D(pa), D(a_s), D(b8), D(s8), c, ldc, n0, n1)
+        torch.cuda.synchronize()
+        got = c.cpu().numpy()
+        want = np.full((M + 2, ldc), -7.0, np.float32)
+        if q4:
+            orc.gemm_q4g(M, N, K, pa, a_s, bq, s, 64, c=want, ldc=ldc, n0=n0, n1=n1)
+        else:
+            orc.gemm_q8c(M, N, K, pa, a_s, b8, s8, c=want, ldc=ldc, n0=n0, n1=n1)
+        assert_bits(got, want, "partial range")
+
+
+def test_config0_full_size_bit_exact(orc):
+    """BASELINE config 0 shape at full size: M=8, N=8192, K=2048, int4 g64."""
+    M, N, K = 8, 8192, 2048
+    x = F.synth_x(M, K, 11)
+    bq, s = F.synth_q4g(N, K, 64, 12, structured=False)
+    c = np.zeros((M, N), np.float32)
+    fg.linear_q4g(x, K, 0, M, N, K, bq, s, 64, c, N)
+    _, _, qs, pa = orc.prep_rows(x, M, K, 0)
+    assert_bits(c, orc.gemm_q4g(M, N, K, pa, qs, bq, s, 64), "config 0")
+
+
+def test_lm_head_full_width_sampled(orc):
+    """N = 262144 LM head at M = 8: every n-block computed on the device, a
+    spread of column ranges checked against the oracle, and the full output
+    equal to the concatenation of independently computed column shards."""
+    M, N, K = 8, 262144, 2048
+    x = F.synth_x(M, K, 21)
+    bq, s = F.synth_q4g(N, K, 64, 22, structured=False)
+    _, _, qs, pa = orc.prep_rows(x, M, K, 0)
+    pad, qsd, bqd, sd = D(pa), D(qs), D(bq), D(s.view(np.uint16))
+    full = torch.empty((M, N), device="cuda")
+    fg.device.gemm_q4g(M, N, K, pad, qsd, bqd, sd, 64, full)
+    shards = torch.empty((M, N), device="cuda")
+    nb = N // 16
+    for r in range(8):  # column shards as an 8-way split would cut them
+        a, b = r * nb // 8 // 4 * 4, (r + 1) * nb // 8 // 4 * 4
+        fg.device.gemm_q4g(M, N, K, pad, qsd, bqd, sd, 64, shards, N, a, b)
+    torch.cuda.synchronize()
+    full_h = full.cpu().numpy()
+    assert np.array_equal(full_h.view(np.uint32), shards.cpu().numpy().view(np.uint32))
+    for a in (0, 4, 4096, 8188, 16380):
+        want = np.zeros((M, N), np.float32)
+        orc.gemm_q4g(M, N, K, pa, qs, bq, s, 64, c=want, n0=a, n1=a + 4)
+        assert_bits(full_h[:, a * 16:(a + 4) * 16], want[:, a * 16:(a + 4) * 16], f"nb {a}")
+
+
+def test_linear_host_path_matches_oracle(orc):
+    """Gemm::run drop-in (host X -> prep -> GEMM -> host C) with a Hadamard."""
+    for (M, K, N, hsz, q4) in [(3, 2048, 512, 128, True), (16, 8192, 256, 128, True),
+                               (8, 2048, 256, 0, False), (40, 1024, 128, 64, False)]:
+        x = F.synth_x(M, K, M + K)
+        _, _, qs, pa = orc.prep_rows(x, M, K, hsz)
+        c = np.zeros((M, N), np.float32)
+        if q4:
+            bq, s = F.synth_q4g(N, K, 64, N)
+            fg.linear_q4g(x, K, hsz, M, N, K, bq, s, 64, c, N)
+            want = orc.gemm_q4g(M, N, K, pa, qs, bq, s, 64)
+        else:
+            b, s = F.synth_q8c(N, K, N)
+            fg.linear_q8c(x, K, hsz, M, N, K, b, s, c, N)
+            want = orc.gemm_q8c(M, N, K, pa, qs, b, s)
+        assert_bits(c, want, f"linear M={M} K={K} hsz={hsz}")
+
+
+@pytest.mark.parametrize("m,k,lda,hsz", [(1, 64, 64, 0), (7, 2048, 2100, 128), (16, 256, 256, 4),
+                                         (20, 512, 512, 32), (256, 2048, 2048, 128),
+                                         (3, 16384, 16384, 2048)])
+def test_prep_device_vs_oracle(orc, m, k, lda, hsz):
+    x = np.random.default_rng(m + k + hsz).standard_normal((m, lda)).astype(np.float32) * 3
+    rot, qa, qs, pa = orc.prep_rows(x, m, k, hsz, lda=lda)
+    rd = torch.empty((m, k), device="cuda")
+    qad = torch.empty((m, k), dtype=torch.int8, device="cuda")
+    qsd = torch.empty(m, device="cuda")
+    pad = torch.full((pa.size,), 99, dtype=torch.int8, device="cuda")
+    fg.device.prep_rows(D(x), lda, qsd, pad, m, k, hsz, rot=rd, qa=qad)
+    torch.cuda.synchronize()
+    assert np.array_equal(rd.cpu().numpy().view(np.uint32), rot.view(np.uint32))
+    assert np.array_equal(qad.cpu().numpy(), qa)
+    assert np.array_equal(qsd.cpu().numpy().view(np.uint32), qs.view(np.uint32))
+    assert np.array_equal(pad.cpu().numpy(), pa)
+
+
+def test_fwht_and_quant_act_host_entries(orc):
+    x = np.random.default_rng(3).standard_normal((4, 1024)).astype(np.float32)
+    y = x.copy()
+    fg.fwht(y, 128)
+    assert np.array_equal(y.view(np.uint32), orc.fwht(x, 128).view(np.uint32))
+    q = np.zeros((4, 1024), np.int8)
+    s = np.zeros(4, np.float32)
+    fg.quant_act(x, 4, 1024, q, s)
+    q0, s0 = orc.quant_act(x)
+    assert np.array_equal(q, q0) and np.array_equal(s.view(np.uint32), s0.view(np.uint32))
+
+
+def test_registry_and_errors():
+    from fastgemma_b200 import _lib
+    L = _lib.lib()
+    blob = np.arange(4096, dtype=np.uint8)
+    before = L.fgm_cuda_registry_bytes()
+    fg.register(blob)
+    assert L.fgm_cuda_lookup(blob.ctypes.data)
+    assert L.fgm_cuda_registry_bytes() == before + 4096
+    assert L.fgm_cuda_register(blob.ctypes.data, 100) == -1  # size mismatch
+    fg.unregister(blob)
+    assert not L.fgm_cuda_lookup(blob.ctypes.data)
+    with pytest.raises(fg.FgmCudaError):
+        fg.unregister(blob)
+    # device path rejects contract violations before launching
+    c = torch.empty(64, device="cuda")
+    assert L.fgm_cuda_gemm_q4g(8, 64, 100, c.data_ptr(), c.data_ptr(), c.data_ptr(),
+                               c.data_ptr(), 64, c.data_ptr(), 64, 0, 4, None) == -1
+
+
+def test_launch_counter_counts_kernels():
+    from fastgemma_b200 import _lib
+    L = _lib.lib()
+    M, N, K = 2, 64, 128
+    a = torch.zeros(16 * K, dtype=torch.int8, device="cuda")
+    s = torch.ones(M, device="cuda")
+    b = torch.zeros(N * K // 2, dtype=torch.uint8, device="cuda")
+    bs = torch.zeros((K // 64) * N, dtype=torch.int16, device="cuda")
+    c = torch.empty((M, N), device="cuda")
+    n0 = L.fgm_cuda_launch_count()
+    fg.device.gemm_q4g(M, N, K, a, s, b, bs, 64, c)
+    torch.cuda.synchronize()
+    assert L.fgm_cuda_launch_count() == n0 + 1
