@@ -406,11 +406,13 @@ def bench_prefill(args, dev, gen, world):
         for name, K, N in PREFILL_SHAPES:
             w = torch.randint(-127, 128, (N * K,), dtype=torch.int8, device=dev, generator=gen)
             s = torch.empty(N, dtype=torch.float32, device=dev).uniform_(0.001, 0.01, generator=gen)
+            D.q8c_prepare(w, N, K)  # tensor-core operand copy, made once per weight
             lw[name] = (w, s)
         ws.append(lw)
     xs = {K: torch.randn((M_PREFILL, K), dtype=torch.float32, device=dev, generator=gen)
           for _, K, _ in PREFILL_SHAPES}
     pas = {K: D.packed_a(M_PREFILL, K, dev) for K in xs}
+    qas = {K: torch.empty((M_PREFILL, K), dtype=torch.int8, device=dev) for K in xs}
     qss = {K: torch.empty(M_PREFILL, dtype=torch.float32, device=dev) for K in xs}
     cs = {name: torch.empty((M_PREFILL, N), dtype=torch.float32, device=dev)
           for name, K, N in PREFILL_SHAPES}
@@ -418,9 +420,10 @@ def bench_prefill(args, dev, gen, world):
     def step():
         for c in range(copies):
             for name, K, N in PREFILL_SHAPES:
-                D.prep_rows(xs[K], K, qss[K], pas[K], M_PREFILL, K, 0)
+                # quantise (row-major int8 for the tensor cores) then the GEMM
+                D.prep_rows(xs[K], K, qss[K], pas[K], M_PREFILL, K, 0, qa=qas[K])
                 w, s = ws[c][name]
-                D.gemm_q8c(M_PREFILL, N, K, pas[K], qss[K], w, s, cs[name])
+                D.gemm_q8c_rows(M_PREFILL, N, K, qas[K], qss[K], w, s, cs[name])
 
     side = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(side):

@@ -294,6 +294,127 @@ static bool use_pdl() {
 
 static bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
+// --------------------------------------------- prepared tensor-core operands
+// int8 weights as the row-major [N][K] operand the tcgen05 kernel reads, keyed
+// by the device address of the .fgm copy they were made from.
+struct Prepared {
+  int8_t *kmajor;
+  size_t bytes;
+  int N, K;
+  CUtensorMap map;
+};
+static std::mutex g_prep_mu;
+static std::unordered_map<const void *, Prepared> g_prep;
+
+static int tc_min_m() {
+  static int v = -1;
+  if (v < 0) {
+    const char *e = getenv("FGM_CUDA_TC_MIN_M");
+    v = (e && *e) ? atoi(e) : 64;
+  }
+  return v;
+}
+
+static int prepare_q8c(const int8_t *B, int N, int K, cudaStream_t st) {
+  std::lock_guard<std::mutex> lk(g_prep_mu);
+  auto it = g_prep.find(B);
+  if (it != g_prep.end()) {
+    if (it->second.N != N || it->second.K != K)
+      return fail(FGM_CUDA_EINVAL, "weight %p prepared as %dx%d, now %dx%d", (const void *)B,
+                  it->second.N, it->second.K, N, K);
+    return FGM_CUDA_OK;
+  }
+  Prepared pr{};
+  pr.bytes = (size_t)N * K;
+  pr.N = N;
+  pr.K = K;
+  if (cudaMalloc(&pr.kmajor, pr.bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(FGM_CUDA_ENOMEM, "cudaMalloc(%zu) for a prepared weight", pr.bytes);
+  }
+  cudaError_t e = launch_q8c_rows(B, pr.kmajor, N, K, st);
+  if (e != cudaSuccess) {
+    cudaFree(pr.kmajor);
+    return cuda_fail(e, "q8c repack");
+  }
+  count_launch();
+  if (!encode_rows_map(&pr.map, pr.kmajor, N, K, K, kTcBoxRowsB)) {
+    cudaFree(pr.kmajor);
+    return fail(FGM_CUDA_ERUNTIME, "cuTensorMapEncodeTiled failed for a prepared weight");
+  }
+  g_prep[B] = pr;
+  return FGM_CUDA_OK;
+}
+
+static bool find_prepared(const void *B, CUtensorMap *map) {
+  std::lock_guard<std::mutex> lk(g_prep_mu);
+  auto it = g_prep.find(B);
+  if (it == g_prep.end()) return false;
+  *map = it->second.map;
+  return true;
+}
+
+static void release_prepared(const void *B) {
+  std::lock_guard<std::mutex> lk(g_prep_mu);
+  auto it = g_prep.find(B);
+  if (it == g_prep.end()) return;
+  cudaFree(it->second.kmajor);
+  g_prep.erase(it);
+}
+
+// A is row-major [M][lda] int8.
+static int run_q8c_tc(int M, int N, int K, const int8_t *A, int lda, const float *a_scale,
+                      const float *b_scale, const CUtensorMap &map, float *C, int ldc, int c_col0,
+                      int32_t *acc, int n0, int n1, cudaStream_t st) {
+  DevInfo *di = nullptr;
+  int rc = dev_info(&di);
+  if (rc) return rc;
+  if (!aligned16(A) || lda % 16 != 0)
+    return fail(FGM_CUDA_EINVAL, "row-major activations need 16-byte aligned rows");
+  if (b_scale && !aligned16(b_scale))
+    return fail(FGM_CUDA_EINVAL, "int8 weight scales must be 16-byte aligned");
+  TcParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.A = A;
+  p.a_scale = a_scale;
+  p.b_scale = b_scale;
+  p.C = C;
+  p.ldc = ldc;
+  p.c_col0 = c_col0;
+  p.acc = acc;
+  p.nb0 = n0;
+  p.n_end = n1 * 16;
+  p.stages = 4;
+  while (p.stages > 2 && q8c_tc_smem_bytes(p.stages) > di->smem_optin) p.stages--;
+  p.err = di->err;
+  cudaError_t e = launch_q8c_tc(p, lda, map, use_pdl(), st);
+  if (e != cudaSuccess) return cuda_fail(e, "gemm_q8c tensor-core launch");
+  count_launch();
+  return FGM_CUDA_OK;
+}
+
+// Tile-packed A on the tensor-core path: a row-major copy in stream-ordered
+// temporary memory (so concurrent streams never share it), then the GEMM.
+static int run_q8c_tc_packed(int M, int N, int K, const int8_t *A, const float *a_scale,
+                             const float *b_scale, const CUtensorMap &map, float *C, int ldc,
+                             int c_col0, int32_t *acc, int n0, int n1, cudaStream_t st) {
+  void *rows = nullptr;
+  FGM_TRY(cudaMallocAsync(&rows, (size_t)M * K, st));
+  cudaError_t e = launch_packed_to_rows(A, static_cast<int8_t *>(rows), M, K, st);
+  int rc = FGM_CUDA_OK;
+  if (e != cudaSuccess) rc = cuda_fail(e, "activation repack");
+  else {
+    count_launch();
+    rc = run_q8c_tc(M, N, K, static_cast<int8_t *>(rows), K, a_scale, b_scale, map, C, ldc,
+                    c_col0, acc, n0, n1, st);
+  }
+  cudaError_t f = cudaFreeAsync(rows, st);
+  if (!rc && f != cudaSuccess) rc = cuda_fail(f, "cudaFreeAsync");
+  return rc;
+}
+
 // ------------------------------------------------------------- launchers
 static int run_gemm(bool q4, int M, int N, int K, const int8_t *A, const float *a_scale,
                     const void *B, const void *b_scale, int group, float *C, int ldc, int c_col0,
@@ -301,6 +422,10 @@ static int run_gemm(bool q4, int M, int N, int K, const int8_t *A, const float *
   if (M == 0 || n0 == n1) return FGM_CUDA_OK;
   if (!aligned16(B) || (q4 && b_scale && !aligned16(b_scale)))
     return fail(FGM_CUDA_EINVAL, "weights and int4 scales must be 16-byte aligned");
+  CUtensorMap map;
+  if (!q4 && M >= tc_min_m() && find_prepared(B, &map))
+    return run_q8c_tc_packed(M, N, K, A, a_scale, static_cast<const float *>(b_scale), map, C,
+                             ldc, c_col0, acc, n0, n1, st);
   DevInfo *di = nullptr;
   int rc = dev_info(&di);
   if (rc) return rc;
@@ -362,6 +487,8 @@ static int host_gemm(bool q4, int M, int N, int K, const int8_t *A, const float 
   if (!dB) {  // unregistered weights: this call's own upload
     if ((rc = h2d(d + o_w, B, wbytes, o_w))) return rc;
     dB = d + o_w;
+  } else if (!q4 && M >= tc_min_m()) {  // resident int8 weights: tensor-core operand copy
+    if ((rc = prepare_q8c(static_cast<const int8_t *>(dB), N, K, g_stream))) return rc;
   }
   if (!dS) {
     if ((rc = h2d(d + o_ws, b_scale, sbytes, o_ws))) return rc;
@@ -393,23 +520,33 @@ static int host_linear(bool q4, const float *src, int lda, int hsz, int M, int N
   const size_t a_len = packed_len(M, K), s_len = (size_t)M * 4, c_len = (size_t)M * N * 4;
   const size_t o_a = align256(x_len), o_s = o_a + align256(a_len), o_c = o_s + align256(s_len);
   const size_t o_w = o_c + align256(c_len), o_ws = o_w + (dB ? 0 : align256(wbytes));
-  const size_t total = o_ws + (dS ? 0 : align256(sbytes));
+  const size_t o_w_end = o_ws + (dS ? 0 : align256(sbytes));
+  const size_t total = o_w_end + align256((size_t)M * K);  // + row-major quantised X
   if ((rc = stage_reserve(total))) return rc;
   char *d = g_stage.d;
   if ((rc = h2d(d, src, x_len, 0))) return rc;
   if (!dB) {
     if ((rc = h2d(d + o_w, B, wbytes, o_w))) return rc;
     dB = d + o_w;
+  } else if (!q4 && M >= tc_min_m()) {
+    if ((rc = prepare_q8c(static_cast<const int8_t *>(dB), N, K, g_stream))) return rc;
   }
   if (!dS) {
     if ((rc = h2d(d + o_ws, b_scale, sbytes, o_ws))) return rc;
     dS = d + o_ws;
   }
-  rc = run_prep((const float *)d, lda, nullptr, nullptr, (float *)(d + o_s), (int8_t *)(d + o_a),
+  CUtensorMap map;
+  const bool tc = !q4 && M >= tc_min_m() && find_prepared(dB, &map);
+  int8_t *qa_rows = tc ? (int8_t *)(d + o_w_end) : nullptr;  // row-major quantised X
+  rc = run_prep((const float *)d, lda, nullptr, qa_rows, (float *)(d + o_s), (int8_t *)(d + o_a),
                 M, K, hsz, 0, M, g_stream);
   if (rc) return rc;
-  rc = run_gemm(q4, M, N, K, (const int8_t *)(d + o_a), (const float *)(d + o_s), dB, dS, group,
-                (float *)(d + o_c), N, 0, nullptr, 0, N / 16, g_stream);
+  if (tc)
+    rc = run_q8c_tc(M, N, K, qa_rows, K, (const float *)(d + o_s), (const float *)dS, map,
+                    (float *)(d + o_c), N, 0, nullptr, 0, N / 16, g_stream);
+  else
+    rc = run_gemm(q4, M, N, K, (const int8_t *)(d + o_a), (const float *)(d + o_s), dB, dS,
+                  group, (float *)(d + o_c), N, 0, nullptr, 0, N / 16, g_stream);
   if (rc) return rc;
   return d2h_rows_sync(C, (size_t)ldc * 4, d + o_c, (size_t)N * 4, M, o_c);
 }
@@ -588,6 +725,7 @@ int fgm_cuda_unregister(const void *host) {
   std::lock_guard<std::mutex> lk(g_reg_mu);
   auto it = g_reg.find(host);
   if (it == g_reg.end()) return fail(FGM_CUDA_EINVAL, "unregister: %p not registered", host);
+  release_prepared(it->second.dev);
   cudaFree(it->second.dev);
   g_reg_bytes -= it->second.bytes;
   g_reg.erase(it);
@@ -633,6 +771,33 @@ int fgm_cuda_prep_rows(const float *src, int lda, float *rot, int8_t *qa, float 
   if (rc) return rc;
   if (r0 < r1 && (!src || !qs || !pa)) return fail(FGM_CUDA_EINVAL, "null pointer");
   return run_prep(src, lda, rot, qa, qs, pa, m, k, hsz, r0, r1, (cudaStream_t)stream);
+}
+
+int fgm_cuda_gemm_q8c_rows(int M, int N, int K, const int8_t *A, int lda, const float *a_scale,
+                           const int8_t *B, const float *b_scale, float *C, int ldc, int n0,
+                           int n1, void *stream) {
+  int rc = check_gemm(M, N, K, ldc, n0, n1, 64, false);
+  if (rc) return rc;
+  if (lda < K || lda % 16) return fail(FGM_CUDA_EINVAL, "lda=%d: need lda >= K, lda %% 16 == 0", lda);
+  if (M == 0 || n0 == n1) return FGM_CUDA_OK;
+  if (!A || !a_scale || !B || !b_scale || !C) return fail(FGM_CUDA_EINVAL, "null pointer");
+  CUtensorMap map;
+  if (!find_prepared(B, &map))
+    return fail(FGM_CUDA_EINVAL, "weight %p is not prepared (fgm_cuda_q8c_prepare)", (const void *)B);
+  return run_q8c_tc(M, N, K, A, lda, a_scale, b_scale, map, C, ldc, 0, nullptr, n0, n1,
+                    (cudaStream_t)stream);
+}
+
+int fgm_cuda_q8c_prepare(const int8_t *B, int N, int K, void *stream) {
+  int rc = check_gemm(1, N, K, N, 0, 0, 64, false);
+  if (rc) return rc;
+  if (!B || !aligned16(B)) return fail(FGM_CUDA_EINVAL, "weights must be 16-byte aligned");
+  return prepare_q8c(B, N, K, (cudaStream_t)stream);
+}
+
+int fgm_cuda_q8c_release(const int8_t *B) {
+  release_prepared(B);
+  return FGM_CUDA_OK;
 }
 
 int fgm_cuda_gemm_q4g_acc(int M, int N, int K, const int8_t *A, const uint8_t *Bq, int group,

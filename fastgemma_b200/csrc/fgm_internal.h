@@ -57,6 +57,40 @@ struct PrepParams {
 
 cudaError_t launch_prep(const PrepParams &p, bool pdl, cudaStream_t st);
 
+// ----------------------------------------------------------- tensor cores
+struct TcParams {
+  int M, N, K;
+  const int8_t *A;        // row-major int8 activations
+  const float *a_scale;
+  const float *b_scale;   // int8 per-channel scales [N]
+  float *C;
+  int ldc, c_col0;
+  int32_t *acc;           // raw accumulators [M][N] instead of C (debug launches)
+  int nb0;                // first n-block
+  int n_end;              // one past the last output column
+  int stages;             // ring depth
+  int *err;
+  int tma_store;          // write C through TMA stores (set by the launcher)
+};
+
+}  // namespace fgm
+#include <cuda.h>
+namespace fgm {
+
+// Row-major [rows][ld] byte matrix as a 2-D TMA view, boxes of box_rows x 128
+// bytes with the 128-byte swizzle.
+bool encode_rows_map(CUtensorMap *map, const void *base, int rows, int K, int ld, int box_rows);
+// .fgm int8 tiles -> row-major [N][K] (the tensor-core weight operand).
+cudaError_t launch_q8c_rows(const int8_t *tiles, int8_t *rows, int N, int K, cudaStream_t st);
+// tile-packed activations -> row-major [M][K].
+cudaError_t launch_packed_to_rows(const int8_t *packed, int8_t *rows, int M, int K,
+                                  cudaStream_t st);
+size_t q8c_tc_smem_bytes(int stages);
+// p.A is row-major with leading dimension lda bytes.
+cudaError_t launch_q8c_tc(const TcParams &p, int lda, const CUtensorMap &tmB, bool pdl,
+                          cudaStream_t st);
+constexpr int kTcBoxRowsB = 128;  // output columns per CTA tile
+
 // Number of kernel launches issued by this library (instrumentation).
 void count_launch(int n = 1);
 

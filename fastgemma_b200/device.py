@@ -50,3 +50,20 @@ def prep_rows(src, lda, qs, pa, m, k, hsz, rot=None, qa=None, r0=0, r1=None, str
 def packed_a(m: int, k: int, device=None) -> torch.Tensor:
     """An uninitialised packed-activation buffer of ``packed_a_len(m, k)`` bytes."""
     return torch.empty((m + 15) // 16 * 16 * k, dtype=torch.int8, device=device or "cuda")
+
+
+def gemm_q8c_rows(M, N, K, A, a_scale, B, b_scale, C, lda=None, ldc=None, n0=0, n1=None,
+                  stream=None):
+    """Prefill int8 GEMM from row-major int8 activations (prepared weight)."""
+    n1 = N // 16 if n1 is None else n1
+    call("fgm_cuda_gemm_q8c_rows", M, N, K, _p(A), K if lda is None else lda, _p(a_scale), _p(B),
+         _p(b_scale), _p(C), N if ldc is None else ldc, n0, n1, _s(stream))
+
+
+def q8c_prepare(B, N, K, stream=None):
+    """Make the tensor-core operand copy of a device int8 weight (large-M path)."""
+    call("fgm_cuda_q8c_prepare", _p(B), N, K, _s(stream))
+
+
+def q8c_release(B):
+    call("fgm_cuda_q8c_release", _p(B))

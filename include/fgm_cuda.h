@@ -154,6 +154,28 @@ int fgm_cuda_gemm_q8c(int M, int N, int K, const int8_t *A, const float *a_scale
                       const int8_t *B, const float *b_scale, float *C, int ldc,
                       int n0, int n1, void *stream);
 
+/* Tensor-core operand copy of a device-resident int8 weight (the .fgm tiles
+ * at B, N x K) as a row-major [N][K] matrix, plus its TMA descriptor, kept
+ * until fgm_cuda_q8c_release(B).  Once a weight is prepared,
+ * fgm_cuda_gemm_q8c / _acc with M >= 64 (FGM_CUDA_TC_MIN_M) run on the
+ * tcgen05 kernel (tile-packed A is first copied to row-major form in
+ * stream-ordered temporary memory); unprepared weights and small M use the
+ * streaming kernel.  Host-pointer entry points prepare registered weights on
+ * first large-M use.  The copy costs N*K device bytes.  No reference
+ * counterpart: the AMX kernel consumes the tiles as they are
+ * (amx_gemm.c:375-410). */
+int fgm_cuda_q8c_prepare(const int8_t *B, int N, int K, void *stream);
+
+/* Prefill form of fgm_cuda_gemm_q8c: activations as the quantiser's row-major
+ * int8 matrix A [M][lda] (fgm_quant_act's q, ops.c:181-204; lda >= K,
+ * lda % 16 == 0) instead of the tile-packed copy, weight prepared with
+ * fgm_cuda_q8c_prepare (EINVAL otherwise).  Always the tcgen05 kernel. */
+int fgm_cuda_gemm_q8c_rows(int M, int N, int K, const int8_t *A, int lda,
+                           const float *a_scale, const int8_t *B,
+                           const float *b_scale, float *C, int ldc, int n0, int n1,
+                           void *stream);
+int fgm_cuda_q8c_release(const int8_t *B);
+
 /* rot and qa may be NULL (not written). */
 int fgm_cuda_prep_rows(const float *src, int lda, float *rot, int8_t *qa,
                        float *qs, int8_t *pa, int m, int k, int hsz, int r0,

@@ -329,3 +329,106 @@ def test_launch_counter_counts_kernels():
     fg.device.gemm_q4g(M, N, K, a, s, b, bs, 64, c)
     torch.cuda.synchronize()
     assert L.fgm_cuda_launch_count() == n0 + 1
+
+
+# ------------------------------------------- prefill: tcgen05 tensor-core path
+@pytest.mark.parametrize("M,K,N,n0,n1", [(64, 1024, 256, 0, 16), (100, 2048, 512, 4, 24),
+                                         (256, 2048, 512, 0, 32), (256, 8192, 256, 0, 16),
+                                         (300, 2048, 384, 0, 24), (1024, 2048, 256, 8, 16)])
+def test_q8c_tensor_core_bit_exact(orc, M, K, N, n0, n1):
+    """M >= 64 with a prepared weight runs tcgen05.mma kind::i8; f32 outputs and
+    int32 accumulators must match the reference arithmetic exactly."""
+    rng = np.random.default_rng(M * 31 + K + N)
+    A = rng.integers(-128, 128, size=(M, K), dtype=np.int8)
+    b, s = F.synth_q8c(N, K, M + 7 * N)
+    a_s = rng.uniform(0.001, 0.05, size=M).astype(np.float32)
+    pa = F.pack_a(A)
+    pad, bd, sd, asd = D(pa), D(b), D(s), D(a_s)
+    fg.device.q8c_prepare(bd, N, K)
+    try:
+        ldc = N + 16
+        c = torch.full((M, ldc), -9.0, device="cuda")
+        fg.device.gemm_q8c(M, N, K, pad, asd, bd, sd, c, ldc, n0, n1)
+        acc = torch.full((M, N), 7, dtype=torch.int32, device="cuda")
+        fg.device.gemm_q8c_acc(M, N, K, pad, bd, acc, n0, n1)
+        torch.cuda.synchronize()
+        from fastgemma_b200 import _lib
+        assert _lib.lib().fgm_cuda_device_status() == 0
+        want = np.full((M, ldc), -9.0, np.float32)
+        orc.gemm_q8c(M, N, K, pa, a_s, b, s, c=want, ldc=ldc, n0=n0, n1=n1)
+        assert_bits(c.cpu().numpy(), want, f"tc q8c M={M} K={K} N={N}")
+        want_acc = orc.gemm_q8c_acc(M, N, K, pa, b, n0, n1)
+        got_acc = acc.cpu().numpy()
+        cols = slice(n0 * 16, n1 * 16)
+        assert np.array_equal(got_acc[:, cols], want_acc[:, cols])
+    finally:
+        fg.device.q8c_release(bd)
+
+
+def test_q8c_prefill_config2_sampled(orc):
+    """BASELINE config 2 at full size (M=256, K=2048, N=16384) on the tensor
+    cores: column blocks across the width checked against the oracle, and the
+    GPU's own two paths (tensor core vs streaming kernel) agree everywhere."""
+    M, K, N = 256, 2048, 16384
+    x = F.synth_x(M, K, 5)
+    b, s = F.synth_q8c(N, K, 6, structured=False)
+    _, _, qs, pa = orc.prep_rows(x, M, K, 0)
+    pad, bd, sd, qsd = D(pa), D(b), D(s), D(qs)
+    c_mma = torch.empty((M, N), device="cuda")
+    fg.device.gemm_q8c(M, N, K, pad, qsd, bd, sd, c_mma)  # not prepared: streaming kernel
+    fg.device.q8c_prepare(bd, N, K)
+    try:
+        c_tc = torch.empty((M, N), device="cuda")
+        fg.device.gemm_q8c(M, N, K, pad, qsd, bd, sd, c_tc)
+        torch.cuda.synchronize()
+        got = c_tc.cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), c_mma.cpu().numpy().view(np.uint32))
+        for a in (0, 252, 512, 1020):
+            want = np.zeros((M, N), np.float32)
+            orc.gemm_q8c(M, N, K, pa, qs, b, s, c=want, n0=a, n1=a + 4)
+            assert_bits(got[:, a * 16:(a + 4) * 16], want[:, a * 16:(a + 4) * 16], f"nb {a}")
+    finally:
+        fg.device.q8c_release(bd)
+
+
+def test_q8c_host_path_prepares_registered_weights(orc):
+    """The host-pointer drop-in with a registered int8 weight at M >= 64 goes
+    through the tensor cores (prepared on first use) and stays bit-exact."""
+    M, K, N = 128, 2048, 256
+    rng = np.random.default_rng(17)
+    A = rng.integers(-128, 128, size=(M, K), dtype=np.int8)
+    b, s = F.synth_q8c(N, K, 18)
+    a_s = rng.uniform(0.001, 0.05, size=M).astype(np.float32)
+    pa = F.pack_a(A)
+    fg.register(b)
+    try:
+        c = np.zeros((M, N), np.float32)
+        fg.gemm_q8c(M, N, K, pa, a_s, b, s, c, N, 0, N // 16)
+        assert_bits(c, orc.gemm_q8c(M, N, K, pa, a_s, b, s), "host tc")
+    finally:
+        fg.unregister(b)
+
+
+@pytest.mark.parametrize("M,K,N", [(256, 2048, 1024), (77, 1024, 256), (512, 8192, 128)])
+def test_q8c_rows_entry_from_quantiser(orc, M, K, N):
+    """Prefill form: quantise on the device (row-major int8 out), then the
+    tensor-core GEMM straight from it; equals prep + reference GEMM."""
+    x = F.synth_x(M, K, M + K + N)
+    b, s = F.synth_q8c(N, K, N + 3)
+    _, qa, qs, pa = orc.prep_rows(x, M, K, 128)
+    xd, bd, sd = D(x), D(b), D(s)
+    qad = torch.empty((M, K), dtype=torch.int8, device="cuda")
+    qsd = torch.empty(M, device="cuda")
+    pad = torch.empty(pa.size, dtype=torch.int8, device="cuda")
+    fg.device.prep_rows(xd, K, qsd, pad, M, K, 128, qa=qad)
+    fg.device.q8c_prepare(bd, N, K)
+    try:
+        c = torch.empty((M, N), device="cuda")
+        fg.device.gemm_q8c_rows(M, N, K, qad, qsd, bd, sd, c)
+        torch.cuda.synchronize()
+        assert np.array_equal(qad.cpu().numpy(), qa)
+        assert_bits(c.cpu().numpy(), orc.gemm_q8c(M, N, K, pa, qs, b, s), f"rows M={M}")
+    finally:
+        fg.device.q8c_release(bd)
+    with pytest.raises(fg.FgmCudaError):  # unprepared weights are refused, not computed slowly
+        fg.device.gemm_q8c_rows(M, N, K, qad, qsd, bd, sd, c)
