@@ -39,6 +39,7 @@ SIGNATURES = {
     "fgm_cuda_q8c_prepare": ([_p, _i, _i, _p], _i),
     "fgm_cuda_gemm_q8c_rows": ([_i, _i, _i, _p, _i, _p, _p, _p, _p, _i, _i, _i, _p], _i),
     "fgm_cuda_q8c_release": ([_p], _i),
+    "fgm_cuda_gemm_q8c_noalloc": ([_i, _i, _i, _p, _p, _p, _p, _p, _i, _i, _i, _p], _i),
     "fgm_cuda_gemm_q4g_acc": ([_i, _i, _i, _p, _p, _i, _p, _i, _i, _p], _i),
     "fgm_cuda_gemm_q8c_acc": ([_i, _i, _i, _p, _p, _p, _i, _i, _p], _i),
 }

@@ -415,6 +415,43 @@ static int run_q8c_tc_packed(int M, int N, int K, const int8_t *A, const float *
   return rc;
 }
 
+// ------------------------------- tensor-core path without device allocation
+// Some callers must not allocate device memory once they are serving: an
+// engine that reserves its whole HBM budget for weights and the KV cache at
+// start-up (a stream-ordered allocation can then fail with out-of-memory in
+// the middle of a request), and host-language callers that reach this library
+// only through the C ABI and hold no say over the process's CUDA memory pools.
+// For them fgm_cuda_gemm_q8c_noalloc keeps the row-major activation copy in
+// this fixed file-scope buffer instead of stream-ordered temporary memory.
+// Every call on a device shares the one buffer, so calls that overlap in time
+// (different streams or host threads) race on it; calls on one stream are
+// ordered and safe.  Nothing in it has to start at zero: the repack writes
+// all M*K bytes before the GEMM reads them, and the rows past M of the last
+// 256-row tile come from the TMA zero fill of the M-row activation view.
+constexpr size_t kStaticRowsBytes = (size_t)4 << 20;  // M*K limit (e.g. 256 x 16384)
+static __device__ __align__(256) int8_t g_static_rows[kStaticRowsBytes];
+
+static std::mutex g_static_mu;
+static int8_t *g_static_ptr[64];
+
+// The buffer's address on the current device, looked up once per device.
+// The first lookup can load the module, so it is set-up work: make the first
+// call on each device before any stream capture.
+static int static_rows(int8_t **out) {
+  int dev = 0;
+  FGM_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(FGM_CUDA_ENODEV, "device index %d", dev);
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if (!g_static_ptr[dev]) {
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_rows);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static activation rows)");
+    g_static_ptr[dev] = static_cast<int8_t *>(p);
+  }
+  *out = g_static_ptr[dev];
+  return FGM_CUDA_OK;
+}
+
 // ------------------------------------------------------------- launchers
 static int run_gemm(bool q4, int M, int N, int K, const int8_t *A, const float *a_scale,
                     const void *B, const void *b_scale, int group, float *C, int ldc, int c_col0,
@@ -786,6 +823,33 @@ int fgm_cuda_gemm_q8c_rows(int M, int N, int K, const int8_t *A, int lda, const 
     return fail(FGM_CUDA_EINVAL, "weight %p is not prepared (fgm_cuda_q8c_prepare)", (const void *)B);
   return run_q8c_tc(M, N, K, A, lda, a_scale, b_scale, map, C, ldc, 0, nullptr, n0, n1,
                     (cudaStream_t)stream);
+}
+
+int fgm_cuda_gemm_q8c_noalloc(int M, int N, int K, const int8_t *A, const float *a_scale,
+                              const int8_t *B, const float *b_scale, float *C, int ldc, int n0,
+                              int n1, void *stream) {
+  int rc = check_gemm(M, N, K, ldc, n0, n1, 64, false);
+  if (rc) return rc;
+  if ((size_t)M * (size_t)K > kStaticRowsBytes)
+    return fail(FGM_CUDA_EINVAL,
+                "M*K=%zu bytes exceeds the static activation buffer of %zu bytes "
+                "(fgm_cuda_gemm_q8c_noalloc)",
+                (size_t)M * (size_t)K, kStaticRowsBytes);
+  if (M == 0 || n0 == n1) return FGM_CUDA_OK;
+  if (!A || !a_scale || !B || !b_scale || !C) return fail(FGM_CUDA_EINVAL, "null pointer");
+  if (!aligned16(A) || !aligned16(B))
+    return fail(FGM_CUDA_EINVAL, "activations and weights must be 16-byte aligned");
+  CUtensorMap map;
+  if (!find_prepared(B, &map))
+    return fail(FGM_CUDA_EINVAL, "weight %p is not prepared (fgm_cuda_q8c_prepare)", (const void *)B);
+  int8_t *rows = nullptr;
+  rc = static_rows(&rows);
+  if (rc) return rc;
+  const cudaStream_t st = (cudaStream_t)stream;
+  const cudaError_t e = launch_packed_to_rows(A, rows, M, K, st);
+  if (e != cudaSuccess) return cuda_fail(e, "activation repack");
+  count_launch();
+  return run_q8c_tc(M, N, K, rows, K, a_scale, b_scale, map, C, ldc, 0, nullptr, n0, n1, st);
 }
 
 int fgm_cuda_q8c_prepare(const int8_t *B, int N, int K, void *stream) {

@@ -60,6 +60,14 @@ def gemm_q8c_rows(M, N, K, A, a_scale, B, b_scale, C, lda=None, ldc=None, n0=0, 
          _p(b_scale), _p(C), N if ldc is None else ldc, n0, n1, _s(stream))
 
 
+def gemm_q8c_noalloc(M, N, K, A, a_scale, B, b_scale, C, ldc=None, n0=0, n1=None, stream=None):
+    """gemm_q8c on the tensor-core kernel with no device allocation (prepared
+    weight, M*K <= 4 MiB; concurrent calls on one device race)."""
+    n1 = N // 16 if n1 is None else n1
+    call("fgm_cuda_gemm_q8c_noalloc", M, N, K, _p(A), _p(a_scale), _p(B), _p(b_scale), _p(C),
+         N if ldc is None else ldc, n0, n1, _s(stream))
+
+
 def q8c_prepare(B, N, K, stream=None):
     """Make the tensor-core operand copy of a device int8 weight (large-M path)."""
     call("fgm_cuda_q8c_prepare", _p(B), N, K, _s(stream))

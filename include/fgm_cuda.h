@@ -176,6 +176,22 @@ int fgm_cuda_gemm_q8c_rows(int M, int N, int K, const int8_t *A, int lda,
                            void *stream);
 int fgm_cuda_q8c_release(const int8_t *B);
 
+/* fgm_cuda_gemm_q8c on the tcgen05 kernel without any device allocation, for
+ * callers that may not allocate once serving (a fully reserved HBM budget, or
+ * a host language with no say over the CUDA memory pools).  No reference
+ * counterpart: the reference CPU kernels read the tile-packed A in place.
+ * The tile-packed A is copied to row-major form in a fixed 4 MiB device
+ * buffer owned by the library instead of stream-ordered temporary memory:
+ * M*K > 4194304 is rejected with EINVAL.  The weight must be prepared with
+ * fgm_cuda_q8c_prepare (EINVAL otherwise); any M >= 1 runs the tensor-core
+ * kernel.  The first call on each device is set-up (it resolves the buffer's
+ * address and the device's status word): make it before any stream capture.
+ * One buffer per device: calls that overlap in time (different streams or
+ * host threads) race on it; calls on one stream are ordered. */
+int fgm_cuda_gemm_q8c_noalloc(int M, int N, int K, const int8_t *A, const float *a_scale,
+                              const int8_t *B, const float *b_scale, float *C, int ldc,
+                              int n0, int n1, void *stream);
+
 /* rot and qa may be NULL (not written). */
 int fgm_cuda_prep_rows(const float *src, int lda, float *rot, int8_t *qa,
                        float *qs, int8_t *pa, int m, int k, int hsz, int r0,
