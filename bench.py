@@ -64,6 +64,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--eager", action="store_true",
+                    help="launch the step's kernels directly instead of replaying a CUDA graph "
+                         "(same kernels, same order; used for ncu launch lists)")
     return ap.parse_args()
 
 
@@ -275,37 +278,57 @@ def main():
           for name, K, N in DECODE_SHAPES}
     wbytes_step = L * sum(sum(q4g_bytes(K, N)) for _, K, N in DECODE_SHAPES)
 
-    def step(events=None):
+    def step():
         for l in range(L):
             for i, x in enumerate(xs):
                 D.prep_rows(x, x.shape[1], qss[i], pas[i], M_DECODE, x.shape[1], 0)
             for name, K, N in DECODE_SHAPES:
                 w, s = layers[l][name]
                 i = DECODE_INPUT[name]
-                if events is not None and name == "gate_up":
-                    events[l][0].record()
                 D.gemm_q4g(M_DECODE, N, K, pas[i], qss[i], w, s, GROUP, cs[name])
-                if events is not None and name == "gate_up":
-                    events[l][1].record()
+
+    def gate_up_only():  # the dominant kernel back to back over the L weight copies
+        i = DECODE_INPUT["gate_up"]
+        K, N = 2048, 16384
+        for l in range(L):
+            w, s = layers[l]["gate_up"]
+            D.gemm_q4g(M_DECODE, N, K, pas[i], qss[i], w, s, GROUP, cs["gate_up"])
 
     side = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(side):
+        c0 = lib.fgm_cuda_launch_count()
         step()
+        launches_per_step = lib.fgm_cuda_launch_count() - c0
     torch.cuda.synchronize()
-    c0 = lib.fgm_cuda_launch_count()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=side):
-        step()
-    launches_per_step = lib.fgm_cuda_launch_count() - c0
-    # a twin graph with event-record nodes around the dominant kernel
-    kev = [(torch.cuda.Event(enable_timing=True, external=True),
-            torch.cuda.Event(enable_timing=True, external=True)) for _ in range(L)]
-    tgraph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(tgraph, stream=side):
-        step(kev)
+    if args.eager:
+        graph = tgraph = None
+
+        def run_step():
+            with torch.cuda.stream(side):
+                step()
+
+        def run_gate_up():
+            with torch.cuda.stream(side):
+                gate_up_only()
+    else:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            step()
+        # the dominant kernel alone: L back-to-back launches over distinct weights
+        tgraph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(tgraph, stream=side):
+            gate_up_only()
+
+        def run_step():
+            with torch.cuda.stream(side):
+                graph.replay()
+
+        def run_gate_up():
+            with torch.cuda.stream(side):
+                tgraph.replay()
 
     for _ in range(max(args.warmup, 3)):
-        graph.replay()
+        run_step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -315,10 +338,10 @@ def main():
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        e0.record()
+        e0.record(side)
         for _ in range(args.steps):
-            graph.replay()
-        e1.record()
+            run_step()
+        e1.record(side)
         torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / args.steps
     value = world * wbytes_step / (ms * 1e-3) / 1e9
@@ -326,9 +349,12 @@ def main():
     # ---- roofline of the dominant kernel (gate/up q4g GEMM), CUDA events
     kdur = []
     for _ in range(5):
-        tgraph.replay()
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k0.record(side)
+        run_gate_up()
+        k1.record(side)
         torch.cuda.synchronize()
-        kdur += [a.elapsed_time(b) * 1e-3 for a, b in kev]
+        kdur.append(k0.elapsed_time(k1) * 1e-3 / L)
     K_, N_ = 2048, 16384
     alg = sum(q4g_bytes(K_, N_)) + M_DECODE * K_ + M_DECODE * 4 + M_DECODE * N_ * 4
     kmean = statistics.mean(kdur)
@@ -351,7 +377,10 @@ def main():
                 "frac": achieved / hbm, "traffic": traffic, "peak_source": peak_src,
                 "kernel": "gemv_kernel<q4g, M<=8> gate/up 2048x16384",
                 "algorithmic_bytes_per_launch": alg, "mean_launch_us": kmean * 1e6,
-                "launches_timed": len(kdur)}
+                "launches_timed": len(kdur) * L,
+                "timing": "CUDA events on the launching stream around "
+                          + ("" if args.eager else "a graph of ")
+                          + f"{L} back-to-back launches over distinct weight copies"}
 
     # ---- prefill: W8A8, M = 256
     prefill = None
@@ -383,7 +412,7 @@ def main():
                             f"scales, {L} distinct layer copies, 4 preps + 5 GEMMs per layer",
                 "weight_bytes_per_step": wbytes_step, "l2": "inputs larger than L2 "
                 f"({wbytes_step / 1e6:.0f} MB of weights per step > 2 x 126 MB)",
-                "graph": "one CUDA graph per step", "parallelism": f"replicas x{world}"},
+                "graph": "eager launches (--eager)" if args.eager else "one CUDA graph per step", "parallelism": f"replicas x{world}"},
             "roofline": roofline,
             "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clk.summary(),
@@ -429,18 +458,24 @@ def bench_prefill(args, dev, gen, world):
     with torch.cuda.stream(side):
         step()
     torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=side):
-        step()
-    for _ in range(3):
-        g.replay()
+    if args.eager:
+        run = step
+    else:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            step()
+        run = g.replay
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            run()
     torch.cuda.synchronize()
     steps = max(5, args.steps // 10)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        g.replay()
-    e1.record()
+    with torch.cuda.stream(side):
+        e0.record(side)
+        for _ in range(steps):
+            run()
+        e1.record(side)
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
     ops = copies * sum(2 * M_PREFILL * N * K for _, K, N in PREFILL_SHAPES)
