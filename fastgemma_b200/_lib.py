@@ -36,6 +36,8 @@ SIGNATURES = {
     "fgm_cuda_gemm_q4g": ([_i, _i, _i, _p, _p, _p, _p, _i, _p, _i, _i, _i, _p], _i),
     "fgm_cuda_gemm_q8c": ([_i, _i, _i, _p, _p, _p, _p, _p, _i, _i, _i, _p], _i),
     "fgm_cuda_prep_rows": ([_p, _i, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p], _i),
+    "fgm_cuda_linear_q4g": ([_p, _i, _i, _i, _i, _i, _p, _p, _i, _p, _i, _i, _i, _p], _i),
+    "fgm_cuda_linear_q8c": ([_p, _i, _i, _i, _i, _i, _p, _p, _p, _i, _i, _i, _p], _i),
     "fgm_cuda_q8c_prepare": ([_p, _i, _i, _p], _i),
     "fgm_cuda_gemm_q8c_rows": ([_i, _i, _i, _p, _i, _p, _p, _p, _p, _i, _i, _i, _p], _i),
     "fgm_cuda_q8c_release": ([_p], _i),

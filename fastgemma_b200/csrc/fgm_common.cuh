@@ -65,4 +65,20 @@ __device__ __forceinline__ int cvt_sat_i8(float v) {
   return i > 127 ? 127 : (i < -128 ? -128 : i);
 }
 
+// The same pair as one saturating round-to-nearest-even conversion plus a
+// select: NaN and |v| >= 2^31 (x86 INT32_MIN) give -128.  Returns the byte in
+// the low 8 bits.
+__device__ __forceinline__ uint32_t q8_x86(float v) {
+  int i;
+  asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(i) : "f"(v));
+  return fabsf(v) < 2147483648.0f ? (uint32_t)i : 0x80u;
+}
+
+// Four values scaled by inv and quantised, packed little-endian in a word.
+__device__ __forceinline__ uint32_t q8_quad(float4 v, float inv) {
+  const uint32_t a = q8_x86(__fmul_rn(v.x, inv)), b = q8_x86(__fmul_rn(v.y, inv));
+  const uint32_t c = q8_x86(__fmul_rn(v.z, inv)), d = q8_x86(__fmul_rn(v.w, inv));
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
 }  // namespace fgm

@@ -497,6 +497,37 @@ static int run_prep(const float *src, int lda, float *rot, int8_t *qa, float *qs
   return FGM_CUDA_OK;
 }
 
+// ------------------------------------------------------------- Gemm::run
+// One projection of fgm-core's Gemm::run (forward.rs:128-158) on device
+// buffers: the prep kernel writes the packed (and, for the tensor cores,
+// row-major) int8 rows to stream-ordered temporary memory, then the GEMM.
+static int run_linear(bool q4, const float *src, int lda, int hsz, int M, int N, int K,
+                      const void *B, const void *b_scale, int group, float *C, int ldc, int n0,
+                      int n1, cudaStream_t st) {
+  if (M == 0 || n0 == n1) return FGM_CUDA_OK;
+  CUtensorMap map;
+  const bool tc = !q4 && M >= tc_min_m() && find_prepared(B, &map);
+  const size_t a_len = packed_len(M, K), o_s = align256(a_len);
+  const size_t o_q = o_s + align256((size_t)M * 4), total = o_q + (tc ? align256((size_t)M * K) : 0);
+  void *tmp = nullptr;
+  FGM_TRY(cudaMallocAsync(&tmp, total, st));
+  char *d = static_cast<char *>(tmp);
+  int8_t *qa = tc ? reinterpret_cast<int8_t *>(d + o_q) : nullptr;
+  float *qs = reinterpret_cast<float *>(d + o_s);
+  int rc = run_prep(src, lda, nullptr, qa, qs, reinterpret_cast<int8_t *>(d), M, K, hsz, 0, M, st);
+  if (!rc) {
+    if (tc)
+      rc = run_q8c_tc(M, N, K, qa, K, qs, static_cast<const float *>(b_scale), map, C, ldc, 0,
+                      nullptr, n0, n1, st);
+    else
+      rc = run_gemm(q4, M, N, K, reinterpret_cast<const int8_t *>(d), qs, B, b_scale, group, C,
+                    ldc, 0, nullptr, n0, n1, st);
+  }
+  const cudaError_t f = cudaFreeAsync(tmp, st);
+  if (!rc && f != cudaSuccess) rc = cuda_fail(f, "cudaFreeAsync");
+  return rc;
+}
+
 // Host-pointer GEMM: stage A and a_scale, resolve weights, run, bring back C.
 static int host_gemm(bool q4, int M, int N, int K, const int8_t *A, const float *a_scale,
                      const void *B, const void *b_scale, int group, float *C, int ldc, int n0,
@@ -808,6 +839,35 @@ int fgm_cuda_prep_rows(const float *src, int lda, float *rot, int8_t *qa, float 
   if (rc) return rc;
   if (r0 < r1 && (!src || !qs || !pa)) return fail(FGM_CUDA_EINVAL, "null pointer");
   return run_prep(src, lda, rot, qa, qs, pa, m, k, hsz, r0, r1, (cudaStream_t)stream);
+}
+
+static int check_linear_dev(const float *src, int lda, int hsz, int M, int N, int K, int ldc,
+                            int n0, int n1, int group, bool q4, const void *B,
+                            const void *b_scale, const float *C) {
+  int rc = check_gemm(M, N, K, ldc, n0, n1, group, q4);
+  if (rc) return rc;
+  if ((rc = check_prep(lda, M, K, hsz, 0, M, false))) return rc;
+  if (M > 0 && n0 < n1 && (!src || !B || !b_scale || !C))
+    return fail(FGM_CUDA_EINVAL, "null pointer");
+  return FGM_CUDA_OK;
+}
+
+int fgm_cuda_linear_q4g(const float *src, int lda, int hsz, int M, int N, int K,
+                        const uint8_t *Bq, const uint16_t *b_scale, int group, float *C, int ldc,
+                        int n0, int n1, void *stream) {
+  int rc = check_linear_dev(src, lda, hsz, M, N, K, ldc, n0, n1, group, true, Bq, b_scale, C);
+  if (rc) return rc;
+  return run_linear(true, src, lda, hsz, M, N, K, Bq, b_scale, group, C, ldc, n0, n1,
+                    (cudaStream_t)stream);
+}
+
+int fgm_cuda_linear_q8c(const float *src, int lda, int hsz, int M, int N, int K,
+                        const int8_t *B, const float *b_scale, float *C, int ldc, int n0, int n1,
+                        void *stream) {
+  int rc = check_linear_dev(src, lda, hsz, M, N, K, ldc, n0, n1, 64, false, B, b_scale, C);
+  if (rc) return rc;
+  return run_linear(false, src, lda, hsz, M, N, K, B, b_scale, 64, C, ldc, n0, n1,
+                    (cudaStream_t)stream);
 }
 
 int fgm_cuda_gemm_q8c_rows(int M, int N, int K, const int8_t *A, int lda, const float *a_scale,

@@ -330,6 +330,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     gemv_kernel(const GemvParams p, const GemvPlan pl) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_abort;
+  __shared__ float s_as[16];  // a_scale of the block's rows
   constexpr int TB = Geo<Q4>::TB;
   constexpr int T = Geo<Q4>::T;
   const bool raw = p.acc != nullptr;
@@ -464,6 +465,13 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     }
     __syncthreads();
   }
+  if (!raw) {  // per-row activation scales for the epilogue
+    if (threadIdx.x < MT * 8) {
+      const int m = mb * 16 + threadIdx.x;
+      s_as[threadIdx.x] = m < p.M ? p.a_scale[m] : 0.0f;
+    }
+    __syncthreads();
+  }
 
   float cf[MT][4];
   int32_t gacc[MT][4];
@@ -557,11 +565,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
           if (raw) {
             p.acc[(size_t)m * p.N + n] = gacc[mt][i];
           } else if (Q4) {
-            p.C[(size_t)m * p.ldc + (n - p.c_col0)] = __fmul_rn(cf[mt][i], p.a_scale[m]);
+            p.C[(size_t)m * p.ldc + (n - p.c_col0)] = __fmul_rn(cf[mt][i], s_as[m - mb * 16]);
           } else {
             const float bs = reinterpret_cast<const float *>(p.b_scale)[n];
             p.C[(size_t)m * p.ldc + (n - p.c_col0)] =
-                __fmul_rn(__int2float_rn(gacc[mt][i]), __fmul_rn(bs, p.a_scale[m]));
+                __fmul_rn(__int2float_rn(gacc[mt][i]), __fmul_rn(bs, s_as[m - mb * 16]));
           }
         }
       continue;
@@ -599,7 +607,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
         for (int g = gpub; g < G; g++)
           c = __fmaf_rn(__int2float_rn(xsum[((g - gpub) * MT * 8 + ml) * 16 + nl]),
                         __half2float(sc[(size_t)(g - gpub) * 16]), c);
-        p.C[(size_t)m * p.ldc + (n - p.c_col0)] = __fmul_rn(c, p.a_scale[m]);
+        p.C[(size_t)m * p.ldc + (n - p.c_col0)] = __fmul_rn(c, s_as[ml]);
       } else {
         const int32_t v = xsum[ml * 16 + nl];
         xsum[ml * 16 + nl] = 0;
@@ -609,7 +617,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
         } else {
           const float bs = reinterpret_cast<const float *>(p.b_scale)[n];
           p.C[(size_t)m * p.ldc + (n - p.c_col0)] =
-              __fmul_rn(__int2float_rn(v), __fmul_rn(bs, p.a_scale[m]));
+              __fmul_rn(__int2float_rn(v), __fmul_rn(bs, s_as[ml]));
         }
       }
     }
@@ -640,13 +648,16 @@ cudaError_t launch_t(const GemvParams &p, const GemvPlan &pl, dim3 grid, bool pd
 template <bool Q4, int MT>
 cudaError_t launch_gk(const GemvParams &p, const GemvPlan &pl, dim3 grid, bool pdl,
                       cudaStream_t st) {
-  if (!Q4) return launch_t<Q4, MT, 1>(p, pl, grid, pdl, st);
-  switch (p.group / kTileK) {  // groups that tile a stage exactly
-    case 1: return launch_t<Q4, MT, 1>(p, pl, grid, pdl, st);
-    case 2: return launch_t<Q4, MT, 2>(p, pl, grid, pdl, st);
-    case 4: return launch_t<Q4, MT, 4>(p, pl, grid, pdl, st);
-    case 8: return launch_t<Q4, MT, 8>(p, pl, grid, pdl, st);
-    default: return launch_t<Q4, MT, 0>(p, pl, grid, pdl, st);  // groups spanning stages
+  if constexpr (!Q4) {
+    return launch_t<Q4, MT, 1>(p, pl, grid, pdl, st);
+  } else {
+    switch (p.group / kTileK) {  // groups that tile a stage exactly
+      case 1: return launch_t<Q4, MT, 1>(p, pl, grid, pdl, st);
+      case 2: return launch_t<Q4, MT, 2>(p, pl, grid, pdl, st);
+      case 4: return launch_t<Q4, MT, 4>(p, pl, grid, pdl, st);
+      case 8: return launch_t<Q4, MT, 8>(p, pl, grid, pdl, st);
+      default: return launch_t<Q4, MT, 0>(p, pl, grid, pdl, st);  // groups spanning stages
+    }
   }
 }
 
@@ -666,22 +677,27 @@ GemvPlan plan_gemv(const GemvParams &p, int nblocks, bool q4, int num_sms, size_
   pl.parts = 1;
   pl.ctas_per_sm = 1;
   pl.chunk_tiles = T;
-  // team size: enough (unit, part) pairs to give every warp of the grid work
+  // team size: enough (unit, part) pairs to give every warp of the grid work,
+  // but every part keeps at least one full ring stage of tiles (the unrolled
+  // stage path; thinner parts only add warps that finish their few tiles at
+  // the same moment and a longer serial fold)
   int Pmax = 1;
   const int want = num_sms * kMaxWarps;
   while (Pmax < kMaxWarps && (long)nblocks * Pmax * 2 <= want) {
     const int P2 = Pmax * 2;
-    const bool parts_ok = q4 ? (G % P2 == 0) : (KB % P2 == 0);
+    const bool parts_ok = (q4 ? (G % P2 == 0) : (KB % P2 == 0)) && KB / P2 >= T;
     if (!parts_ok) break;
     Pmax = P2;
   }
   pl.stage_bytes = (T * TB + 127) / 128 * 128;
   const size_t a_bytes = (size_t)KB * MT * 8 * 64;
-  // Largest team size whose exchange area still leaves a useful ring.  Warps
-  // per CTA: enough to cover every (unit, part) pair across all SMs, at most
-  // kMaxWarps, a multiple of the team size.  Then the deepest ring that fits,
-  // preferring activations in shared memory.
+  // Activations in shared memory first (reading them per tile from global
+  // memory exposes L2 latency on every tile), then the largest team size whose
+  // exchange area still leaves a useful ring.  Warps per CTA: enough to cover
+  // every (unit, part) pair across all SMs, at most kMaxWarps, a multiple of
+  // the team size.  Then the deepest ring that fits.
   bool found = false;
+  for (int with_a = 1; with_a >= 0 && !found; with_a--) {
   for (int P = Pmax; P >= 1 && !found; P /= 2) {
     const long pairs = (long)nblocks * P;
     int want_warps = (int)((pairs + num_sms - 1) / num_sms);
@@ -698,7 +714,7 @@ GemvPlan plan_gemv(const GemvParams &p, int nblocks, bool q4, int num_sms, size_
     for (int warps = want_warps; warps >= P && !found; warps -= P) {
       const int teams = warps / P;
       const size_t bars_w = (size_t)warps * 8 * 8;
-      for (int with_a = 1; with_a >= 0 && !found; with_a--) {
+      {
         const size_t fixed = (size_t)teams * xchg_bytes + (with_a ? a_bytes : 0) + bars_w;
         for (int S = 6; S >= 2; S--) {
           const size_t total = fixed + (size_t)warps * S * pl.stage_bytes;
@@ -716,7 +732,11 @@ GemvPlan plan_gemv(const GemvParams &p, int nblocks, bool q4, int num_sms, size_
       }
     }
   }
-  if (!found) pl.smem_bytes = smem_limit + 1;  // caller reports the failure
+  }
+  if (!found) {  // caller reports the failure; stages = 0 marks the plan unusable
+    pl.stages = 0;
+    pl.smem_bytes = smem_limit + 1;
+  }
   const int teams = pl.warps / pl.parts;
   const int ctas_needed = (nblocks + teams - 1) / teams;
   pl.grid_x = ctas_needed < num_sms ? ctas_needed : num_sms;
@@ -727,7 +747,8 @@ cudaError_t launch_gemv(const GemvParams &p, int nblocks, bool q4, bool pdl, int
                         size_t smem_limit, cudaStream_t st) {
   if (nblocks <= 0 || p.M <= 0) return cudaSuccess;
   const GemvPlan pl = plan_gemv(p, nblocks, q4, num_sms, smem_limit);
-  if (pl.smem_bytes > smem_limit) return cudaErrorInvalidConfiguration;
+  if (pl.stages < 2 || pl.warps < 1 || pl.smem_bytes > smem_limit)
+    return cudaErrorInvalidConfiguration;
   const dim3 grid(pl.grid_x, (p.M + 15) / 16);
   const bool mt1 = p.M <= 8;
   if (q4)

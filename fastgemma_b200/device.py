@@ -47,6 +47,21 @@ def prep_rows(src, lda, qs, pa, m, k, hsz, rot=None, qa=None, r0=0, r1=None, str
          _s(stream))
 
 
+def linear_q4g(src, lda, hsz, M, N, K, Bq, b_scale, group, C, ldc=None, n0=0, n1=None,
+               stream=None):
+    """Gemm::run for one int4 projection: f32 rows in, C out (prep fused for M <= 16)."""
+    n1 = N // 16 if n1 is None else n1
+    call("fgm_cuda_linear_q4g", _p(src), lda, hsz, M, N, K, _p(Bq), _p(b_scale), group, _p(C),
+         N if ldc is None else ldc, n0, n1, _s(stream))
+
+
+def linear_q8c(src, lda, hsz, M, N, K, B, b_scale, C, ldc=None, n0=0, n1=None, stream=None):
+    """Gemm::run for one int8 projection (tensor cores for prepared weights, M >= 64)."""
+    n1 = N // 16 if n1 is None else n1
+    call("fgm_cuda_linear_q8c", _p(src), lda, hsz, M, N, K, _p(B), _p(b_scale), _p(C),
+         N if ldc is None else ldc, n0, n1, _s(stream))
+
+
 def packed_a(m: int, k: int, device=None) -> torch.Tensor:
     """An uninitialised packed-activation buffer of ``packed_a_len(m, k)`` bytes."""
     return torch.empty((m + 15) // 16 * 16 * k, dtype=torch.int8, device=device or "cuda")

@@ -154,6 +154,20 @@ int fgm_cuda_gemm_q8c(int M, int N, int K, const int8_t *A, const float *a_scale
                       const int8_t *B, const float *b_scale, float *C, int ldc,
                       int n0, int n1, void *stream);
 
+/* One projection of fgm-core's Gemm::run (forward.rs:128-158) on device
+ * buffers: f32 rows src [M][lda] are rotated (hsz), quantised per row and
+ * multiplied into C [M][ldc], columns [n0*16, n1*16), on `stream`.  The
+ * device form of fgm_linear_q4g_cuda / fgm_linear_q8c_cuda: the prep kernel
+ * writes the int8 rows to stream-ordered temporary memory, then the GEMM
+ * (tcgen05 for prepared int8 weights and M >= 64).  Same contracts as
+ * fgm_cuda_gemm_* and fgm_cuda_prep_rows. */
+int fgm_cuda_linear_q4g(const float *src, int lda, int hsz, int M, int N, int K,
+                        const uint8_t *Bq, const uint16_t *b_scale, int group,
+                        float *C, int ldc, int n0, int n1, void *stream);
+int fgm_cuda_linear_q8c(const float *src, int lda, int hsz, int M, int N, int K,
+                        const int8_t *B, const float *b_scale, float *C, int ldc,
+                        int n0, int n1, void *stream);
+
 /* Tensor-core operand copy of a device-resident int8 weight (the .fgm tiles
  * at B, N x K) as a row-major [N][K] matrix, plus its TMA descriptor, kept
  * until fgm_cuda_q8c_release(B).  Once a weight is prepared,

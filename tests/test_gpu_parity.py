@@ -267,9 +267,93 @@ def test_linear_host_path_matches_oracle(orc):
         assert_bits(c, want, f"linear M={M} K={K} hsz={hsz}")
 
 
+# (M, K, N, hsz, group, lda - K): decode and prefill row counts, Hadamard
+# sizes from none to 2048, padded and unaligned row pitches
+LINEAR_CASES = [(1, 2048, 512, 0, 64, 0), (8, 2048, 2048, 128, 64, 4), (3, 192, 128, 64, 64, 0),
+                (16, 1024, 256, 128, 128, 8), (13, 3072, 256, 16, 64, 0),
+                (8, 8192, 256, 128, 64, 0), (5, 2048, 256, 1024, 256, 0),
+                (8, 2048, 256, 8, 64, 0), (2, 4096, 128, 2, 512, 0), (9, 64, 64, 32, 64, 0),
+                (8, 2048, 256, 128, 64, 1), (20, 2048, 256, 128, 64, 0),
+                (4, 16384, 128, 128, 64, 0), (6, 4096, 128, 2048, 64, 0)]
+
+
+@pytest.mark.parametrize("M,K,N,hsz,group,pad", LINEAR_CASES)
+def test_linear_device_matches_prep_then_gemm(orc, M, K, N, hsz, group, pad):
+    """fgm_cuda_linear_q4g / _q8c (Gemm::run on device buffers) against the
+    oracle's prep_rows followed by its GEMM: bit-exact f32 in the written
+    column range, untouched elsewhere."""
+    lda = K + pad
+    rng = np.random.default_rng(M * 7 + K + hsz + pad)
+    x = (rng.standard_normal((M, lda)) * rng.uniform(0.1, 4, size=(M, 1))).astype(np.float32)
+    if M > 2:
+        x[1] = 0  # an all-zero row quantises with scale 1
+    _, _, qs, pa = orc.prep_rows(x, M, K, hsz, lda=lda)
+    bq, s4 = F.synth_q4g(N, K, group, N + K)
+    b8, s8 = F.synth_q8c(N, K, N + 3)
+    ldc, n0, n1 = N + 16, (4 if N >= 128 else 0), N // 16
+    xd = D(x)
+    c4 = torch.full((M, ldc), -5.0, device="cuda")
+    c8 = torch.full((M, ldc), -5.0, device="cuda")
+    fg.device.linear_q4g(xd, lda, hsz, M, N, K, D(bq), D(s4), group, c4, ldc, n0, n1)
+    fg.device.linear_q8c(xd, lda, hsz, M, N, K, D(b8), D(s8), c8, ldc, n0, n1)
+    torch.cuda.synchronize()
+    from fastgemma_b200 import _lib
+    assert _lib.lib().fgm_cuda_device_status() == 0
+    want4 = np.full((M, ldc), -5.0, np.float32)
+    orc.gemm_q4g(M, N, K, pa, qs, bq, s4, group, c=want4, ldc=ldc, n0=n0, n1=n1)
+    assert_bits(c4.cpu().numpy(), want4, f"linear_q4g M={M} K={K} hsz={hsz}")
+    want8 = np.full((M, ldc), -5.0, np.float32)
+    orc.gemm_q8c(M, N, K, pa, qs, b8, s8, c=want8, ldc=ldc, n0=n0, n1=n1)
+    assert_bits(c8.cpu().numpy(), want8, f"linear_q8c M={M} K={K} hsz={hsz}")
+
+
+def test_linear_device_special_values(orc):
+    """Rows the x86 conversion pair treats specially (ops.c:186-197): a
+    denormal maximum (1/s overflows to inf), +-inf entries (NaN products ->
+    INT32_MIN -> -128), values near FLT_MAX, negative zeros.  The fused
+    preamble and the prep kernel must both reproduce the reference."""
+    M, K, N = 8, 1024, 128
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    x[0] = rng.standard_normal(K).astype(np.float32) * np.float32(1e-41)  # denormals
+    x[1, 5], x[1, 77] = np.inf, -np.inf
+    x[2] = rng.uniform(-3.4e38, 3.4e38, K).astype(np.float32)
+    x[3] = -0.0
+    x[4, 10] = 3e-39  # one denormal next to normal values
+    bq, s4 = F.synth_q4g(N, K, 64, 9)
+    for hsz in (0, 64):
+        _, _, qs, pa = orc.prep_rows(x, M, K, hsz)
+        c = torch.full((M, N), -5.0, device="cuda")
+        fg.device.linear_q4g(D(x), K, hsz, M, N, K, D(bq), D(s4), 64, c)
+        torch.cuda.synchronize()
+        want = orc.gemm_q4g(M, N, K, pa, qs, bq, s4, 64)
+        got = c.cpu().numpy()
+        same = (got.view(np.uint32) == want.view(np.uint32)) | (np.isnan(got) & np.isnan(want))
+        assert same.all(), f"hsz={hsz}: {int((~same).sum())} differ"
+
+
+def test_linear_q8c_device_tensor_core_path(orc):
+    """M >= 64 with a prepared weight: prep into temporary memory, then tcgen05."""
+    M, K, N, hsz = 256, 2048, 512, 128
+    x = np.random.default_rng(11).standard_normal((M, K)).astype(np.float32)
+    _, _, qs, pa = orc.prep_rows(x, M, K, hsz)
+    b8, s8 = F.synth_q8c(N, K, 17)
+    bd = D(b8)
+    fg.device.q8c_prepare(bd, N, K)
+    try:
+        c = torch.empty((M, N), device="cuda")
+        fg.device.linear_q8c(D(x), K, hsz, M, N, K, bd, D(s8), c)
+        torch.cuda.synchronize()
+        assert_bits(c.cpu().numpy(), orc.gemm_q8c(M, N, K, pa, qs, b8, s8), "linear_q8c tc")
+    finally:
+        fg.device.q8c_release(bd)
+
+
 @pytest.mark.parametrize("m,k,lda,hsz", [(1, 64, 64, 0), (7, 2048, 2100, 128), (16, 256, 256, 4),
                                          (20, 512, 512, 32), (256, 2048, 2048, 128),
-                                         (3, 16384, 16384, 2048)])
+                                         (3, 16384, 16384, 2048), (5, 3072, 3075, 1024),
+                                         (9, 16384, 16384, 128), (2, 192, 192, 64),
+                                         (4, 8192, 8192, 512), (33, 32768, 32768, 128)])
 def test_prep_device_vs_oracle(orc, m, k, lda, hsz):
     x = np.random.default_rng(m + k + hsz).standard_normal((m, lda)).astype(np.float32) * 3
     rot, qa, qs, pa = orc.prep_rows(x, m, k, hsz, lda=lda)
