@@ -122,6 +122,19 @@ __device__ __forceinline__ void scale_pair(uint32_t v, int base, int g8, float &
   s1 = f16_to_f32(w1 >> sh);
 }
 
+// Exact int32 -> f32 for |x| <= 2^22 without the quarter-rate converter:
+// 1.5 * 2^23 + x is an exact float whose mantissa holds x, so subtracting
+// 1.5 * 2^23 recovers x.  A scale group's sum fits when the group has at
+// most 4096 values (|a * w| <= 128 * 8 per product); larger groups convert
+// with cvt (i2f_group).
+constexpr int kExactGroupMax = 4096;
+__device__ __forceinline__ float i2f_exact(int32_t x) {
+  return __fadd_rn(__int_as_float(x + 0x4B400000), -12582912.0f);
+}
+__device__ __forceinline__ float i2f_group(int32_t x, bool exact_ok) {
+  return exact_ok ? i2f_exact(x) : __int2float_rn(x);
+}
+
 // Per-lane constants shared by the stage routines.
 struct Lane {
   int g8, tig, lane;
@@ -197,13 +210,11 @@ __device__ __forceinline__ void stage_full(uint32_t st, uint32_t ab, const Lane 
     if (MODE == 0) {
       float s0, s1;
       scale_pair(lg < 4 ? sc0 : sc1, (lg & 3) * 8, L.g8, s0, s1);
-      s0 = __fmul_rn(s0, 0.0625f);
-      s1 = __fmul_rn(s1, 0.0625f);
 #pragma unroll
       for (int mt = 0; mt < MT; mt++)
 #pragma unroll
         for (int i = 0; i < 4; i++)
-          cf[mt][i] = __fmaf_rn(__int2float_rn(gacc[mt][i]), i < 2 ? s0 : s1, cf[mt][i]);
+          cf[mt][i] = __fmaf_rn(i2f_exact(gacc[mt][i] >> 4), i < 2 ? s0 : s1, cf[mt][i]);
     } else {
 #pragma unroll
       for (int mt = 0; mt < MT; mt++)
@@ -299,7 +310,8 @@ __device__ __forceinline__ void stage_generic(uint32_t st, uint32_t a_sm, const 
       for (int mt = 0; mt < MT; mt++)
 #pragma unroll
         for (int i = 0; i < 4; i++)
-          cf[mt][i] = __fmaf_rn(__int2float_rn(gacc[mt][i] >> 4), i < 2 ? s0 : s1, cf[mt][i]);
+          cf[mt][i] = __fmaf_rn(i2f_group(gacc[mt][i] >> 4, GK || p.group <= kExactGroupMax),
+                                i < 2 ? s0 : s1, cf[mt][i]);
     } else {
 #pragma unroll
       for (int mt = 0; mt < MT; mt++)
@@ -601,11 +613,12 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
           continue;
         }
         // continue part 0's chain through the published groups, in order
+        const bool exact_ok = p.group <= kExactGroupMax;
         const __half *sc = reinterpret_cast<const __half *>(xscale) + nl;
         float c = cpart[o];
 #pragma unroll 8
         for (int g = gpub; g < G; g++)
-          c = __fmaf_rn(__int2float_rn(xsum[((g - gpub) * MT * 8 + ml) * 16 + nl]),
+          c = __fmaf_rn(i2f_group(xsum[((g - gpub) * MT * 8 + ml) * 16 + nl], exact_ok),
                         __half2float(sc[(size_t)(g - gpub) * 16]), c);
         p.C[(size_t)m * p.ldc + (n - p.c_col0)] = __fmul_rn(c, s_as[ml]);
       } else {

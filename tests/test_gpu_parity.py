@@ -188,6 +188,25 @@ def test_q4g_group_sizes_and_row_blocks(orc, group, M):
     assert_bits(c.cpu().numpy(), orc.gemm_q4g(M, N, K, pa, a_s, bq, s, group))
 
 
+@pytest.mark.parametrize("group", [64, 512, 4096, 8192])
+def test_q4g_extreme_group_sums(orc, group):
+    """Scale-group sums at and past 2^22 (every product +1024 or -1016): the
+    kernel's exact int32 -> f32 conversion covers groups of up to 4096
+    values, larger groups take the converter; both must match exactly."""
+    M, K, N = 3, 8192, 64
+    A = np.full((M, K), -128, np.int8)
+    A[1] = 127
+    A[2, 1::2] = 127
+    bq = np.full(N * K // 2, 0x88, np.uint8)  # every weight -8
+    s = np.full((K // group, N), 1.0, np.float16)
+    a_s = np.ones(M, np.float32)
+    pa = F.pack_a(A)
+    c = torch.zeros((M, N), device="cuda")
+    fg.device.gemm_q4g(M, N, K, D(pa), D(a_s), D(bq), D(s.view(np.uint16)), group, c)
+    torch.cuda.synchronize()
+    assert_bits(c.cpu().numpy(), orc.gemm_q4g(M, N, K, pa, a_s, bq, s, group))
+
+
 def test_partial_range_ldc_and_untouched(orc):
     """Only rows < M and columns [n0*16, n1*16) are written (amx_gemm.c:333)."""
     M, N, K, n0, n1, ldc = 5, 512, 1024, 8, 20, 600
