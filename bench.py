@@ -18,6 +18,8 @@ CUDA graph and replayed.
 (GB/s).  ``e2e`` = the same metric through the host-pointer C ABI
 (fgm_linear_q4g_cuda: pinned host X in, pinned host C out, every call).
 ``prefill`` = BASELINE config 2 (W8A8, M = 256) in int8 TOPS.
+``lm_head`` = BASELINE config 3's int4 LM head (N = 262144, M = 8) split by
+output columns over the ranks with an NCCL all-gather of the logits.
 ``cpu_baseline`` = the reference's own CPU kernels (AMX, else VNNI) on the
 host cores over a bounded sample of the same workload.
 
@@ -45,6 +47,7 @@ DECODE_SHAPES = [("q", 2048, 2048), ("kv", 2048, 512), ("o", 2048, 2048),
 # which activation feeds each projection: q and kv share the attention input
 DECODE_INPUT = {"q": 0, "kv": 0, "o": 1, "gate_up": 2, "down": 3}
 PREFILL_SHAPES = [("gate_up", 2048, 16384), ("down", 8192, 2048)]
+LM_HEAD_N = 262144
 M_DECODE, GROUP, M_PREFILL = 8, 64, 256
 
 
@@ -64,6 +67,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-lm-head", action="store_true")
     ap.add_argument("--eager", action="store_true",
                     help="launch the step's kernels directly instead of replaying a CUDA graph "
                          "(same kernels, same order; used for ncu launch lists)")
@@ -382,6 +386,11 @@ def main():
                           + ("" if args.eager else "a graph of ")
                           + f"{L} back-to-back launches over distinct weight copies"}
 
+    # ---- LM head, column-sharded over the ranks
+    lm_head = None
+    if not args.no_lm_head:
+        lm_head = bench_lm_head(args, dev, gen, world, rank)
+
     # ---- prefill: W8A8, M = 256
     prefill = None
     if not args.no_prefill:
@@ -416,13 +425,59 @@ def main():
             "roofline": roofline,
             "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clk.summary(),
-            "e2e": e2e, "prefill": prefill, "cpu_baseline": cpu,
+            "e2e": e2e, "prefill": prefill, "lm_head": lm_head, "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         del graph, tgraph
         dist.destroy_process_group()
+
+
+def bench_lm_head(args, dev, gen, world, rank):
+    """BASELINE config 3's LM head (int4, N = 262144, K = 2048, M = 8) split by
+    output columns over the ranks, logits all-gathered over NCCL."""
+    import torch
+    from fastgemma_b200 import device as D
+    from fastgemma_b200 import shard as S
+    N, K, M = LM_HEAD_N, 2048, M_DECODE
+    nb0, nb1 = S.shard_nblocks(N // 16, world, rank)
+    cols = (nb1 - nb0) * 16
+    w = torch.randint(0, 256, (cols * K // 2,), dtype=torch.uint8, device=dev, generator=gen)
+    s = torch.empty((K // GROUP, cols), dtype=torch.float32, device=dev).uniform_(
+        0.005, 0.02, generator=gen).half()
+    sh = S.ColumnShardedGemm("q4g", None, None, N, K, GROUP, rank=rank, world=world, device=dev,
+                             shard=(w, s))
+    x = torch.randn((M, K), dtype=torch.float32, device=dev, generator=gen)
+    pa = D.packed_a(M, K, dev)
+    qs = torch.empty(M, dtype=torch.float32, device=dev)
+    D.prep_rows(x, K, qs, pa, M, K, 0)
+    out = torch.empty((M, N), dtype=torch.float32, device=dev)
+    steps = max(10, args.steps // 4)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
+
+    ms_gemm = timed(lambda: sh.local(M, pa, qs))
+    ms_step = timed(lambda: sh(M, pa, qs, out))
+    wbytes = sum(q4g_bytes(K, N))
+    return {"value": wbytes / (ms_step * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms_step,
+            "gemm_ms": ms_gemm, "steps": steps,
+            "workload": f"BASELINE config 3 LM head: int4 q4g {N}x{K} group {GROUP} f16 scales, "
+                        f"M={M}, {world}-way output-column shards + NCCL all-gather of the "
+                        f"logits (group-32 f32 scales are outside the fgm-kernels format)"}
 
 
 def bench_prefill(args, dev, gen, world):

@@ -535,3 +535,27 @@ def test_q8c_rows_entry_from_quantiser(orc, M, K, N):
         fg.device.q8c_release(bd)
     with pytest.raises(fg.FgmCudaError):  # unprepared weights are refused, not computed slowly
         fg.device.gemm_q8c_rows(M, N, K, qad, qsd, bd, sd, c)
+
+
+# ------------------------------------------------ column-sharded large-N GEMM
+@pytest.mark.parametrize("kind,world", [("q4g", 1), ("q4g", 2), ("q4g", 8), ("q8c", 3)])
+def test_column_shards_on_device_assemble_to_the_whole_gemm(orc, kind, world):
+    """Every rank's shard (the LM-head split) run on one device and assembled
+    equals the unsplit GEMM bit for bit."""
+    from fastgemma_b200 import shard as S
+    M, N, K = 8, 4096, 2048
+    if kind == "q4g":
+        blob, scale = F.synth_q4g(N, K, 64, 21, structured=False)
+    else:
+        blob, scale = F.synth_q8c(N, K, 21, structured=False)
+    rng = np.random.default_rng(4)
+    pa = F.pack_a(rng.integers(-128, 128, size=(M, K), dtype=np.int8))
+    a_s = rng.uniform(0.01, 0.1, size=M).astype(np.float32)
+    shards = [S.ColumnShardedGemm(kind, blob, scale, N, K, 64, rank=r, world=world, device="cuda")
+              for r in range(world)]
+    blocks = torch.stack([sh.local(M, D(pa), D(a_s)).clone() for sh in shards])
+    out = S.assemble(blocks, shards[0].ranges, torch.empty((M, N), device="cuda"))
+    torch.cuda.synchronize()
+    want = (orc.gemm_q4g(M, N, K, pa, a_s, blob, scale, 64) if kind == "q4g"
+            else orc.gemm_q8c(M, N, K, pa, a_s, blob, scale))
+    assert_bits(out.cpu().numpy(), want, f"{kind} world={world}")
