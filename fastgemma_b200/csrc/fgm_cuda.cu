@@ -386,10 +386,8 @@ static int run_q8c_tc(int M, int N, int K, const int8_t *A, int lda, const float
   p.acc = acc;
   p.nb0 = n0;
   p.n_end = n1 * 16;
-  p.stages = 4;
-  while (p.stages > 2 && q8c_tc_smem_bytes(p.stages) > di->smem_optin) p.stages--;
   p.err = di->err;
-  cudaError_t e = launch_q8c_tc(p, lda, map, use_pdl(), st);
+  cudaError_t e = launch_q8c_tc(p, lda, map, use_pdl(), di->sms, di->smem_optin, st);
   if (e != cudaSuccess) return cuda_fail(e, "gemm_q8c tensor-core launch");
   count_launch();
   return FGM_CUDA_OK;

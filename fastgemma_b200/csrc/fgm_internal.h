@@ -68,9 +68,11 @@ struct TcParams {
   int32_t *acc;           // raw accumulators [M][N] instead of C (debug launches)
   int nb0;                // first n-block
   int n_end;              // one past the last output column
-  int stages;             // ring depth
+  int stages;             // ring depth (set by the launcher)
   int *err;
   int tma_store;          // write C through TMA stores (set by the launcher)
+  int splits;             // K split across a cluster of this many CTAs (set by the launcher)
+  int out_v4;             // C rows 16-byte aligned: vector stores allowed (set by the launcher)
 };
 
 }  // namespace fgm
@@ -85,10 +87,10 @@ cudaError_t launch_q8c_rows(const int8_t *tiles, int8_t *rows, int N, int K, cud
 // tile-packed activations -> row-major [M][K].
 cudaError_t launch_packed_to_rows(const int8_t *packed, int8_t *rows, int M, int K,
                                   cudaStream_t st);
-size_t q8c_tc_smem_bytes(int stages);
-// p.A is row-major with leading dimension lda bytes.
+// p.A is row-major with leading dimension lda bytes.  The launcher picks the
+// tile height, K split (cluster size) and ring depth for the device.
 cudaError_t launch_q8c_tc(const TcParams &p, int lda, const CUtensorMap &tmB, bool pdl,
-                          cudaStream_t st);
+                          int num_sms, size_t smem_limit, cudaStream_t st);
 constexpr int kTcBoxRowsB = 128;  // output columns per CTA tile
 
 // Number of kernel launches issued by this library (instrumentation).

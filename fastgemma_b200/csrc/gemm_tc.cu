@@ -18,17 +18,27 @@
 //
 // Pipeline
 // --------
-// One CTA owns a 256 x 128 output tile (two M=128 halves sharing each B
-// tile) and walks K in 128-byte stages through a 4-deep ring: warp 0 (one
-// lane) issues the TMA loads, warp 1 (one lane) issues four K=32 MMAs per
-// half per stage and commits each stage back to the producer, warp 2 owns
-// the tensor-memory allocation, warps 4-7 drain the accumulators (tcgen05.ld,
-// 32 lanes each) and apply the f32 epilogue.  Every mbarrier wait is bounded
-// in time; a kernel that gives up sets the device error flag and still
-// releases its tensor memory.
+// One CTA owns a BM x 128 output tile (BM = 256: two M=128 halves sharing
+// each B tile; BM = 128 when that leaves too few tiles) and walks its K range in 128-byte stages through a 4-deep ring: warp
+// 0 (one lane) issues the TMA loads, warp 1 (one lane) issues four K=32 MMAs
+// per half per stage and commits each stage back to the producer, warp 2 owns
+// the tensor-memory allocation; then all eight warps drain the accumulators
+// (tcgen05.ld, each warp its TMEM lane quadrant and half of the columns) and
+// apply the f32 epilogue, staged in shared memory for TMA stores.
+//
+// When the output has too few tiles to occupy the SMs (the 8192 x 2048 down
+// projection has 16), a cluster of up to 8 CTAs splits each tile's K range.
+// The int32 partial tiles meet in the CTAs' idle operand rings: after a
+// cluster barrier every CTA pushes each partial row into the shared memory of
+// the CTA that owns it (rows z*BM/splits.. belong to CTA z), which sums them
+// after a second barrier.  Integer addition is exact in any order, so the
+// result is bit-identical to the unsplit sum.  Every mbarrier wait is bounded
+// in time; a kernel that gives up sets the device error flag, still reaches
+// every cluster barrier and releases its tensor memory.
 
 #include <cuda.h>
 
+#include <atomic>
 #include <cstring>
 
 #include "fgm_common.cuh"
@@ -39,40 +49,67 @@ namespace fgm {
 
 namespace {
 
-constexpr int kTcBM = 256;  // two M=128 halves
+constexpr int kTcBMax = 256;  // at most two M=128 halves per tile
 constexpr int kTcBN = 128;
 constexpr int kTcBK = 128;  // bytes of K per stage
 constexpr int kTcThreads = 256;
-constexpr int kTcA = kTcBM * kTcBK;
 constexpr int kTcB = kTcBN * kTcBK;
-constexpr int kTcStage = kTcA + kTcB;
-constexpr int kTcTmemCols = 2 * kTcBN;
+static_assert(kTcThreads == kTcBMax, "one thread per tile row loads the activation scales");
+
+// Tile geometry for H M-halves of 128 rows (H = 1 or 2).
+template <int H>
+struct TcTile {
+  static constexpr int BM = 128 * H;
+  static constexpr int A = BM * kTcBK;       // activation bytes per stage
+  static constexpr int Stage = A + kTcB;     // bytes per ring stage
+  static constexpr int TmemCols = H * kTcBN;  // int32 accumulator columns
+  static constexpr size_t Out = (size_t)(kTcBN / 32) * BM * 128;  // staged output tile
+};
 
 __device__ __forceinline__ void st_global_v4(float *p, float a, float b, float c, float d) {
   asm volatile("st.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
                : "memory");
 }
 
+// Split-K buffers in the idle operand ring, int32 rows of 512 bytes (32
+// sixteen-byte chunks, chunk c of row r stored at chunk c ^ (r & 7):
+// conflict-free for the per-row writes and the per-chunk reads):
+//   send  [BM rows]: this CTA's partial tile; rows [j*R, (j+1)*R) go to CTA j
+//   recv  [splits-1 slots][R rows] at BM*512: the other CTAs' partials of
+//         this CTA's own rows [z*R, (z+1)*R), slot (j < z ? j : j - 1).
+__device__ __forceinline__ uint32_t row_off(int r, int chunk) {
+  return (uint32_t)(r * 512 + ((chunk ^ (r & 7)) << 4));
+}
+
+template <int H>
 __global__ void __launch_bounds__(kTcThreads, 1)
     q8c_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmC, const TcParams p) {
+  using T = TcTile<H>;
+  constexpr int BM = T::BM;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // stage buffers must sit on 1 KB boundaries for the swizzle pattern
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int S = p.stages;
-  constexpr size_t kOutBytes = (size_t)(kTcBN / 32) * kTcBM * 128;  // staged f32 tile
-  const size_t ring = (size_t)S * kTcStage > kOutBytes ? (size_t)S * kTcStage : kOutBytes;
+  const size_t ring = (size_t)S * T::Stage > T::Out ? (size_t)S * T::Stage : T::Out;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + ring);
   uint64_t *empty = full + S;
   uint64_t *accum = empty + S;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
-  __shared__ int s_fail;
+  uint64_t *recv_bar = accum + 1;  // split K: the peers' partials have landed
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(recv_bar + 1);
+  __shared__ int s_fail, s_any_fail;
+  __shared__ float s_as[kTcBMax];  // a_scale of the tile's rows
+  __shared__ float s_bs[kTcBN];  // b_scale of the tile's columns
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KS = (p.K + kTcBK - 1) / kTcBK;
-  const int m0 = blockIdx.y * kTcBM;
+  const int m0 = blockIdx.y * BM;
   const int n0 = p.nb0 * 16 + blockIdx.x * kTcBN;
+  // K slice of this CTA: the cluster's CTAs split the tile's K range evenly
+  const int splits = p.splits, z = splits > 1 ? (int)tc::cluster_ctarank() : 0;
+  const int ks0 = (int)((long)KS * z / splits), ks1 = (int)((long)KS * (z + 1) / splits);
+  const int nks = ks1 - ks0;
 
   if (threadIdx.x == 0) {
     s_fail = 0;
@@ -81,12 +118,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc::mbar_init(&empty[s], 1);
     }
     tc::mbar_init(accum, 1);
+    tc::mbar_init(recv_bar, 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmA);
     tc::prefetch_tmap(&tmB);
   }
+  if (threadIdx.x < kTcBN) {  // weight scales do not depend on earlier kernels
+    const int n = n0 + threadIdx.x;
+    s_bs[threadIdx.x] = (p.b_scale && n < p.n_end) ? p.b_scale[n] : 0.0f;
+  }
   if (warp == 2) {
-    tc::tmem_alloc(tmem_slot, kTcTmemCols);
+    tc::tmem_alloc(tmem_slot, T::TmemCols);
     tc::tmem_relinquish();
   }
   tc::fence_before_sync();
@@ -97,121 +139,202 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (warp == 0 && lane == 0) {  // ---------------------------------- producer
     asm volatile("griddepcontrol.wait;" ::: "memory");  // activations from earlier kernels
-    for (int ks = 0; ks < KS; ks++) {
-      const int s = ks % S;
-      if (ks >= S && !tc::mbar_wait(&empty[s], ((ks / S) & 1) ^ 1)) {
+    for (int i = 0; i < nks; i++) {
+      const int s = i % S;
+      if (i >= S && !tc::mbar_wait(&empty[s], ((i / S) & 1) ^ 1)) {
         s_fail = 1;
         break;
       }
-      uint8_t *sa = smem + (size_t)s * kTcStage;
-      tc::mbar_expect_tx(&full[s], kTcStage);
-      tc::tma_load_2d(sa, &tmA, &full[s], ks * kTcBK, m0);
-      tc::tma_load_2d(sa + kTcA, &tmB, &full[s], ks * kTcBK, n0);
+      uint8_t *sa = smem + (size_t)s * T::Stage;
+      tc::mbar_expect_tx(&full[s], T::Stage);
+      tc::tma_load_2d(sa, &tmA, &full[s], (ks0 + i) * kTcBK, m0);
+      tc::tma_load_2d(sa + T::A, &tmB, &full[s], (ks0 + i) * kTcBK, n0);
     }
   } else if (warp == 1 && lane == 0) {  // ---------------------------- MMA
     const uint32_t idesc = tc::idesc_i8(128, kTcBN);
-    for (int ks = 0; ks < KS; ks++) {
-      const int s = ks % S;
-      if (!tc::mbar_wait(&full[s], (ks / S) & 1)) {
+    for (int i = 0; i < nks; i++) {
+      const int s = i % S;
+      if (!tc::mbar_wait(&full[s], (i / S) & 1)) {
         s_fail = 1;
         break;
       }
       tc::fence_after_sync();
-      const uint32_t sa = tc::smem_u32(smem + (size_t)s * kTcStage);
-      const uint32_t sb = sa + kTcA;
+      const uint32_t sa = tc::smem_u32(smem + (size_t)s * T::Stage);
+      const uint32_t sb = sa + T::A;
 #pragma unroll
-      for (int h = 0; h < 2; h++)
+      for (int h = 0; h < H; h++)
 #pragma unroll
         for (int j = 0; j < kTcBK / 32; j++)  // K=32 slices of the 128-byte stage
           tc::mma_i8(tmem + h * kTcBN, tc::sdesc_sw128(sa + h * 128 * kTcBK + j * 32),
-                     tc::sdesc_sw128(sb + j * 32), idesc, (ks | j) != 0);
+                     tc::sdesc_sw128(sb + j * 32), idesc, (i | j) != 0);
       tc::mma_commit(&empty[s]);  // stage s is free once these MMAs complete
     }
     tc::mma_commit(accum);
-  } else if (warp >= 4) {  // ------------------------------------- epilogue
-    const int q = warp - 4;  // TMEM lane quadrant
-    bool ok = tc::mbar_wait(accum, 0);
-    if (!ok) s_fail = 1;
-    tc::fence_after_sync();
-    if (ok) {
-      asm volatile("griddepcontrol.wait;" ::: "memory");
-      // f32 tile staged in the (now idle) ring as four 32-column blocks of
-      // [256 rows][128 B], 128-byte swizzled, then written by TMA stores that
-      // the output map clips to rows < M and columns [nb0*16, n_end).
-      const bool tma_out = p.tma_store && !p.acc;
+  }
+  __syncwarp();
+
+  // ------------------------------------------------------------ epilogue
+  // All eight warps drain the accumulators: warp w reads TMEM lane quadrant
+  // w % 4 (rows 32(w%4).. of each M half) and the 64-column half w / 4.
+  const bool ok = __all_sync(0xffffffffu, tc::mbar_wait(accum, 0));  // warp-uniform
+  if (!ok) s_fail = 1;
+  tc::fence_after_sync();
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // a_scale comes from earlier kernels
+  if (threadIdx.x < BM) {
+    const int m = m0 + threadIdx.x;
+    s_as[threadIdx.x] = (p.a_scale && m < p.M) ? p.a_scale[m] : 0.0f;
+  }
+  __syncthreads();
+  // split K: every CTA of the cluster is past its main loop (its ring is free
+  // to receive partials, its failure flag final) before anyone pushes
+  if (splits > 1) {
+    // expect every peer's copy before anyone can send one
+    if (threadIdx.x == 0)
+      tc::mbar_expect_tx(recv_bar, (uint32_t)((splits - 1) * (BM / splits) * 512));
+    tc::cluster_sync();
+    if (threadIdx.x == 0) {  // did any CTA of the cluster fail?
+      int any = 0;
+      for (int src = 0; src < splits; src++) {
+        int f;
+        asm volatile("ld.shared::cluster.u32 %0, [%1];"
+                     : "=r"(f)
+                     : "r"(tc::mapa(tc::smem_u32(&s_fail), (uint32_t)src))
+                     : "memory");
+        any |= f;
+      }
+      s_any_fail = any;
+    }
+  }
+  const int q = warp & 3, ch = warp >> 2;
+  const bool tma_out = p.tma_store != 0;  // launcher: no raw output, no split, aligned
+  if (ok && !s_fail) {
 #pragma unroll 1
-      for (int h = 0; h < 2; h++) {
-        const int ml = h * 128 + q * 32 + lane;
-        const int m = m0 + ml;
-        const bool row_ok = m < p.M;
-        const float as = (row_ok && p.a_scale) ? p.a_scale[m] : 0.0f;
-        // 64 columns per round: two 32-column TMEM loads in flight, one wait
-#pragma unroll 1
-        for (int c64 = 0; c64 < kTcBN / 64; c64++) {
-          uint32_t v[64];
-          const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + h * kTcBN + c64 * 64;
-          tc::tmem_ld_x32(ta, v);
-          tc::tmem_ld_x32(ta + 32, v + 32);
-          tc::tmem_wait_ld();
+    for (int h = 0; h < H; h++) {
+      const int ml = h * 128 + q * 32 + lane;
+      const int m = m0 + ml;
+      const bool row_ok = m < p.M;
+      const float as = s_as[ml];
+      uint32_t v[64];
+      const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + h * kTcBN + ch * 64;
+      tc::tmem_ld_x32(ta, v);
+      tc::tmem_ld_x32(ta + 32, v + 32);
+      tc::tmem_wait_ld();
+      if (splits > 1) {  // int32 partial row into the send buffer
 #pragma unroll
-          for (int cc = 0; cc < 4; cc++) {
-            const int c = c64 * 4 + cc;  // 16-column chunk of the tile
-            const int n = n0 + c * 16;
-            if (p.acc) {
-              if (row_ok && n < p.n_end)
-                for (int e = 0; e < 16; e++)
-                  p.acc[(size_t)m * p.N + n + e] = (int32_t)v[cc * 16 + e];
-              continue;
-            }
-            if (n >= p.n_end) continue;
-            float o[16];
-            const float4 *bs4 = reinterpret_cast<const float4 *>(p.b_scale + n);
+        for (int c4 = 0; c4 < 16; c4++)
+          *reinterpret_cast<uint4 *>(smem + row_off(ml, ch * 16 + c4)) =
+              make_uint4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
+        continue;
+      }
 #pragma unroll
-            for (int e4 = 0; e4 < 4; e4++) {
-              const float4 b = __ldg(bs4 + e4);
-              const uint32_t *u = v + cc * 16 + 4 * e4;
-              o[4 * e4 + 0] = __fmul_rn(__int2float_rn((int32_t)u[0]), __fmul_rn(b.x, as));
-              o[4 * e4 + 1] = __fmul_rn(__int2float_rn((int32_t)u[1]), __fmul_rn(b.y, as));
-              o[4 * e4 + 2] = __fmul_rn(__int2float_rn((int32_t)u[2]), __fmul_rn(b.z, as));
-              o[4 * e4 + 3] = __fmul_rn(__int2float_rn((int32_t)u[3]), __fmul_rn(b.w, as));
-            }
-            if (tma_out) {
-              uint8_t *rowp = smem + (size_t)(c >> 1) * (kTcBM * 128) + (size_t)ml * 128;
+      for (int cc = 0; cc < 4; cc++) {
+        const int c = ch * 4 + cc;  // 16-column chunk of the tile
+        const int n = n0 + c * 16;
+        if (p.acc) {
+          if (row_ok && n < p.n_end)
+            for (int e = 0; e < 16; e++) p.acc[(size_t)m * p.N + n + e] = (int32_t)v[cc * 16 + e];
+          continue;
+        }
+        if (n >= p.n_end) continue;
+        float o[16];
 #pragma unroll
-              for (int t = 0; t < 4; t++) {
-                const int j = (c & 1) * 4 + t;  // 16-byte chunk inside the 128-byte row
-                *reinterpret_cast<float4 *>(rowp + ((j ^ (ml & 7)) << 4)) =
-                    make_float4(o[4 * t], o[4 * t + 1], o[4 * t + 2], o[4 * t + 3]);
-              }
-            } else if (row_ok) {
-              float *dst = p.C + (size_t)m * p.ldc + (n - p.c_col0);
+        for (int e = 0; e < 16; e++)
+          o[e] = __fmul_rn(__int2float_rn((int32_t)v[cc * 16 + e]), __fmul_rn(s_bs[c * 16 + e], as));
+        if (tma_out) {
+          uint8_t *rowp = smem + (size_t)(c >> 1) * (BM * 128) + (size_t)ml * 128;
 #pragma unroll
-              for (int e = 0; e < 16; e += 4)
-                st_global_v4(dst + e, o[e], o[e + 1], o[e + 2], o[e + 3]);
-            }
+          for (int t = 0; t < 4; t++) {
+            const int j = (c & 1) * 4 + t;  // 16-byte chunk inside the 128-byte row
+            *reinterpret_cast<float4 *>(rowp + ((j ^ (ml & 7)) << 4)) =
+                make_float4(o[4 * t], o[4 * t + 1], o[4 * t + 2], o[4 * t + 3]);
+          }
+        } else if (row_ok) {
+          float *dst = p.C + (size_t)m * p.ldc + (n - p.c_col0);
+          if (p.out_v4) {
+#pragma unroll
+            for (int e = 0; e < 16; e += 4) st_global_v4(dst + e, o[e], o[e + 1], o[e + 2], o[e + 3]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; e++) dst[e] = o[e];
           }
         }
       }
-      if (tma_out) {
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
-        if (threadIdx.x == 128) {
-          const int col0 = blockIdx.x * kTcBN;  // relative to the output map's origin
-          for (int b = 0; b < kTcBN / 32; b++)
-            if (p.nb0 * 16 + col0 + b * 32 < p.n_end)
-              tc::tma_store_2d(&tmC, smem + (size_t)b * (kTcBM * 128), col0 + b * 32, m0);
-          tc::bulk_commit();
-          tc::bulk_wait_read();
-        }
+    }
+  }
+  if (tma_out) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x == 0 && ok && !s_fail) {
+      const int col0 = blockIdx.x * kTcBN;  // relative to the output map's origin
+      for (int b = 0; b < kTcBN / 32; b++)
+        if (p.nb0 * 16 + col0 + b * 32 < p.n_end)
+          tc::tma_store_2d(&tmC, smem + (size_t)b * (BM * 128), col0 + b * 32, m0);
+      tc::bulk_commit();
+      tc::bulk_wait_read();
+    }
+  }
+  if (splits > 1) {
+    // One bulk copy per peer moves the rows it owns from this CTA's send
+    // buffer into its receive slot (completing on its mbarrier); then CTA z
+    // sums rows [z*R, (z+1)*R) over its own partial and the received ones
+    // (int32, exact in any order), scales them and stores them.  Copies go
+    // out even from a failed CTA so no receiver is left waiting; if any CTA
+    // failed, the cluster skips the stores and the flag is raised.  The last
+    // barrier keeps every send buffer alive until its copies have landed.
+    const int R = BM / splits;
+    const uint32_t send = tc::smem_u32(smem), recv = send + (uint32_t)BM * 512;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // partials -> copy engine
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int j = 0; j < splits; j++) {
+        if (j == z) continue;
+        const int slot = z < j ? z : z - 1;
+        tc::bulk_s2cluster(tc::mapa(recv + (uint32_t)(slot * R * 512), (uint32_t)j),
+                           send + (uint32_t)(j * R * 512), (uint32_t)(R * 512),
+                           tc::mapa(tc::smem_u32(recv_bar), (uint32_t)j));
       }
     }
+    const bool got = __all_sync(0xffffffffu, tc::mbar_wait(recv_bar, 0));
+    if (!got) s_fail = 1;
+    __syncthreads();
+    const int fail_any = s_any_fail || s_fail;
+    for (int sl = threadIdx.x; sl < R * 32; sl += kTcThreads) {
+      const int rl = sl / 32, chunk = sl % 32;
+      const int m = m0 + z * R + rl, n = n0 + chunk * 4;
+      uint4 acc = *reinterpret_cast<const uint4 *>(smem + row_off(z * R + rl, chunk));
+      for (int slot = 0; slot < splits - 1; slot++) {
+        const uint4 u = *reinterpret_cast<const uint4 *>(smem + BM * 512 + slot * R * 512 +
+                                                         row_off(rl, chunk));
+        acc.x += u.x;
+        acc.y += u.y;
+        acc.z += u.z;
+        acc.w += u.w;
+      }
+      if (fail_any || m >= p.M || n >= p.n_end) continue;
+      const uint32_t a4[4] = {acc.x, acc.y, acc.z, acc.w};
+      if (p.acc) {
+        for (int e = 0; e < 4; e++) p.acc[(size_t)m * p.N + n + e] = (int32_t)a4[e];
+        continue;
+      }
+      const float as = s_as[z * R + rl];
+      float o[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++)
+        o[e] = __fmul_rn(__int2float_rn((int32_t)a4[e]), __fmul_rn(s_bs[chunk * 4 + e], as));
+      float *dst = p.C + (size_t)m * p.ldc + (n - p.c_col0);
+      if (p.out_v4)
+        st_global_v4(dst, o[0], o[1], o[2], o[3]);
+      else
+        for (int e = 0; e < 4; e++) dst[e] = o[e];
+    }
+    tc::cluster_sync();
   }
   tc::fence_before_sync();
   __syncthreads();
   if (s_fail && threadIdx.x == 0 && p.err) atomicExch(p.err, 2);
   if (warp == 2) {
     tc::fence_after_sync();
-    tc::tmem_dealloc(tmem, kTcTmemCols);
+    tc::tmem_dealloc(tmem, T::TmemCols);
   }
 }
 
@@ -296,53 +419,157 @@ cudaError_t launch_packed_to_rows(const int8_t *packed, int8_t *rows, int M, int
   return cudaGetLastError();
 }
 
-size_t q8c_tc_smem_bytes(int stages) {
-  size_t ring = (size_t)stages * kTcStage;
-  const size_t out = (size_t)(kTcBN / 32) * kTcBM * 128;  // staged f32 tile
-  if (ring < out) ring = out;
-  return ring + (size_t)(2 * stages + 1) * 8 + 16 + 1024;
+template <int H>
+size_t tc_smem_bytes(int stages) {
+  using T = TcTile<H>;
+  size_t ring = (size_t)stages * T::Stage;
+  if (ring < T::Out) ring = T::Out;
+  return ring + (size_t)(2 * stages + 2) * 8 + 16 + 1024;
+}
+
+constexpr size_t kTcStaticReserve = 4096;  // the kernel's static shared memory (about 2 KB)
+
+template <int H>
+int tc_stages(size_t smem_limit) {
+  int st = 8;
+  while (st > 2 && tc_smem_bytes<H>(st) + kTcStaticReserve > smem_limit) st--;
+  return st;
+}
+
+// Clusters of `s` CTAs of kernel<H> that can be resident at once (cached).
+template <int H>
+int tc_max_clusters(int s, size_t smem) {
+  static std::atomic<int> cache[9];
+  int v = cache[s].load(std::memory_order_relaxed);
+  if (v > 0) return v;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, 1, s);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = (unsigned)s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaFuncSetAttribute(q8c_tc_kernel<H>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess ||
+      cudaOccupancyMaxActiveClusters(&v, q8c_tc_kernel<H>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    v = 0;  // unknown: no split for this size
+  }
+  cache[s].store(v > 0 ? v : -1, std::memory_order_relaxed);
+  return v;
+}
+
+// Tile height and K split for a launch.  Every candidate runs in one wave
+// (split launches: all clusters resident at once; unsplit: waves counted);
+// the choice minimises the operand bytes one CTA must stream per wave,
+// since the main loop is bound by each SM's load throughput.
+struct TcChoice {
+  int H, splits, stages;
+  size_t smem;
+};
+
+TcChoice plan_tc(int M, int ncols, int K, int num_sms, size_t smem_limit) {
+  const int KS = (K + kTcBK - 1) / kTcBK;
+  TcChoice best{2, 1, tc_stages<2>(smem_limit), 0};
+  best.smem = tc_smem_bytes<2>(best.stages);
+  double best_cost = -1;
+  for (int H = 2; H >= 1; H--) {
+    const int stages = H == 2 ? tc_stages<2>(smem_limit) : tc_stages<1>(smem_limit);
+    const size_t smem = H == 2 ? tc_smem_bytes<2>(stages) : tc_smem_bytes<1>(stages);
+    const long tiles = (long)((ncols + kTcBN - 1) / kTcBN) * ((M + 128 * H - 1) / (128 * H));
+    for (int s = 1; s <= 8; s *= 2) {
+      if (s > 1 && KS < 4 * s) break;
+      // split K stages the send tile and the received slots in the ring
+      const size_t ring = (size_t)stages * (size_t)(128 * H + kTcBN) * kTcBK;
+      if (s > 1 && (size_t)(128 * H) * 512 * (2 * s - 1) / s > ring) continue;
+      const long ctas = tiles * s;
+      double waves;
+      if (s == 1) {
+        waves = (double)((ctas + num_sms - 1) / num_sms);
+      } else {
+        if (ctas > num_sms) break;
+        const int mc = H == 2 ? tc_max_clusters<2>(s, smem) : tc_max_clusters<1>(s, smem);
+        if (tiles > mc) continue;
+        waves = 1.0;
+      }
+      const double cost = waves * (double)(128 * H + kTcBN) * ((double)K / s);
+      if (best_cost < 0 || cost < best_cost * 0.999) {
+        best_cost = cost;
+        best = TcChoice{H, s, stages, smem};
+      }
+    }
+  }
+  return best;
 }
 
 // f32 output region [rows][cols] at base (row pitch ld bytes) as a 2-D TMA
 // view for stores: boxes of 256 rows x 32 floats, 128-byte swizzle.
-static bool encode_out_map(CUtensorMap *map, void *base, int rows, int cols, size_t ld) {
+static bool encode_out_map(CUtensorMap *map, void *base, int rows, int cols, size_t ld,
+                           int box_rows) {
   auto enc = get_encode();
   if (!enc) return false;
   const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)ld};
-  const cuuint32_t box[2] = {32, (cuuint32_t)kTcBM};
+  const cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-cudaError_t launch_q8c_tc(const TcParams &p_in, int lda, const CUtensorMap &tmB, bool pdl,
-                          cudaStream_t st) {
-  TcParams p = p_in;
-  CUtensorMap tmA, tmC;
-  if (!encode_rows_map(&tmA, p.A, p.M, p.K, lda, kTcBM)) return cudaErrorInvalidValue;
-  // TMA stores need a 16-byte aligned origin and row pitch
-  float *origin = p.C ? p.C + (p.nb0 * 16 - p.c_col0) : nullptr;
-  p.tma_store = !p.acc && p.C && ((uintptr_t)origin & 15) == 0 && (p.ldc % 4) == 0 &&
-                encode_out_map(&tmC, origin, p.M, p.n_end - p.nb0 * 16, (size_t)p.ldc * 4);
-  if (!p.tma_store) memset(&tmC, 0, sizeof(tmC));
-  const size_t smem = q8c_tc_smem_bytes(p.stages);
-  cudaError_t e = cudaFuncSetAttribute(q8c_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
+template <int H>
+cudaError_t launch_tc_h(const TcParams &p, const CUtensorMap &tmA, const CUtensorMap &tmB,
+                        const CUtensorMap &tmC, size_t smem, bool pdl, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(q8c_tc_kernel<H>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int ncols = p.n_end - p.nb0 * 16;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((ncols + kTcBN - 1) / kTcBN, (p.M + kTcBM - 1) / kTcBM);
+  cfg.gridDim = dim3((ncols + kTcBN - 1) / kTcBN, (p.M + 128 * H - 1) / (128 * H), p.splits);
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (p.splits > 1) {  // the CTAs splitting one tile's K form a cluster
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = (unsigned)p.splits;
+    na++;
+  }
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    na++;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, q8c_tc_kernel, tmA, tmB, tmC, p);
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, q8c_tc_kernel<H>, tmA, tmB, tmC, p);
+}
+
+cudaError_t launch_q8c_tc(const TcParams &p_in, int lda, const CUtensorMap &tmB, bool pdl,
+                          int num_sms, size_t smem_limit, cudaStream_t st) {
+  TcParams p = p_in;
+  const TcChoice c = plan_tc(p.M, p.n_end - p.nb0 * 16, p.K, num_sms, smem_limit);
+  if (c.smem + kTcStaticReserve > smem_limit) return cudaErrorInvalidConfiguration;
+  p.stages = c.stages;
+  p.splits = c.splits;
+  const int BM = 128 * c.H;
+  CUtensorMap tmA, tmC;
+  if (!encode_rows_map(&tmA, p.A, p.M, p.K, lda, BM)) return cudaErrorInvalidValue;
+  // TMA and vector stores need 16-byte aligned rows
+  float *origin = p.C ? p.C + (p.nb0 * 16 - p.c_col0) : nullptr;
+  p.out_v4 = p.C && ((uintptr_t)origin & 15) == 0 && (p.ldc % 4) == 0;
+  p.tma_store = !p.acc && p.out_v4 && p.splits == 1 &&
+                encode_out_map(&tmC, origin, p.M, p.n_end - p.nb0 * 16, (size_t)p.ldc * 4, BM);
+  if (!p.tma_store) memset(&tmC, 0, sizeof(tmC));
+  return c.H == 2 ? launch_tc_h<2>(p, tmA, tmB, tmC, c.smem, pdl, st)
+                  : launch_tc_h<1>(p, tmA, tmB, tmC, c.smem, pdl, st);
 }
 
 }  // namespace fgm

@@ -52,6 +52,10 @@ def shard_ranges(nblocks: int, world: int) -> list[tuple[int, int]]:
 def assemble(gathered: torch.Tensor, ranges: list[tuple[int, int]], out: torch.Tensor) -> torch.Tensor:
     """Place rank g's column block ``gathered[g, :, :cols_g]`` at columns
     ``[nb0_g*16, nb1_g*16)`` of ``out`` [M, N]."""
+    G, M, cols = gathered.shape
+    if all((b - a) * 16 == cols for a, b in ranges) and out.is_contiguous():
+        out.view(M, G, cols).copy_(gathered.permute(1, 0, 2))  # equal shards: one copy
+        return out
     for g, (a, b) in enumerate(ranges):
         if b > a:
             out[:, a * 16:b * 16] = gathered[g, :, :(b - a) * 16]

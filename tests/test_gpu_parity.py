@@ -435,12 +435,17 @@ def test_launch_counter_counts_kernels():
 
 
 # ------------------------------------------- prefill: tcgen05 tensor-core path
-@pytest.mark.parametrize("M,K,N,n0,n1", [(64, 1024, 256, 0, 16), (100, 2048, 512, 4, 24),
-                                         (256, 2048, 512, 0, 32), (256, 8192, 256, 0, 16),
-                                         (300, 2048, 384, 0, 24), (1024, 2048, 256, 8, 16)])
-def test_q8c_tensor_core_bit_exact(orc, M, K, N, n0, n1):
-    """M >= 64 with a prepared weight runs tcgen05.mma kind::i8; f32 outputs and
-    int32 accumulators must match the reference arithmetic exactly."""
+@pytest.mark.parametrize("M,K,N,n0,n1,cpad", [(64, 1024, 256, 0, 16, 16), (100, 2048, 512, 4, 24, 16),
+                                             (256, 2048, 512, 0, 32, 16), (256, 8192, 256, 0, 16, 16),
+                                             (300, 2048, 384, 0, 24, 16), (1024, 2048, 256, 8, 16, 16),
+                                             (256, 8192, 256, 4, 12, 3), (130, 4096, 1024, 0, 64, 5),
+                                             (256, 16384, 2048, 0, 128, 16),
+                                             (256, 2048, 6144, 0, 384, 16)])
+def test_q8c_tensor_core_bit_exact(orc, M, K, N, n0, n1, cpad):
+    """M >= 64 with a prepared weight runs tcgen05.mma kind::i8 (K split over a
+    cluster when the output has few tiles); f32 outputs and int32
+    accumulators must match the reference arithmetic exactly, with aligned
+    and unaligned output rows (ldc = N + cpad)."""
     rng = np.random.default_rng(M * 31 + K + N)
     A = rng.integers(-128, 128, size=(M, K), dtype=np.int8)
     b, s = F.synth_q8c(N, K, M + 7 * N)
@@ -449,7 +454,7 @@ def test_q8c_tensor_core_bit_exact(orc, M, K, N, n0, n1):
     pad, bd, sd, asd = D(pa), D(b), D(s), D(a_s)
     fg.device.q8c_prepare(bd, N, K)
     try:
-        ldc = N + 16
+        ldc = N + cpad
         c = torch.full((M, ldc), -9.0, device="cuda")
         fg.device.gemm_q8c(M, N, K, pad, asd, bd, sd, c, ldc, n0, n1)
         acc = torch.full((M, N), 7, dtype=torch.int32, device="cuda")
