@@ -471,10 +471,12 @@ def bench_lm_head(args, dev, gen, world, rank):
         return max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
 
     ms_gemm = timed(lambda: sh.local(M, pa, qs))
+    local = sh.local(M, pa, qs)
+    ms_gather = timed(lambda: sh.gather(local, out))
     ms_step = timed(lambda: sh(M, pa, qs, out))
     wbytes = sum(q4g_bytes(K, N))
     return {"value": wbytes / (ms_step * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms_step,
-            "gemm_ms": ms_gemm, "steps": steps,
+            "gemm_ms": ms_gemm, "gather_ms": ms_gather, "steps": steps,
             "workload": f"BASELINE config 3 LM head: int4 q4g {N}x{K} group {GROUP} f16 scales, "
                         f"M={M}, {world}-way output-column shards + NCCL all-gather of the "
                         f"logits (group-32 f32 scales are outside the fgm-kernels format)"}

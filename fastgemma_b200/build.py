@@ -20,6 +20,8 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libfgm_cuda.so")
+HOST = os.path.join(PKG, "host")
+HOST_LIB = os.path.join(PKG, "libfgm_host.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2",
@@ -68,7 +70,24 @@ def build(verbose: bool = False, extra: list[str] | None = None) -> str:
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
+    build_host(verbose)
     return LIB
+
+
+def build_host(verbose: bool = False) -> str:
+    """The C++ host layer (host/fgm_host.cpp) over the C ABI: libfgm_host.so,
+    linked against libfgm_cuda.so beside it."""
+    srcs = [os.path.join(HOST, "fgm_host.cpp")]
+    deps = srcs + [os.path.join(HOST, "fgm_host.hpp"), os.path.join(INCLUDE, "fgm_cuda.h"), LIB]
+    if os.path.exists(HOST_LIB) and os.path.getmtime(HOST_LIB) >= _newest(deps):
+        return HOST_LIB
+    cxx = shutil.which("g++") or "g++"
+    cmd = [cxx, "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall", "-I", INCLUDE, "-I", HOST,
+           "-o", HOST_LIB] + srcs + ["-L", PKG, "-lfgm_cuda", "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    return HOST_LIB
 
 
 if __name__ == "__main__":
