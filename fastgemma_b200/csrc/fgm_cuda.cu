@@ -23,6 +23,11 @@ void count_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_r
 
 static thread_local std::string t_err;
 
+// Bumped whenever a device address a cached call graph may hold can change
+// (registry, staging growth, prepared weights); see host_linear.
+static std::atomic<uint64_t> g_gen{1};
+static void bump_gen() { g_gen.fetch_add(1, std::memory_order_relaxed); }
+
 static int fail(int code, const char *fmt, ...) {
   char buf[512];
   va_list ap;
@@ -148,6 +153,7 @@ static int reg_upload(const void *host, size_t bytes, const void **dev) {
   }
   g_reg[host] = RegEntry{d, bytes};
   g_reg_bytes += bytes;
+  bump_gen();
   *dev = d;
   return FGM_CUDA_OK;
 }
@@ -191,6 +197,7 @@ static int stage_reserve(size_t bytes) {
       return fail(FGM_CUDA_ENOMEM, "cudaMallocHost(%zu)", cap);
     }
     g_stage.hcap = cap;
+    bump_gen();
   }
   if (bytes > g_stage.dcap) {
     size_t cap = std::max(bytes, g_stage.dcap * 2);
@@ -202,6 +209,7 @@ static int stage_reserve(size_t bytes) {
       return fail(FGM_CUDA_ENOMEM, "cudaMalloc(%zu)", cap);
     }
     g_stage.dcap = cap;
+    bump_gen();
   }
   return FGM_CUDA_OK;
 }
@@ -225,6 +233,51 @@ static int h2d(void *dst, const void *src, size_t bytes, size_t hoff) {
     memcpy(g_stage.h + hoff, src, bytes);
     FGM_TRY(cudaMemcpyAsync(dst, g_stage.h + hoff, bytes, cudaMemcpyHostToDevice, g_stream));
   }
+  return FGM_CUDA_OK;
+}
+
+// A device-readable address for `bytes` of host data: page-locked memory is
+// read in place over PCIe (unified addressing, no copy); pageable memory is
+// copied into the pinned staging buffer at `hoff` (a host memcpy, no DMA).
+// The caller keeps the data untouched until its work has completed (the
+// host-pointer entry points synchronise before returning).
+static int host_readable(const void *src, size_t bytes, size_t hoff, const void **dev) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, src) == cudaSuccess && a.type == cudaMemoryTypeHost &&
+      a.devicePointer) {
+    *dev = a.devicePointer;
+    return FGM_CUDA_OK;
+  }
+  cudaGetLastError();
+  memcpy(g_stage.h + hoff, src, bytes);
+  void *dp = nullptr;
+  FGM_TRY(cudaHostGetDevicePointer(&dp, g_stage.h + hoff, 0));
+  *dev = dp;
+  return FGM_CUDA_OK;
+}
+
+// Copy-back of rows [0, rows) x `width` bytes of a compact device matrix to
+// host memory with pitch `hpitch`: enqueue (straight into page-locked
+// memory, else into staging at `hoff`), then finish (wait, and move staged
+// rows into place).
+static int d2h_rows_enqueue(void *dst, size_t hpitch, const void *dsrc, size_t width, int rows,
+                            size_t hoff, bool pinned) {
+  if (rows <= 0 || width == 0) return FGM_CUDA_OK;
+  if (pinned)
+    FGM_TRY(cudaMemcpy2DAsync(dst, hpitch, dsrc, width, width, rows, cudaMemcpyDeviceToHost,
+                              g_stream));
+  else
+    FGM_TRY(cudaMemcpyAsync(g_stage.h + hoff, dsrc, width * rows, cudaMemcpyDeviceToHost,
+                            g_stream));
+  return FGM_CUDA_OK;
+}
+
+static int d2h_rows_finish(void *dst, size_t hpitch, size_t width, int rows, size_t hoff,
+                           bool pinned) {
+  FGM_TRY(cudaStreamSynchronize(g_stream));
+  if (!pinned)
+    for (int r = 0; r < rows; r++)
+      memcpy((char *)dst + (size_t)r * hpitch, g_stage.h + hoff + (size_t)r * width, width);
   return FGM_CUDA_OK;
 }
 
@@ -343,6 +396,7 @@ static int prepare_q8c(const int8_t *B, int N, int K, cudaStream_t st) {
     return fail(FGM_CUDA_ERUNTIME, "cuTensorMapEncodeTiled failed for a prepared weight");
   }
   g_prep[B] = pr;
+  bump_gen();
   return FGM_CUDA_OK;
 }
 
@@ -360,6 +414,7 @@ static void release_prepared(const void *B) {
   if (it == g_prep.end()) return;
   cudaFree(it->second.kmajor);
   g_prep.erase(it);
+  bump_gen();
 }
 
 // A is row-major [M][lda] int8.
@@ -566,6 +621,74 @@ static int host_gemm(bool q4, int M, int N, int K, const int8_t *A, const float 
   return d2h_rows_sync(C + (size_t)n0 * 16, (size_t)ldc * 4, d + o_c, (size_t)cols * 4, M, o_c);
 }
 
+// ----------------------------------------------------- replayed host calls
+// A host-pointer call repeating the pointers and shapes of an earlier one
+// (the steady state of an inference loop) replays an instantiated CUDA graph
+// of its device work -- prep, GEMM, copy-back -- with one launch instead of
+// one API call and one queue gap per operation.  The graph is captured on
+// the second occurrence (the first one warms every per-shape cache outside
+// capture).  Every graph is dropped when g_gen moves.
+struct CallKey {
+  const void *src, *B, *bs;
+  void *C;
+  int q4, lda, hsz, M, N, K, group, ldc, src_pinned, c_pinned;
+  bool operator==(const CallKey &o) const { return memcmp(this, &o, sizeof(CallKey)) == 0; }
+};
+struct CallKeyHash {
+  size_t operator()(const CallKey &k) const {
+    const unsigned char *p = reinterpret_cast<const unsigned char *>(&k);
+    size_t h = 1469598103934665603ull;
+    for (size_t i = 0; i < sizeof(CallKey); i++) h = (h ^ p[i]) * 1099511628211ull;
+    return h;
+  }
+};
+constexpr size_t kMaxCallGraphs = 512;
+static std::unordered_map<CallKey, cudaGraphExec_t, CallKeyHash> g_call_graphs;
+static std::unordered_map<CallKey, int, CallKeyHash> g_calls_seen;
+static uint64_t g_call_graphs_gen = 0;
+
+static void drop_call_graphs() {
+  for (auto &kv : g_call_graphs) cudaGraphExecDestroy(kv.second);
+  g_call_graphs.clear();
+  g_calls_seen.clear();
+}
+
+// Run `enqueue` (device work on g_stream) for `key`: replay, capture or plain.
+template <class F>
+static int run_call(const CallKey &key, F &&enqueue) {
+  const uint64_t gen = g_gen.load(std::memory_order_relaxed);
+  if (g_call_graphs_gen != gen) {
+    drop_call_graphs();
+    g_call_graphs_gen = gen;
+  }
+  auto it = g_call_graphs.find(key);
+  if (it != g_call_graphs.end()) {
+    FGM_TRY(cudaGraphLaunch(it->second, g_stream));
+    return FGM_CUDA_OK;
+  }
+  if (!g_calls_seen.count(key)) {
+    g_calls_seen[key] = 1;
+    return enqueue();
+  }
+  if (g_call_graphs.size() >= kMaxCallGraphs) drop_call_graphs();
+  FGM_TRY(cudaStreamBeginCapture(g_stream, cudaStreamCaptureModeThreadLocal));
+  const int rc = enqueue();
+  cudaGraph_t graph = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(g_stream, &graph);
+  if (rc) {
+    if (ce == cudaSuccess && graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  FGM_TRY(ce);
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  FGM_TRY(ie);
+  g_call_graphs[key] = exec;
+  FGM_TRY(cudaGraphLaunch(exec, g_stream));
+  return FGM_CUDA_OK;
+}
+
 // Host-pointer Gemm::run (forward.rs:128-158): prep on the device, then GEMM.
 static int host_linear(bool q4, const float *src, int lda, int hsz, int M, int N, int K,
                        const void *B, const void *b_scale, int group, float *C, int ldc) {
@@ -590,7 +713,9 @@ static int host_linear(bool q4, const float *src, int lda, int hsz, int M, int N
   const size_t total = o_w_end + align256((size_t)M * K);  // + row-major quantised X
   if ((rc = stage_reserve(total))) return rc;
   char *d = g_stage.d;
-  if ((rc = h2d(d, src, x_len, 0))) return rc;
+  const bool cacheable = dB && dS;  // registered weights: every address is stable
+  const void *xsrc = nullptr;  // X is read by the prep kernel straight from host memory
+  if ((rc = host_readable(src, x_len, 0, &xsrc))) return rc;
   if (!dB) {
     if ((rc = h2d(d + o_w, B, wbytes, o_w))) return rc;
     dB = d + o_w;
@@ -604,17 +729,43 @@ static int host_linear(bool q4, const float *src, int lda, int hsz, int M, int N
   CUtensorMap map;
   const bool tc = !q4 && M >= tc_min_m() && find_prepared(dB, &map);
   int8_t *qa_rows = tc ? (int8_t *)(d + o_w_end) : nullptr;  // row-major quantised X
-  rc = run_prep((const float *)d, lda, nullptr, qa_rows, (float *)(d + o_s), (int8_t *)(d + o_a),
-                M, K, hsz, 0, M, g_stream);
+  const bool c_pinned = is_pinned(C);
+  auto enqueue = [&]() -> int {
+    int r = run_prep(static_cast<const float *>(xsrc), lda, nullptr, qa_rows, (float *)(d + o_s),
+                     (int8_t *)(d + o_a), M, K, hsz, 0, M, g_stream);
+    if (r) return r;
+    if (tc)
+      r = run_q8c_tc(M, N, K, qa_rows, K, (const float *)(d + o_s), (const float *)dS, map,
+                     (float *)(d + o_c), N, 0, nullptr, 0, N / 16, g_stream);
+    else
+      r = run_gemm(q4, M, N, K, (const int8_t *)(d + o_a), (const float *)(d + o_s), dB, dS,
+                   group, (float *)(d + o_c), N, 0, nullptr, 0, N / 16, g_stream);
+    if (r) return r;
+    return d2h_rows_enqueue(C, (size_t)ldc * 4, d + o_c, (size_t)N * 4, M, o_c, c_pinned);
+  };
+  if (cacheable) {
+    CallKey key;
+    memset(&key, 0, sizeof(key));
+    key.src = src;
+    key.B = B;
+    key.bs = b_scale;
+    key.C = C;
+    key.q4 = q4;
+    key.lda = lda;
+    key.hsz = hsz;
+    key.M = M;
+    key.N = N;
+    key.K = K;
+    key.group = group;
+    key.ldc = ldc;
+    key.src_pinned = xsrc == static_cast<const void *>(src);
+    key.c_pinned = c_pinned;
+    rc = run_call(key, enqueue);
+  } else {
+    rc = enqueue();
+  }
   if (rc) return rc;
-  if (tc)
-    rc = run_q8c_tc(M, N, K, qa_rows, K, (const float *)(d + o_s), (const float *)dS, map,
-                    (float *)(d + o_c), N, 0, nullptr, 0, N / 16, g_stream);
-  else
-    rc = run_gemm(q4, M, N, K, (const int8_t *)(d + o_a), (const float *)(d + o_s), dB, dS,
-                  group, (float *)(d + o_c), N, 0, nullptr, 0, N / 16, g_stream);
-  if (rc) return rc;
-  return d2h_rows_sync(C, (size_t)ldc * 4, d + o_c, (size_t)N * 4, M, o_c);
+  return d2h_rows_finish(C, (size_t)ldc * 4, (size_t)N * 4, M, o_c, c_pinned);
 }
 
 }  // namespace fgm
@@ -795,6 +946,7 @@ int fgm_cuda_unregister(const void *host) {
   cudaFree(it->second.dev);
   g_reg_bytes -= it->second.bytes;
   g_reg.erase(it);
+  bump_gen();
   return FGM_CUDA_OK;
 }
 

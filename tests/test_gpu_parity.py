@@ -286,6 +286,37 @@ def test_linear_host_path_matches_oracle(orc):
         assert_bits(c, want, f"linear M={M} K={K} hsz={hsz}")
 
 
+def test_linear_host_repeated_calls_replay_and_invalidate(orc):
+    """Repeating a host-pointer call with the same buffers replays a cached
+    graph (third call on): results must follow the new contents of X every
+    time, and re-registering changed weights at the same address must drop
+    the cached graphs."""
+    M, K, N, hsz = 8, 2048, 512, 128
+    bq, s = F.synth_q4g(N, K, 64, 77)
+    s = np.ascontiguousarray(s)
+    fg.register(bq)
+    fg.register(s)
+    try:
+        pinned_x = torch.empty((M, K), dtype=torch.float32).pin_memory()
+        pinned_c = torch.empty((M, N), dtype=torch.float32).pin_memory()
+        x_np = np.zeros((M, K), np.float32)
+        c_np = np.zeros((M, N), np.float32)
+        rng = np.random.default_rng(8)
+        for i in range(5):
+            for x_buf, c_buf, arr in ((x_np, c_np, None), (pinned_x.numpy(), pinned_c.numpy(), 1)):
+                x_buf[:] = rng.standard_normal((M, K)).astype(np.float32)
+                fg.linear_q4g(x_buf, K, hsz, M, N, K, bq, s, 64, c_buf, N)
+                _, _, qs, pa = orc.prep_rows(x_buf, M, K, hsz)
+                assert_bits(c_buf, orc.gemm_q4g(M, N, K, pa, qs, bq, s, 64), f"call {i} {arr}")
+            if i == 2:  # new weights at the same host address
+                fg.unregister(bq)
+                bq[:] = F.synth_q4g(N, K, 64, 78)[0]
+                fg.register(bq)
+    finally:
+        fg.unregister(bq)
+        fg.unregister(s)
+
+
 # (M, K, N, hsz, group, lda - K): decode and prefill row counts, Hadamard
 # sizes from none to 2048, padded and unaligned row pitches
 LINEAR_CASES = [(1, 2048, 512, 0, 64, 0), (8, 2048, 2048, 128, 64, 4), (3, 192, 128, 64, 64, 0),
