@@ -473,13 +473,21 @@ def bench_lm_head(args, dev, gen, world, rank):
     ms_gemm = timed(lambda: sh.local(M, pa, qs))
     local = sh.local(M, pa, qs)
     ms_gather = timed(lambda: sh.gather(local, out))
-    ms_step = timed(lambda: sh(M, pa, qs, out))
+    ms_nccl = timed(lambda: sh(M, pa, qs, out))
+    # the product path: GEMM + all-gather fused in one kernel per rank (NVLink stores)
+    shf = S.ColumnShardedGemm("q4g", None, None, N, K, GROUP, rank=rank, world=world, device=dev,
+                              shard=(w, s), fused=True, max_rows=M)
+    ms_step = timed(lambda: shf(M, pa, qs))
+    shf.close()
     wbytes = sum(q4g_bytes(K, N))
     return {"value": wbytes / (ms_step * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms_step,
-            "gemm_ms": ms_gemm, "gather_ms": ms_gather, "steps": steps,
+            "gemm_ms": ms_gemm, "nccl_gather_ms": ms_gather, "nccl_step_ms": ms_nccl,
+            "steps": steps,
             "workload": f"BASELINE config 3 LM head: int4 q4g {N}x{K} group {GROUP} f16 scales, "
-                        f"M={M}, {world}-way output-column shards + NCCL all-gather of the "
-                        f"logits (group-32 f32 scales are outside the fgm-kernels format)"}
+                        f"M={M}, {world}-way output-column shards; value: one kernel per rank "
+                        f"that also stores its columns into every peer's logits over NVLink; "
+                        f"nccl_*: the same GEMM followed by an NCCL all-gather (group-32 f32 "
+                        f"scales are outside the fgm-kernels format)"}
 
 
 def bench_prefill(args, dev, gen, world):

@@ -1062,6 +1062,101 @@ int fgm_cuda_gemm_q8c_noalloc(int M, int N, int K, const int8_t *A, const float 
   return run_q8c_tc(M, N, K, rows, K, a_scale, b_scale, map, C, ldc, 0, nullptr, n0, n1, st);
 }
 
+// ------------------------------------------------ peer memory, fused gather
+int fgm_cuda_ipc_alloc(size_t bytes, void **dev_ptr) {
+  if (!dev_ptr || !bytes) return fail(FGM_CUDA_EINVAL, "ipc_alloc: null pointer or zero size");
+  void *d = nullptr;
+  if (cudaMalloc(&d, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(FGM_CUDA_ENOMEM, "cudaMalloc(%zu) for a shared buffer", bytes);
+  }
+  const cudaError_t e = cudaMemset(d, 0, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    return cuda_fail(e, "cudaMemset");
+  }
+  *dev_ptr = d;
+  return FGM_CUDA_OK;
+}
+
+int fgm_cuda_ipc_free(void *dev_ptr) {
+  if (dev_ptr) FGM_TRY(cudaFree(dev_ptr));
+  return FGM_CUDA_OK;
+}
+
+int fgm_cuda_ipc_handle(const void *dev_ptr, void *handle) {
+  if (!dev_ptr || !handle) return fail(FGM_CUDA_EINVAL, "ipc_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  FGM_TRY(cudaIpcGetMemHandle(&h, const_cast<void *>(dev_ptr)));
+  static_assert(sizeof(h) == FGM_CUDA_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  return FGM_CUDA_OK;
+}
+
+int fgm_cuda_ipc_open(const void *handle, void **dev_ptr) {
+  if (!dev_ptr || !handle) return fail(FGM_CUDA_EINVAL, "ipc_open: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  FGM_TRY(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return FGM_CUDA_OK;
+}
+
+int fgm_cuda_ipc_close(void *dev_ptr) {
+  if (dev_ptr) FGM_TRY(cudaIpcCloseMemHandle(dev_ptr));
+  return FGM_CUDA_OK;
+}
+
+int fgm_cuda_gemm_q4g_gather(int M, int N, int K, const int8_t *A, const float *a_scale,
+                             const uint8_t *Bq, const uint16_t *b_scale, int group, int col0,
+                             int ldc, void *const *out, unsigned long long *const *sig, int rank,
+                             int world, int slot, unsigned long long uses, void *stream) {
+  int rc = check_gemm(M, N, K, N, 0, N / 16, group, true);
+  if (rc) return rc;
+  if (world < 1 || world > kMaxGatherRanks || rank < 0 || rank >= world)
+    return fail(FGM_CUDA_EINVAL, "gather: rank %d of world %d (at most %d ranks)", rank, world,
+                kMaxGatherRanks);
+  if (M > 16) return fail(FGM_CUDA_EINVAL, "gather: M=%d > 16 (decode GEMM only)", M);
+  if (col0 < 0 || col0 % 16 != 0 || ldc % 4 != 0 || col0 + N > ldc)
+    return fail(FGM_CUDA_EINVAL, "gather: columns [%d, %d) of ldc=%d", col0, col0 + N, ldc);
+  if ((slot != 0 && slot != 1) || uses == 0)
+    return fail(FGM_CUDA_EINVAL, "gather: slot %d, uses %llu", slot, uses);
+  if (!out || !sig || !A || !a_scale || !Bq || !b_scale)
+    return fail(FGM_CUDA_EINVAL, "null pointer");
+  for (int q = 0; q < world; q++)
+    if (!out[q] || !sig[q] || !aligned16(out[q]) || !aligned16(sig[q]))
+      return fail(FGM_CUDA_EINVAL, "gather: rank %d buffers missing or unaligned", q);
+  if (M == 0) return FGM_CUDA_OK;
+  if (!aligned16(Bq) || !aligned16(b_scale))
+    return fail(FGM_CUDA_EINVAL, "weights and int4 scales must be 16-byte aligned");
+  DevInfo *di = nullptr;
+  if ((rc = dev_info(&di))) return rc;
+  GemvParams p{};
+  p.err = di->err;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.group = group;
+  p.A = A;
+  p.a_scale = a_scale;
+  p.B = Bq;
+  p.b_scale = b_scale;
+  p.C = static_cast<float *>(out[rank]) + col0;
+  p.ldc = ldc;
+  p.g.rank = rank;
+  p.g.world = world;
+  p.g.slot = slot;
+  p.g.uses = uses;
+  for (int q = 0; q < world; q++) {
+    p.g.out[q] = static_cast<float *>(out[q]);
+    p.g.sig[q] = sig[q];
+  }
+  const cudaError_t e =
+      launch_gemv(p, N / 16, true, use_pdl(), di->sms, di->smem_optin, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "gemm_q4g_gather launch");
+  count_launch();
+  return FGM_CUDA_OK;
+}
+
 int fgm_cuda_q8c_prepare(const int8_t *B, int N, int K, void *stream) {
   int rc = check_gemm(1, N, K, N, 0, 0, 64, false);
   if (rc) return rc;

@@ -7,6 +7,19 @@
 
 namespace fgm {
 
+constexpr int kMaxGatherRanks = 8;
+
+// Fused all-gather of a column-sharded decode GEMM (gemv.cu): every rank's
+// output buffer has the same [M][ldc] layout; this rank's finished columns
+// are also stored into each peer's buffer over NVLink, and system-scope
+// counters tell each rank when its buffer is complete.  world = 0: off.
+struct GatherParams {
+  float *out[kMaxGatherRanks];               // each rank's output buffer for this call
+  unsigned long long *sig[kMaxGatherRanks];  // each rank's signal words (8 x u64)
+  int rank, world, slot;                     // slot: which of the double buffers
+  unsigned long long uses;                   // calls that used this slot so far, this one included
+};
+
 struct GemvParams {
   int M, N, K, group;       // group: int4 scale group; unused for int8
   const int8_t *A;          // packed activations [ceil(M/16)][K/64][16][64]
@@ -19,6 +32,7 @@ struct GemvParams {
   int32_t *acc;             // raw accumulator output (debug launches)
   int nb0;                  // first n-block of the range
   int *err;                 // device flag set when a bounded wait gives up (may be null)
+  GatherParams g;           // fused all-gather (g.world = 0: none)
 };
 
 // Launch geometry of the streaming decode kernel (gemv.cu).

@@ -135,6 +135,47 @@ __device__ __forceinline__ float i2f_group(int32_t x, bool exact_ok) {
   return exact_ok ? i2f_exact(x) : __int2float_rn(x);
 }
 
+// ------------------------------------------------------ fused all-gather
+// Signal words of one rank (u64 each, zeroed once, never reset -- counts
+// grow by a known amount per call): [slot] = ranks whose last CTA finished
+// pushing into this rank's buffer `slot`; [2 + slot] = ranks that started a
+// call using `slot` (their buffer is free to overwrite); [4 + slot] = this
+// rank's CTAs done pushing.
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *a) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+  return v;
+}
+
+// Wait until *a >= want, at most 2 s (then false).
+__device__ __forceinline__ bool spin_until_geq(const unsigned long long *a, unsigned long long want) {
+  if (ld_acquire_sys(a) >= want) return true;
+  const uint64_t t0 = tc::globaltimer_ns();
+  while (ld_acquire_sys(a) < want) {
+    if (tc::globaltimer_ns() - t0 > 2000000000ull) return false;
+    __nanosleep(64);
+  }
+  return true;
+}
+
+__device__ __forceinline__ void st_v4_global(float *p, float4 v) {
+  asm volatile("st.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+
+// One 8-row block of n-block nb, already stored at p.C, copied to every
+// peer's buffer: lane = (row, 16-byte chunk), 64 contiguous bytes per row.
+__device__ __forceinline__ void push_rows(const GemvParams &p, int nb, int m0, int lane) {
+  const int m = m0 + (lane >> 2);
+  if (m >= p.M) return;
+  const size_t off = (size_t)m * p.ldc + (size_t)(nb * 16 - p.c_col0) + (lane & 3) * 4;
+  const float4 v = *reinterpret_cast<const float4 *>(p.C + off);
+  const size_t shift = (size_t)(p.C - p.g.out[p.g.rank]);
+  for (int q = 0; q < p.g.world; q++)
+    if (q != p.g.rank) st_v4_global(p.g.out[q] + shift + off, v);
+}
+
 // Per-lane constants shared by the stage routines.
 struct Lane {
   int g8, tig, lane;
@@ -446,6 +487,21 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     scale_fetch(sc_b0, sc_b1);
   }
   pdl_wait();  // activations and outputs are ordered after earlier kernels
+  if (p.g.world > 0 && threadIdx.x == 0) {
+    if (blockIdx.x == 0 && blockIdx.y == 0) {
+      // everything before this call on this stream is complete, including the
+      // readers of this slot's previous contents: tell every rank it may write
+      for (int q = 0; q < p.g.world; q++) atomicAdd_system(p.g.sig[q] + 2 + p.g.slot, 1ull);
+    }
+    // every rank's buffer must be free before this CTA pushes into it (the
+    // weight stream is already in flight meanwhile); units are pushed as they
+    // finish, after the block barrier that publishes s_abort
+    const unsigned long long need = (unsigned long long)p.g.world * p.g.uses;
+    if (!spin_until_geq(p.g.sig[p.g.rank] + 2 + p.g.slot, need)) {
+      s_abort = 1;
+      if (p.err) atomicExch(p.err, 3);
+    }
+  }
 
   if (pl.a_bytes) {  // stage this row block's activations, B-fragment order
     // 16-byte pieces: piece c of a 64-byte row holds k-quads 4c..4c+3, which
@@ -584,6 +640,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
                 __fmul_rn(__int2float_rn(gacc[mt][i]), __fmul_rn(bs, s_as[m - mb * 16]));
           }
         }
+      if (p.g.world > 0 && !*reinterpret_cast<volatile int *>(&s_abort)) {
+        __syncwarp();  // this warp's stores of the unit are visible to its lanes
+#pragma unroll
+        for (int r0 = 0; r0 < MT * 8; r0 += 8) push_rows(p, nb, mb * 16 + r0, lane);
+      }
       continue;
     }
     if (!Q4) {  // int8 split K: add the int32 partials
@@ -635,6 +696,27 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
       }
     }
     team_sync(team, P * 32);
+    if (p.g.world > 0 && part < MT && !*reinterpret_cast<volatile int *>(&s_abort))
+      push_rows(p, nb, mb * 16 + part * 8, lane);
+  }
+
+  if (p.g.world > 0) {
+    // ---- fused all-gather: every unit of this CTA has been pushed; publish
+    // the pushes, count this CTA, and let the rank's last CTA signal every
+    // rank and wait until its own buffer holds all ranks' columns.
+    const GatherParams &g = p.g;
+    const unsigned long long need = (unsigned long long)g.world * g.uses;
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned long long done = atomicAdd(g.sig[g.rank] + 4 + g.slot, 1ull) + 1;
+      if (done == g.uses * gridDim.x * gridDim.y) {  // this rank's last CTA
+        __threadfence_system();
+        for (int q = 0; q < g.world; q++) atomicAdd_system(g.sig[q] + g.slot, 1ull);
+        // the call completes when every rank's columns are in this buffer
+        if (!spin_until_geq(g.sig[g.rank] + g.slot, need) && p.err) atomicExch(p.err, 3);
+      }
+    }
   }
 }
 

@@ -9,8 +9,12 @@ thread pool splits one GEMM across threads (fgm-core/src/pool.rs:110-124) --
 from its own slice of the weight: a contiguous byte range of the .fgm blob in
 its [N/16][K/64] tile order (the q4g scales [K/group][N] need one strided
 slice per group row).  Activations are replicated: every rank quantises the
-same X.  The full output is assembled with one all-gather of the per-rank
-column blocks over the process group (NCCL over NVLink on GPUs, gloo on CPU).
+same X.  The full output is assembled either with one all-gather of the
+per-rank column blocks over the process group (NCCL over NVLink on GPUs,
+gloo on CPU), or -- ``fused=True``, the int4 decode GEMM -- inside the GEMM
+kernel itself: each rank's finished columns are stored straight into every
+peer's output over NVLink (CUDA IPC buffers, system-scope counters), one
+kernel per rank and no separate collective.
 
 One process per GPU; ``torch.distributed`` is the plumbing, the GEMM is the
 library's kernel on each rank's shard.
@@ -62,6 +66,65 @@ def assemble(gathered: torch.Tensor, ranges: list[tuple[int, int]], out: torch.T
     return out
 
 
+class _DeviceArray:
+    """A raw device allocation seen by torch without a copy."""
+
+    def __init__(self, ptr: int, shape, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
+class PeerBuffers:
+    """Every rank's double-buffered output [2][rows][N] f32 and signal words,
+    allocated by the owner and opened by every peer (CUDA IPC, one node).
+    Collective: all ranks of the group construct it together."""
+
+    def __init__(self, rows: int, N: int, rank: int, world: int, pg=None):
+        import ctypes as C
+        from ._lib import call, lib
+        self.rows, self.N, self.rank, self.world = rows, N, rank, world
+        self.slot_bytes = rows * N * 4
+        out, sig = C.c_void_p(), C.c_void_p()
+        call("fgm_cuda_ipc_alloc", 2 * self.slot_bytes, C.byref(out))
+        call("fgm_cuda_ipc_alloc", 64, C.byref(sig))
+        self._own = (out.value, sig.value)
+        h_out, h_sig = (C.c_ubyte * 64)(), (C.c_ubyte * 64)()
+        call("fgm_cuda_ipc_handle", out, h_out)
+        call("fgm_cuda_ipc_handle", sig, h_sig)
+        handles = [None] * world
+        mine = (bytes(h_out), bytes(h_sig))
+        if world > 1:
+            dist.all_gather_object(handles, mine, group=pg)
+        else:
+            handles = [mine]
+        self.out, self.sig, self._opened = [], [], []
+        for q, (ho, hs) in enumerate(handles):
+            if q == rank:
+                self.out.append(out.value)
+                self.sig.append(sig.value)
+                continue
+            po, ps = C.c_void_p(), C.c_void_p()
+            call("fgm_cuda_ipc_open", (C.c_ubyte * 64).from_buffer_copy(ho), C.byref(po))
+            call("fgm_cuda_ipc_open", (C.c_ubyte * 64).from_buffer_copy(hs), C.byref(ps))
+            self.out.append(po.value)
+            self.sig.append(ps.value)
+            self._opened += [po.value, ps.value]
+        self._lib = lib()
+
+    def view(self, slot: int, M: int, device) -> torch.Tensor:
+        ptr = self.out[self.rank] + slot * self.slot_bytes
+        return torch.as_tensor(_DeviceArray(ptr, (self.rows, self.N)), device=device)[:M]
+
+    def close(self):
+        from ._lib import call
+        for p in self._opened:
+            call("fgm_cuda_ipc_close", p)
+        self._opened = []
+        for p in self._own:
+            call("fgm_cuda_ipc_free", p)
+        self._own = ()
+
+
 def _device_gemm(sh: "ColumnShardedGemm", M, A, a_scale, C):
     from . import device as D
     if sh.cols == 0:
@@ -84,7 +147,8 @@ class ColumnShardedGemm:
 
     def __init__(self, kind: str, blob: np.ndarray | None, scale: np.ndarray | None, N: int,
                  K: int, group: int = 64, *, rank: int | None = None, world: int | None = None,
-                 pg=None, device=None, gemm: Callable | None = None, shard=None):
+                 pg=None, device=None, gemm: Callable | None = None, shard=None,
+                 fused: bool = False, max_rows: int = 16):
         if kind not in ("q4g", "q8c"):
             raise ValueError(f"kind must be q4g or q8c, not {kind!r}")
         self.kind, self.N, self.K, self.group, self.pg = kind, N, K, group, pg
@@ -108,6 +172,14 @@ class ColumnShardedGemm:
         self._gemm = gemm or _device_gemm
         self._local = None
         self._gathered = None
+        # fused: one kernel per call computes this rank's columns and stores
+        # them into every rank's output over NVLink (int4 decode GEMM only)
+        self.peers = None
+        self._calls = 0
+        if fused:
+            if kind != "q4g" or max_rows > 16:
+                raise ValueError("the fused gather covers the int4 decode GEMM (M <= 16)")
+            self.peers = PeerBuffers(max_rows, N, self.rank, self.world, pg)
 
     def local(self, M: int, A, a_scale) -> torch.Tensor:
         """This rank's columns, [M, max_cols] (columns past ``cols`` unused)."""
@@ -132,7 +204,39 @@ class ColumnShardedGemm:
             dist.all_gather(list(self._gathered.unbind(0)), local.contiguous(), group=self.pg)
         return assemble(self._gathered, self.ranges, out)
 
+    def fused_call(self, M: int, A, a_scale, stream=None) -> torch.Tensor:
+        """GEMM + all-gather in one kernel per rank; returns this rank's view
+        of the full [M, N] output (valid until the call after next)."""
+        import ctypes as C
+        from ._lib import call
+        pb = self.peers
+        if M > pb.rows:
+            raise ValueError(f"M={M} > max_rows={pb.rows}")
+        slot, uses = self._calls & 1, self._calls // 2 + 1
+        self._calls += 1
+        outs = (C.c_void_p * self.world)(*[o + slot * pb.slot_bytes for o in pb.out])
+        sigs = (C.c_void_p * self.world)(*pb.sig)
+        st = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        A_p = A.data_ptr() if hasattr(A, "data_ptr") else A
+        s_p = a_scale.data_ptr() if hasattr(a_scale, "data_ptr") else a_scale
+        call("fgm_cuda_gemm_q4g_gather", M, self.cols, self.K, A_p, s_p, self.w.data_ptr(),
+             self.s.data_ptr(), self.group, self.nb0 * 16, self.N, outs, sigs, self.rank,
+             self.world, slot, uses, st)
+        return pb.view(slot, M, self.device)
+
+    def close(self):
+        if self.peers is not None:
+            torch.cuda.synchronize(self.device)
+            self.peers.close()
+            self.peers = None
+
     def __call__(self, M: int, A, a_scale, out: torch.Tensor | None = None) -> torch.Tensor:
+        if self.peers is not None:
+            res = self.fused_call(M, A, a_scale)
+            if out is not None:
+                out.copy_(res)
+                return out
+            return res
         if self.world == 1 and (out is None or out.is_contiguous()):  # the whole GEMM, in place
             if out is None:
                 out = torch.empty((M, self.N), dtype=torch.float32, device=self.device)

@@ -223,6 +223,38 @@ int fgm_cuda_gemm_q4g_acc(int M, int N, int K, const int8_t *A, const uint8_t *B
 int fgm_cuda_gemm_q8c_acc(int M, int N, int K, const int8_t *A, const int8_t *B,
                           int32_t *acc, int n0, int n1, void *stream);
 
+/* ----------------------------------- column-sharded GEMM, fused gather
+ * The large-N products (the LM head, forward.rs:301, :687) split by output
+ * columns over the GPUs of one node.  No reference counterpart: the
+ * reference splits the same column ranges over CPU threads (pool.rs:110-124)
+ * and needs no exchange.
+ *
+ * Peer memory: each rank allocates its buffers with fgm_cuda_ipc_alloc
+ * (zeroed), exports FGM_CUDA_IPC_HANDLE_BYTES-byte handles, and opens the
+ * other ranks' handles (same node). */
+#define FGM_CUDA_IPC_HANDLE_BYTES 64
+int fgm_cuda_ipc_alloc(size_t bytes, void **dev_ptr);
+int fgm_cuda_ipc_free(void *dev_ptr);
+int fgm_cuda_ipc_handle(const void *dev_ptr, void *handle);
+int fgm_cuda_ipc_open(const void *handle, void **dev_ptr);
+int fgm_cuda_ipc_close(void *dev_ptr);
+
+/* This rank's share of a column-sharded int4 decode GEMM with the all-gather
+ * fused into it: Bq/b_scale hold this rank's N columns (a shard of the .fgm
+ * blob), which land at columns [col0, col0 + N) of every rank's output
+ * out[q] ([M][ldc] f32, M <= 16) -- locally and over NVLink into each peer.
+ * sig[q] are the ranks' signal words (8 x u64, from fgm_cuda_ipc_alloc).
+ * Collective: every rank calls with the same slot (0/1, double buffers) and
+ * uses (calls so far with that slot, this one included).  When the kernel
+ * completes on `stream`, out[rank] holds all ranks' columns; it stays valid
+ * until the call after next.  Every cross-GPU wait is bounded (2 s, then
+ * fgm_cuda_device_status reports FGM_CUDA_ETIMEOUT). */
+int fgm_cuda_gemm_q4g_gather(int M, int N, int K, const int8_t *A, const float *a_scale,
+                             const uint8_t *Bq, const uint16_t *b_scale, int group,
+                             int col0, int ldc, void *const *out,
+                             unsigned long long *const *sig, int rank, int world,
+                             int slot, unsigned long long uses, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -595,3 +595,31 @@ def test_column_shards_on_device_assemble_to_the_whole_gemm(orc, kind, world):
     want = (orc.gemm_q4g(M, N, K, pa, a_s, blob, scale, 64) if kind == "q4g"
             else orc.gemm_q8c(M, N, K, pa, a_s, blob, scale))
     assert_bits(out.cpu().numpy(), want, f"{kind} world={world}")
+
+
+def test_fused_gather_single_rank_calls(orc):
+    """The fused GEMM + gather kernel at world size 1 (its own buffer and
+    counters): several calls alternate the double buffers and each result
+    matches the oracle."""
+    from fastgemma_b200 import shard as S
+    M, N, K = 8, 2048, 2048
+    blob, scale = F.synth_q4g(N, K, 64, 91, structured=False)
+    sh = S.ColumnShardedGemm("q4g", blob, scale, N, K, 64, rank=0, world=1, device="cuda",
+                             fused=True)
+    try:
+        rng = np.random.default_rng(9)
+        outs = []
+        for i in range(4):
+            A = rng.integers(-128, 128, size=(M, K), dtype=np.int8)
+            a_s = rng.uniform(0.01, 0.1, size=M).astype(np.float32)
+            pa = F.pack_a(A)
+            got = sh(M, D(pa), D(a_s))
+            torch.cuda.synchronize()
+            from fastgemma_b200 import _lib
+            assert _lib.lib().fgm_cuda_device_status() == 0
+            assert_bits(got.cpu().numpy(), orc.gemm_q4g(M, N, K, pa, a_s, blob, scale, 64),
+                        f"call {i}")
+            outs.append(got)
+        assert outs[0].data_ptr() == outs[2].data_ptr() != outs[1].data_ptr()
+    finally:
+        sh.close()
