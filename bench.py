@@ -479,9 +479,11 @@ def bench_lm_head(args, dev, gen, world, rank):
                               shard=(w, s), fused=True, max_rows=M)
     ms_step = timed(lambda: shf(M, pa, qs))
     shf.close()
+    ms_argmax = timed(lambda: sh.argmax(M, pa, qs))  # tokens without gathering logits
     wbytes = sum(q4g_bytes(K, N))
     return {"value": wbytes / (ms_step * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms_step,
             "gemm_ms": ms_gemm, "nccl_gather_ms": ms_gather, "nccl_step_ms": ms_nccl,
+            "argmax_step_ms": ms_argmax,
             "steps": steps,
             "workload": f"BASELINE config 3 LM head: int4 q4g {N}x{K} group {GROUP} f16 scales, "
                         f"M={M}, {world}-way output-column shards; value: one kernel per rank "

@@ -1062,6 +1062,33 @@ int fgm_cuda_gemm_q8c_noalloc(int M, int N, int K, const int8_t *A, const float 
   return run_q8c_tc(M, N, K, rows, K, a_scale, b_scale, map, C, ldc, 0, nullptr, n0, n1, st);
 }
 
+// ---------------------------------------------------------- row argmax
+int fgm_cuda_argmax_partials(const float *C, int M, int N, int ldc, int col0, float *vals,
+                             int32_t *idx, void *stream) {
+  if (M < 0 || N <= 0 || ldc < N || col0 < 0)
+    return fail(FGM_CUDA_EINVAL, "argmax: M=%d N=%d ldc=%d col0=%d", M, N, ldc, col0);
+  if (M == 0) return FGM_CUDA_OK;
+  if (!C || !vals || !idx) return fail(FGM_CUDA_EINVAL, "null pointer");
+  const cudaError_t e =
+      launch_argmax_partials(C, M, N, ldc, col0, vals, idx, use_pdl(), (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "argmax launch");
+  count_launch();
+  return FGM_CUDA_OK;
+}
+
+int fgm_cuda_argmax_parts(int N) { return N > 0 ? argmax_chunk_count(N) : 0; }
+
+int fgm_cuda_argmax_merge(const float *vals, const int32_t *idx, int M, int P, int32_t *out,
+                          void *stream) {
+  if (M < 0 || P <= 0) return fail(FGM_CUDA_EINVAL, "argmax merge: M=%d P=%d", M, P);
+  if (M == 0) return FGM_CUDA_OK;
+  if (!vals || !idx || !out) return fail(FGM_CUDA_EINVAL, "null pointer");
+  const cudaError_t e = launch_argmax_merge(vals, idx, M, P, out, use_pdl(), (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "argmax merge launch");
+  count_launch();
+  return FGM_CUDA_OK;
+}
+
 // ------------------------------------------------ peer memory, fused gather
 int fgm_cuda_ipc_alloc(size_t bytes, void **dev_ptr) {
   if (!dev_ptr || !bytes) return fail(FGM_CUDA_EINVAL, "ipc_alloc: null pointer or zero size");

@@ -107,6 +107,14 @@ cudaError_t launch_q8c_tc(const TcParams &p, int lda, const CUtensorMap &tmB, bo
                           int num_sms, size_t smem_limit, cudaStream_t st);
 constexpr int kTcBoxRowsB = 128;  // output columns per CTA tile
 
+// Row argmax (argmax.cu): partials over column chunks, then merges.
+constexpr int kArgmaxChunk = 8192;
+int argmax_chunk_count(int N);
+cudaError_t launch_argmax_partials(const float *C, int M, int N, int ldc, int col0, float *pv,
+                                   int *pi, bool pdl, cudaStream_t st);
+cudaError_t launch_argmax_merge(const float *pv, const int *pi, int M, int P, int *out, bool pdl,
+                                cudaStream_t st);
+
 // Number of kernel launches issued by this library (instrumentation).
 void count_launch(int n = 1);
 

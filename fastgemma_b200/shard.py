@@ -224,6 +224,31 @@ class ColumnShardedGemm:
              self.world, slot, uses, st)
         return pb.view(slot, M, self.device)
 
+    def argmax(self, M: int, A, a_scale, stream=None) -> torch.Tensor:
+        """Token choice for each row (engine.rs:75-83) without gathering the
+        logits: this rank's columns reduce to per-row (value, index) pairs,
+        the ranks exchange M pairs each, and the pairs merge into int32 [M]."""
+        from ._lib import call, lib
+        local = self.local(M, A, a_scale)
+        st = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        parts = lib().fgm_cuda_argmax_parts(self.max_cols)
+        vals = torch.empty((M, parts), dtype=torch.float32, device=self.device)
+        idx = torch.empty((M, parts), dtype=torch.int32, device=self.device)
+        call("fgm_cuda_argmax_partials", local.data_ptr(), M, self.cols, self.max_cols,
+             self.nb0 * 16, vals.data_ptr(), idx.data_ptr(), st)
+        if self.world > 1:
+            gv = torch.empty((self.world, M, parts), dtype=torch.float32, device=self.device)
+            gi = torch.empty((self.world, M, parts), dtype=torch.int32, device=self.device)
+            if vals.is_cuda:
+                dist.all_gather_into_tensor(gv, vals, group=self.pg)
+                dist.all_gather_into_tensor(gi, idx, group=self.pg)
+            vals = gv.permute(1, 0, 2).reshape(M, self.world * parts).contiguous()
+            idx = gi.permute(1, 0, 2).reshape(M, self.world * parts).contiguous()
+        out = torch.empty(M, dtype=torch.int32, device=self.device)
+        call("fgm_cuda_argmax_merge", vals.data_ptr(), idx.data_ptr(), M, vals.shape[1],
+             out.data_ptr(), st)
+        return out
+
     def close(self):
         if self.peers is not None:
             torch.cuda.synchronize(self.device)
@@ -231,7 +256,7 @@ class ColumnShardedGemm:
             self.peers = None
 
     def __call__(self, M: int, A, a_scale, out: torch.Tensor | None = None) -> torch.Tensor:
-        if self.peers is not None:
+        if self.peers is not None and self.world > 1:
             res = self.fused_call(M, A, a_scale)
             if out is not None:
                 out.copy_(res)

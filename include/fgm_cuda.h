@@ -223,6 +223,23 @@ int fgm_cuda_gemm_q4g_acc(int M, int N, int K, const int8_t *A, const uint8_t *B
 int fgm_cuda_gemm_q8c_acc(int M, int N, int K, const int8_t *A, const int8_t *B,
                           int32_t *acc, int n0, int n1, void *stream);
 
+/* ------------------------------------------------------------ row argmax
+ * The token choice that follows the LM head (fgm-serve/src/engine.rs:75-83,
+ * :297-302): per row the first index of the largest value, NaN never
+ * chosen, 0 when nothing exceeds -inf.  Split so a column-sharded LM head
+ * exchanges a few pairs instead of the logits:
+ * fgm_cuda_argmax_partials writes, for each row m of C [M][ldc] (columns
+ * [0, N), reported as col0 + column), fgm_cuda_argmax_parts(N) partial
+ * (value, index) pairs at vals/idx[m * parts + p] (index -1: nothing above
+ * -inf); fgm_cuda_argmax_merge folds P pairs per row (row m's at m * P ...)
+ * into out[m].  Partials from several ranks concatenated per row merge the
+ * same way. */
+int fgm_cuda_argmax_parts(int N);
+int fgm_cuda_argmax_partials(const float *C, int M, int N, int ldc, int col0, float *vals,
+                             int32_t *idx, void *stream);
+int fgm_cuda_argmax_merge(const float *vals, const int32_t *idx, int M, int P, int32_t *out,
+                          void *stream);
+
 /* ----------------------------------- column-sharded GEMM, fused gather
  * The large-N products (the LM head, forward.rs:301, :687) split by output
  * columns over the GPUs of one node.  No reference counterpart: the

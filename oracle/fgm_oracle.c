@@ -285,3 +285,17 @@ void orc_fill_lcg(uint32_t *state, int lo, int hi, size_t n, int32_t *out) {
   }
   *state = rs;
 }
+
+/* Token choice after the LM head (fgm-serve/src/engine.rs:75-83,
+ * fgm-bench/src/main.rs:201-209): scan ascending from (0, -inf), keep the
+ * first strictly greater value. */
+int orc_argmax(const float *v, int n) {
+  int best = 0;
+  float bv = -INFINITY;
+  for (int i = 0; i < n; i++)
+    if (v[i] > bv) {
+      bv = v[i];
+      best = i;
+    }
+  return best;
+}

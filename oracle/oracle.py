@@ -79,6 +79,7 @@ class Oracle:
         _decl(L, "orc_unpack_q4_tiles", [_p, C.c_size_t, _p])
         _decl(L, "orc_fill_xorshift", [_p, _i, _i, C.c_size_t, _p])
         _decl(L, "orc_fill_lcg", [_p, _i, _i, C.c_size_t, _p])
+        _decl(L, "orc_argmax", [_p, _i], _i)
         _load_pool(L)
         self.kind = "port"
 
@@ -159,6 +160,12 @@ class Oracle:
         acc = np.zeros((M, N), np.int32)
         self.lib.orc_gemm_q8c_acc(M, N, K, _ptr(ap), _ptr(b), _ptr(acc), n0, n1)
         return acc
+
+    def argmax_rows(self, c: np.ndarray) -> np.ndarray:
+        """Per row of c [M, N]: the reference's argmax (engine.rs:75-83)."""
+        c = np.ascontiguousarray(c, dtype=np.float32)
+        return np.array([self.lib.orc_argmax(_ptr(c[m]), c.shape[1]) for m in range(c.shape[0])],
+                        np.int32)
 
     def unpack_q4_tiles(self, bq: np.ndarray) -> np.ndarray:
         nt = bq.size // 512

@@ -613,7 +613,7 @@ def test_fused_gather_single_rank_calls(orc):
             A = rng.integers(-128, 128, size=(M, K), dtype=np.int8)
             a_s = rng.uniform(0.01, 0.1, size=M).astype(np.float32)
             pa = F.pack_a(A)
-            got = sh(M, D(pa), D(a_s))
+            got = sh.fused_call(M, D(pa), D(a_s))
             torch.cuda.synchronize()
             from fastgemma_b200 import _lib
             assert _lib.lib().fgm_cuda_device_status() == 0
@@ -623,3 +623,74 @@ def test_fused_gather_single_rank_calls(orc):
         assert outs[0].data_ptr() == outs[2].data_ptr() != outs[1].data_ptr()
     finally:
         sh.close()
+
+
+@pytest.mark.parametrize("M,N,col0", [(8, 262144, 0), (3, 5000, 16), (16, 8192, 0), (1, 64, 128)])
+def test_argmax_partials_and_merge_match_the_reference_scan(orc, M, N, col0):
+    """Row argmax (engine.rs:75-83) from chunk partials: ties keep the first
+    index, NaN never wins, an all -inf / NaN row answers 0."""
+    from fastgemma_b200 import _lib
+    L = _lib.lib()
+    rng = np.random.default_rng(N + M)
+    c = rng.standard_normal((M, N)).astype(np.float32)
+    if M > 2:
+        c[1, :] = -np.inf
+        c[1, 7] = np.nan  # nothing above -inf: 0
+        c[2, N // 3] = c[2, N - 5] = 99.0  # a tie: the earlier one
+        c[2, N // 2] = np.nan
+    if M > 5:
+        c[5, :] = c[5, 11]  # all equal: index 11's value first occurs at 0
+        c[5, 0] = c[5, 11] - 1
+    parts = L.fgm_cuda_argmax_parts(N)
+    cd = D(c)
+    vals = torch.empty((M, parts), device="cuda")
+    idx = torch.empty((M, parts), dtype=torch.int32, device="cuda")
+    out = torch.empty(M, dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    _lib.call("fgm_cuda_argmax_partials", cd.data_ptr(), M, N, N, col0, vals.data_ptr(),
+              idx.data_ptr(), s)
+    _lib.call("fgm_cuda_argmax_merge", vals.data_ptr(), idx.data_ptr(), M, parts, out.data_ptr(), s)
+    torch.cuda.synchronize()
+    want = orc.argmax_rows(c)
+    got = out.cpu().numpy()
+    offset = np.where(np.isin(np.arange(M), [1] if M > 2 else []), 0, col0)
+    assert np.array_equal(got, want + offset), (got, want)
+
+
+@pytest.mark.parametrize("world", [1, 2, 8])
+def test_sharded_lm_head_argmax_equals_argmax_of_whole_logits(orc, world):
+    """Every rank's shard reduced to (value, index) pairs and merged (the
+    exchange emulated on one device) picks the token the reference picks from
+    the whole logits."""
+    from fastgemma_b200 import _lib
+    from fastgemma_b200 import shard as S
+    M, N, K = 8, 16384, 2048
+    blob, scale = F.synth_q4g(N, K, 64, 55, structured=False)
+    rng = np.random.default_rng(12)
+    pa = F.pack_a(rng.integers(-128, 128, size=(M, K), dtype=np.int8))
+    a_s = rng.uniform(0.01, 0.1, size=M).astype(np.float32)
+    shards = [S.ColumnShardedGemm("q4g", blob, scale, N, K, 64, rank=r, world=world,
+                                  device="cuda") for r in range(world)]
+    L = _lib.lib()
+    s = torch.cuda.current_stream().cuda_stream
+    parts = L.fgm_cuda_argmax_parts(shards[0].max_cols)
+    vs, ids = [], []
+    for sh in shards:
+        loc = sh.local(M, D(pa), D(a_s))
+        v = torch.empty((M, parts), device="cuda")
+        i = torch.empty((M, parts), dtype=torch.int32, device="cuda")
+        _lib.call("fgm_cuda_argmax_partials", loc.data_ptr(), M, sh.cols, sh.max_cols,
+                  sh.nb0 * 16, v.data_ptr(), i.data_ptr(), s)
+        vs.append(v.clone())
+        ids.append(i.clone())
+    vals = torch.cat(vs, 1).contiguous()
+    idx = torch.cat(ids, 1).contiguous()
+    out = torch.empty(M, dtype=torch.int32, device="cuda")
+    _lib.call("fgm_cuda_argmax_merge", vals.data_ptr(), idx.data_ptr(), M, vals.shape[1],
+              out.data_ptr(), s)
+    torch.cuda.synchronize()
+    logits = orc.gemm_q4g(M, N, K, pa, a_s, blob, scale, 64)
+    assert np.array_equal(out.cpu().numpy(), orc.argmax_rows(logits))
+    if world == 1:
+        assert np.array_equal(shards[0].argmax(M, D(pa), D(a_s)).cpu().numpy(),
+                              orc.argmax_rows(logits))

@@ -38,6 +38,9 @@ def _rank_main(rank, world, port, out_dir, fused=False):
             out = sh(M, pa, qs)
             torch.cuda.synchronize()
             np.save(os.path.join(out_dir, f"r{rank}_c{call}.npy"), out.cpu().numpy())
+        tok = sh.argmax(M, pa, qs)  # pairs exchanged instead of logits
+        torch.cuda.synchronize()
+        np.save(os.path.join(out_dir, f"r{rank}_tok.npy"), tok.cpu().numpy())
         sh.close()
     finally:
         dist.destroy_process_group()
@@ -62,6 +65,8 @@ def test_column_sharded_lm_head(orc, tmp_path, fused):
     _, _, qs, pa = orc.prep_rows(x, M, K, 128)
     want = orc.gemm_q4g(M, N, K, pa, qs, blob, scale, 64)
     for r in range(world):
+        tok = np.load(os.path.join(tmp_path, f"r{r}_tok.npy"))
+        assert np.array_equal(tok, orc.argmax_rows(want)), f"rank {r} argmax"
         for call in range(3 if fused else 1):
             got = np.load(os.path.join(tmp_path, f"r{r}_c{call}.npy"))
             assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"rank {r} call {call}"
