@@ -68,6 +68,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-lm-head", action="store_true")
+    ap.add_argument("--warm", action="store_true",
+                    help="each decode GEMM prefetches the next projection's weights into L2")
     ap.add_argument("--eager", action="store_true",
                     help="launch the step's kernels directly instead of replaying a CUDA graph "
                          "(same kernels, same order; used for ncu launch lists)")
@@ -282,14 +284,25 @@ def main():
           for name, K, N in DECODE_SHAPES}
     wbytes_step = L * sum(sum(q4g_bytes(K, N)) for _, K, N in DECODE_SHAPES)
 
+    # the decode order of the projections; with --warm each GEMM warms L2 with
+    # the weights of the one after it (the last wraps to the next step's first)
+    order = [(l, name) for l in range(L) for name, _, _ in DECODE_SHAPES]
+
     def step():
+        j = 0
         for l in range(L):
             for i, x in enumerate(xs):
                 D.prep_rows(x, x.shape[1], qss[i], pas[i], M_DECODE, x.shape[1], 0)
             for name, K, N in DECODE_SHAPES:
                 w, s = layers[l][name]
                 i = DECODE_INPUT[name]
-                D.gemm_q4g(M_DECODE, N, K, pas[i], qss[i], w, s, GROUP, cs[name])
+                if not args.warm:
+                    D.gemm_q4g(M_DECODE, N, K, pas[i], qss[i], w, s, GROUP, cs[name])
+                else:
+                    nl, nname = order[(j + 1) % len(order)]
+                    D.gemm_q4g_warm(M_DECODE, N, K, pas[i], qss[i], w, s, GROUP, cs[name],
+                                    layers[nl][nname])
+                j += 1
 
     def gate_up_only():  # the dominant kernel back to back over the L weight copies
         i = DECODE_INPUT["gate_up"]

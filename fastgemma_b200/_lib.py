@@ -35,6 +35,10 @@ SIGNATURES = {
     "fgm_cuda_registry_bytes": ([], _sz),
     "fgm_cuda_gemm_q4g": ([_i, _i, _i, _p, _p, _p, _p, _i, _p, _i, _i, _i, _p], _i),
     "fgm_cuda_gemm_q8c": ([_i, _i, _i, _p, _p, _p, _p, _p, _i, _i, _i, _p], _i),
+    "fgm_cuda_gemm_q4g_warm": ([_i, _i, _i, _p, _p, _p, _p, _i, _p, _i, _i, _i,
+                                _p, _sz, _p, _sz, _p], _i),
+    "fgm_cuda_gemm_q8c_warm": ([_i, _i, _i, _p, _p, _p, _p, _p, _i, _i, _i,
+                                _p, _sz, _p, _sz, _p], _i),
     "fgm_cuda_prep_rows": ([_p, _i, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p], _i),
     "fgm_cuda_linear_q4g": ([_p, _i, _i, _i, _i, _i, _p, _p, _i, _p, _i, _i, _i, _p], _i),
     "fgm_cuda_linear_q8c": ([_p, _i, _i, _i, _i, _i, _p, _p, _p, _i, _i, _i, _p], _i),

@@ -506,9 +506,14 @@ static int static_rows(int8_t **out) {
 }
 
 // ------------------------------------------------------------- launchers
+struct Warm {
+  const void *p[2] = {nullptr, nullptr};
+  size_t bytes[2] = {0, 0};
+};
+
 static int run_gemm(bool q4, int M, int N, int K, const int8_t *A, const float *a_scale,
                     const void *B, const void *b_scale, int group, float *C, int ldc, int c_col0,
-                    int32_t *acc, int n0, int n1, cudaStream_t st) {
+                    int32_t *acc, int n0, int n1, cudaStream_t st, const Warm &warm = Warm()) {
   if (M == 0 || n0 == n1) return FGM_CUDA_OK;
   if (!aligned16(B) || (q4 && b_scale && !aligned16(b_scale)))
     return fail(FGM_CUDA_EINVAL, "weights and int4 scales must be 16-byte aligned");
@@ -534,6 +539,10 @@ static int run_gemm(bool q4, int M, int N, int K, const int8_t *A, const float *
   p.c_col0 = c_col0;
   p.acc = acc;
   p.nb0 = n0;
+  for (int r = 0; r < 2; r++) {
+    p.warm[r] = static_cast<const uint8_t *>(warm.p[r]);
+    p.warm_bytes[r] = warm.p[r] ? warm.bytes[r] : 0;
+  }
   cudaError_t e = launch_gemv(p, n1 - n0, q4, use_pdl(), di->sms, di->smem_optin, st);
   if (e != cudaSuccess) return cuda_fail(e, q4 ? "gemm_q4g launch" : "gemm_q8c launch");
   count_launch();
@@ -970,6 +979,44 @@ int fgm_cuda_gemm_q4g(int M, int N, int K, const int8_t *A, const float *a_scale
     return fail(FGM_CUDA_EINVAL, "null pointer");
   return run_gemm(true, M, N, K, A, a_scale, Bq, b_scale, group, C, ldc, 0, nullptr, n0, n1,
                   (cudaStream_t)stream);
+}
+
+static int make_warm(const void *w, size_t w_bytes, const void *s, size_t s_bytes, Warm *out) {
+  if ((w && !aligned16(w)) || (s && !aligned16(s)))
+    return fail(FGM_CUDA_EINVAL, "warm regions must be 16-byte aligned");
+  out->p[0] = w;
+  out->bytes[0] = w_bytes;
+  out->p[1] = s;
+  out->bytes[1] = s_bytes;
+  return FGM_CUDA_OK;
+}
+
+int fgm_cuda_gemm_q4g_warm(int M, int N, int K, const int8_t *A, const float *a_scale,
+                           const uint8_t *Bq, const uint16_t *b_scale, int group, float *C,
+                           int ldc, int n0, int n1, const void *next_w, size_t next_w_bytes,
+                           const void *next_s, size_t next_s_bytes, void *stream) {
+  int rc = check_gemm(M, N, K, ldc, n0, n1, group, true);
+  if (rc) return rc;
+  if (M > 0 && n0 < n1 && (!A || !a_scale || !Bq || !b_scale || !C))
+    return fail(FGM_CUDA_EINVAL, "null pointer");
+  Warm w;
+  if ((rc = make_warm(next_w, next_w_bytes, next_s, next_s_bytes, &w))) return rc;
+  return run_gemm(true, M, N, K, A, a_scale, Bq, b_scale, group, C, ldc, 0, nullptr, n0, n1,
+                  (cudaStream_t)stream, w);
+}
+
+int fgm_cuda_gemm_q8c_warm(int M, int N, int K, const int8_t *A, const float *a_scale,
+                           const int8_t *B, const float *b_scale, float *C, int ldc, int n0,
+                           int n1, const void *next_w, size_t next_w_bytes, const void *next_s,
+                           size_t next_s_bytes, void *stream) {
+  int rc = check_gemm(M, N, K, ldc, n0, n1, 64, false);
+  if (rc) return rc;
+  if (M > 0 && n0 < n1 && (!A || !a_scale || !B || !b_scale || !C))
+    return fail(FGM_CUDA_EINVAL, "null pointer");
+  Warm w;
+  if ((rc = make_warm(next_w, next_w_bytes, next_s, next_s_bytes, &w))) return rc;
+  return run_gemm(false, M, N, K, A, a_scale, B, b_scale, 64, C, ldc, 0, nullptr, n0, n1,
+                  (cudaStream_t)stream, w);
 }
 
 int fgm_cuda_gemm_q8c(int M, int N, int K, const int8_t *A, const float *a_scale,

@@ -33,6 +33,11 @@ struct GemvParams {
   int nb0;                  // first n-block of the range
   int *err;                 // device flag set when a bounded wait gives up (may be null)
   GatherParams g;           // fused all-gather (g.world = 0: none)
+  // L2 warm-up of the weights the NEXT launch will stream (up to two regions,
+  // 16-byte aligned; bytes 0 = none), prefetched once this launch's own
+  // weight stream is queued
+  const uint8_t *warm[2];
+  size_t warm_bytes[2];
 };
 
 // Launch geometry of the streaming decode kernel (gemv.cu).

@@ -135,6 +135,28 @@ __device__ __forceinline__ float i2f_group(int32_t x, bool exact_ok) {
   return exact_ok ? i2f_exact(x) : __int2float_rn(x);
 }
 
+// Fire-and-forget L2 prefetch of [src, src + bytes): no completion to wait
+// for, so a late or dropped prefetch only costs a later miss.
+__device__ __forceinline__ void prefetch_l2_bulk(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// This CTA's slice of the next launch's weight regions, 32 KB per prefetch,
+// spread over the lanes of one warp.
+__device__ __forceinline__ void warm_next(const GemvParams &p, int lane) {
+  constexpr size_t kPiece = 32768;
+#pragma unroll
+  for (int r = 0; r < 2; r++) {
+    const size_t total = p.warm_bytes[r] & ~(size_t)15;
+    if (total == 0) continue;
+    const size_t per = ((total + gridDim.x - 1) / gridDim.x + 15) & ~(size_t)15;
+    const size_t lo = (size_t)blockIdx.x * per;
+    const size_t hi = lo + per < total ? lo + per : total;
+    for (size_t o = lo + (size_t)lane * kPiece; o < hi; o += 32 * kPiece)
+      prefetch_l2_bulk(p.warm[r] + o, (uint32_t)(hi - o < kPiece ? hi - o : kPiece));
+  }
+}
+
 // ------------------------------------------------------ fused all-gather
 // Signal words of one rank (u64 each, zeroed once, never reset -- counts
 // grow by a known amount per call): [slot] = ranks whose last CTA finished
@@ -481,6 +503,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
 
   const int prologue = items < S ? items : S;
   for (int it = 0; it < prologue; it++) issue();
+  // the next launch's weights follow this launch's own stage requests into
+  // the memory system, so HBM keeps streaming across the kernel boundary
+  if (blockIdx.y == 0 && warp == NW - 1 && (p.warm_bytes[0] | p.warm_bytes[1])) warm_next(p, lane);
   uint32_t sc_a0 = 0, sc_a1 = 0, sc_b0 = 0, sc_b1 = 0;  // stages it and it+1
   if (want_sc && GK) {
     scale_fetch(sc_a0, sc_a1);

@@ -31,6 +31,29 @@ def gemm_q8c(M, N, K, A, a_scale, B, b_scale, C, ldc=None, n0=0, n1=None, stream
          N if ldc is None else ldc, n0, n1, _s(stream))
 
 
+def _warm_args(warm):
+    """(weights, scales) tensors of the next launch -> the four warm arguments."""
+    w, s = (tuple(warm) + (None, None))[:2] if warm is not None else (None, None)
+    nbytes = lambda t: 0 if t is None else t.numel() * t.element_size()
+    return _p(w), nbytes(w), _p(s), nbytes(s)
+
+
+def gemm_q4g_warm(M, N, K, A, a_scale, Bq, b_scale, group, C, warm, ldc=None, n0=0, n1=None,
+                  stream=None):
+    """gemm_q4g that also prefetches warm = (next weights, next scales) into L2."""
+    n1 = N // 16 if n1 is None else n1
+    call("fgm_cuda_gemm_q4g_warm", M, N, K, _p(A), _p(a_scale), _p(Bq), _p(b_scale), group,
+         _p(C), N if ldc is None else ldc, n0, n1, *_warm_args(warm), _s(stream))
+
+
+def gemm_q8c_warm(M, N, K, A, a_scale, B, b_scale, C, warm, ldc=None, n0=0, n1=None,
+                  stream=None):
+    """gemm_q8c that also prefetches warm = (next weights, next scales) into L2."""
+    n1 = N // 16 if n1 is None else n1
+    call("fgm_cuda_gemm_q8c_warm", M, N, K, _p(A), _p(a_scale), _p(B), _p(b_scale), _p(C),
+         N if ldc is None else ldc, n0, n1, *_warm_args(warm), _s(stream))
+
+
 def gemm_q4g_acc(M, N, K, A, Bq, group, acc, n0=0, n1=None, stream=None):
     n1 = N // 16 if n1 is None else n1
     call("fgm_cuda_gemm_q4g_acc", M, N, K, _p(A), _p(Bq), group, _p(acc), n0, n1, _s(stream))

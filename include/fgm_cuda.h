@@ -154,6 +154,25 @@ int fgm_cuda_gemm_q8c(int M, int N, int K, const int8_t *A, const float *a_scale
                       const int8_t *B, const float *b_scale, float *C, int ldc,
                       int n0, int n1, void *stream);
 
+/* fgm_cuda_gemm_q4g / fgm_cuda_gemm_q8c that also warm L2 for the launch
+ * that follows: once this GEMM's own weight stream is queued, its CTAs
+ * prefetch [next_w, next_w + next_w_bytes) and [next_s, next_s +
+ * next_s_bytes) (16-byte aligned; a null pointer or 0 bytes = none) into L2,
+ * so HBM keeps streaming across the kernel boundary and the next decode GEMM
+ * finds its weights on chip.  The prefetch has no completion and changes no
+ * result.  A decode forward knows its layer order, so it passes the next
+ * projection's tile blob and scales.  No reference counterpart: the
+ * reference's CPU GEMMs (amx_gemm.c:333-475) stream from DRAM per call. */
+int fgm_cuda_gemm_q4g_warm(int M, int N, int K, const int8_t *A, const float *a_scale,
+                           const uint8_t *Bq, const uint16_t *b_scale, int group, float *C,
+                           int ldc, int n0, int n1, const void *next_w, size_t next_w_bytes,
+                           const void *next_s, size_t next_s_bytes, void *stream);
+
+int fgm_cuda_gemm_q8c_warm(int M, int N, int K, const int8_t *A, const float *a_scale,
+                           const int8_t *B, const float *b_scale, float *C, int ldc, int n0,
+                           int n1, const void *next_w, size_t next_w_bytes, const void *next_s,
+                           size_t next_s_bytes, void *stream);
+
 /* One projection of fgm-core's Gemm::run (forward.rs:128-158) on device
  * buffers: f32 rows src [M][lda] are rotated (hsz), quantised per row and
  * multiplied into C [M][ldc], columns [n0*16, n1*16), on `stream`.  The

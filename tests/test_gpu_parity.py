@@ -154,6 +154,36 @@ def test_decode_q4g_shapes_bit_exact(orc, M, K, N):
         assert np.array_equal(acc.cpu().numpy(), orc.gemm_q4g_acc(M, N, K, pa, bq, 64))
 
 
+def test_warm_entries_change_no_result(orc):
+    """The L2-warming GEMM entries give the plain entries' bits, for a chain
+    where each launch prefetches the next one's weights (the last one none),
+    and reject unaligned regions."""
+    rng = np.random.default_rng(5)
+    M, K = 8, 2048
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    _, _, qs, pa = orc.prep_rows(x, M, K, 0)
+    pad, qsd = D(pa), D(qs)
+    chain = [F.synth_q4g(N, K, 64, 90 + N, structured=False) for N in (2048, 512, 16384)]
+    dev = [(D(bq), D(s.view(np.uint16))) for bq, s in chain]
+    for j, ((bq, s), (bqd, sd)) in enumerate(zip(chain, dev)):
+        N = s.shape[1]
+        c = torch.full((M, N), float("nan"), device="cuda")
+        nxt = dev[j + 1] if j + 1 < len(dev) else None
+        fg.device.gemm_q4g_warm(M, N, K, pad, qsd, bqd, sd, 64, c, nxt)
+        torch.cuda.synchronize()
+        assert_bits(c.cpu().numpy(), orc.gemm_q4g(M, N, K, pa, qs, bq, s, 64), f"warm q4g {N}")
+    b, s8 = F.synth_q8c(1024, K, 3)
+    a_s = rng.uniform(0.001, 0.05, size=M).astype(np.float32)
+    c = torch.full((M, 1024), float("nan"), device="cuda")
+    fg.device.gemm_q8c_warm(M, 1024, K, pad, D(a_s), D(b), D(s8), c, dev[0])
+    torch.cuda.synchronize()
+    assert_bits(c.cpu().numpy(), orc.gemm_q8c(M, 1024, K, pa, a_s, b, s8), "warm q8c")
+    from fastgemma_b200 import _lib
+    bqd, sd = dev[0]
+    with pytest.raises(_lib.FgmCudaError, match="16-byte"):
+        fg.device.gemm_q4g_warm(M, 2048, K, pad, qsd, bqd, sd, 64, c, (bqd[1:], None))
+
+
 @pytest.mark.parametrize("M,K,N", [(1, 2048, 512), (8, 2048, 2048), (16, 8192, 256),
                                    (17, 2048, 256), (64, 1024, 512), (256, 2048, 512),
                                    (256, 8192, 256)])
