@@ -528,6 +528,14 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     }
   }
 
+  // the row block's activation scales ride in the same round trip as the
+  // activation staging (one L2 latency after griddepcontrol.wait, not two)
+  const bool load_as = !raw && threadIdx.x < MT * 8;
+  float as_v = 0.0f;
+  if (load_as) {
+    const int m = mb * 16 + threadIdx.x;
+    as_v = m < p.M ? p.a_scale[m] : 0.0f;
+  }
   if (pl.a_bytes) {  // stage this row block's activations, B-fragment order
     // 16-byte pieces: piece c of a 64-byte row holds k-quads 4c..4c+3, which
     // land at word positions j*4 + c.  Loads go out in independent batches.
@@ -556,15 +564,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
         }
       }
     }
-    __syncthreads();
   }
-  if (!raw) {  // per-row activation scales for the epilogue
-    if (threadIdx.x < MT * 8) {
-      const int m = mb * 16 + threadIdx.x;
-      s_as[threadIdx.x] = m < p.M ? p.a_scale[m] : 0.0f;
-    }
-    __syncthreads();
-  }
+  if (load_as) s_as[threadIdx.x] = as_v;
+  if (pl.a_bytes || !raw) __syncthreads();
 
   float cf[MT][4];
   int32_t gacc[MT][4];
