@@ -58,6 +58,10 @@ namespace fgm {
 namespace {
 
 constexpr int kMaxWarps = 16;
+// Words per published row of group values in the split-K exchange area: 16
+// columns plus 4 words of padding, so the rows 2*tig (+1) that one store
+// instruction's lanes write fall in distinct banks.
+constexpr int kPubRow = 20;
 
 template <bool Q4>
 struct Geo {
@@ -208,53 +212,63 @@ struct Lane {
 // One ring stage of NT tiles, NT a compile-time count (no per-tile guards, so
 // all of the stage's loads are issued before its MMAs).  MODE 0: fold each
 // completed scale group into cf (int4, P = 1).  MODE 1: publish each
-// completed group's int32 sum to pub[g][row][col] (int4 split K or int32
-// output).  MODE 2: accumulate into gacc (int8).  Stages start on a group
-// boundary (GK divides NT).
+// completed group's int32 sum to pub[g][row][col] (int32 output).  MODE 2:
+// accumulate into gacc (int8).  MODE 3: publish each completed group's sum
+// as the exact f32 the fold will use, with the group's f32 scales (int4 split
+// K parts 1..P-1), so the team's serial fold is a load pair and an FMA per
+// group.  Stages start on a group boundary (GK divides NT).
 template <bool Q4, int MT, int GK, int NT, int MODE>
 __device__ __forceinline__ void stage_full(uint32_t st, uint32_t ab, const Lane &L, int g0,
                                            uint32_t sc0, uint32_t sc1, float (&cf)[MT][4],
                                            int32_t (&gacc)[MT][4], int32_t *pub,
                                            uint32_t *pub_sc) {
   constexpr int TB = Geo<Q4>::TB;
-  uint32_t w[NT][Q4 ? 4 : 8];
-  uint32_t b[NT][MT][4];
+  // tiles whose operands are loaded together before their MMAs: the whole
+  // stage for 8-row blocks, half of it for 16 (register budget)
+  constexpr int CH = (MT == 1 || NT < 8) ? NT : NT / 2;
 #pragma unroll
-  for (int t = 0; t < NT; t++) {
+  for (int t0 = 0; t0 < NT; t0 += CH) {
+  uint32_t w[CH][Q4 ? 4 : 8];
+  uint32_t b[CH][MT][4];
+#pragma unroll
+  for (int tc = 0; tc < CH; tc++) {
+    const int t = t0 + tc;
 #pragma unroll
     for (int q = 0; q < 4; q++) {  // tile rows q*4 + tig
       if (Q4) {
-        w[t][q] = lds32(st + t * TB + L.w_off + q * 128);
+        w[tc][q] = lds32(st + t * TB + L.w_off + q * 128);
       } else {
-        w[t][2 * q] = lds32(st + t * TB + L.w_off + q * 256);
-        w[t][2 * q + 1] = lds32(st + t * TB + L.w_off + q * 256 + 32);
+        w[tc][2 * q] = lds32(st + t * TB + L.w_off + q * 256);
+        w[tc][2 * q + 1] = lds32(st + t * TB + L.w_off + q * 256 + 32);
       }
     }
 #pragma unroll
     for (int mt = 0; mt < MT; mt++) {
       const uint4 v = lds128(ab + (t * MT + mt) * 512 + L.a_off);
-      b[t][mt][0] = v.x;
-      b[t][mt][1] = v.y;
-      b[t][mt][2] = v.z;
-      b[t][mt][3] = v.w;
+      b[tc][mt][0] = v.x;
+      b[tc][mt][1] = v.y;
+      b[tc][mt][2] = v.z;
+      b[tc][mt][3] = v.w;
     }
   }
 #pragma unroll
-  for (int t = 0; t < NT; t++) {
+  for (int tc = 0; tc < CH; tc++) {
+    const int t = t0 + tc;
     int32_t ta[MT][4];
 #pragma unroll
     for (int mt = 0; mt < MT; mt++) {
       if (Q4) {
-        mma_s8_m16n8k32_c(ta[mt], nib_lo_x16(w[t][0]), nib_hi_x16(w[t][0]), nib_lo_x16(w[t][1]),
-                          nib_hi_x16(w[t][1]), b[t][mt][0], b[t][mt][1], 0, 0, 0, 0);
-        mma_s8_m16n8k32_c(ta[mt], nib_lo_x16(w[t][2]), nib_hi_x16(w[t][2]), nib_lo_x16(w[t][3]),
-                          nib_hi_x16(w[t][3]), b[t][mt][2], b[t][mt][3], ta[mt][0], ta[mt][1],
-                          ta[mt][2], ta[mt][3]);
-      } else {
-        mma_s8_m16n8k32_c(ta[mt], w[t][0], w[t][1], w[t][2], w[t][3], b[t][mt][0], b[t][mt][1], 0,
-                          0, 0, 0);
-        mma_s8_m16n8k32_c(ta[mt], w[t][4], w[t][5], w[t][6], w[t][7], b[t][mt][2], b[t][mt][3],
+        mma_s8_m16n8k32_c(ta[mt], nib_lo_x16(w[tc][0]), nib_hi_x16(w[tc][0]),
+                          nib_lo_x16(w[tc][1]), nib_hi_x16(w[tc][1]), b[tc][mt][0], b[tc][mt][1],
+                          0, 0, 0, 0);
+        mma_s8_m16n8k32_c(ta[mt], nib_lo_x16(w[tc][2]), nib_hi_x16(w[tc][2]),
+                          nib_lo_x16(w[tc][3]), nib_hi_x16(w[tc][3]), b[tc][mt][2], b[tc][mt][3],
                           ta[mt][0], ta[mt][1], ta[mt][2], ta[mt][3]);
+      } else {
+        mma_s8_m16n8k32_c(ta[mt], w[tc][0], w[tc][1], w[tc][2], w[tc][3], b[tc][mt][0],
+                          b[tc][mt][1], 0, 0, 0, 0);
+        mma_s8_m16n8k32_c(ta[mt], w[tc][4], w[tc][5], w[tc][6], w[tc][7], b[tc][mt][2],
+                          b[tc][mt][3], ta[mt][0], ta[mt][1], ta[mt][2], ta[mt][3]);
       }
     }
     if (MODE == 2) {
@@ -279,15 +293,32 @@ __device__ __forceinline__ void stage_full(uint32_t st, uint32_t ab, const Lane 
         for (int i = 0; i < 4; i++)
           cf[mt][i] = __fmaf_rn(i2f_exact(gacc[mt][i] >> 4), i < 2 ? s0 : s1, cf[mt][i]);
     } else {
+      const size_t gb = (size_t)(g0 + lg) * MT * 8;
+      if (MODE == 3) {
+        float s0, s1;
+        scale_pair(lg < 4 ? sc0 : sc1, (lg & 3) * 8, L.g8, s0, s1);
+        float *pf = reinterpret_cast<float *>(pub);
 #pragma unroll
-      for (int mt = 0; mt < MT; mt++)
+        for (int mt = 0; mt < MT; mt++)
 #pragma unroll
-        for (int i = 0; i < 4; i++)
-          pub[((size_t)(g0 + lg) * MT * 8 + mt * 8 + 2 * L.tig + (i & 1)) * 16 + L.g8 +
-              (i >= 2 ? 8 : 0)] = gacc[mt][i] >> 4;
-      if (pub_sc && (L.lane >> 3) == (lg & 3))  // the 8 lanes holding this row
-        pub_sc[(size_t)(g0 + lg) * 8 + (L.lane & 7)] = lg < 4 ? sc0 : sc1;
+          for (int i = 0; i < 4; i++)
+            pf[(gb + mt * 8 + 2 * L.tig + (i & 1)) * kPubRow + L.g8 + (i >= 2 ? 8 : 0)] =
+                i2f_exact(gacc[mt][i] >> 4);
+        if (L.tig == 0) {
+          float *ps = reinterpret_cast<float *>(pub_sc) + (size_t)(g0 + lg) * 16;
+          ps[L.g8] = s0;
+          ps[L.g8 + 8] = s1;
+        }
+      } else {
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+          for (int i = 0; i < 4; i++)
+            pub[(gb + mt * 8 + 2 * L.tig + (i & 1)) * kPubRow + L.g8 + (i >= 2 ? 8 : 0)] =
+                gacc[mt][i] >> 4;
+      }
     }
+  }
   }
   if (MODE != 2)  // the stage ended on a group boundary: nothing carries over
 #pragma unroll
@@ -359,8 +390,9 @@ __device__ __forceinline__ void stage_generic(uint32_t st, uint32_t a_sm, const 
     if ((gt + 1) % gk != 0) continue;
     const int g = gt / gk;
     const int lg = (gt - gt0) / gk;  // group index inside the stage (GK > 0 only)
-    if (MODE == 0) {
-      float s0, s1;
+    const bool exact_ok = GK || p.group <= kExactGroupMax;
+    float s0 = 0.0f, s1 = 0.0f;
+    if (MODE == 0 || MODE == 3) {
       if (GK) {  // groups tile the stage: the prefetched rows hold this group
         scale_pair(lg < 4 ? sc0 : sc1, (lg & 3) * 8, L.g8, s0, s1);
       } else {
@@ -369,28 +401,35 @@ __device__ __forceinline__ void stage_generic(uint32_t st, uint32_t a_sm, const 
         s0 = __half2float(sr[L.g8]);
         s1 = __half2float(sr[L.g8 + 8]);
       }
+    }
+    if (MODE == 0) {
 #pragma unroll
       for (int mt = 0; mt < MT; mt++)
 #pragma unroll
         for (int i = 0; i < 4; i++)
-          cf[mt][i] = __fmaf_rn(i2f_group(gacc[mt][i] >> 4, GK || p.group <= kExactGroupMax),
-                                i < 2 ? s0 : s1, cf[mt][i]);
+          cf[mt][i] = __fmaf_rn(i2f_group(gacc[mt][i] >> 4, exact_ok), i < 2 ? s0 : s1, cf[mt][i]);
     } else {
+      const size_t gb = (size_t)(g - gbase) * MT * 8;
+      if (MODE == 3) {
+        float *pf = reinterpret_cast<float *>(pub);
 #pragma unroll
-      for (int mt = 0; mt < MT; mt++)
+        for (int mt = 0; mt < MT; mt++)
 #pragma unroll
-        for (int i = 0; i < 4; i++)
-          pub[((size_t)(g - gbase) * MT * 8 + mt * 8 + 2 * L.tig + (i & 1)) * 16 + L.g8 +
-              (i >= 2 ? 8 : 0)] = gacc[mt][i] >> 4;
-      if (pub_sc) {
-        if (GK) {
-          if ((L.lane >> 3) == (lg & 3))
-            pub_sc[(size_t)(g - gbase) * 8 + (L.lane & 7)] = lg < 4 ? sc0 : sc1;
-        } else if (L.lane < 8) {
-          pub_sc[(size_t)(g - gbase) * 8 + L.lane] = *reinterpret_cast<const uint32_t *>(
-              reinterpret_cast<const uint8_t *>(p.b_scale) +
-              ((size_t)g * p.N + (size_t)nb * 16) * 2 + L.lane * 4);
+          for (int i = 0; i < 4; i++)
+            pf[(gb + mt * 8 + 2 * L.tig + (i & 1)) * kPubRow + L.g8 + (i >= 2 ? 8 : 0)] =
+                i2f_group(gacc[mt][i] >> 4, exact_ok);
+        if (L.tig == 0) {
+          float *ps = reinterpret_cast<float *>(pub_sc) + (size_t)(g - gbase) * 16;
+          ps[L.g8] = s0;
+          ps[L.g8 + 8] = s1;
         }
+      } else {
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+          for (int i = 0; i < 4; i++)
+            pub[(gb + mt * 8 + 2 * L.tig + (i & 1)) * kPubRow + L.g8 + (i >= 2 ? 8 : 0)] =
+                gacc[mt][i] >> 4;
       }
     }
 #pragma unroll
@@ -426,8 +465,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
   uint8_t *after_ring = smem + (size_t)NW * S * pl.stage_bytes;
   int32_t *xsum = reinterpret_cast<int32_t *>(after_ring + (size_t)team * pl.xchg_bytes);
   // part 0's running f32 outputs, handed to the team after the last group,
-  // then the published groups' f16 scale rows (8 words each)
-  float *cpart = reinterpret_cast<float *>(xsum + (size_t)(G - gpub) * MT * 128);
+  // then the published groups' f32 scale rows (16 floats each)
+  float *cpart = reinterpret_cast<float *>(xsum + (size_t)(G - gpub) * MT * 8 * kPubRow);
   uint32_t *xscale = reinterpret_cast<uint32_t *>(cpart + MT * 128);
   uint32_t *pub_sc = (Q4 && !raw && P > 1) ? xscale : nullptr;
   uint32_t *a_sm = reinterpret_cast<uint32_t *>(after_ring + (size_t)teams * pl.xchg_bytes);
@@ -501,8 +540,12 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     }
   };
 
+  // Stages requested before griddepcontrol.wait overlap a predecessor that is
+  // still running; the rest go out after the activation loads, so those loads
+  // do not queue behind a full weight stream (they gate every MMA).
   const int prologue = items < S ? items : S;
-  for (int it = 0; it < prologue; it++) issue();
+  const int pre = prologue < pl.pre_stages ? prologue : pl.pre_stages;
+  for (int it = 0; it < pre; it++) issue();
   // the next launch's weights follow this launch's own stage requests into
   // the memory system, so HBM keeps streaming across the kernel boundary
   if (blockIdx.y == 0 && warp == NW - 1 && (p.warm_bytes[0] | p.warm_bytes[1])) warm_next(p, lane);
@@ -541,7 +584,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     // land at word positions j*4 + c.  Loads go out in independent batches.
     constexpr int kBatchLd = 8;
     const int pieces = KB * MT * 8 * 4;
-    for (int base = threadIdx.x; base < pieces; base += kBatchLd * blockDim.x) {
+    const int step = kBatchLd * blockDim.x;
+    for (int b0 = 0; b0 < pieces; b0 += step) {  // the same trip count in every thread
+      const int base = b0 + threadIdx.x;
       uint4 v[kBatchLd];
 #pragma unroll
       for (int u = 0; u < kBatchLd; u++) {
@@ -551,6 +596,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
           v[u] = *reinterpret_cast<const uint4 *>(abase + (size_t)tile * kATile + row * 64 + c * 16);
         }
       }
+      if (b0 == 0)  // the first batch is in flight: now the rest of the weight prologue
+        for (int it = pre; it < prologue; it++) issue();
 #pragma unroll
       for (int u = 0; u < kBatchLd; u++) {
         const int i = base + u * blockDim.x;
@@ -564,6 +611,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
         }
       }
     }
+  } else {
+    for (int it = pre; it < prologue; it++) issue();
   }
   if (load_as) s_as[threadIdx.x] = as_v;
   if (pl.a_bytes || !raw) __syncthreads();
@@ -614,12 +663,19 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
         else
           stage_generic<Q4, MT, GK, 0>(st, a_sm_u, abase, a_in, L, gt0, nt, gk, nb, p, sc0, sc1,
                                        cf, gacc, nullptr, 0, nullptr);
-      } else {
+      } else if (raw) {
         if (fast)
           stage_full<Q4, MT, GK ? GK : 1, T, 1>(st, ab, L, gt0 / gk - gpub, sc0, sc1, cf, gacc,
-                                                xsum, pub_sc);
+                                                xsum, nullptr);
         else
           stage_generic<Q4, MT, GK, 1>(st, a_sm_u, abase, a_in, L, gt0, nt, gk, nb, p, sc0, sc1,
+                                       cf, gacc, xsum, gpub, nullptr);
+      } else {
+        if (fast)
+          stage_full<Q4, MT, GK ? GK : 1, T, 3>(st, ab, L, gt0 / gk - gpub, sc0, sc1, cf, gacc,
+                                                xsum, pub_sc);
+        else
+          stage_generic<Q4, MT, GK, 3>(st, a_sm_u, abase, a_in, L, gt0, nt, gk, nb, p, sc0, sc1,
                                        cf, gacc, xsum, gpub, pub_sc);
       }
     }
@@ -645,7 +701,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
         for (int o = lane; o < G * MT * 128; o += 32) {
           const int g = o / (MT * 128), r = o % (MT * 128), ml = r >> 4, nl = r & 15;
           const int m = mb * 16 + ml;
-          if (m < p.M) p.acc[((size_t)m * G + g) * p.N + nb * 16 + nl] = xsum[o];
+          if (m < p.M)
+            p.acc[((size_t)m * G + g) * p.N + nb * 16 + nl] =
+                xsum[((size_t)g * MT * 8 + ml) * kPubRow + nl];
         }
         __syncwarp();
         continue;
@@ -697,17 +755,16 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
         if (m >= p.M) continue;
         if (raw) {
           for (int g = 0; g < G; g++)
-            p.acc[((size_t)m * G + g) * p.N + n] = xsum[(g * MT * 8 + ml) * 16 + nl];
+            p.acc[((size_t)m * G + g) * p.N + n] = xsum[((size_t)g * MT * 8 + ml) * kPubRow + nl];
           continue;
         }
         // continue part 0's chain through the published groups, in order
-        const bool exact_ok = p.group <= kExactGroupMax;
-        const __half *sc = reinterpret_cast<const __half *>(xscale) + nl;
+        const float *xf = reinterpret_cast<const float *>(xsum) + ml * kPubRow + nl;
+        const float *xs = reinterpret_cast<const float *>(xscale) + nl;
         float c = cpart[o];
+        const int ng = G - gpub;
 #pragma unroll 8
-        for (int g = gpub; g < G; g++)
-          c = __fmaf_rn(i2f_group(xsum[((g - gpub) * MT * 8 + ml) * 16 + nl], exact_ok),
-                        __half2float(sc[(size_t)(g - gpub) * 16]), c);
+        for (int g = 0; g < ng; g++) c = __fmaf_rn(xf[(size_t)g * MT * 8 * kPubRow], xs[g * 16], c);
         p.C[(size_t)m * p.ldc + (n - p.c_col0)] = __fmul_rn(c, s_as[ml]);
       } else {
         const int32_t v = xsum[ml * 16 + nl];
@@ -827,9 +884,10 @@ GemvPlan plan_gemv(const GemvParams &p, int nblocks, bool q4, int num_sms, size_
     if (want_warps > kMaxWarps) want_warps = kMaxWarps;
     if (want_warps < P) want_warps = P;
     size_t xchg = 0;
-    if (q4 && raw) xchg = (size_t)G * MT * 128 * 4;  // every group's int32 sum
-    else if (q4 && P > 1)  // groups of parts 1..P-1 with their scale rows, part 0's chain
-      xchg = (size_t)(G - G / P) * (MT * 128 * 4 + 32) + (size_t)MT * 128 * 4;
+    const size_t grp = (size_t)MT * 8 * kPubRow * 4;  // one group's published values
+    if (q4 && raw) xchg = (size_t)G * grp;             // every group's int32 sum
+    else if (q4 && P > 1)  // groups of parts 1..P-1 with their f32 scale rows, part 0's chain
+      xchg = (size_t)(G - G / P) * (grp + 64) + (size_t)MT * 128 * 4;
     else if (P > 1) xchg = (size_t)MT * 128 * 4;  // int8 partials
     const int xchg_bytes = (int)((xchg + 127) / 128 * 128);
     // fewer warps per CTA when the exchange areas would not fit otherwise
@@ -845,6 +903,7 @@ GemvPlan plan_gemv(const GemvParams &p, int nblocks, bool q4, int num_sms, size_
             pl.parts = P;
             pl.xchg_bytes = xchg_bytes;
             pl.stages = S;
+            pl.pre_stages = 1;
             pl.a_bytes = with_a ? (int)a_bytes : 0;
             pl.smem_bytes = total;
             found = true;
