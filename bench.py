@@ -364,14 +364,20 @@ def main():
     value = world * wbytes_step / (ms * 1e-3) / 1e9
 
     # ---- roofline of the dominant kernel (gate/up q4g GEMM), CUDA events
-    kdur = []
-    for _ in range(5):
+    # R replays of the L-launch chain per event pair: L*R launches back to back
+    # (inputs 12 x 17.9 MB > L2), so one host-side graph launch gap is spread
+    # over L*R kernels instead of L
+    kdur, R = [], 8
+    run_gate_up()
+    torch.cuda.synchronize()
+    for _ in range(3):
         k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         k0.record(side)
-        run_gate_up()
+        for _ in range(R):
+            run_gate_up()
         k1.record(side)
         torch.cuda.synchronize()
-        kdur.append(k0.elapsed_time(k1) * 1e-3 / L)
+        kdur.append(k0.elapsed_time(k1) * 1e-3 / (L * R))
     K_, N_ = 2048, 16384
     alg = sum(q4g_bytes(K_, N_)) + M_DECODE * K_ + M_DECODE * 4 + M_DECODE * N_ * 4
     kmean = statistics.mean(kdur)
@@ -394,9 +400,9 @@ def main():
                 "frac": achieved / hbm, "traffic": traffic, "peak_source": peak_src,
                 "kernel": "gemv_kernel<q4g, M<=8> gate/up 2048x16384",
                 "algorithmic_bytes_per_launch": alg, "mean_launch_us": kmean * 1e6,
-                "launches_timed": len(kdur) * L,
+                "launches_timed": len(kdur) * L * R,
                 "timing": "CUDA events on the launching stream around "
-                          + ("" if args.eager else "a graph of ")
+                          + (f"{R} passes of " if args.eager else f"{R} replays of a graph of ")
                           + f"{L} back-to-back launches over distinct weight copies"}
 
     # ---- LM head, column-sharded over the ranks

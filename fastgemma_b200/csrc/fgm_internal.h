@@ -48,6 +48,7 @@ struct GemvPlan {
   int chunk_tiles;  // weight tiles per ring stage
   int stages;       // ring depth per warp
   int pre_stages;   // ring stages each warp requests before griddepcontrol.wait
+  int pub_row;      // words per published row in the split-K exchange area
   int stage_bytes;
   int xchg_bytes;   // per-team exchange area for split K
   int a_bytes;      // activations staged in shared memory (0: read from global)

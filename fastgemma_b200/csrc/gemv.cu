@@ -60,8 +60,12 @@ namespace {
 constexpr int kMaxWarps = 16;
 // Words per published row of group values in the split-K exchange area: 16
 // columns plus 4 words of padding, so the rows 2*tig (+1) that one store
-// instruction's lanes write fall in distinct banks.
+// instruction's lanes write fall in distinct banks.  For 16-row blocks the
+// planner drops the padding (kPubRowDense) when it would cost the launch its
+// activation staging or split-K parts; 8-row blocks always pad (compile-time
+// stride, immediate offsets).
 constexpr int kPubRow = 20;
+constexpr int kPubRowDense = 16;
 
 template <bool Q4>
 struct Geo {
@@ -205,6 +209,7 @@ __device__ __forceinline__ void push_rows(const GemvParams &p, int nb, int m0, i
 // Per-lane constants shared by the stage routines.
 struct Lane {
   int g8, tig, lane;
+  int pr;          // words per published row (GemvPlan::pub_row)
   uint32_t w_off;  // weight word (row tig, column g8) inside a tile
   uint32_t a_off;  // activation row g8, k-quads t..12+t, inside a tile's 8 rows
 };
@@ -302,7 +307,8 @@ __device__ __forceinline__ void stage_full(uint32_t st, uint32_t ab, const Lane 
         for (int mt = 0; mt < MT; mt++)
 #pragma unroll
           for (int i = 0; i < 4; i++)
-            pf[(gb + mt * 8 + 2 * L.tig + (i & 1)) * kPubRow + L.g8 + (i >= 2 ? 8 : 0)] =
+            pf[(gb + mt * 8 + 2 * L.tig + (i & 1)) * (MT == 1 ? kPubRow : L.pr) + L.g8 +
+               (i >= 2 ? 8 : 0)] =
                 i2f_exact(gacc[mt][i] >> 4);
         if (L.tig == 0) {
           float *ps = reinterpret_cast<float *>(pub_sc) + (size_t)(g0 + lg) * 16;
@@ -314,7 +320,8 @@ __device__ __forceinline__ void stage_full(uint32_t st, uint32_t ab, const Lane 
         for (int mt = 0; mt < MT; mt++)
 #pragma unroll
           for (int i = 0; i < 4; i++)
-            pub[(gb + mt * 8 + 2 * L.tig + (i & 1)) * kPubRow + L.g8 + (i >= 2 ? 8 : 0)] =
+            pub[(gb + mt * 8 + 2 * L.tig + (i & 1)) * (MT == 1 ? kPubRow : L.pr) + L.g8 +
+                (i >= 2 ? 8 : 0)] =
                 gacc[mt][i] >> 4;
       }
     }
@@ -416,7 +423,8 @@ __device__ __forceinline__ void stage_generic(uint32_t st, uint32_t a_sm, const 
         for (int mt = 0; mt < MT; mt++)
 #pragma unroll
           for (int i = 0; i < 4; i++)
-            pf[(gb + mt * 8 + 2 * L.tig + (i & 1)) * kPubRow + L.g8 + (i >= 2 ? 8 : 0)] =
+            pf[(gb + mt * 8 + 2 * L.tig + (i & 1)) * (MT == 1 ? kPubRow : L.pr) + L.g8 +
+               (i >= 2 ? 8 : 0)] =
                 i2f_group(gacc[mt][i] >> 4, exact_ok);
         if (L.tig == 0) {
           float *ps = reinterpret_cast<float *>(pub_sc) + (size_t)(g - gbase) * 16;
@@ -428,7 +436,8 @@ __device__ __forceinline__ void stage_generic(uint32_t st, uint32_t a_sm, const 
         for (int mt = 0; mt < MT; mt++)
 #pragma unroll
           for (int i = 0; i < 4; i++)
-            pub[(gb + mt * 8 + 2 * L.tig + (i & 1)) * kPubRow + L.g8 + (i >= 2 ? 8 : 0)] =
+            pub[(gb + mt * 8 + 2 * L.tig + (i & 1)) * (MT == 1 ? kPubRow : L.pr) + L.g8 +
+                (i >= 2 ? 8 : 0)] =
                 gacc[mt][i] >> 4;
       }
     }
@@ -466,7 +475,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
   int32_t *xsum = reinterpret_cast<int32_t *>(after_ring + (size_t)team * pl.xchg_bytes);
   // part 0's running f32 outputs, handed to the team after the last group,
   // then the published groups' f32 scale rows (16 floats each)
-  float *cpart = reinterpret_cast<float *>(xsum + (size_t)(G - gpub) * MT * 8 * kPubRow);
+  float *cpart = reinterpret_cast<float *>(xsum + (size_t)(G - gpub) * MT * 8 *
+                                            (MT == 1 ? kPubRow : pl.pub_row));
   uint32_t *xscale = reinterpret_cast<uint32_t *>(cpart + MT * 128);
   uint32_t *pub_sc = (Q4 && !raw && P > 1) ? xscale : nullptr;
   uint32_t *a_sm = reinterpret_cast<uint32_t *>(after_ring + (size_t)teams * pl.xchg_bytes);
@@ -481,6 +491,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
   L.lane = lane;
   L.g8 = lane >> 2;
   L.tig = lane & 3;
+  L.pr = MT == 1 ? kPubRow : pl.pub_row;
   L.w_off = Q4 ? (uint32_t)(L.tig * 32 + L.g8 * 4) : (uint32_t)(L.tig * 64 + L.g8 * 4);
   L.a_off = (uint32_t)(L.g8 * 64 + L.tig * 16);
 
@@ -703,7 +714,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
           const int m = mb * 16 + ml;
           if (m < p.M)
             p.acc[((size_t)m * G + g) * p.N + nb * 16 + nl] =
-                xsum[((size_t)g * MT * 8 + ml) * kPubRow + nl];
+                xsum[((size_t)g * MT * 8 + ml) * L.pr + nl];
         }
         __syncwarp();
         continue;
@@ -755,16 +766,17 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
         if (m >= p.M) continue;
         if (raw) {
           for (int g = 0; g < G; g++)
-            p.acc[((size_t)m * G + g) * p.N + n] = xsum[((size_t)g * MT * 8 + ml) * kPubRow + nl];
+            p.acc[((size_t)m * G + g) * p.N + n] = xsum[((size_t)g * MT * 8 + ml) * L.pr + nl];
           continue;
         }
         // continue part 0's chain through the published groups, in order
-        const float *xf = reinterpret_cast<const float *>(xsum) + ml * kPubRow + nl;
+        const float *xf = reinterpret_cast<const float *>(xsum) + ml * L.pr + nl;
         const float *xs = reinterpret_cast<const float *>(xscale) + nl;
         float c = cpart[o];
         const int ng = G - gpub;
+        const size_t gstride = (size_t)MT * 8 * L.pr;
 #pragma unroll 8
-        for (int g = 0; g < ng; g++) c = __fmaf_rn(xf[(size_t)g * MT * 8 * kPubRow], xs[g * 16], c);
+        for (int g = 0; g < ng; g++) c = __fmaf_rn(xf[g * gstride], xs[g * 16], c);
         p.C[(size_t)m * p.ldc + (n - p.c_col0)] = __fmul_rn(c, s_as[ml]);
       } else {
         const int32_t v = xsum[ml * 16 + nl];
@@ -875,6 +887,9 @@ GemvPlan plan_gemv(const GemvParams &p, int nblocks, bool q4, int num_sms, size_
   // exchange area still leaves a useful ring.  Warps per CTA: enough to cover
   // every (unit, part) pair across all SMs, at most kMaxWarps, a multiple of
   // the team size.  Then the deepest ring that fits.
+  // One search per exchange row stride; the padded stride wins unless the
+  // dense one keeps the activations staged or more split-K parts.
+  auto search = [&](int pub_row, GemvPlan &out) {
   bool found = false;
   for (int with_a = 1; with_a >= 0 && !found; with_a--) {
   for (int P = Pmax; P >= 1 && !found; P /= 2) {
@@ -884,7 +899,7 @@ GemvPlan plan_gemv(const GemvParams &p, int nblocks, bool q4, int num_sms, size_
     if (want_warps > kMaxWarps) want_warps = kMaxWarps;
     if (want_warps < P) want_warps = P;
     size_t xchg = 0;
-    const size_t grp = (size_t)MT * 8 * kPubRow * 4;  // one group's published values
+    const size_t grp = (size_t)MT * 8 * pub_row * 4;  // one group's published values
     if (q4 && raw) xchg = (size_t)G * grp;             // every group's int32 sum
     else if (q4 && P > 1)  // groups of parts 1..P-1 with their f32 scale rows, part 0's chain
       xchg = (size_t)(G - G / P) * (grp + 64) + (size_t)MT * 128 * 4;
@@ -899,13 +914,14 @@ GemvPlan plan_gemv(const GemvParams &p, int nblocks, bool q4, int num_sms, size_
         for (int S = 6; S >= 2; S--) {
           const size_t total = fixed + (size_t)warps * S * pl.stage_bytes;
           if (total <= smem_limit) {
-            pl.warps = warps;
-            pl.parts = P;
-            pl.xchg_bytes = xchg_bytes;
-            pl.stages = S;
-            pl.pre_stages = 1;
-            pl.a_bytes = with_a ? (int)a_bytes : 0;
-            pl.smem_bytes = total;
+            out.warps = warps;
+            out.parts = P;
+            out.xchg_bytes = xchg_bytes;
+            out.stages = S;
+            out.pre_stages = 1;
+            out.pub_row = pub_row;
+            out.a_bytes = with_a ? (int)a_bytes : 0;
+            out.smem_bytes = total;
             found = true;
             break;
           }
@@ -913,6 +929,16 @@ GemvPlan plan_gemv(const GemvParams &p, int nblocks, bool q4, int num_sms, size_
       }
     }
   }
+  }
+  return found;
+  };
+  GemvPlan dense = pl;
+  bool found = search(kPubRow, pl);
+  if (MT == 2 && search(kPubRowDense, dense) &&
+      (!found || (dense.a_bytes && !pl.a_bytes) ||
+       ((dense.a_bytes != 0) == (pl.a_bytes != 0) && dense.parts > pl.parts))) {
+    pl = dense;
+    found = true;
   }
   if (!found) {  // caller reports the failure; stages = 0 marks the plan unusable
     pl.stages = 0;
