@@ -497,12 +497,16 @@ def bench_lm_head(args, dev, gen, world, rank):
     shf = S.ColumnShardedGemm("q4g", None, None, N, K, GROUP, rank=rank, world=world, device=dev,
                               shard=(w, s), fused=True, max_rows=M)
     ms_step = timed(lambda: shf(M, pa, qs))
+    # token choice (row argmax of the logits): on the fused path each rank
+    # scans the gathered logits; on the NCCL path the ranks exchange only
+    # per-row (value, index) pairs
+    ms_argmax = timed(lambda: shf.argmax(M, pa, qs))
     shf.close()
-    ms_argmax = timed(lambda: sh.argmax(M, pa, qs))  # tokens without gathering logits
+    ms_argmax_pairs = timed(lambda: sh.argmax(M, pa, qs))
     wbytes = sum(q4g_bytes(K, N))
     return {"value": wbytes / (ms_step * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms_step,
             "gemm_ms": ms_gemm, "nccl_gather_ms": ms_gather, "nccl_step_ms": ms_nccl,
-            "argmax_step_ms": ms_argmax,
+            "argmax_step_ms": ms_argmax, "argmax_pairs_ms": ms_argmax_pairs,
             "steps": steps,
             "workload": f"BASELINE config 3 LM head: int4 q4g {N}x{K} group {GROUP} f16 scales, "
                         f"M={M}, {world}-way output-column shards; value: one kernel per rank "

@@ -225,12 +225,26 @@ class ColumnShardedGemm:
         return pb.view(slot, M, self.device)
 
     def argmax(self, M: int, A, a_scale, stream=None) -> torch.Tensor:
-        """Token choice for each row (engine.rs:75-83) without gathering the
-        logits: this rank's columns reduce to per-row (value, index) pairs,
-        the ranks exchange M pairs each, and the pairs merge into int32 [M]."""
+        """Token choice for each row (engine.rs:75-83).  With peer buffers
+        (fused=True, several ranks) the fused GEMM + all-gather kernel already
+        leaves every rank the whole logits matrix, so each rank scans it on
+        device.  Otherwise this rank's columns reduce to per-row (value,
+        index) pairs, the ranks exchange those pairs (not the logits), and
+        the pairs merge into int32 [M]."""
         from ._lib import call, lib
-        local = self.local(M, A, a_scale)
         st = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        if self.peers is not None and self.world > 1:
+            logits = self.fused_call(M, A, a_scale, stream)
+            parts = lib().fgm_cuda_argmax_parts(self.N)
+            vals = torch.empty((M, parts), dtype=torch.float32, device=self.device)
+            idx = torch.empty((M, parts), dtype=torch.int32, device=self.device)
+            call("fgm_cuda_argmax_partials", logits.data_ptr(), M, self.N, self.N, 0,
+                 vals.data_ptr(), idx.data_ptr(), st)
+            out = torch.empty(M, dtype=torch.int32, device=self.device)
+            call("fgm_cuda_argmax_merge", vals.data_ptr(), idx.data_ptr(), M, parts,
+                 out.data_ptr(), st)
+            return out
+        local = self.local(M, A, a_scale)
         parts = lib().fgm_cuda_argmax_parts(self.max_cols)
         vals = torch.empty((M, parts), dtype=torch.float32, device=self.device)
         idx = torch.empty((M, parts), dtype=torch.int32, device=self.device)

@@ -38,7 +38,7 @@ def _rank_main(rank, world, port, out_dir, fused=False):
             out = sh(M, pa, qs)
             torch.cuda.synchronize()
             np.save(os.path.join(out_dir, f"r{rank}_c{call}.npy"), out.cpu().numpy())
-        tok = sh.argmax(M, pa, qs)  # pairs exchanged instead of logits
+        tok = sh.argmax(M, pa, qs)  # NCCL path: pairs exchanged; fused path: gathered logits scanned
         torch.cuda.synchronize()
         np.save(os.path.join(out_dir, f"r{rank}_tok.npy"), tok.cpu().numpy())
         sh.close()
