@@ -75,10 +75,11 @@ def build(verbose: bool = False, extra: list[str] | None = None) -> str:
 
 
 def build_host(verbose: bool = False) -> str:
-    """The C++ host layer (host/fgm_host.cpp) over the C ABI: libfgm_host.so,
+    """The C++ host layer (host/fgm_host.cpp, host/fgm_model.cpp) over the C ABI: libfgm_host.so,
     linked against libfgm_cuda.so beside it."""
-    srcs = [os.path.join(HOST, "fgm_host.cpp")]
-    deps = srcs + [os.path.join(HOST, "fgm_host.hpp"), os.path.join(INCLUDE, "fgm_cuda.h"), LIB]
+    srcs = [os.path.join(HOST, "fgm_host.cpp"), os.path.join(HOST, "fgm_model.cpp")]
+    deps = srcs + [os.path.join(HOST, "fgm_host.hpp"), os.path.join(HOST, "fgm_model.hpp"),
+                   os.path.join(INCLUDE, "fgm_cuda.h"), LIB]
     if os.path.exists(HOST_LIB) and os.path.getmtime(HOST_LIB) >= _newest(deps):
         return HOST_LIB
     cxx = shutil.which("g++") or "g++"
