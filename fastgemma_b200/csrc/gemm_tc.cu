@@ -18,8 +18,10 @@
 //
 // Pipeline
 // --------
-// One CTA owns a BM x 128 output tile (BM = 256: two M=128 halves sharing
-// each B tile; BM = 128 when that leaves too few tiles) and walks its K range in 128-byte stages through a 4-deep ring: warp
+// One CTA owns a BM x NB output tile -- 128 x 256 (N=256 MMAs: the fewest
+// operand bytes per MAC), 256 x 128 (two M=128 halves sharing each B tile)
+// or 128 x 128 (when K must be split) -- and walks its K range in 128-byte
+// stages through a 4-deep ring: warp
 // 0 (one lane) issues the TMA loads, warp 1 (one lane) issues four K=32 MMAs
 // per half per stage and commits each stage back to the producer, warp 2 owns
 // the tensor-memory allocation; then all eight warps drain the accumulators
@@ -50,20 +52,24 @@ namespace fgm {
 namespace {
 
 constexpr int kTcBMax = 256;  // at most two M=128 halves per tile
-constexpr int kTcBN = 128;
-constexpr int kTcBK = 128;  // bytes of K per stage
+constexpr int kTcBN = 128;     // tile width of the split-capable tiles
+constexpr int kTcBNMax = 256;  // widest tile (one M=128 half, N=256 MMAs)
+constexpr int kTcBK = 128;     // bytes of K per stage
 constexpr int kTcThreads = 256;
-constexpr int kTcB = kTcBN * kTcBK;
-static_assert(kTcThreads == kTcBMax, "one thread per tile row loads the activation scales");
+static_assert(kTcThreads == kTcBMax && kTcThreads == kTcBNMax,
+              "one thread per tile row / column loads the scales");
 
-// Tile geometry for H M-halves of 128 rows (H = 1 or 2).
-template <int H>
+// Tile geometry for H M-halves of 128 rows (H = 1 or 2) and NB columns (128,
+// or 256 with H = 1: N=256 MMAs read a quarter fewer operand bytes per MAC
+// from shared memory and halve the MMA count).
+template <int H, int NB = kTcBN>
 struct TcTile {
+  static_assert(NB == 128 || (NB == 256 && H == 1), "tile shapes: 128/256 x 128, 128 x 256");
   static constexpr int BM = 128 * H;
-  static constexpr int A = BM * kTcBK;       // activation bytes per stage
-  static constexpr int Stage = A + kTcB;     // bytes per ring stage
-  static constexpr int TmemCols = H * kTcBN;  // int32 accumulator columns
-  static constexpr size_t Out = (size_t)(kTcBN / 32) * BM * 128;  // staged output tile
+  static constexpr int A = BM * kTcBK;          // activation bytes per stage
+  static constexpr int Stage = A + NB * kTcBK;  // bytes per ring stage
+  static constexpr int TmemCols = H * NB;       // int32 accumulator columns
+  static constexpr size_t Out = (size_t)(NB / 32) * BM * 128;  // staged output tile
 };
 
 __device__ __forceinline__ void st_global_v4(float *p, float a, float b, float c, float d) {
@@ -81,11 +87,11 @@ __device__ __forceinline__ uint32_t row_off(int r, int chunk) {
   return (uint32_t)(r * 512 + ((chunk ^ (r & 7)) << 4));
 }
 
-template <int H>
+template <int H, int NB>
 __global__ void __launch_bounds__(kTcThreads, 1)
     q8c_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmC, const TcParams p) {
-  using T = TcTile<H>;
+  using T = TcTile<H, NB>;
   constexpr int BM = T::BM;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // stage buffers must sit on 1 KB boundaries for the swizzle pattern
@@ -100,12 +106,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(recv_bar + 1);
   __shared__ int s_fail, s_any_fail;
   __shared__ float s_as[kTcBMax];  // a_scale of the tile's rows
-  __shared__ float s_bs[kTcBN];  // b_scale of the tile's columns
+  __shared__ float s_bs[NB];  // b_scale of the tile's columns
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KS = (p.K + kTcBK - 1) / kTcBK;
   const int m0 = blockIdx.y * BM;
-  const int n0 = p.nb0 * 16 + blockIdx.x * kTcBN;
+  const int n0 = p.nb0 * 16 + blockIdx.x * NB;
   // K slice of this CTA: the cluster's CTAs split the tile's K range evenly
   const int splits = p.splits, z = splits > 1 ? (int)tc::cluster_ctarank() : 0;
   const int ks0 = (int)((long)KS * z / splits), ks1 = (int)((long)KS * (z + 1) / splits);
@@ -123,7 +129,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc::prefetch_tmap(&tmA);
     tc::prefetch_tmap(&tmB);
   }
-  if (threadIdx.x < kTcBN) {  // weight scales do not depend on earlier kernels
+  if (threadIdx.x < NB) {  // weight scales do not depend on earlier kernels
     const int n = n0 + threadIdx.x;
     s_bs[threadIdx.x] = (p.b_scale && n < p.n_end) ? p.b_scale[n] : 0.0f;
   }
@@ -149,9 +155,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc::mbar_expect_tx(&full[s], T::Stage);
       tc::tma_load_2d(sa, &tmA, &full[s], (ks0 + i) * kTcBK, m0);
       tc::tma_load_2d(sa + T::A, &tmB, &full[s], (ks0 + i) * kTcBK, n0);
+      if (NB == 256)  // the weight map's boxes are 128 rows: the second half
+        tc::tma_load_2d(sa + T::A + 128 * kTcBK, &tmB, &full[s], (ks0 + i) * kTcBK, n0 + 128);
     }
   } else if (warp == 1 && lane == 0) {  // ---------------------------- MMA
-    const uint32_t idesc = tc::idesc_i8(128, kTcBN);
+    const uint32_t idesc = tc::idesc_i8(128, NB);
     for (int i = 0; i < nks; i++) {
       const int s = i % S;
       if (!tc::mbar_wait(&full[s], (i / S) & 1)) {
@@ -165,7 +173,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int h = 0; h < H; h++)
 #pragma unroll
         for (int j = 0; j < kTcBK / 32; j++)  // K=32 slices of the 128-byte stage
-          tc::mma_i8(tmem + h * kTcBN, tc::sdesc_sw128(sa + h * 128 * kTcBK + j * 32),
+          tc::mma_i8(tmem + h * NB, tc::sdesc_sw128(sa + h * 128 * kTcBK + j * 32),
                      tc::sdesc_sw128(sb + j * 32), idesc, (i | j) != 0);
       tc::mma_commit(&empty[s]);  // stage s is free once these MMAs complete
     }
@@ -175,7 +183,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   // ------------------------------------------------------------ epilogue
   // All eight warps drain the accumulators: warp w reads TMEM lane quadrant
-  // w % 4 (rows 32(w%4).. of each M half) and the 64-column half w / 4.
+  // w % 4 (rows 32(w%4).. of each M half) and the column half w / 4 (NB/2
+  // columns, in passes of 64).
   const bool ok = __all_sync(0xffffffffu, tc::mbar_wait(accum, 0));  // warp-uniform
   if (!ok) s_fail = 1;
   tc::fence_after_sync();
@@ -214,21 +223,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int m = m0 + ml;
       const bool row_ok = m < p.M;
       const float as = s_as[ml];
+#pragma unroll 1
+      for (int cb = 0; cb < NB / 128; cb++) {  // 64 of this warp's NB/2 columns per pass
       uint32_t v[64];
-      const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + h * kTcBN + ch * 64;
+      const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + h * NB + ch * (NB / 2) + cb * 64;
       tc::tmem_ld_x32(ta, v);
       tc::tmem_ld_x32(ta + 32, v + 32);
       tc::tmem_wait_ld();
-      if (splits > 1) {  // int32 partial row into the send buffer
+      if constexpr (NB == 128) {
+        if (splits > 1) {  // int32 partial row into the send buffer
 #pragma unroll
-        for (int c4 = 0; c4 < 16; c4++)
-          *reinterpret_cast<uint4 *>(smem + row_off(ml, ch * 16 + c4)) =
-              make_uint4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
-        continue;
+          for (int c4 = 0; c4 < 16; c4++)
+            *reinterpret_cast<uint4 *>(smem + row_off(ml, ch * 16 + c4)) =
+                make_uint4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
+          continue;
+        }
       }
 #pragma unroll
       for (int cc = 0; cc < 4; cc++) {
-        const int c = ch * 4 + cc;  // 16-column chunk of the tile
+        const int c = ch * (NB / 32) + cb * 4 + cc;  // 16-column chunk of the tile
         const int n = n0 + c * 16;
         if (p.acc) {
           if (row_ok && n < p.n_end)
@@ -259,20 +272,44 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
       }
+      if constexpr (NB == 256) {
+        // 256-wide tiles drain in two passes; the four 32-column blocks a pass
+        // completed go out while the next pass drains.  The branch is
+        // block-uniform here (a warp whose accumulator wait failed raised
+        // s_fail before the barrier above), so the block barrier is safe.
+        if (tma_out) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncthreads();
+          if (threadIdx.x == 0) {
+            const int col0 = blockIdx.x * NB;  // relative to the output map's origin
+            for (int half = 0; half < 2; half++)
+              for (int b2 = 0; b2 < 2; b2++) {
+                const int b = half * 4 + cb * 2 + b2;  // 32-column block of the tile
+                if (p.nb0 * 16 + col0 + b * 32 < p.n_end)
+                  tc::tma_store_2d(&tmC, smem + (size_t)b * (BM * 128), col0 + b * 32, m0);
+              }
+            tc::bulk_commit();
+          }
+        }
+      }
+      }
     }
   }
   if (tma_out) {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
     if (threadIdx.x == 0 && ok && !s_fail) {
-      const int col0 = blockIdx.x * kTcBN;  // relative to the output map's origin
-      for (int b = 0; b < kTcBN / 32; b++)
-        if (p.nb0 * 16 + col0 + b * 32 < p.n_end)
-          tc::tma_store_2d(&tmC, smem + (size_t)b * (BM * 128), col0 + b * 32, m0);
-      tc::bulk_commit();
+      if constexpr (NB == 128) {  // (256-wide tiles stored theirs pass by pass)
+        const int col0 = blockIdx.x * NB;  // relative to the output map's origin
+        for (int b = 0; b < NB / 32; b++)
+          if (p.nb0 * 16 + col0 + b * 32 < p.n_end)
+            tc::tma_store_2d(&tmC, smem + (size_t)b * (BM * 128), col0 + b * 32, m0);
+        tc::bulk_commit();
+      }
       tc::bulk_wait_read();
     }
   }
+  if constexpr (NB == 128) {
   if (splits > 1) {
     // One bulk copy per peer moves the rows it owns from this CTA's send
     // buffer into its receive slot (completing on its mbarrier); then CTA z
@@ -328,6 +365,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int e = 0; e < 4; e++) dst[e] = o[e];
     }
     tc::cluster_sync();
+  }
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -419,9 +457,9 @@ cudaError_t launch_packed_to_rows(const int8_t *packed, int8_t *rows, int M, int
   return cudaGetLastError();
 }
 
-template <int H>
+template <int H, int NB = kTcBN>
 size_t tc_smem_bytes(int stages) {
-  using T = TcTile<H>;
+  using T = TcTile<H, NB>;
   size_t ring = (size_t)stages * T::Stage;
   if (ring < T::Out) ring = T::Out;
   return ring + (size_t)(2 * stages + 2) * 8 + 16 + 1024;
@@ -429,10 +467,10 @@ size_t tc_smem_bytes(int stages) {
 
 constexpr size_t kTcStaticReserve = 4096;  // the kernel's static shared memory (about 2 KB)
 
-template <int H>
+template <int H, int NB = kTcBN>
 int tc_stages(size_t smem_limit) {
   int st = 8;
-  while (st > 2 && tc_smem_bytes<H>(st) + kTcStaticReserve > smem_limit) st--;
+  while (st > 2 && tc_smem_bytes<H, NB>(st) + kTcStaticReserve > smem_limit) st--;
   return st;
 }
 
@@ -453,9 +491,9 @@ int tc_max_clusters(int s, size_t smem) {
   attr[0].val.clusterDim.z = (unsigned)s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaFuncSetAttribute(q8c_tc_kernel<H>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaFuncSetAttribute(q8c_tc_kernel<H, kTcBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem) != cudaSuccess ||
-      cudaOccupancyMaxActiveClusters(&v, q8c_tc_kernel<H>, &cfg) != cudaSuccess) {
+      cudaOccupancyMaxActiveClusters(&v, q8c_tc_kernel<H, kTcBN>, &cfg) != cudaSuccess) {
     cudaGetLastError();
     v = 0;  // unknown: no split for this size
   }
@@ -470,13 +508,22 @@ int tc_max_clusters(int s, size_t smem) {
 struct TcChoice {
   int H, splits, stages;
   size_t smem;
+  int NB;
 };
 
 TcChoice plan_tc(int M, int ncols, int K, int num_sms, size_t smem_limit) {
   const int KS = (K + kTcBK - 1) / kTcBK;
-  TcChoice best{2, 1, tc_stages<2>(smem_limit), 0};
+  TcChoice best{2, 1, tc_stages<2>(smem_limit), 0, kTcBN};
   best.smem = tc_smem_bytes<2>(best.stages);
   double best_cost = -1;
+  {  // 128 x 256 tiles first: on a tie in operand bytes the N=256 MMAs win
+    const int stages = tc_stages<1, 256>(smem_limit);
+    const size_t smem = tc_smem_bytes<1, 256>(stages);
+    const long tiles = (long)((ncols + 255) / 256) * ((M + 127) / 128);
+    const double waves = (double)((tiles + num_sms - 1) / num_sms);
+    best_cost = waves * (double)(128 + 256) * K;
+    best = TcChoice{1, 1, stages, smem, 256};
+  }
   for (int H = 2; H >= 1; H--) {
     const int stages = H == 2 ? tc_stages<2>(smem_limit) : tc_stages<1>(smem_limit);
     const size_t smem = H == 2 ? tc_smem_bytes<2>(stages) : tc_smem_bytes<1>(stages);
@@ -499,7 +546,7 @@ TcChoice plan_tc(int M, int ncols, int K, int num_sms, size_t smem_limit) {
       const double cost = waves * (double)(128 * H + kTcBN) * ((double)K / s);
       if (best_cost < 0 || cost < best_cost * 0.999) {
         best_cost = cost;
-        best = TcChoice{H, s, stages, smem};
+        best = TcChoice{H, s, stages, smem, kTcBN};
       }
     }
   }
@@ -521,15 +568,15 @@ static bool encode_out_map(CUtensorMap *map, void *base, int rows, int cols, siz
              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int H>
+template <int H, int NB>
 cudaError_t launch_tc_h(const TcParams &p, const CUtensorMap &tmA, const CUtensorMap &tmB,
                         const CUtensorMap &tmC, size_t smem, bool pdl, cudaStream_t st) {
-  cudaError_t e = cudaFuncSetAttribute(q8c_tc_kernel<H>,
+  cudaError_t e = cudaFuncSetAttribute(q8c_tc_kernel<H, NB>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int ncols = p.n_end - p.nb0 * 16;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((ncols + kTcBN - 1) / kTcBN, (p.M + 128 * H - 1) / (128 * H), p.splits);
+  cfg.gridDim = dim3((ncols + NB - 1) / NB, (p.M + 128 * H - 1) / (128 * H), p.splits);
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -549,7 +596,7 @@ cudaError_t launch_tc_h(const TcParams &p, const CUtensorMap &tmA, const CUtenso
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, q8c_tc_kernel<H>, tmA, tmB, tmC, p);
+  return cudaLaunchKernelEx(&cfg, q8c_tc_kernel<H, NB>, tmA, tmB, tmC, p);
 }
 
 cudaError_t launch_q8c_tc(const TcParams &p_in, int lda, const CUtensorMap &tmB, bool pdl,
@@ -568,8 +615,9 @@ cudaError_t launch_q8c_tc(const TcParams &p_in, int lda, const CUtensorMap &tmB,
   p.tma_store = !p.acc && p.out_v4 && p.splits == 1 &&
                 encode_out_map(&tmC, origin, p.M, p.n_end - p.nb0 * 16, (size_t)p.ldc * 4, BM);
   if (!p.tma_store) memset(&tmC, 0, sizeof(tmC));
-  return c.H == 2 ? launch_tc_h<2>(p, tmA, tmB, tmC, c.smem, pdl, st)
-                  : launch_tc_h<1>(p, tmA, tmB, tmC, c.smem, pdl, st);
+  if (c.NB == 256) return launch_tc_h<1, 256>(p, tmA, tmB, tmC, c.smem, pdl, st);
+  return c.H == 2 ? launch_tc_h<2, kTcBN>(p, tmA, tmB, tmC, c.smem, pdl, st)
+                  : launch_tc_h<1, kTcBN>(p, tmA, tmB, tmC, c.smem, pdl, st);
 }
 
 }  // namespace fgm
