@@ -144,19 +144,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0 && lane == 0) {  // ---------------------------------- producer
+    auto load_b = [&](uint8_t *sa, int i, int s) {
+      tc::tma_load_2d(sa + T::A, &tmB, &full[s], (ks0 + i) * kTcBK, n0);
+      if (NB == 256)  // the weight map's boxes are 128 rows: the second half
+        tc::tma_load_2d(sa + T::A + 128 * kTcBK, &tmB, &full[s], (ks0 + i) * kTcBK, n0 + 128);
+    };
+    // The weights do not come from earlier kernels: the first ring fill's
+    // weight boxes go out before griddepcontrol.wait (each stage's barrier
+    // already expects its activation box too), overlapping the predecessor.
+    const int pre = nks < S ? nks : S;
+    for (int i = 0; i < pre; i++) {
+      uint8_t *sa = smem + (size_t)i * T::Stage;
+      tc::mbar_expect_tx(&full[i], T::Stage);
+      load_b(sa, i, i);
+    }
     asm volatile("griddepcontrol.wait;" ::: "memory");  // activations from earlier kernels
-    for (int i = 0; i < nks; i++) {
+    for (int i = 0; i < pre; i++)
+      tc::tma_load_2d(smem + (size_t)i * T::Stage, &tmA, &full[i], (ks0 + i) * kTcBK, m0);
+    for (int i = pre; i < nks; i++) {
       const int s = i % S;
-      if (i >= S && !tc::mbar_wait(&empty[s], ((i / S) & 1) ^ 1)) {
+      if (!tc::mbar_wait(&empty[s], ((i / S) & 1) ^ 1)) {
         s_fail = 1;
         break;
       }
       uint8_t *sa = smem + (size_t)s * T::Stage;
       tc::mbar_expect_tx(&full[s], T::Stage);
       tc::tma_load_2d(sa, &tmA, &full[s], (ks0 + i) * kTcBK, m0);
-      tc::tma_load_2d(sa + T::A, &tmB, &full[s], (ks0 + i) * kTcBK, n0);
-      if (NB == 256)  // the weight map's boxes are 128 rows: the second half
-        tc::tma_load_2d(sa + T::A + 128 * kTcBK, &tmB, &full[s], (ks0 + i) * kTcBK, n0 + 128);
+      load_b(sa, i, s);
     }
   } else if (warp == 1 && lane == 0) {  // ---------------------------- MMA
     const uint32_t idesc = tc::idesc_i8(128, NB);
