@@ -739,6 +739,17 @@ static int host_linear(bool q4, const float *src, int lda, int hsz, int M, int N
   const bool tc = !q4 && M >= tc_min_m() && find_prepared(dB, &map);
   int8_t *qa_rows = tc ? (int8_t *)(d + o_w_end) : nullptr;  // row-major quantised X
   const bool c_pinned = is_pinned(C);
+  // Page-locked C: the decode GEMM stores its outputs straight into it
+  // through the device mapping, so no copy-engine round trip follows the
+  // kernel.  Tensor-core tiles (TMA stores) go through the device buffer.
+  float *c_mapped = nullptr;
+  if (c_pinned && !tc) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, C) == cudaSuccess && a.devicePointer)
+      c_mapped = static_cast<float *>(a.devicePointer);
+    else
+      cudaGetLastError();
+  }
   auto enqueue = [&]() -> int {
     int r = run_prep(static_cast<const float *>(xsrc), lda, nullptr, qa_rows, (float *)(d + o_s),
                      (int8_t *)(d + o_a), M, K, hsz, 0, M, g_stream);
@@ -748,8 +759,10 @@ static int host_linear(bool q4, const float *src, int lda, int hsz, int M, int N
                      (float *)(d + o_c), N, 0, nullptr, 0, N / 16, g_stream);
     else
       r = run_gemm(q4, M, N, K, (const int8_t *)(d + o_a), (const float *)(d + o_s), dB, dS,
-                   group, (float *)(d + o_c), N, 0, nullptr, 0, N / 16, g_stream);
+                   group, c_mapped ? c_mapped : (float *)(d + o_c), c_mapped ? ldc : N, 0,
+                   nullptr, 0, N / 16, g_stream);
     if (r) return r;
+    if (c_mapped) return FGM_CUDA_OK;
     return d2h_rows_enqueue(C, (size_t)ldc * 4, d + o_c, (size_t)N * 4, M, o_c, c_pinned);
   };
   if (cacheable) {
@@ -774,6 +787,10 @@ static int host_linear(bool q4, const float *src, int lda, int hsz, int M, int N
     rc = enqueue();
   }
   if (rc) return rc;
+  if (c_mapped) {
+    FGM_TRY(cudaStreamSynchronize(g_stream));
+    return FGM_CUDA_OK;
+  }
   return d2h_rows_finish(C, (size_t)ldc * 4, (size_t)N * 4, M, o_c, c_pinned);
 }
 
