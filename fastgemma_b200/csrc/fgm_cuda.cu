@@ -624,6 +624,24 @@ static int host_gemm(bool q4, int M, int N, int K, const int8_t *A, const float 
     if ((rc = h2d(d + o_ws, b_scale, sbytes, o_ws))) return rc;
     dS = d + o_ws;
   }
+  // Page-locked C (decode GEMM): outputs go straight into it through the
+  // device mapping, element (m, n) at C[m*ldc + n]; otherwise through the
+  // device buffer and one copy.
+  float *c_mapped = nullptr;
+  if (!(!q4 && M >= tc_min_m()) && is_pinned(C)) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, C) == cudaSuccess && a.devicePointer)
+      c_mapped = static_cast<float *>(a.devicePointer);
+    else
+      cudaGetLastError();
+  }
+  if (c_mapped) {
+    rc = run_gemm(q4, M, N, K, (const int8_t *)d, (const float *)(d + o_s), dB, dS, group,
+                  c_mapped + (size_t)n0 * 16, ldc, n0 * 16, nullptr, n0, n1, g_stream);
+    if (rc) return rc;
+    FGM_TRY(cudaStreamSynchronize(g_stream));
+    return FGM_CUDA_OK;
+  }
   rc = run_gemm(q4, M, N, K, (const int8_t *)d, (const float *)(d + o_s), dB, dS, group,
                 (float *)(d + o_c), cols, n0 * 16, nullptr, n0, n1, g_stream);
   if (rc) return rc;

@@ -262,6 +262,50 @@ def test_partial_range_ldc_and_untouched(orc):
         assert_bits(got, want, "partial range")
 
 
+@pytest.mark.parametrize("pinned", [True, False])
+def test_host_entries_partial_range_into_host_c(orc, pinned):
+    """The reference-facing host entries (fgm_gemm_q4g_cuda / _q8c_cuda,
+    fgm_linear_q4g_cuda) write only rows < M and columns [n0*16, n1*16) of a
+    host C with ldc > N -- page-locked C is stored to directly by the decode
+    GEMM, pageable C through the copy-back -- twice in a row."""
+    from fastgemma_b200 import _lib
+    M, N, K, n0, n1, ldc = 5, 512, 1024, 8, 20, 600
+    rng = np.random.default_rng(8)
+    pa = F.pack_a(rng.integers(-128, 128, size=(M, K), dtype=np.int8))
+    bq, s = F.synth_q4g(N, K, 64, 5)
+    b8, s8 = F.synth_q8c(N, K, 6)
+    a_s = rng.uniform(0.001, 0.05, size=M).astype(np.float32)
+
+    def host_c():
+        t = torch.full((M + 2, ldc), -7.0)
+        return t.pin_memory() if pinned else t
+
+    for q4 in (True, False):
+        want = np.full((M + 2, ldc), -7.0, np.float32)
+        if q4:
+            orc.gemm_q4g(M, N, K, pa, a_s, bq, s, 64, c=want, ldc=ldc, n0=n0, n1=n1)
+        else:
+            orc.gemm_q8c(M, N, K, pa, a_s, b8, s8, c=want, ldc=ldc, n0=n0, n1=n1)
+        for _ in range(2):
+            c = host_c()
+            if q4:
+                _lib.call("fgm_gemm_q4g_cuda", M, N, K, pa.ctypes.data, a_s.ctypes.data,
+                          bq.ctypes.data, s.ctypes.data, 64, c.data_ptr(), ldc, n0, n1)
+            else:
+                _lib.call("fgm_gemm_q8c_cuda", M, N, K, pa.ctypes.data, a_s.ctypes.data,
+                          b8.ctypes.data, s8.ctypes.data, c.data_ptr(), ldc, n0, n1)
+            assert_bits(c.numpy(), want, f"host entry q4={q4} pinned={pinned}")
+    x = F.synth_x(M, K, 9)
+    _, _, qs, pa2 = orc.prep_rows(x, M, K, 0)
+    want = np.full((M + 2, ldc), -7.0, np.float32)
+    orc.gemm_q4g(M, N, K, pa2, qs, bq, s, 64, c=want, ldc=ldc)
+    for _ in range(2):
+        c = host_c()
+        _lib.call("fgm_linear_q4g_cuda", x.ctypes.data, K, 0, M, N, K, bq.ctypes.data,
+                  s.ctypes.data, 64, c.data_ptr(), ldc)
+        assert_bits(c.numpy(), want, f"linear pinned={pinned}")
+
+
 def test_config0_full_size_bit_exact(orc):
     """BASELINE config 0 shape at full size: M=8, N=8192, K=2048, int4 g64."""
     M, N, K = 8, 8192, 2048
