@@ -77,6 +77,10 @@ struct PrepParams {
 };
 
 cudaError_t launch_prep(const PrepParams &p, bool pdl, cudaStream_t st);
+// Copy two host regions (device-readable: page-locked or staging) into
+// device memory with one kernel.
+cudaError_t launch_pull(const void *s1, void *d1, size_t n1, const void *s2, void *d2, size_t n2,
+                        bool pdl, cudaStream_t st);
 
 // ----------------------------------------------------------- tensor cores
 struct TcParams {

@@ -263,7 +263,52 @@ __global__ void __launch_bounds__(512, 1) prep_fast_kernel(const PrepParams p) {
   }
 }
 
+// Two host-resident byte regions (page-locked, read through their device
+// mapping) copied into device memory by one small kernel: the packed
+// activations and their scales of a host-pointer GEMM call, without a
+// copy-engine round trip each.  Word copies when both ends are 4-byte
+// aligned, byte copies otherwise.
+__global__ void pull_kernel(const uint8_t *s1, uint8_t *d1, size_t n1, const uint8_t *s2,
+                            uint8_t *d2, size_t n2) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the buffers' earlier readers are done
+  const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (int r = 0; r < 2; r++) {
+    const uint8_t *s = r ? s2 : s1;
+    uint8_t *d = r ? d2 : d1;
+    const size_t n = r ? n2 : n1;
+    if (!n) continue;
+    if ((((uintptr_t)s | (uintptr_t)d | n) & 3) == 0) {
+      const uint32_t *sw = reinterpret_cast<const uint32_t *>(s);
+      uint32_t *dw = reinterpret_cast<uint32_t *>(d);
+      for (size_t i = tid; i < n / 4; i += stride) dw[i] = sw[i];
+    } else {
+      for (size_t i = tid; i < n; i += stride) d[i] = s[i];
+    }
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_pull(const void *s1, void *d1, size_t n1, const void *s2, void *d2, size_t n2,
+                        bool pdl, cudaStream_t st) {
+  const size_t words = (n1 > n2 ? n1 : n2) / 4 + 1;
+  unsigned blocks = (unsigned)((words + 255) / 256);
+  if (blocks > 64) blocks = 64;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, pull_kernel, static_cast<const uint8_t *>(s1),
+                            static_cast<uint8_t *>(d1), n1, static_cast<const uint8_t *>(s2),
+                            static_cast<uint8_t *>(d2), n2);
+}
 
 size_t prep_smem_bytes(int k) { return (size_t)k * sizeof(float); }
 
