@@ -28,6 +28,8 @@ int as_int(size_t v, const char *what) {
 
 }  // namespace
 
+int as_int_checked(size_t v, const char *what) { return as_int(v, what); }
+
 const char *name(Backend b) {
   switch (b) {
     case Backend::Amx: return "amx";
@@ -222,6 +224,22 @@ const QLinear &DualW::pick(size_t m, WeightSel sel) const {
 void Gemm::run(const Pool &pool, const QLinear &w, const float *a, size_t m, size_t lda,
                float *out) {
   const size_t kk = w.k, n = w.n;
+  // The CUDA backend runs rotate + quantise + pack and the GEMM as one call
+  // (the packed rows never come back to the host); the prep/gemm pair below
+  // is kept for shapes that call does not take (N not a multiple of 64).
+  if (k::backend() == k::Backend::Cuda && n % 64 == 0 && m > 0) {
+    const int M = k::as_int_checked(m, "m"), N = k::as_int_checked(n, "n");
+    const int Kd = k::as_int_checked(kk, "k"), L = k::as_int_checked(lda, "lda");
+    const int H = k::as_int_checked(w.hadamard, "hadamard");
+    int rc;
+    if (w.bits == 4)
+      rc = fgm_linear_q4g_cuda(a, L, H, M, N, Kd, w.q4, w.s4,
+                               k::as_int_checked(w.group == 0 ? 64 : w.group, "group"), out, N);
+    else
+      rc = fgm_linear_q8c_cuda(a, L, H, M, N, Kd, w.q8, w.s8, out, N);
+    if (rc != FGM_CUDA_OK) throw k::Error(rc, std::string("Gemm::run: ") + fgm_cuda_last_error());
+    return;
+  }
   if (rot_.size() < m * kk) rot_.resize(m * kk);
   if (qa_.size() < m * kk) qa_.resize(m * kk);
   if (qs_.size() < (m ? m : 1)) qs_.resize(m ? m : 1);

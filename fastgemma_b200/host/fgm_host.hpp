@@ -42,6 +42,9 @@ Backend backend();
 // lib.rs:155-157
 inline size_t packed_a_len(size_t m, size_t k) { return (m + 15) / 16 * 16 * k; }
 
+// v as the C ABI's int; throws Error(EINVAL) past INT_MAX.
+int as_int_checked(size_t v, const char *what);
+
 // A borrowed slice: pointer + element count (the Rust &[T] / &mut [T]).
 template <class T>
 struct Slice {
@@ -174,8 +177,10 @@ class DualW {
   bool has_hi_;
 };
 
-// forward.rs:115-158: rotate, quantise, tile-pack, dispatch.  Scratch is
-// grown once and kept (no allocation in steady state).
+// forward.rs:115-158: rotate, quantise, tile-pack, dispatch.  On the CUDA
+// backend one fgm_linear_* call does all of it (the packed rows stay on the
+// device); the host scratch below serves shapes that call does not take and
+// is grown once and kept (no allocation in steady state).
 class Gemm {
  public:
   void run(const Pool &pool, const QLinear &w, const float *a, size_t m, size_t lda, float *out);
