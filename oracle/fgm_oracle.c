@@ -299,3 +299,222 @@ int orc_argmax(const float *v, int n) {
     }
   return best;
 }
+
+/* ====================================================================
+ * Decode-chain glue (ops.c:55-147, :317-352) and the int8-KV attention
+ * (ops.c:354-640, :641-665).  The reference runs these 16 floats at a time
+ * (AVX-512) with a scalar libm tail; the restatement below reproduces the
+ * vector arithmetic lane by lane, in the same order, so its outputs match
+ * the compiled reference bit for bit wherever the reference does not call
+ * libm (n a multiple of 16; rope always calls cosf/sinf).
+ * ==================================================================== */
+
+/* One lane of the reference's exp (ops.c:21-39): the Cephes range reduction
+ * exp(x) = 2^n * exp(z), n = rint(x * log2 e), z = x - n*ln2 in two parts,
+ * a degree-5 polynomial by fused multiply-adds, 2^n from the exponent bits.
+ * Inputs are clamped to [-88, 88] first (max then min, so NaN -> -88). */
+float orc_exp_lane(float x) {
+  x = fmaxf(x, -88.0f);
+  x = fminf(x, 88.0f);
+  const float fx = rintf(x * 1.44269504088896341f);
+  float z = fmaf(-fx, 0.693359375f, x);
+  z = fmaf(-fx, -2.12194440e-4f, z);
+  float y = 1.9875691500E-4f;
+  y = fmaf(y, z, 1.3981999507E-3f);
+  y = fmaf(y, z, 8.3334519073E-3f);
+  y = fmaf(y, z, 4.1665795894E-2f);
+  y = fmaf(y, z, 1.6666665459E-1f);
+  y = fmaf(y, z, 5.0000001201E-1f);
+  y = fmaf(y, z * z, z);
+  y = y + 1.0f;
+  const int32_t n = (int32_t)fx;
+  const uint32_t bits = (uint32_t)(n + 127) << 23;
+  float p2;
+  memcpy(&p2, &bits, 4);
+  return y * p2;
+}
+
+/* _mm512_reduce_add_ps as the reference's compiler lowers it: halves
+ * (lanes i, i+8), then quarters (i, i+4), then pairs (i, i+2), then the
+ * last two. */
+float orc_reduce16(const float *a) {
+  float t8[8], t4[4], t2[2];
+  for (int i = 0; i < 8; i++) t8[i] = a[i] + a[i + 8];
+  for (int i = 0; i < 4; i++) t4[i] = t8[i] + t8[i + 4];
+  for (int i = 0; i < 2; i++) t2[i] = t4[i] + t4[i + 2];
+  return t2[0] + t2[1];
+}
+
+/* ops.c:59-92: out = x * (mean(x^2) + eps)^-1/2 (* w when w != NULL). */
+void orc_rmsnorm(float *out, const float *x, const float *w, int n, float eps) {
+  float acc[16] = {0};
+  int i = 0;
+  for (; i + 16 <= n; i += 16)
+    for (int j = 0; j < 16; j++) acc[j] = fmaf(x[i + j], x[i + j], acc[j]);
+  float ss = orc_reduce16(acc);
+  for (; i < n; i++) ss = fmaf(x[i], x[i], ss);
+  const float inv = 1.0f / sqrtf(ss / (float)n + eps);
+  for (i = 0; i < n; i++) out[i] = w ? (x[i] * inv) * w[i] : x[i] * inv;
+}
+
+/* ops.c:96-107: tanh-approximated GELU on one lane. */
+static float gelu_lane(float x) {
+  const float x3 = (x * x) * x;
+  const float u = 0.7978845608028654f * fmaf(0.044715f, x3, x);
+  const float e = orc_exp_lane(u + u);
+  const float t = 1.0f - 2.0f / (e + 1.0f);
+  return (0.5f * x) * (1.0f + t);
+}
+
+/* ops.c:119-131: out = gelu(gate) * up. */
+void orc_gelu_mul(float *out, const float *gate, const float *up, int n) {
+  int i = 0;
+  for (; i + 16 <= n; i += 16)
+    for (int j = 0; j < 16; j++) out[i + j] = gelu_lane(gate[i + j]) * up[i + j];
+  for (; i < n; i++) {
+    const float v = gate[i];
+    out[i] = 0.5f * v * (1.0f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v))) * up[i];
+  }
+}
+
+/* ops.c:317-337 */
+void orc_add(float *a, const float *b, int n) {
+  for (int i = 0; i < n; i++) a[i] += b[i];
+}
+void orc_mul(float *a, const float *b, int n) {
+  for (int i = 0; i < n; i++) a[i] *= b[i];
+}
+void orc_scale(float *a, float s, int n) {
+  for (int i = 0; i < n; i++) a[i] *= s;
+}
+
+/* ops.c:340-352: x = cap * tanh(x / cap), tanh from the exp lane. */
+void orc_softcap(float *x, int n, float cap) {
+  const float ci = 1.0f / cap;
+  int i = 0;
+  for (; i + 16 <= n; i += 16)
+    for (int j = 0; j < 16; j++) {
+      const float u = x[i + j] * ci;
+      const float e = orc_exp_lane(u + u);
+      x[i + j] = cap * (1.0f - 2.0f / (e + 1.0f));
+    }
+  for (; i < n; i++) x[i] = cap * tanhf(x[i] / cap);
+}
+
+/* ops.c:135-147: half-split rotary embedding of n_heads heads in place.
+ * fused: the two products-and-sum as fused multiply-adds (a build that
+ * contracts the reference's scalar expressions) or as separate roundings. */
+void orc_rope(float *x, int n_heads, int head_dim, const float *inv_freq, int pos, int fused) {
+  const int h = head_dim / 2;
+  for (int j = 0; j < h; j++) {
+    const float a = (float)pos * inv_freq[j];
+    const float c = cosf(a), s = sinf(a);
+    for (int hh = 0; hh < n_heads; hh++) {
+      float *p = x + (size_t)hh * head_dim;
+      const float lo = p[j], hi = p[j + h];
+      if (fused) {
+        p[j] = fmaf(lo, c, -(hi * s));
+        p[j + h] = fmaf(hi, c, lo * s);
+      } else {
+        p[j] = lo * c - hi * s;
+        p[j + h] = hi * c + lo * s;
+      }
+    }
+  }
+}
+
+/* ops.c:653-660: one int8 V row into the slot-interleaved cache. */
+void orc_store_v_t(int8_t *vt, const int8_t *src, int n, int slot) {
+  int8_t *dst = vt + (size_t)(slot >> 2) * n * 4 + (slot & 3);
+  for (int j = 0; j < n; j++) dst[(size_t)j * 4] = src[j];
+}
+
+/* ops.c:378-640 (fgm_attend_q8_heads), heads [h0, h1) of one query row
+ * against positions [start, end) of an int8 KV cache: K [slot][kv_heads *
+ * head_dim] with per-slot scales ks, V slot-interleaved (orc_store_v_t) with
+ * scales vs; ring = 0 for a linear cache, else slots are positions mod ring.
+ *  - Q per head: s = max|q| / 127, q8 = clamp(rint(q * 127/max), -127, 127);
+ *  - score_t = (float)(q8 . k_t) * s * ks_t  (the reference's biased VNNI
+ *    dot minus its correction is exactly q8 . k_t);
+ *  - softmax over 16-position chunks with the exp lane, sums per lane then
+ *    reduced, the tail with libm expf; inv = 1 / sum;
+ *  - weight w_t = score_t * inv * vs_t, quantised to 16 bits of wmax:
+ *    iw = (int)(w_t * 65535/wmax + 0.5), split into hi / lo bytes;
+ *  - out = (float)(256 * sum hi_t v_t + sum lo_t v_t) * (wmax / 65535).
+ * scratch holds (end - start) floats. */
+void orc_attend_q8_heads(float *out, const float *q, const int8_t *kc, const float *ks,
+                         const int8_t *vc, const float *vs, int n_heads, int kv_heads,
+                         int head_dim, int start, int end, float *scratch, int h0, int h1,
+                         int ring) {
+  const int kvd = kv_heads * head_dim, grp = n_heads / kv_heads;
+  for (int h = h0; h < h1; h++) {
+    const float *qh = q + (size_t)h * head_dim;
+    const int kvh = h / grp;
+    float *sc = scratch;
+    int8_t qq[512];
+    float qamax = 0.0f;
+    for (int i = 0; i < head_dim; i++) {
+      const float a = fabsf(qh[i]);
+      if (a > qamax) qamax = a;
+    }
+    const float qscale = qamax / 127.0f;
+    const float qinv = qamax > 0.0f ? 127.0f / qamax : 0.0f;
+    for (int i = 0; i < head_dim; i++) {
+      int v = (int)lrintf(qh[i] * qinv);
+      v = v > 127 ? 127 : (v < -127 ? -127 : v);
+      qq[i] = (int8_t)v;
+    }
+    float mx = -INFINITY;
+    for (int t = start; t < end; t++) {
+      const int sl = ring ? t % ring : t;
+      const int8_t *kp = kc + (size_t)sl * kvd + (size_t)kvh * head_dim;
+      int32_t dot = 0;
+      for (int i = 0; i < head_dim; i++) dot += (int32_t)kp[i] * (int32_t)qq[i];
+      const float s = (float)dot * qscale * ks[sl];
+      sc[t - start] = s;
+      if (s > mx) mx = s;
+    }
+    const int n = end - start;
+    float lanes[16] = {0};
+    int u = 0;
+    for (; u + 16 <= n; u += 16)
+      for (int j = 0; j < 16; j++) {
+        const float e = orc_exp_lane(sc[u + j] - mx);
+        sc[u + j] = e;
+        lanes[j] = lanes[j] + e;
+      }
+    float sum = orc_reduce16(lanes);
+    for (; u < n; u++) {
+      sc[u] = expf(sc[u] - mx);
+      sum += sc[u];
+    }
+    const float inv = 1.0f / sum;
+    float wmax = 0.0f;
+    for (int t = start; t < end; t++) {
+      const float w = sc[t - start] * inv * vs[ring ? t % ring : t];
+      if (w > wmax) wmax = w;
+    }
+    float *oh = out + (size_t)h * head_dim;
+    if (!(wmax > 0.0f)) {
+      for (int i = 0; i < head_dim; i++) oh[i] = 0.0f;
+      continue;
+    }
+    const float wq_scale = wmax / 65535.0f, wq_inv = 65535.0f / wmax;
+    int32_t acc_hi[512], acc_lo[512];
+    for (int i = 0; i < head_dim; i++) acc_hi[i] = acc_lo[i] = 0;
+    for (int t = start; t < end; t++) {
+      const int sl = ring ? t % ring : t;
+      int iw = (int)(sc[t - start] * inv * vs[sl] * wq_inv + 0.5f);
+      if (iw > 65535) iw = 65535;
+      if (iw < 0) iw = 0;
+      const int hi = iw >> 8, lo = iw & 255;
+      const int8_t *vrow = vc + ((size_t)(sl >> 2) * kvd + (size_t)kvh * head_dim) * 4 + (sl & 3);
+      for (int i = 0; i < head_dim; i++) {
+        acc_hi[i] += hi * (int32_t)vrow[(size_t)i * 4];
+        acc_lo[i] += lo * (int32_t)vrow[(size_t)i * 4];
+      }
+    }
+    for (int i = 0; i < head_dim; i++)
+      oh[i] = (float)(int32_t)(((uint32_t)acc_hi[i] << 8) + (uint32_t)acc_lo[i]) * wq_scale;
+  }
+}

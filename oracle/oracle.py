@@ -57,8 +57,68 @@ def _load_pool(lib):
         _decl(lib, name, args, res)
 
 
-class Oracle:
+class _Glue:
+    """The decode-chain glue and attention, same methods on both libraries
+    (prefix ``orc_`` for the restatement, ``fgm_`` for the reference)."""
+
+    prefix = ""
+
+    def _f(self, name):
+        return getattr(self.lib, self.prefix + name)
+
+    def rmsnorm(self, x, w, eps):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty_like(x)
+        n = x.shape[-1]
+        for r in range(x.size // n):
+            xo, oo = x.reshape(-1, n)[r], out.reshape(-1, n)[r]
+            if w is None:
+                self._f("rmsnorm_noscale")(_ptr(oo), _ptr(xo), n, C.c_float(eps)) \
+                    if self.prefix == "fgm_" else \
+                    self._f("rmsnorm")(_ptr(oo), _ptr(xo), None, n, C.c_float(eps))
+            else:
+                self._f("rmsnorm")(_ptr(oo), _ptr(xo), _ptr(np.ascontiguousarray(w, np.float32)),
+                                   n, C.c_float(eps))
+        return out
+
+    def gelu_mul(self, gate, up):
+        gate = np.ascontiguousarray(gate, np.float32)
+        up = np.ascontiguousarray(up, np.float32)
+        out = np.empty_like(gate)
+        self._f("gelu_mul")(_ptr(out), _ptr(gate), _ptr(up), gate.size)
+        return out
+
+    def add(self, a, b):
+        a = np.ascontiguousarray(a, np.float32).copy()
+        self._f("add")(_ptr(a), _ptr(np.ascontiguousarray(b, np.float32)), a.size)
+        return a
+
+    def softcap(self, x, cap):
+        x = np.ascontiguousarray(x, np.float32).copy()
+        self._f("softcap")(_ptr(x), x.size, C.c_float(cap))
+        return x
+
+    def store_v_t(self, vt, src, slot):
+        src = np.ascontiguousarray(src, np.int8)
+        self._f("store_v_t")(_ptr(vt), _ptr(src), src.size, slot)
+
+    def attend_q8(self, q, kc, ks, vc, vs, n_heads, kv_heads, head_dim, start, end, ring=0):
+        q = np.ascontiguousarray(q, np.float32)
+        out = np.zeros(n_heads * head_dim, np.float32)
+        cap = max(end, ring, 1)
+        scratch = np.zeros(2 * cap + 2 * head_dim + 64, np.float32)
+        args = [_ptr(out), _ptr(q), _ptr(kc), _ptr(ks), _ptr(vc), _ptr(vs), n_heads, kv_heads,
+                head_dim, start, end, _ptr(scratch), 0, n_heads, ring]
+        if self.prefix == "fgm_":
+            args.append(cap)
+        self._f("attend_q8_heads")(*args)
+        return out
+
+
+class Oracle(_Glue):
     """The scalar C restatement (``fgm_oracle.c``)."""
+
+    prefix = "orc_"
 
     def __init__(self, path: str = ORACLE_SO):
         if not os.path.exists(path):
@@ -80,8 +140,25 @@ class Oracle:
         _decl(L, "orc_fill_xorshift", [_p, _i, _i, C.c_size_t, _p])
         _decl(L, "orc_fill_lcg", [_p, _i, _i, C.c_size_t, _p])
         _decl(L, "orc_argmax", [_p, _i], _i)
+        _decl(L, "orc_exp_lane", [C.c_float], C.c_float)
+        _decl(L, "orc_rmsnorm", [_p, _p, _p, _i, C.c_float])
+        _decl(L, "orc_gelu_mul", [_p, _p, _p, _i])
+        _decl(L, "orc_add", [_p, _p, _i])
+        _decl(L, "orc_softcap", [_p, _i, C.c_float])
+        _decl(L, "orc_rope", [_p, _i, _i, _p, _i, _i])
+        _decl(L, "orc_store_v_t", [_p, _p, _i, _i])
+        _decl(L, "orc_attend_q8_heads", [_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p, _i, _i,
+                                         _i])
         _load_pool(L)
         self.kind = "port"
+
+    def rope(self, x, n_heads, head_dim, inv_freq, pos, fused=True):
+        """ops.c:135-147 as the reference build compiles it (products and sum
+        fused); fused=False rounds each product."""
+        x = np.ascontiguousarray(x, np.float32).copy()
+        self.lib.orc_rope(_ptr(x), n_heads, head_dim,
+                          _ptr(np.ascontiguousarray(inv_freq, np.float32)), pos, int(fused))
+        return x
 
     # -- the reference harnesses' PRNGs --------------------------------------
     def xorshift(self, state: np.ndarray, lo: int, hi: int, n: int) -> np.ndarray:
@@ -179,8 +256,10 @@ class Oracle:
         return C.cast(getattr(self.lib, table[name]), _p).value
 
 
-class Reference:
+class Reference(_Glue):
     """The reference kernels compiled from their own sources (``oracle/_ref``)."""
+
+    prefix = "fgm_"
 
     def __init__(self, path: str = REF_SO):
         if not os.path.exists(path):
@@ -199,6 +278,15 @@ class Reference:
         _decl(L, "fgm_quant_act", [_p, _i, _i, _p, _p])
         _decl(L, "fgm_fwht", [_p, _i, _i])
         _decl(L, "fgm_pack_a", [_i, _i, _p, _p])
+        _decl(L, "fgm_rmsnorm", [_p, _p, _p, _i, C.c_float])
+        _decl(L, "fgm_rmsnorm_noscale", [_p, _p, _i, C.c_float])
+        _decl(L, "fgm_gelu_mul", [_p, _p, _p, _i])
+        _decl(L, "fgm_add", [_p, _p, _i])
+        _decl(L, "fgm_softcap", [_p, _i, C.c_float])
+        _decl(L, "fgm_rope", [_p, _i, _i, _p, _i])
+        _decl(L, "fgm_store_v_t", [_p, _p, _i, _i])
+        _decl(L, "fgm_attend_q8_heads", [_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p, _i, _i,
+                                         _i, _i])
         _load_pool(L)
         self.has_amx = bool(L.fgm_cpu_has_amx())
         self.has_vnni = bool(L.fgm_cpu_has_avx512_vnni())
@@ -251,6 +339,12 @@ class Reference:
         self.lib.fgm_prep_rows(_ptr(src), lda, _ptr(rot), _ptr(qa), _ptr(qs), _ptr(pa),
                                m, k, hsz, 0, m)
         return rot, qa, qs, pa
+
+    def rope(self, x, n_heads, head_dim, inv_freq, pos):
+        x = np.ascontiguousarray(x, np.float32).copy()
+        self.lib.fgm_rope(_ptr(x), n_heads, head_dim,
+                          _ptr(np.ascontiguousarray(inv_freq, np.float32)), pos)
+        return x
 
     def fn(self, name):
         table = {"q4g": self._gemm_name("fgm_gemm_q4g"),

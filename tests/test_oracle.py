@@ -183,3 +183,71 @@ def test_oracle_matches_reference_live_prep(orc, ref, m, k, lda, hsz):
     b = ref.prep_rows(x, m, k, hsz, lda=lda)
     for u, v in zip(a, b):
         assert np.array_equal(u.view(np.uint8), v.view(np.uint8))
+
+
+# ------------------------------------------------ decode-chain glue, attention
+@pytest.mark.parametrize("n", [16, 256, 2048, 8192])
+def test_glue_ops_match_reference_live(orc, ref, n):
+    """rmsnorm (with and without weight), gelu_mul, add, softcap (ops.c:59-147,
+    :317-352): bit-exact against the reference kernels for n a multiple of 16
+    (the vector path; the reference's scalar tails call libm)."""
+    rng = np.random.default_rng(n)
+    x = (rng.standard_normal((3, n)) * 3).astype(np.float32)
+    w = rng.standard_normal(n).astype(np.float32)
+    g = (rng.standard_normal(n) * 4).astype(np.float32)
+    u = rng.standard_normal(n).astype(np.float32)
+    same = lambda a, b: np.array_equal(a.view(np.uint32), b.view(np.uint32))  # noqa: E731
+    assert same(orc.rmsnorm(x, w, 1e-6), ref.rmsnorm(x, w, 1e-6))
+    assert same(orc.rmsnorm(x, None, 1e-6), ref.rmsnorm(x, None, 1e-6))
+    assert same(orc.gelu_mul(g, u), ref.gelu_mul(g, u))
+    assert same(orc.add(g, u), ref.add(g, u))
+    assert same(orc.softcap(g * 10, 30.0), ref.softcap(g * 10, 30.0))
+
+
+@pytest.mark.parametrize("pos", [0, 7, 513, 4095])
+def test_rope_matches_reference_live(orc, ref, pos):
+    rng = np.random.default_rng(pos)
+    nh, hd = 8, 256
+    inv = (1.0 / (10000 ** (np.arange(0, hd, 2) / hd))).astype(np.float32)
+    inv[-16:] = 0.0  # proportional RoPE's pass-through tail
+    x = rng.standard_normal(nh * hd).astype(np.float32)
+    a, b = orc.rope(x, nh, hd, inv, pos), ref.rope(x, nh, hd, inv, pos)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def _kv_cache(orc, rng, cap, kv_heads, hd):
+    kc = rng.integers(-127, 128, (cap, kv_heads * hd)).astype(np.int8)
+    ks = rng.uniform(0.001, 0.02, cap).astype(np.float32)
+    vt = np.zeros((cap + 4) * kv_heads * hd, np.int8)
+    for s in range(cap):
+        orc.store_v_t(vt, rng.integers(-127, 128, kv_heads * hd).astype(np.int8), s)
+    vs = rng.uniform(0.001, 0.02, cap).astype(np.float32)
+    return kc, ks, vt, vs
+
+
+@pytest.mark.parametrize("end,start,ring,hd", [(64, 0, 0, 256), (100, 0, 0, 256),
+                                               (1024, 0, 0, 256), (1024, 17, 0, 512),
+                                               (300, 40, 0, 256), (600, 500, 128, 256),
+                                               (257, 129, 128, 256)])
+def test_attention_matches_reference_live(orc, ref, end, start, ring, hd):
+    """fgm_attend_q8_heads (ops.c:378-640): per-head int8 Q, int8 K scores,
+    softmax with the Cephes exp lanes (libm expf on the tail), 16-bit split
+    weights against the slot-interleaved int8 V; linear and ring caches
+    (a ring window never longer than the ring, as the reference uses it)."""
+    rng = np.random.default_rng(end + start + ring + hd)
+    kc, ks, vt, vs = _kv_cache(orc, rng, ring or end, 2, hd)
+    q = (rng.standard_normal(8 * hd) * 2).astype(np.float32)
+    a = orc.attend_q8(q, kc, ks, vt, vs, 8, 2, hd, start, end, ring)
+    b = ref.attend_q8(q, kc, ks, vt, vs, 8, 2, hd, start, end, ring)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_store_v_t_matches_reference_live(orc, ref):
+    rng = np.random.default_rng(11)
+    n, cap = 512, 37
+    a, b = np.zeros((cap + 3) * n, np.int8), np.zeros((cap + 3) * n, np.int8)
+    for slot in range(cap):
+        src = rng.integers(-127, 128, n).astype(np.int8)
+        orc.store_v_t(a, src, slot)
+        ref.store_v_t(b, src, slot)
+    assert np.array_equal(a, b)
