@@ -49,6 +49,17 @@ SIGNATURES = {
     "fgm_cuda_argmax_parts": ([_i], _i),
     "fgm_cuda_argmax_partials": ([_p, _i, _i, _i, _i, _p, _p, _p], _i),
     "fgm_cuda_argmax_merge": ([_p, _p, _i, _i, _p, _p], _i),
+    "fgm_cuda_rmsnorm": ([_p, _p, _p, _i, _i, C.c_float, _p], _i),
+    "fgm_cuda_gelu_mul": ([_p, _p, _p, _i, _i, _p], _i),
+    "fgm_cuda_add": ([_p, _p, _sz, _p], _i),
+    "fgm_cuda_mul": ([_p, _p, _sz, _p], _i),
+    "fgm_cuda_scale": ([_p, C.c_float, _sz, _p], _i),
+    "fgm_cuda_softcap": ([_p, _i, _i, C.c_float, _p], _i),
+    "fgm_cuda_rope": ([_p, _i, _i, _i, _i, _p, _p, _p], _i),
+    "fgm_cuda_quant_act": ([_p, _i, _i, _p, _p, _p], _i),
+    "fgm_cuda_store_v_t": ([_p, _sz, _p, _i, _i, _i, _i, _p], _i),
+    "fgm_cuda_attend_q8": ([_p, _i, _p, _i, _p, _sz, _p, _sz, _p, _sz, _p, _sz, _i, _i, _i, _i,
+                            _i, _i, _i, _p], _i),
     "fgm_cuda_ipc_alloc": ([_sz, C.POINTER(_p)], _i),
     "fgm_cuda_ipc_free": ([_p], _i),
     "fgm_cuda_ipc_handle": ([_p, _p], _i),

@@ -1211,6 +1211,138 @@ int fgm_cuda_argmax_merge(const float *vals, const int32_t *idx, int M, int P, i
   return FGM_CUDA_OK;
 }
 
+// ------------------------------------------- decode-chain glue, attention
+static int glue_done(cudaError_t e, const char *what) {
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  count_launch();
+  return FGM_CUDA_OK;
+}
+
+int fgm_cuda_rmsnorm(float *out, const float *x, const float *w, int rows, int n, float eps,
+                     void *stream) {
+  if (rows < 0 || n <= 0 || n > 49152)
+    return fail(FGM_CUDA_EINVAL, "rmsnorm: rows=%d n=%d (need 0 < n <= 49152)", rows, n);
+  if (rows == 0) return FGM_CUDA_OK;
+  if (!out || !x) return fail(FGM_CUDA_EINVAL, "null pointer");
+  return glue_done(launch_rmsnorm(out, x, w, rows, n, eps, use_pdl(), (cudaStream_t)stream),
+                   "rmsnorm launch");
+}
+
+int fgm_cuda_gelu_mul(float *out, const float *gate, const float *up, int rows, int n,
+                      void *stream) {
+  if (rows < 0 || n <= 0) return fail(FGM_CUDA_EINVAL, "gelu_mul: rows=%d n=%d", rows, n);
+  if (rows == 0) return FGM_CUDA_OK;
+  if (!out || !gate || !up) return fail(FGM_CUDA_EINVAL, "null pointer");
+  return glue_done(launch_gelu_mul(out, gate, up, rows, n, use_pdl(), (cudaStream_t)stream),
+                   "gelu_mul launch");
+}
+
+static int elementwise(float *a, const float *b, float sc, size_t n, int op, void *stream) {
+  if (n == 0) return FGM_CUDA_OK;
+  if (!a || (op != 2 && !b)) return fail(FGM_CUDA_EINVAL, "null pointer");
+  return glue_done(launch_elementwise(a, b, sc, n, op, use_pdl(), (cudaStream_t)stream),
+                   "elementwise launch");
+}
+
+int fgm_cuda_add(float *a, const float *b, size_t n, void *stream) {
+  return elementwise(a, b, 0.0f, n, 0, stream);
+}
+
+int fgm_cuda_mul(float *a, const float *b, size_t n, void *stream) {
+  return elementwise(a, b, 0.0f, n, 1, stream);
+}
+
+int fgm_cuda_scale(float *a, float s, size_t n, void *stream) {
+  return elementwise(a, nullptr, s, n, 2, stream);
+}
+
+int fgm_cuda_softcap(float *x, int rows, int n, float cap, void *stream) {
+  if (rows < 0 || n <= 0) return fail(FGM_CUDA_EINVAL, "softcap: rows=%d n=%d", rows, n);
+  if (rows == 0) return FGM_CUDA_OK;
+  if (!x) return fail(FGM_CUDA_EINVAL, "null pointer");
+  return glue_done(launch_softcap(x, rows, n, cap, use_pdl(), (cudaStream_t)stream),
+                   "softcap launch");
+}
+
+int fgm_cuda_rope(float *x, int x_ld, int rows, int n_heads, int head_dim, const float *inv_freq,
+                  const int *pos, void *stream) {
+  if (rows < 0 || n_heads <= 0 || head_dim <= 0 || head_dim % 2 || x_ld < n_heads * head_dim)
+    return fail(FGM_CUDA_EINVAL, "rope: rows=%d heads=%d head_dim=%d x_ld=%d", rows, n_heads,
+                head_dim, x_ld);
+  if (rows == 0) return FGM_CUDA_OK;
+  if (!x || !inv_freq || !pos) return fail(FGM_CUDA_EINVAL, "null pointer");
+  return glue_done(launch_rope(x, x_ld, rows, n_heads, head_dim, inv_freq, pos, use_pdl(),
+                               (cudaStream_t)stream),
+                   "rope launch");
+}
+
+int fgm_cuda_quant_act(const float *x, int rows, int k, int8_t *q, float *scale, void *stream) {
+  int rc = check_prep(k, rows, k, 0, 0, rows, true);
+  if (rc) return rc;
+  if (rows == 0) return FGM_CUDA_OK;
+  if (!x || !q || !scale) return fail(FGM_CUDA_EINVAL, "null pointer");
+  return run_prep(x, k, nullptr, q, scale, nullptr, rows, k, 0, 0, rows, (cudaStream_t)stream);
+}
+
+int fgm_cuda_store_v_t(int8_t *vt, size_t vt_stride, const int8_t *src, int src_ld, int rows,
+                       int n, int slot, void *stream) {
+  if (rows < 0 || n <= 0 || slot < 0 || src_ld < n)
+    return fail(FGM_CUDA_EINVAL, "store_v_t: rows=%d n=%d slot=%d src_ld=%d", rows, n, slot,
+                src_ld);
+  if (rows == 0) return FGM_CUDA_OK;
+  if (!vt || !src) return fail(FGM_CUDA_EINVAL, "null pointer");
+  return glue_done(launch_store_v_t(vt, vt_stride, src, src_ld, rows, n, slot, use_pdl(),
+                                    (cudaStream_t)stream),
+                   "store_v_t launch");
+}
+
+int fgm_cuda_attend_q8(float *out, int out_ld, const float *q, int q_ld, const int8_t *kc,
+                       size_t kc_stride, const float *ks, size_t ks_stride, const int8_t *vt,
+                       size_t vt_stride, const float *vs, size_t vs_stride, int rows, int n_heads,
+                       int kv_heads, int head_dim, int start, int end, int ring, void *stream) {
+  if (rows < 0 || n_heads <= 0 || kv_heads <= 0 || n_heads % kv_heads != 0)
+    return fail(FGM_CUDA_EINVAL, "attend: rows=%d heads=%d kv_heads=%d", rows, n_heads, kv_heads);
+  if (head_dim <= 0 || head_dim % 64 != 0 || head_dim > 512)
+    return fail(FGM_CUDA_EINVAL, "attend: head_dim=%d (need a multiple of 64, at most 512)",
+                head_dim);
+  if (start < 0 || end <= start || ring < 0 || (ring > 0 && end - start > ring))
+    return fail(FGM_CUDA_EINVAL, "attend: positions [%d, %d) ring=%d (a ring window must fit the ring)",
+                start, end, ring);
+  if (out_ld < n_heads * head_dim || q_ld < n_heads * head_dim)
+    return fail(FGM_CUDA_EINVAL, "attend: out_ld=%d q_ld=%d < heads*head_dim", out_ld, q_ld);
+  if (rows == 0) return FGM_CUDA_OK;
+  if (!out || !q || !kc || !ks || !vt || !vs) return fail(FGM_CUDA_EINVAL, "null pointer");
+  DevInfo *di = nullptr;
+  int rc = dev_info(&di);
+  if (rc) return rc;
+  AttnParams p{};
+  p.out = out;
+  p.out_ld = out_ld;
+  p.q = q;
+  p.q_ld = q_ld;
+  p.kc = kc;
+  p.ks = ks;
+  p.vt = vt;
+  p.vs = vs;
+  p.kc_stride = kc_stride;
+  p.ks_stride = ks_stride;
+  p.vt_stride = vt_stride;
+  p.vs_stride = vs_stride;
+  p.n_heads = n_heads;
+  p.kv_heads = kv_heads;
+  p.head_dim = head_dim;
+  p.start = start;
+  p.end = end;
+  p.ring = ring;
+  p.wbase = ring ? 0 : (start & ~3);
+  p.wslots = ring ? ((ring + 3) & ~3) : (((end + 3) & ~3) - p.wbase);
+  if (attend_smem_bytes(p) + 2048 > di->smem_optin)
+    return fail(FGM_CUDA_EINVAL, "attend: %d positions need %zu bytes of shared memory", end - start,
+                attend_smem_bytes(p));
+  return glue_done(launch_attend_q8(p, rows, use_pdl(), di->smem_optin, (cudaStream_t)stream),
+                   "attend launch");
+}
+
 // ------------------------------------------------ peer memory, fused gather
 int fgm_cuda_ipc_alloc(size_t bytes, void **dev_ptr) {
   if (!dev_ptr || !bytes) return fail(FGM_CUDA_EINVAL, "ipc_alloc: null pointer or zero size");

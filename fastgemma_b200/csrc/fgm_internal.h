@@ -72,11 +72,41 @@ struct PrepParams {
   float *rot;    // may be null
   int8_t *qa;    // may be null
   float *qs;
-  int8_t *pa;
+  int8_t *pa;    // may be null (quantised rows only, no tile packing)
   int m, k, hsz, r0, r1;
 };
 
 cudaError_t launch_prep(const PrepParams &p, bool pdl, cudaStream_t st);
+
+// ---- decode-chain glue and int8-KV attention (glue.cu)
+cudaError_t launch_rmsnorm(float *out, const float *x, const float *w, int rows, int n, float eps,
+                           bool pdl, cudaStream_t st);
+cudaError_t launch_gelu_mul(float *out, const float *gate, const float *up, int rows, int n,
+                            bool pdl, cudaStream_t st);
+// op 0: a += b, 1: a *= b, 2: a *= s
+cudaError_t launch_elementwise(float *a, const float *b, float s, size_t n, int op, bool pdl,
+                               cudaStream_t st);
+cudaError_t launch_softcap(float *x, int rows, int n, float cap, bool pdl, cudaStream_t st);
+cudaError_t launch_rope(float *x, int x_ld, int rows, int n_heads, int head_dim,
+                        const float *inv_freq, const int *pos, bool pdl, cudaStream_t st);
+cudaError_t launch_store_v_t(int8_t *vt, size_t vt_stride, const int8_t *src, int src_ld, int rows,
+                             int n, int slot, bool pdl, cudaStream_t st);
+struct AttnParams {
+  float *out;
+  int out_ld;
+  const float *q;
+  int q_ld;
+  const int8_t *kc;       // K [slot][kv_heads * head_dim] per query row
+  const float *ks;        // K scales [slot]
+  const int8_t *vt;       // V, slot-interleaved (store_v_t)
+  const float *vs;        // V scales [slot]
+  size_t kc_stride, ks_stride, vt_stride, vs_stride;  // per query row (elements)
+  int n_heads, kv_heads, head_dim, start, end, ring;
+  int wbase, wslots;      // cache slots [wbase, wbase + wslots) the window can touch
+};
+size_t attend_smem_bytes(const AttnParams &p);
+cudaError_t launch_attend_q8(const AttnParams &p, int rows, bool pdl, size_t smem_limit,
+                             cudaStream_t st);
 // Copy two host regions (device-readable: page-locked or staging) into
 // device memory with one kernel.
 cudaError_t launch_pull(const void *s1, void *d1, size_t n1, const void *s2, void *d2, size_t n2,

@@ -62,7 +62,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepParams p) 
     for (int i = threadIdx.x * 4; i < k; i += kPrepThreads * 4) {
       uint32_t v = 0;
       if (r < p.m) v = *reinterpret_cast<const uint32_t *>(p.qa + (size_t)r * k + i);
-      *reinterpret_cast<uint32_t *>(pa_row + (size_t)(i / 64) * kATile + (i % 64)) = v;
+      if (p.pa) *reinterpret_cast<uint32_t *>(pa_row + (size_t)(i / 64) * kATile + (i % 64)) = v;
     }
     return;
   }
@@ -110,7 +110,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepParams p) 
       packed |= (uint32_t)(q & 0xFF) << (8 * e);
     }
     if (p.qa) *reinterpret_cast<uint32_t *>(p.qa + (size_t)r * k + i) = packed;
-    *reinterpret_cast<uint32_t *>(pa_row + (size_t)(i / 64) * kATile + (i % 64)) = packed;
+    if (p.pa) *reinterpret_cast<uint32_t *>(pa_row + (size_t)(i / 64) * kATile + (i % 64)) = packed;
   }
 }
 
@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(512, 1) prep_fast_kernel(const PrepParams p) {
     for (int i = threadIdx.x * 4; i < k; i += blockDim.x * 4) {
       uint32_t v = 0;
       if (r < p.m) v = *reinterpret_cast<const uint32_t *>(p.qa + (size_t)r * k + i);
-      *reinterpret_cast<uint32_t *>(pa_row + (size_t)(i / 64) * kATile + (i % 64)) = v;
+      if (p.pa) *reinterpret_cast<uint32_t *>(pa_row + (size_t)(i / 64) * kATile + (i % 64)) = v;
     }
     return;
   }
@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(512, 1) prep_fast_kernel(const PrepParams p) {
     if (p.rot) *reinterpret_cast<float4 *>(p.rot + (size_t)r * k + kk) = v[j];
     const uint32_t w = q8_quad(v[j], inv);
     if (p.qa) *reinterpret_cast<uint32_t *>(p.qa + (size_t)r * k + kk) = w;
-    *reinterpret_cast<uint32_t *>(pa_row + (size_t)(kk / 64) * kATile + (kk % 64)) = w;
+    if (p.pa) *reinterpret_cast<uint32_t *>(pa_row + (size_t)(kk / 64) * kATile + (kk % 64)) = w;
   }
 }
 

@@ -113,3 +113,53 @@ def q8c_prepare(B, N, K, stream=None):
 
 def q8c_release(B):
     call("fgm_cuda_q8c_release", _p(B))
+
+
+# ------------------------------------------- decode-chain glue, attention
+def rmsnorm(out, x, w, rows, n, eps, stream=None):
+    """ops.c:59-92 over rows of n (w None: the no-scale form)."""
+    call("fgm_cuda_rmsnorm", _p(out), _p(x), _p(w), rows, n, eps, _s(stream))
+
+
+def gelu_mul(out, gate, up, rows, n, stream=None):
+    """ops.c:119-131: out = gelu_tanh(gate) * up."""
+    call("fgm_cuda_gelu_mul", _p(out), _p(gate), _p(up), rows, n, _s(stream))
+
+
+def add(a, b, stream=None):
+    call("fgm_cuda_add", _p(a), _p(b), a.numel(), _s(stream))
+
+
+def mul(a, b, stream=None):
+    call("fgm_cuda_mul", _p(a), _p(b), a.numel(), _s(stream))
+
+
+def scale(a, s, stream=None):
+    call("fgm_cuda_scale", _p(a), s, a.numel(), _s(stream))
+
+
+def softcap(x, rows, n, cap, stream=None):
+    call("fgm_cuda_softcap", _p(x), rows, n, cap, _s(stream))
+
+
+def rope(x, x_ld, rows, n_heads, head_dim, inv_freq, pos, stream=None):
+    """ops.c:135-147 in place; pos: int32 device tensor [rows]."""
+    call("fgm_cuda_rope", _p(x), x_ld, rows, n_heads, head_dim, _p(inv_freq), _p(pos), _s(stream))
+
+
+def quant_act(x, rows, k, q, scale, stream=None):
+    """ops.c:181-204 (quant_kv: one row)."""
+    call("fgm_cuda_quant_act", _p(x), rows, k, _p(q), _p(scale), _s(stream))
+
+
+def store_v_t(vt, vt_stride, src, src_ld, rows, n, slot, stream=None):
+    """ops.c:653-660 for `rows` caches."""
+    call("fgm_cuda_store_v_t", _p(vt), vt_stride, _p(src), src_ld, rows, n, slot, _s(stream))
+
+
+def attend_q8(out, out_ld, q, q_ld, kc, kc_stride, ks, ks_stride, vt, vt_stride, vs, vs_stride,
+              rows, n_heads, kv_heads, head_dim, start, end, ring=0, stream=None):
+    """ops.c:378-640 for `rows` query rows, each against its own int8 KV cache."""
+    call("fgm_cuda_attend_q8", _p(out), out_ld, _p(q), q_ld, _p(kc), kc_stride, _p(ks), ks_stride,
+         _p(vt), vt_stride, _p(vs), vs_stride, rows, n_heads, kv_heads, head_dim, start, end, ring,
+         _s(stream))

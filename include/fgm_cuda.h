@@ -242,6 +242,60 @@ int fgm_cuda_gemm_q4g_acc(int M, int N, int K, const int8_t *A, const uint8_t *B
 int fgm_cuda_gemm_q8c_acc(int M, int N, int K, const int8_t *A, const int8_t *B,
                           int32_t *acc, int n0, int n1, void *stream);
 
+/* ------------------------------------------- decode-chain glue, attention
+ * The operations between the GEMMs of the reference's decode forward pass
+ * (fgm-core/src/forward.rs:469-654), on device buffers and a stream, as
+ * fgm-kernels computes them (crates/fgm-kernels/csrc/ops.c).  Bit-identical
+ * to the reference for row lengths that are multiples of 16; the reference's
+ * libm pieces (scalar tails, rope's cos / sin, the softmax tail's exp) are
+ * evaluated in double precision and rounded once. */
+
+/* ops.c:59-92 (fgm_rmsnorm; fgm_rmsnorm_noscale when w is NULL): each of
+ * `rows` rows of n: out = x * (mean(x^2) + eps)^-1/2 (* w). n <= 49152. */
+int fgm_cuda_rmsnorm(float *out, const float *x, const float *w, int rows, int n, float eps,
+                     void *stream);
+
+/* ops.c:119-131 (fgm_gelu_mul): out = gelu_tanh(gate) * up over rows of n. */
+int fgm_cuda_gelu_mul(float *out, const float *gate, const float *up, int rows, int n,
+                      void *stream);
+
+/* ops.c:317-337 (fgm_add, fgm_mul, fgm_scale) over n floats, in place. */
+int fgm_cuda_add(float *a, const float *b, size_t n, void *stream);
+int fgm_cuda_mul(float *a, const float *b, size_t n, void *stream);
+int fgm_cuda_scale(float *a, float s, size_t n, void *stream);
+
+/* ops.c:340-352 (fgm_softcap): x = cap * tanh(x / cap) over rows of n. */
+int fgm_cuda_softcap(float *x, int rows, int n, float cap, void *stream);
+
+/* ops.c:135-147 (fgm_rope): half-split rotary embedding of n_heads heads,
+ * in place, for `rows` rows (row r at x + r*x_ld) at positions pos[r] (a
+ * device array). */
+int fgm_cuda_rope(float *x, int x_ld, int rows, int n_heads, int head_dim, const float *inv_freq,
+                  const int *pos, void *stream);
+
+/* ops.c:181-204, :641-644 (fgm_quant_act, fgm_quant_kv): rows of k f32 to
+ * int8 with one scale per row (k % 64 == 0). */
+int fgm_cuda_quant_act(const float *x, int rows, int k, int8_t *q, float *scale, void *stream);
+
+/* ops.c:653-660 (fgm_store_v_t): for each of `rows` caches (vt +
+ * r*vt_stride bytes), store the int8 V row src + r*src_ld (n bytes) at
+ * `slot` of the slot-interleaved layout vt[((slot/4)*n + j)*4 + slot%4]. */
+int fgm_cuda_store_v_t(int8_t *vt, size_t vt_stride, const int8_t *src, int src_ld, int rows,
+                       int n, int slot, void *stream);
+
+/* ops.c:378-640 (fgm_attend_q8 / fgm_attend_q8_heads): for each of `rows`
+ * query rows (its own KV cache at the given per-row strides, in elements),
+ * all n_heads heads of q + r*q_ld attend to positions [start, end) of an
+ * int8 cache: K [slot][kv_heads*head_dim] with scales ks [slot], V in the
+ * store_v_t layout (holding whole groups of four slots) with scales vs.
+ * ring = 0: slot = position; ring > 0: slot = position % ring and the
+ * window must not be longer than the ring.  head_dim % 64 == 0, <= 512;
+ * the window needs 4 bytes of shared memory per position. */
+int fgm_cuda_attend_q8(float *out, int out_ld, const float *q, int q_ld, const int8_t *kc,
+                       size_t kc_stride, const float *ks, size_t ks_stride, const int8_t *vt,
+                       size_t vt_stride, const float *vs, size_t vs_stride, int rows, int n_heads,
+                       int kv_heads, int head_dim, int start, int end, int ring, void *stream);
+
 /* ------------------------------------------------------------ row argmax
  * The token choice that follows the LM head (fgm-serve/src/engine.rs:75-83,
  * :297-302): per row the first index of the largest value, NaN never

@@ -1,0 +1,148 @@
+"""The decode-chain glue and the int8-KV attention on the device
+(csrc/glue.cu) against the oracle's restatement of ops.c, itself pinned
+bit-exact against the reference kernels (tests/test_oracle.py).  Row lengths
+that are multiples of 16 must match bit for bit; the reference's libm pieces
+(scalar tails, rope, the softmax tail) are compared to REL_TOL."""
+import numpy as np
+import pytest
+
+import fastgemma_b200.device as D
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+REL_TOL, ABS_TOL = 2e-6, 1e-6
+
+
+@pytest.fixture(scope="module", autouse=True)
+def cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    torch.cuda.set_device(0)
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def same(got, want, exact, what):
+    got, want = np.asarray(got, np.float32), np.asarray(want, np.float32)
+    if exact:
+        bad = got.view(np.uint32) != want.view(np.uint32)
+        assert not bad.any(), f"{what}: {int(bad.sum())} differ, e.g. {got[bad][:3]} vs {want[bad][:3]}"
+    else:
+        assert np.allclose(got, want, rtol=REL_TOL, atol=ABS_TOL), \
+            f"{what}: max abs {np.abs(got - want).max()}"
+
+
+@pytest.mark.parametrize("n", [16, 2048, 8192, 2056])
+def test_rmsnorm_gelu_softcap_elementwise(orc, n):
+    rng = np.random.default_rng(n)
+    rows = 5
+    x = (rng.standard_normal((rows, n)) * 3).astype(np.float32)
+    w = rng.standard_normal(n).astype(np.float32)
+    exact = n % 16 == 0
+    for wt in (w, None):
+        out = torch.empty((rows, n), device="cuda")
+        D.rmsnorm(out, dev(x), None if wt is None else dev(wt), rows, n, 1e-6)
+        torch.cuda.synchronize()
+        same(out.cpu().numpy(), orc.rmsnorm(x, wt, 1e-6), exact, f"rmsnorm n={n}")
+    g = (rng.standard_normal((rows, n)) * 4).astype(np.float32)
+    u = rng.standard_normal((rows, n)).astype(np.float32)
+    out = torch.empty((rows, n), device="cuda")
+    D.gelu_mul(out, dev(g), dev(u), rows, n)
+    torch.cuda.synchronize()
+    want = np.stack([orc.gelu_mul(g[r], u[r]) for r in range(rows)])
+    same(out.cpu().numpy(), want, exact, f"gelu_mul n={n}")
+    xc = dev(g * 10)
+    D.softcap(xc, rows, n, 30.0)
+    torch.cuda.synchronize()
+    want = np.stack([orc.softcap(g[r] * 10, 30.0) for r in range(rows)])
+    same(xc.cpu().numpy(), want, exact, f"softcap n={n}")
+    a = dev(g)
+    D.add(a, dev(u))
+    D.mul(a, dev(u))
+    D.scale(a, 0.375)
+    torch.cuda.synchronize()
+    same(a.cpu().numpy(), ((g + u) * u) * np.float32(0.375), True, "add/mul/scale")
+
+
+def test_rope_rows_with_their_positions(orc):
+    rng = np.random.default_rng(3)
+    rows, nh, hd = 4, 8, 256
+    inv = (1.0 / (10000 ** (np.arange(0, hd, 2) / hd))).astype(np.float32)
+    inv[-16:] = 0.0
+    x = rng.standard_normal((rows, nh * hd)).astype(np.float32)
+    pos = np.array([0, 7, 513, 4095], np.int32)
+    xd = dev(x)
+    D.rope(xd, nh * hd, rows, nh, hd, dev(inv), dev(pos))
+    torch.cuda.synchronize()
+    want = np.stack([orc.rope(x[r], nh, hd, inv, int(pos[r])) for r in range(rows)])
+    same(xd.cpu().numpy(), want, False, "rope")
+
+
+def test_quant_act_and_store_v_t(orc):
+    rng = np.random.default_rng(4)
+    rows, k = 3, 512
+    x = rng.standard_normal((rows, k)).astype(np.float32)
+    x[1, :] = 0.0
+    q = torch.empty((rows, k), dtype=torch.int8, device="cuda")
+    s = torch.empty(rows, device="cuda")
+    D.quant_act(dev(x), rows, k, q, s)
+    torch.cuda.synchronize()
+    wq, ws = orc.quant_act(x)
+    assert np.array_equal(q.cpu().numpy(), wq)
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), ws.view(np.uint32))
+    cap, n = 10, 512
+    vt = torch.zeros((rows, (cap + 2) * n), dtype=torch.int8, device="cuda")
+    want = np.zeros((rows, (cap + 2) * n), np.int8)
+    for slot in (0, 3, 4, 9):
+        src = rng.integers(-127, 128, (rows, n)).astype(np.int8)
+        D.store_v_t(vt, (cap + 2) * n, dev(src), n, rows, n, slot)
+        for r in range(rows):
+            orc.store_v_t(want[r], src[r], slot)
+    torch.cuda.synchronize()
+    assert np.array_equal(vt.cpu().numpy(), want)
+
+
+def _caches(orc, rng, rows, cap, kvh, hd):
+    kc = rng.integers(-127, 128, (rows, cap, kvh * hd)).astype(np.int8)
+    ks = rng.uniform(0.001, 0.02, (rows, cap)).astype(np.float32)
+    vslots = (cap + 3) // 4 * 4
+    vt = np.zeros((rows, vslots * kvh * hd), np.int8)
+    for r in range(rows):
+        for sl in range(cap):
+            orc.store_v_t(vt[r], rng.integers(-127, 128, kvh * hd).astype(np.int8), sl)
+    vs = rng.uniform(0.001, 0.02, (rows, cap)).astype(np.float32)
+    return kc, ks, vt, vs
+
+
+@pytest.mark.parametrize("end,start,ring,hd", [(64, 0, 0, 256), (1024, 0, 0, 256),
+                                               (1024, 16, 0, 512), (100, 0, 0, 256),
+                                               (300, 41, 0, 128), (600, 500, 128, 256),
+                                               (257, 129, 128, 256)])
+def test_attention_rows_against_oracle(orc, end, start, ring, hd):
+    """Three query rows, each with its own cache; 8 heads over 2 KV heads.
+    Windows whose length is a multiple of 16 are bit-exact; others differ
+    only through the softmax tail's exp (libm in the reference)."""
+    rng = np.random.default_rng(end * 7 + start + ring + hd)
+    rows, nh, kvh = 3, 8, 2
+    cap = ring or end
+    kc, ks, vt, vs = _caches(orc, rng, rows, cap, kvh, hd)
+    q = (rng.standard_normal((rows, nh * hd)) * 2).astype(np.float32)
+    out = torch.full((rows, nh * hd), float("nan"), device="cuda")
+    D.attend_q8(out, nh * hd, dev(q), nh * hd, dev(kc), cap * kvh * hd, dev(ks), cap, dev(vt),
+                vt.shape[1], dev(vs), cap, rows, nh, kvh, hd, start, end, ring)
+    torch.cuda.synchronize()
+    want = np.stack([orc.attend_q8(q[r], kc[r], ks[r], vt[r], vs[r], nh, kvh, hd, start, end, ring)
+                     for r in range(rows)])
+    same(out.cpu().numpy(), want, (end - start) % 16 == 0, f"attend [{start},{end}) ring={ring}")
+
+
+def test_attention_rejects_bad_windows():
+    from fastgemma_b200 import _lib
+    z = torch.zeros(4096, device="cuda")
+    zi = torch.zeros(4096, dtype=torch.int8, device="cuda")
+    with pytest.raises(_lib.FgmCudaError, match="ring"):
+        D.attend_q8(z, 256, z, 256, zi, 0, z, 0, zi, 0, z, 0, 1, 1, 1, 256, 0, 200, 128)
+    with pytest.raises(_lib.FgmCudaError, match="head_dim"):
+        D.attend_q8(z, 256, z, 256, zi, 0, z, 0, zi, 0, z, 0, 1, 1, 1, 96, 0, 16, 0)
