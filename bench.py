@@ -67,6 +67,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-chain", action="store_true",
+                    help="skip the full decode step (BASELINE config 3)")
+    ap.add_argument("--chain-context", type=int, default=1024)
     ap.add_argument("--no-lm-head", action="store_true")
     ap.add_argument("--warm", action="store_true",
                     help="each decode GEMM prefetches the next projection's weights into L2")
@@ -410,6 +413,11 @@ def main():
     if not args.no_lm_head:
         lm_head = bench_lm_head(args, dev, gen, world, rank)
 
+    # ---- full decode step: every op between the GEMMs too
+    chain = None
+    if not args.no_chain:
+        chain = bench_decode_chain(args, dev, gen, world)
+
     # ---- prefill: W8A8, M = 256
     prefill = None
     if not args.no_prefill:
@@ -444,7 +452,8 @@ def main():
             "roofline": roofline,
             "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clk.summary(),
-            "e2e": e2e, "prefill": prefill, "lm_head": lm_head, "cpu_baseline": cpu,
+            "e2e": e2e, "prefill": prefill, "lm_head": lm_head, "decode_chain": chain,
+            "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -513,6 +522,141 @@ def bench_lm_head(args, dev, gen, world, rank):
                         f"that also stores its columns into every peer's logits over NVLink; "
                         f"nccl_*: the same GEMM followed by an NCCL all-gather (group-32 f32 "
                         f"scales are outside the fgm-kernels format)"}
+
+
+def bench_decode_chain(args, dev, gen, world):
+    """one decode step of a Gemma-E2B-shaped stack for 8
+    sequences -- 30 layers (hidden 2048, 8 query heads and 2 KV heads of
+    dim 256, MLP 8192), every projection int4 q4g, then the int4 LM head
+    (262144 x 2048) and the token choice -- with all the operations between
+    the GEMMs (forward.rs:469-654): norms, per-head q/k/v norms, rope, int8
+    KV-cache writes, the int8-KV attention over `--chain-context` positions,
+    gelu_mul, residual adds, final softcap.  Random-init weights, synthetic
+    caches; one CUDA graph per step.  Each rank runs its own 8 sequences."""
+    import torch
+    from fastgemma_b200 import _lib
+    from fastgemma_b200 import device as D
+    L, M, H, NH, KVH, HD, FF = 30, M_DECODE, 2048, 8, 2, 256, 8192
+    T = args.chain_context
+    KVD = KVH * HD
+    shapes = [("q", H, NH * HD), ("k", H, KVD), ("v", H, KVD), ("o", NH * HD, H),
+              ("gate", H, FF), ("up", H, FF), ("down", FF, H)]
+
+    def q4(k, n):
+        w = torch.randint(0, 256, (n * k // 2,), dtype=torch.uint8, device=dev, generator=gen)
+        s = torch.empty((k // GROUP, n), device=dev).uniform_(0.005, 0.02, generator=gen).half()
+        return w, s
+
+    def norm(n):
+        return torch.empty(n, device=dev).uniform_(0.5, 1.5, generator=gen)
+
+    layers = []
+    for _ in range(L):
+        lw = {name: q4(k, n) for name, k, n in shapes}
+        lw.update({nm: norm(n) for nm, n in (("in", H), ("qn", HD), ("kn", HD), ("pa", H),
+                                            ("pf", H), ("pff", H))})
+        vslots = (T + 3) // 4 * 4
+        lw["kc"] = torch.randint(-127, 128, (M, T, KVD), dtype=torch.int8, device=dev,
+                                 generator=gen)
+        lw["ks"] = torch.empty((M, T), device=dev).uniform_(0.001, 0.02, generator=gen)
+        lw["vt"] = torch.randint(-127, 128, (M, vslots * KVD), dtype=torch.int8, device=dev,
+                                 generator=gen)
+        lw["vs"] = torch.empty((M, T), device=dev).uniform_(0.001, 0.02, generator=gen)
+        layers.append(lw)
+    lm_w, lm_s = q4(H, LM_HEAD_N)
+    final_norm = norm(H)
+    inv_freq = (1.0 / (10000.0 ** (torch.arange(0, HD, 2, device=dev, dtype=torch.float32) / HD)))
+    pos = torch.full((M,), T - 1, dtype=torch.int32, device=dev)
+    x = torch.randn((M, H), device=dev, generator=gen)
+    f32 = lambda *shape: torch.empty(shape, device=dev)  # noqa: E731
+    h, q, k, v, attn, o = f32(M, H), f32(M, NH * HD), f32(M, KVD), f32(M, KVD), f32(M, NH * HD), \
+        f32(M, H)
+    gate, up, act, dn = f32(M, FF), f32(M, FF), f32(M, FF), f32(M, H)
+    logits = f32(M, LM_HEAD_N)
+    pa = {K: D.packed_a(M, K, dev) for K in (H, FF)}
+    qs = torch.empty(M, device=dev)
+    k8, v8 = (torch.empty((M, KVD), dtype=torch.int8, device=dev) for _ in range(2))
+    ksc, vsc = torch.empty(M, device=dev), torch.empty(M, device=dev)
+    parts = _lib.lib().fgm_cuda_argmax_parts(LM_HEAD_N)
+    avals = torch.empty((M, parts), device=dev)
+    aidx = torch.empty((M, parts), dtype=torch.int32, device=dev)
+    tok = torch.empty(M, dtype=torch.int32, device=dev)
+    slot = T - 1
+
+    def linear(src, K, N, wts, out):
+        D.prep_rows(src, K, qs, pa[K], M, K, 0)
+        D.gemm_q4g(M, N, K, pa[K], qs, wts[0], wts[1], GROUP, out)
+
+    def step():
+        for lw in layers:
+            D.rmsnorm(h, x, lw["in"], M, H, 1e-6)
+            D.prep_rows(h, H, qs, pa[H], M, H, 0)
+            for name, out in (("q", q), ("k", k), ("v", v)):
+                D.gemm_q4g(M, out.shape[1], H, pa[H], qs, lw[name][0], lw[name][1], GROUP, out)
+            D.rmsnorm(q, q, lw["qn"], M * NH, HD, 1e-6)
+            D.rmsnorm(k, k, lw["kn"], M * KVH, HD, 1e-6)
+            D.rmsnorm(v, v, None, M * KVH, HD, 1e-6)
+            D.rope(q, NH * HD, M, NH, HD, inv_freq, pos)
+            D.rope(k, KVD, M, KVH, HD, inv_freq, pos)
+            D.quant_act(k, M, KVD, k8, ksc)
+            D.quant_act(v, M, KVD, v8, vsc)
+            lw["kc"][:, slot, :].copy_(k8)
+            lw["ks"][:, slot].copy_(ksc)
+            D.store_v_t(lw["vt"], lw["vt"].shape[1], v8, KVD, M, KVD, slot)
+            lw["vs"][:, slot].copy_(vsc)
+            D.attend_q8(attn, NH * HD, q, NH * HD, lw["kc"], T * KVD, lw["ks"], T, lw["vt"],
+                        lw["vt"].shape[1], lw["vs"], T, M, NH, KVH, HD, 0, T)
+            linear(attn, NH * HD, H, lw["o"], o)
+            D.rmsnorm(o, o, lw["pa"], M, H, 1e-6)
+            D.add(x, o)
+            D.rmsnorm(h, x, lw["pf"], M, H, 1e-6)
+            D.prep_rows(h, H, qs, pa[H], M, H, 0)
+            D.gemm_q4g(M, FF, H, pa[H], qs, lw["gate"][0], lw["gate"][1], GROUP, gate)
+            D.gemm_q4g(M, FF, H, pa[H], qs, lw["up"][0], lw["up"][1], GROUP, up)
+            D.gelu_mul(act, gate, up, M, FF)
+            linear(act, FF, H, lw["down"], dn)
+            D.rmsnorm(dn, dn, lw["pff"], M, H, 1e-6)
+            D.add(x, dn)
+        D.rmsnorm(h, x, final_norm, M, H, 1e-6)
+        linear(h, H, LM_HEAD_N, (lm_w, lm_s), logits)
+        D.softcap(logits, M, LM_HEAD_N, 30.0)
+        _lib.call("fgm_cuda_argmax_partials", logits.data_ptr(), M, LM_HEAD_N, LM_HEAD_N, 0,
+                  avals.data_ptr(), aidx.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        _lib.call("fgm_cuda_argmax_merge", avals.data_ptr(), aidx.data_ptr(), M, parts,
+                  tok.data_ptr(), torch.cuda.current_stream().cuda_stream)
+
+    side = torch.cuda.Stream(device=dev)
+    lib = _lib.lib()
+    with torch.cuda.stream(side):
+        c0 = lib.fgm_cuda_launch_count()
+        step()
+        ours = lib.fgm_cuda_launch_count() - c0
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        step()
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            g.replay()
+    torch.cuda.synchronize()
+    steps = max(5, args.steps // 10)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(side):
+        e0.record(side)
+        for _ in range(steps):
+            g.replay()
+        e1.record(side)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
+    wbytes = L * sum(sum(q4g_bytes(k_, n_)) for _, k_, n_ in shapes) + sum(q4g_bytes(H, LM_HEAD_N))
+    del g
+    return {"value": world * M / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+            "weight_gbs": world * wbytes / (ms * 1e-3) / 1e9, "steps": steps,
+            "library_launches_per_step": ours, "context": T,
+            "workload": f"BASELINE config 3: 30 layers (hidden 2048, 8 q heads / 2 KV heads of "
+                        f"256, MLP 8192, int4 g64 projections), {M} sequences at context {T}, "
+                        f"norms, rope, int8 KV writes, int8-KV attention, gelu_mul, residuals, "
+                        f"int4 LM head 262144 x 2048, softcap, argmax; one CUDA graph per step"}
 
 
 def bench_prefill(args, dev, gen, world):

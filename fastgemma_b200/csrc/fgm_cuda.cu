@@ -1300,7 +1300,7 @@ int fgm_cuda_attend_q8(float *out, int out_ld, const float *q, int q_ld, const i
                        size_t kc_stride, const float *ks, size_t ks_stride, const int8_t *vt,
                        size_t vt_stride, const float *vs, size_t vs_stride, int rows, int n_heads,
                        int kv_heads, int head_dim, int start, int end, int ring, void *stream) {
-  if (rows < 0 || n_heads <= 0 || kv_heads <= 0 || n_heads % kv_heads != 0)
+  if (rows < 0 || rows > 65535 || n_heads <= 0 || kv_heads <= 0 || n_heads % kv_heads != 0)
     return fail(FGM_CUDA_EINVAL, "attend: rows=%d heads=%d kv_heads=%d", rows, n_heads, kv_heads);
   if (head_dim <= 0 || head_dim % 64 != 0 || head_dim > 512)
     return fail(FGM_CUDA_EINVAL, "attend: head_dim=%d (need a multiple of 64, at most 512)",
@@ -1336,9 +1336,14 @@ int fgm_cuda_attend_q8(float *out, int out_ld, const float *q, int q_ld, const i
   p.ring = ring;
   p.wbase = ring ? 0 : (start & ~3);
   p.wslots = ring ? ((ring + 3) & ~3) : (((end + 3) & ~3) - p.wbase);
-  if (attend_smem_bytes(p) + 2048 > di->smem_optin)
-    return fail(FGM_CUDA_EINVAL, "attend: %d positions need %zu bytes of shared memory", end - start,
-                attend_smem_bytes(p));
+  if ((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vt) | kc_stride | vt_stride) & 3)
+    return fail(FGM_CUDA_EINVAL, "attend: K / V caches and their row strides must be 4-byte aligned");
+  p.vec16 = ((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vt) | kc_stride |
+              vt_stride) & 15) == 0;
+  if (!attend_layout(p, di->smem_optin))
+    return fail(FGM_CUDA_EINVAL, "attend: %d positions, %d query heads per KV head, head_dim %d "
+                "do not fit in shared memory (at most 16 heads per KV head)", end - start,
+                n_heads / kv_heads, head_dim);
   return glue_done(launch_attend_q8(p, rows, use_pdl(), di->smem_optin, (cudaStream_t)stream),
                    "attend launch");
 }

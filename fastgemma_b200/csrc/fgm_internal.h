@@ -103,8 +103,18 @@ struct AttnParams {
   size_t kc_stride, ks_stride, vt_stride, vs_stride;  // per query row (elements)
   int n_heads, kv_heads, head_dim, start, end, ring;
   int wbase, wslots;      // cache slots [wbase, wbase + wslots) the window can touch
+  // set by attend_layout: a cluster of `cluster` CTAs per (row, KV head); CTA
+  // c owns the cache slot groups [c*gchunk, +gchunk) above wbase, scores them
+  // in stages of kp slots and multiplies them in stages of vg groups; the
+  // lane sums gather `win` positions at a time; 16-byte copies when vec16;
+  // vgp: V stage storage in groups (vg rounded up to whole 32-slot steps)
+  int cluster, gchunk, kp, vg, vgp, win, vec16;
+  unsigned off_ks, off_k, off_v, off_e, off_win, off_w, off_acc;  // shared memory layout (bytes)
+  size_t smem;
 };
-size_t attend_smem_bytes(const AttnParams &p);
+// Fills the cluster split and the shared memory layout; false when the
+// window does not fit in smem_limit bytes.
+bool attend_layout(AttnParams &p, size_t smem_limit);
 cudaError_t launch_attend_q8(const AttnParams &p, int rows, bool pdl, size_t smem_limit,
                              cudaStream_t st);
 // Copy two host regions (device-readable: page-locked or staging) into

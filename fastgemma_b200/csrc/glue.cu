@@ -13,15 +13,20 @@
 // softmax tail's expf) are evaluated in double precision and rounded once,
 // which agrees with a correctly rounded libm; they are checked to a tolerance.
 //
-// Attention (ops.c:378-640) is one CTA per (query row, head): the per-head
-// int8 quantisation of Q, exact int8 Q.K dot products (dp4a), the softmax
-// with the reference's lane order for the sum, the 16-bit split weights and
-// the exact P.V against the slot-interleaved V cache (dp4a, unsigned weight
-// bytes times signed V bytes).  Integer sums are exact in any order; every
-// float step follows the reference's order, so the output is bit-identical.
+// Attention (ops.c:378-640) is one cluster of CTAs per (query row, KV head),
+// split by cache slot: the per-head int8 quantisation of Q, exact int8 Q.K
+// dot products and the exact P.V against the slot-interleaved V cache
+// (signed V bytes times the unsigned bytes of the 16-bit split weights) on
+// the tensor cores, the softmax with the reference's lane order for the sum.
+// Integer sums are exact in any order; every float step follows the
+// reference's order, so the output is bit-identical.
+
+#include <cooperative_groups.h>
 
 #include "fgm_common.cuh"
 #include "fgm_internal.h"
+
+namespace cg = cooperative_groups;
 
 namespace fgm {
 
@@ -181,149 +186,413 @@ __global__ void store_v_t_kernel(int8_t *vt, size_t vt_stride, const int8_t *src
     dst[(size_t)j * 4] = src[(size_t)r * src_ld + j];
 }
 
-__device__ __forceinline__ int dp4a_ss(int a, int b, int c) {
-  int d;
-  asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
-
-// signed V bytes times unsigned weight bytes
-__device__ __forceinline__ int dp4a_su(int a, unsigned b, int c) {
-  int d;
-  asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
-
-__device__ __forceinline__ float block_max(float v, float *red) {
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float u = __shfl_xor_sync(0xffffffffu, v, o);
     v = u > v ? u : v;
   }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float m = red[0];
-  for (int w = 1; w < (int)(blockDim.x >> 5); w++) m = red[w] > m ? red[w] : m;
-  return m;
+  return v;
 }
 
-// ops.c:378-640, one (head, query row) per CTA.  Shared memory: the row's
-// scores [n], the slot-indexed weight bytes hi / lo [W] (W: cache slots that
-// can be touched, a multiple of 4), Q as int8.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// D += A(16x32 s8, row) * B(32x8 u8, col), int32 accumulate: signed V bytes
+// times unsigned weight bytes.
+__device__ __forceinline__ void mma_s8u8_m16n8k32(int32_t (&d)[4], uint32_t a0, uint32_t a1,
+                                                  uint32_t a2, uint32_t a3, uint32_t b0,
+                                                  uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t lds32(const void *p) {
+  return *reinterpret_cast<const uint32_t *>(p);
+}
+
+// ops.c:378-640 for one query row and one KV head with the G query heads
+// that share it, split over a cluster of C CTAs by cache slot: CTA `rank`
+// owns the slots [wbase + rank*cs, +cs) (cs = 4*gchunk, whole V groups) and
+// scores, exponentiates, weights and multiplies the window positions held
+// there.  Everything that needs a fixed order stays exact: the softmax max
+// and the weight max are order-free, every CTA runs the reference's 16 lane
+// sums over the whole window itself (gathering the other CTAs'
+// exponentials through distributed shared memory, window by window), and
+// the integer sums -- Q.K on the tensor cores (mma s8 x s8), P.V likewise
+// (s8 V x u8 weight bytes) -- meet by integer atomics in the CTA that owns
+// each output dimension.  Shared memory (offsets from the host): Q as int8
+// [GM][hd], K and V scales [cs], a K stage [kp][hd + 16], a V stage
+// [vgp][hd * 4 + 32] (slot-interleaved), the exponentials [GM][cs], the
+// gather window [GM][win], the stage's weight bytes [2 GM][vgp * 4 + 16]
+// (column 2h: high bytes of head h, 2h + 1: low bytes) and the int32
+// accumulators [2 GM][hd].  Row paddings keep the fragment loads free of
+// bank conflicts.
+template <int GM>
 __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParams p) {
+  constexpr int nt = kGlueThreads, nw = kGlueThreads / 32;
+  constexpr int kTiles = (512 / 16) * ((2 * GM + 7) / 8) / nw;  // P.V tiles per warp, at most
+  cg::cluster_group cluster = cg::this_cluster();
   extern __shared__ __align__(16) uint8_t sm[];
-  __shared__ float red[32];
-  __shared__ float lanes[16];
-  __shared__ float s_sum;
-  __shared__ __align__(16) int8_t qq[512];
+  __shared__ float s_qscale[GM], s_lmax[GM], s_mx[GM], s_inv[GM], s_lwmax[GM], s_wmax[GM],
+      s_wqs[GM], s_wqi[GM];
+  __shared__ float s_lanes[GM][16];
+  __shared__ float s_red[nw][GM];
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int h = blockIdx.x, r = blockIdx.y;
-  const int hd = p.head_dim, kvd = p.kv_heads * hd, kvh = h / (p.n_heads / p.kv_heads);
-  const int n = p.end - p.start, W = p.wslots;
-  float *sc = reinterpret_cast<float *>(sm);
-  uint8_t *whi = sm + (size_t)n * 4, *wlo = whi + W;
-  const float *qh = p.q + (size_t)r * p.q_ld + (size_t)h * hd;
-  const int8_t *kc = p.kc + (size_t)r * p.kc_stride;
+  const int G = p.n_heads / p.kv_heads, C = p.cluster;
+  const int rank = (int)cluster.block_rank();
+  const int kvh = blockIdx.x / C, r = blockIdx.y;
+  const int hd = p.head_dim, kvd = p.kv_heads * hd, n = p.end - p.start;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, gid = lane >> 2, tig = lane & 3;
+  const int cs = p.gchunk * 4, kld = hd + 16, vld = hd * 4 + 32, kp = p.kp, vg = p.vg;
+  const int wld = p.vgp * 4 + 16, win = p.win;
+  const int S0 = min(p.wbase + p.wslots, p.wbase + rank * cs);
+  const int ns = min(p.wbase + p.wslots, S0 + cs) - S0;  // a multiple of 4
+  const int tb = p.ring ? p.start - p.start % p.ring : 0;
+  int8_t *qq = reinterpret_cast<int8_t *>(sm);
+  float *ksm = reinterpret_cast<float *>(sm + p.off_ks);
+  float *vsm = ksm + cs;
+  int8_t *kst = reinterpret_cast<int8_t *>(sm + p.off_k);
+  int8_t *vst = reinterpret_cast<int8_t *>(sm + p.off_v);
+  float *ev = reinterpret_cast<float *>(sm + p.off_e);
+  float *wbuf = reinterpret_cast<float *>(sm + p.off_win);
+  uint8_t *wst = sm + p.off_w;
+  int *acc = reinterpret_cast<int *>(sm + p.off_acc);
+  const int8_t *kc = p.kc + (size_t)r * p.kc_stride + (size_t)kvh * hd;
   const float *ks = p.ks + (size_t)r * p.ks_stride;
-  const int8_t *vt = p.vt + (size_t)r * p.vt_stride;
+  const int8_t *vt = p.vt + (size_t)r * p.vt_stride + (size_t)kvh * hd * 4;
   const float *vs = p.vs + (size_t)r * p.vs_stride;
-  float *oh = p.out + (size_t)r * p.out_ld + (size_t)h * hd;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  const int full = n & ~15;
+
+  // window position held by cache slot s, or -1
+  auto pos_of = [&](int s) -> int {
+    if (p.ring) {
+      if (s >= p.ring) return -1;
+      int t = tb + s;
+      if (t < p.start) t += p.ring;
+      return t < p.end ? t - p.start : -1;
+    }
+    return (s >= p.start && s < p.end) ? s - p.start : -1;
+  };
+  const int wdt = p.vec16 ? 16 : 4;
+  auto load_k = [&](int sa, int sb) {  // this CTA's slots [sa, sb), rows of this KV head
+    const int per = hd / wdt, rpp = nt / per, piece = tid % per;
+    if (tid < rpp * per)
+      for (int j = sa + tid / per; j < sb; j += rpp) {
+        if (pos_of(S0 + j) < 0) continue;
+        int8_t *dst = kst + (j - sa) * kld + piece * wdt;
+        const int8_t *src = kc + (size_t)(S0 + j) * kvd + piece * wdt;
+        if (p.vec16)
+          cp_async16(dst, src);
+        else
+          cp_async4(dst, src);
+      }
+    cp_async_commit();
+  };
+  auto load_v = [&](int ga, int gb) {  // this CTA's slot groups [ga, gb)
+    const int per = hd * 4 / wdt;
+    const int8_t *src = vt + (size_t)(S0 / 4) * kvd * 4;
+    auto copy = [&](int g, int piece) {
+      int8_t *dst = vst + (g - ga) * vld + piece * wdt;
+      const int8_t *s = src + (size_t)g * kvd * 4 + piece * wdt;
+      if (p.vec16)
+        cp_async16(dst, s);
+      else
+        cp_async4(dst, s);
+    };
+    if (per <= nt) {
+      const int rpp = nt / per;
+      if (tid < rpp * per)
+        for (int g = ga + tid / per; g < gb; g += rpp) copy(g, tid % per);
+    } else {
+      for (int g = ga; g < gb; g++)
+        for (int piece = tid; piece < per; piece += nt) copy(g, piece);
+    }
+    cp_async_commit();
+  };
+
+  for (int i = tid; i < GM * 2 * hd; i += nt) acc[i] = 0;
+  for (int j = tid; j < ns; j += nt)
+    if (pos_of(S0 + j) >= 0) {
+      cp_async4(ksm + j, ks + S0 + j);
+      cp_async4(vsm + j, vs + S0 + j);
+    }
+  load_k(0, min(ns, kp));  // commits the scales with the first K stage
+  load_v(0, min(ns / 4, vg));
 
   // ---- Q per head: int8 with one scale (ops.c:412-431)
-  float a = 0.0f;
-  for (int i = tid; i < hd; i += blockDim.x) {
-    const float v = fabsf(qh[i]);
-    a = v > a ? v : a;
-  }
-  const float qamax = block_max(a, red);
-  const float qscale = __fdiv_rn(qamax, 127.0f);
-  const float qinv = qamax > 0.0f ? __fdiv_rn(127.0f, qamax) : 0.0f;
-  for (int i = tid; i < hd; i += blockDim.x) {
-    int v = __float2int_rn(__fmul_rn(qh[i], qinv));
-    qq[i] = (int8_t)(v > 127 ? 127 : (v < -127 ? -127 : v));
-  }
-  for (int i = tid; i < W; i += blockDim.x) whi[i] = wlo[i] = 0;
-  __syncthreads();
-
-  // ---- scores: one warp per position, exact int8 dot (ops.c:432-474)
-  const int words = hd / 4;
-  const int *q4 = reinterpret_cast<const int *>(qq);
-  float mloc = -INFINITY;
-  for (int t = p.start + warp; t < p.end; t += nw) {
-    const int sl = p.ring ? t % p.ring : t;
-    const int *kp = reinterpret_cast<const int *>(kc + (size_t)sl * kvd + (size_t)kvh * hd);
-    int dot = 0;
-    for (int wi = lane; wi < words; wi += 32) dot = dp4a_ss(kp[wi], q4[wi], dot);
-    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-    const float s = __fmul_rn(__fmul_rn((float)dot, qscale), ks[sl]);
-    if (lane == 0) sc[t - p.start] = s;
-    mloc = s > mloc ? s : mloc;
-  }
-  const float mx = block_max(mloc, red);
-
-  // ---- softmax: exp lanes over the 16-position chunks, libm on the tail;
-  // the sum in the reference's order (per lane, reduced, then the tail)
-  const int full = n & ~15;
-  for (int u = tid; u < n; u += blockDim.x) {
-    const float d = __fsub_rn(sc[u], mx);
-    sc[u] = u < full ? exp_lane(d) : (float)exp((double)d);
-  }
-  __syncthreads();
-  if (tid < 16) {
-    float l = 0.0f;
-    for (int u = tid; u < full; u += 16) l = __fadd_rn(l, sc[u]);
-    lanes[tid] = l;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    float sum = reduce16(lanes);
-    for (int u = full; u < n; u++) sum = __fadd_rn(sum, sc[u]);
-    s_sum = sum;
-  }
-  __syncthreads();
-  const float inv = __fdiv_rn(1.0f, s_sum);
-
-  // ---- weights w_t = e_t * inv * vs_t, quantised to 16 bits of their max
-  float wl = 0.0f;
-  for (int t = p.start + tid; t < p.end; t += blockDim.x) {
-    const float w = __fmul_rn(__fmul_rn(sc[t - p.start], inv), vs[p.ring ? t % p.ring : t]);
-    wl = w > wl ? w : wl;
-  }
-  const float wmax = block_max(wl, red);
-  if (!(wmax > 0.0f)) {
-    for (int i = tid; i < hd; i += blockDim.x) oh[i] = 0.0f;
-    return;
-  }
-  const float wq_scale = __fdiv_rn(wmax, 65535.0f), wq_inv = __fdiv_rn(65535.0f, wmax);
-  for (int t = p.start + tid; t < p.end; t += blockDim.x) {
-    const int sl = p.ring ? t % p.ring : t;
-    const float x = __fadd_rn(
-        __fmul_rn(__fmul_rn(__fmul_rn(sc[t - p.start], inv), vs[sl]), wq_inv), 0.5f);
-    int iw = (int)x;
-    iw = iw > 65535 ? 65535 : (iw < 0 ? 0 : iw);
-    whi[sl - p.wbase] = (uint8_t)(iw >> 8);
-    wlo[sl - p.wbase] = (uint8_t)(iw & 255);
-  }
-  __syncthreads();
-
-  // ---- P.V against the slot-interleaved V cache (ops.c:560-625): thread
-  // per dim, four slots per dp4a, exact int32 sums
-  const uint32_t *wh4 = reinterpret_cast<const uint32_t *>(whi);
-  const uint32_t *wl4 = reinterpret_cast<const uint32_t *>(wlo);
-  for (int i = tid; i < hd; i += blockDim.x) {
-    int ah = 0, al = 0;
-    for (int g = 0; g < W / 4; g++) {
-      const uint32_t bh = wh4[g], bl = wl4[g];
-      if ((bh | bl) == 0) continue;
-      const int v = *reinterpret_cast<const int *>(
-          vt + (((size_t)(p.wbase / 4 + g) * kvd + (size_t)kvh * hd + i) * 4));
-      ah = dp4a_su(v, bh, ah);
-      al = dp4a_su(v, bl, al);
+  for (int h = warp; h < G; h += nw) {
+    const float *qh = p.q + (size_t)r * p.q_ld + (size_t)(kvh * G + h) * hd;
+    float qv[16];
+    float a = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 16; k++) {
+      qv[k] = lane + 32 * k < hd ? qh[lane + 32 * k] : 0.0f;
+      const float v = fabsf(qv[k]);
+      a = v > a ? v : a;
     }
-    oh[i] = __fmul_rn((float)(int)(((uint32_t)ah << 8) + (uint32_t)al), wq_scale);
+    const float qamax = warp_max(a);
+    const float qinv = qamax > 0.0f ? __fdiv_rn(127.0f, qamax) : 0.0f;
+#pragma unroll
+    for (int k = 0; k < 16; k++)
+      if (lane + 32 * k < hd) {
+        const int v = __float2int_rn(__fmul_rn(qv[k], qinv));
+        qq[h * hd + lane + 32 * k] = (int8_t)(v > 127 ? 127 : (v < -127 ? -127 : v));
+      }
+    if (lane == 0) s_qscale[h] = __fdiv_rn(qamax, 127.0f);
+  }
+
+  // ---- scores: exact int8 dots (ops.c:432-474), slots x heads on the
+  // tensor cores; an empty slot scores -inf here and weighs 0 below
+  for (int sa = 0; sa < ns; sa += kp) {
+    const int sb = min(ns, sa + kp), rows = sb - sa;
+    if (sa) {
+      load_k(sa, sb);
+      cp_async_wait<0>();
+    } else {
+      cp_async_wait<1>();
+    }
+    __syncthreads();
+    const int mt = (rows + 15) >> 4, tiles = mt * ((G + 7) >> 3);
+    for (int tile = warp; tile < tiles; tile += nw) {
+      const int m0 = (tile % mt) * 16, n0 = (tile / mt) * 8;
+      const int8_t *ar = kst + (m0 + gid) * kld + tig * 4;
+      const int8_t *br = qq + min(n0 + gid, G - 1) * hd + tig * 4;
+      int32_t d[4] = {0, 0, 0, 0};
+      for (int kb = 0; kb < hd; kb += 32)
+        mma_s8_m16n8k32(d, lds32(ar + kb), lds32(ar + 8 * kld + kb), lds32(ar + kb + 16),
+                        lds32(ar + 8 * kld + kb + 16), lds32(br + kb), lds32(br + kb + 16));
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int row = m0 + gid + (e >> 1) * 8, h = n0 + 2 * tig + (e & 1), j = sa + row;
+        if (row < rows && h < G)
+          ev[h * cs + j] = pos_of(S0 + j) < 0
+                               ? -INFINITY
+                               : __fmul_rn(__fmul_rn((float)d[e], s_qscale[h]), ksm[j]);
+      }
+    }
+    __syncthreads();
+  }
+  for (int h = warp; h < G; h += nw) {
+    float m = -INFINITY;
+    for (int j = lane; j < ns; j += 32) {
+      const float v = ev[h * cs + j];
+      m = v > m ? v : m;
+    }
+    m = warp_max(m);
+    if (lane == 0) s_lmax[h] = m;
+  }
+  cluster.sync();
+  if (tid < G) {
+    float v[8];
+#pragma unroll
+    for (int c = 0; c < 8; c++) v[c] = c < C ? cluster.map_shared_rank(s_lmax, c)[tid] : -INFINITY;
+    float m = v[0];
+#pragma unroll
+    for (int c = 1; c < 8; c++) m = v[c] > m ? v[c] : m;
+    s_mx[tid] = m;
+  }
+  __syncthreads();
+
+  // ---- exponentials: the reference's exp lanes over the 16-position
+  // chunks, libm (here: double, rounded once) on the tail
+  for (int idx = tid; idx < G * ns; idx += nt) {
+    const int h = idx / ns, j = idx - h * ns;
+    const int u = pos_of(S0 + j);
+    float *e = ev + h * cs + j;
+    if (u < 0) {
+      *e = 0.0f;
+    } else {
+      const float d = __fsub_rn(*e, s_mx[h]);
+      *e = u < full ? exp_lane(d) : (float)exp((double)d);
+    }
+  }
+  cluster.sync();
+
+  // ---- the sum in the reference's order: 16 lanes over the full chunks,
+  // reduced, then the tail.  Windows of `win` positions (a multiple of 16)
+  // are gathered from the owning CTAs first.
+  {
+    float l = 0.0f;
+    const int h = tid >> 4, ln = tid & 15;
+    for (int w0 = 0; w0 < n; w0 += win) {
+      const int wn = min(n, w0 + win) - w0;
+      int s0 = p.start + w0;
+      if (p.ring) s0 %= p.ring;
+      s0 -= p.wbase;
+      __syncthreads();
+      for (int i0 = 0; i0 < wn; i0 += 2 * nt) {
+        float v[2][GM];
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+          const int i = i0 + k * nt + tid;
+          if (i < wn) {
+            int s = s0 + i;
+            if (p.ring && s >= p.ring) s -= p.ring;
+            const int c = s / cs;
+            const float *pe = cluster.map_shared_rank(ev, c) + (s - c * cs);
+#pragma unroll
+            for (int hh = 0; hh < GM; hh++) v[k][hh] = hh < G ? pe[hh * cs] : 0.0f;
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+          const int i = i0 + k * nt + tid;
+          if (i < wn)
+#pragma unroll
+            for (int hh = 0; hh < GM; hh++)
+              if (hh < G) wbuf[hh * win + i] = v[k][hh];
+        }
+      }
+      __syncthreads();
+      if (tid < G * 16)
+        for (int u = w0 + ln; u < min(w0 + wn, full); u += 16)
+          l = __fadd_rn(l, wbuf[h * win + u - w0]);
+    }
+    if (tid < G * 16) s_lanes[h][ln] = l;
+    __syncthreads();
+    if (tid < G) {
+      const int wl = ((n - 1) / win) * win;  // the last window holds the tail
+      float sum = reduce16(s_lanes[tid]);
+      for (int u = full; u < n; u++) sum = __fadd_rn(sum, wbuf[tid * win + u - wl]);
+      s_inv[tid] = __fdiv_rn(1.0f, sum);
+    }
+    __syncthreads();
+  }
+
+  // ---- weights w_t = e_t * inv * vs_t: their max per head over the window
+  {
+    float wl[GM];
+#pragma unroll
+    for (int h = 0; h < GM; h++) wl[h] = 0.0f;
+    for (int j = tid; j < ns; j += nt) {
+      if (pos_of(S0 + j) < 0) continue;
+      const float vsv = vsm[j];
+#pragma unroll
+      for (int h = 0; h < GM; h++)
+        if (h < G) {
+          const float w = __fmul_rn(__fmul_rn(ev[h * cs + j], s_inv[h]), vsv);
+          wl[h] = w > wl[h] ? w : wl[h];
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < GM; h++) wl[h] = warp_max(wl[h]);
+    if (lane == 0)
+#pragma unroll
+      for (int h = 0; h < GM; h++) s_red[warp][h] = wl[h];
+  }
+  __syncthreads();
+  if (tid < G) {
+    float m = s_red[0][tid];
+    for (int w = 1; w < nw; w++) m = s_red[w][tid] > m ? s_red[w][tid] : m;
+    s_lwmax[tid] = m;
+  }
+  cluster.sync();
+  if (tid < G) {
+    float v[8];
+#pragma unroll
+    for (int c = 0; c < 8; c++) v[c] = c < C ? cluster.map_shared_rank(s_lwmax, c)[tid] : 0.0f;
+    float m = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 8; c++) m = v[c] > m ? v[c] : m;
+    s_wmax[tid] = m;
+    s_wqs[tid] = __fdiv_rn(m, 65535.0f);
+    s_wqi[tid] = m > 0.0f ? __fdiv_rn(65535.0f, m) : 0.0f;
+  }
+  __syncthreads();
+
+  // ---- P.V over this CTA's slot groups (ops.c:560-625): weights quantised
+  // to 16 bits of their max, split in hi / lo bytes; dims x (head, hi / lo)
+  // on the tensor cores, 32 slots per step, exact int32 sums
+  const int pm = hd >> 4, ptiles = pm * ((2 * G + 7) >> 3);
+  int32_t pacc[kTiles][4];
+#pragma unroll
+  for (int q = 0; q < kTiles; q++) pacc[q][0] = pacc[q][1] = pacc[q][2] = pacc[q][3] = 0;
+  for (int ga = 0; ga < ns / 4; ga += vg) {
+    const int gb = min(ns / 4, ga + vg), nsl = (gb - ga) * 4, kpad = (nsl + 31) & ~31;
+    if (ga) {
+      __syncthreads();
+      load_v(ga, gb);
+    }
+    for (int j = tid; j < kpad; j += nt) {
+      const int js = ga * 4 + j;
+      const bool live = j < nsl && pos_of(S0 + js) >= 0;
+#pragma unroll
+      for (int h = 0; h < GM; h++)
+        if (h < G) {
+          int iw = 0;
+          if (live && s_wmax[h] > 0.0f) {
+            const float x = __fadd_rn(
+                __fmul_rn(__fmul_rn(__fmul_rn(ev[h * cs + js], s_inv[h]), vsm[js]), s_wqi[h]),
+                0.5f);
+            iw = (int)x;
+            iw = iw > 65535 ? 65535 : (iw < 0 ? 0 : iw);
+          }
+          wst[(2 * h) * wld + j] = (uint8_t)(iw >> 8);
+          wst[(2 * h + 1) * wld + j] = (uint8_t)(iw & 255);
+        }
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < kTiles; q++) {
+      const int tile = warp + q * nw;
+      if (tile < ptiles) {
+        const int m0 = (tile % pm) * 16, n0 = (tile / pm) * 8;
+        const int8_t *ar = vst + tig * vld + (m0 + gid) * 4;
+        const uint8_t *br = wst + min(n0 + gid, 2 * G - 1) * wld + tig * 4;
+        for (int kb = 0; kb < kpad; kb += 32) {
+          const int8_t *a = ar + (kb >> 2) * vld;
+          mma_s8u8_m16n8k32(pacc[q], lds32(a), lds32(a + 32), lds32(a + 4 * vld),
+                            lds32(a + 4 * vld + 32), lds32(br + kb), lds32(br + kb + 16));
+        }
+      }
+    }
+  }
+  // integer sums meet in the CTA that owns the dimension
+  const int dper = hd / C;
+#pragma unroll
+  for (int q = 0; q < kTiles; q++) {
+    const int tile = warp + q * nw;
+    if (tile < ptiles) {
+      const int m0 = (tile % pm) * 16, n0 = (tile / pm) * 8;
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int i = m0 + gid + (e >> 1) * 8, col = n0 + 2 * tig + (e & 1);
+        if (col < 2 * G && pacc[q][e])
+          atomicAdd(cluster.map_shared_rank(acc, i / dper) + col * hd + i, pacc[q][e]);
+      }
+    }
+  }
+  cluster.sync();
+  for (int idx = tid; idx < G * dper; idx += nt) {
+    const int h = idx / dper, i = rank * dper + (idx - h * dper);
+    float o = 0.0f;
+    if (s_wmax[h] > 0.0f)
+      o = __fmul_rn((float)(int)(((uint32_t)acc[(2 * h) * hd + i] << 8) +
+                                 (uint32_t)acc[(2 * h + 1) * hd + i]),
+                    s_wqs[h]);
+    p.out[(size_t)r * p.out_ld + (size_t)(kvh * G + h) * hd + i] = o;
   }
 }
 
@@ -396,18 +665,89 @@ cudaError_t launch_store_v_t(int8_t *vt, size_t vt_stride, const int8_t *src, in
                     vt_stride, src, src_ld, n, slot);
 }
 
-size_t attend_smem_bytes(const AttnParams &p) {
-  return (size_t)(p.end - p.start) * 4 + 2 * (size_t)p.wslots;
+namespace {
+
+unsigned align16(size_t x) { return (unsigned)((x + 15) & ~(size_t)15); }
+
+int gm_of(const AttnParams &p) {
+  const int g = p.n_heads / p.kv_heads;
+  int gm = 1;
+  while (gm < g) gm <<= 1;
+  return gm;
+}
+
+template <int GM>
+cudaError_t launch_attend_gm(const AttnParams &p, int rows, bool pdl, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(attend_q8_kernel<GM>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(p.cluster * p.kv_heads), (unsigned)rows);
+  cfg.blockDim = dim3(kGlueThreads);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)p.cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, attend_q8_kernel<GM>, p);
+}
+
+}  // namespace
+
+bool attend_layout(AttnParams &p, size_t smem_limit) {
+  const int n = p.end - p.start, hd = p.head_dim, gm = gm_of(p);
+  if (gm > 16) return false;
+  int c = 1;
+  while (c < 8 && n >= 64 * c) c <<= 1;  // about 32 positions or more per CTA
+  p.cluster = c;
+  p.gchunk = (p.wslots / 4 + c - 1) / c;
+  const int cs = 4 * p.gchunk;
+  p.win = (4096 / gm) & ~15;
+  if (p.win > ((n + 15) & ~15)) p.win = (n + 15) & ~15;
+  const size_t kld = (size_t)hd + 16, vld = (size_t)hd * 4 + 32;
+  const size_t fixed = align16((size_t)gm * hd) + align16((size_t)2 * cs * 4) +
+                       align16((size_t)gm * cs * 4) + align16((size_t)gm * p.win * 4) +
+                       (size_t)gm * 2 * hd * 4 + 4096;  // + static shared memory
+  // smallest stages: 16 K rows, 8 V groups with their weight bytes
+  const size_t kv_min = 16 * kld + 8 * vld + 2 * (size_t)gm * (32 + 16);
+  if (fixed + kv_min > smem_limit) return false;
+  const size_t stage = (smem_limit - fixed) / 2 < 65536 ? (smem_limit - fixed) / 2 : 65536;
+  p.kp = (int)(stage / kld) & ~15;
+  if (p.kp > ((cs + 15) & ~15)) p.kp = (cs + 15) & ~15;
+  if (p.kp > kGlueThreads) p.kp = kGlueThreads;
+  if (p.kp < 16) p.kp = 16;
+  p.vg = (int)(stage / (vld + 2 * (size_t)gm * 4)) & ~7;
+  if (p.vg > p.gchunk) p.vg = p.gchunk;
+  if (p.vg < 1) p.vg = 1;
+  p.vgp = (p.vg + 7) & ~7;
+  p.off_ks = align16((size_t)gm * hd);
+  p.off_k = p.off_ks + align16((size_t)2 * cs * 4);
+  p.off_v = p.off_k + align16((size_t)p.kp * kld);
+  p.off_e = p.off_v + align16((size_t)p.vgp * vld);
+  p.off_win = p.off_e + align16((size_t)gm * cs * 4);
+  p.off_w = p.off_win + align16((size_t)gm * p.win * 4);
+  p.off_acc = p.off_w + align16((size_t)2 * gm * (p.vgp * 4 + 16));
+  p.smem = p.off_acc + (size_t)gm * 2 * hd * 4;
+  return p.smem + 4096 <= smem_limit;
 }
 
 cudaError_t launch_attend_q8(const AttnParams &p, int rows, bool pdl, size_t smem_limit,
                              cudaStream_t st) {
-  const size_t smem = attend_smem_bytes(p);
-  if (smem + 2048 > smem_limit) return cudaErrorInvalidConfiguration;
-  cudaError_t e = cudaFuncSetAttribute(attend_q8_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  return launch_pdl(attend_q8_kernel, dim3(p.n_heads, rows), dim3(kGlueThreads), smem, pdl, st, p);
+  if (p.smem + 4096 > smem_limit) return cudaErrorInvalidConfiguration;
+  switch (gm_of(p)) {
+    case 1: return launch_attend_gm<1>(p, rows, pdl, st);
+    case 2: return launch_attend_gm<2>(p, rows, pdl, st);
+    case 4: return launch_attend_gm<4>(p, rows, pdl, st);
+    case 8: return launch_attend_gm<8>(p, rows, pdl, st);
+    case 16: return launch_attend_gm<16>(p, rows, pdl, st);
+    default: return cudaErrorInvalidConfiguration;
+  }
 }
 
 }  // namespace fgm

@@ -138,6 +138,47 @@ def test_attention_rows_against_oracle(orc, end, start, ring, hd):
     same(out.cpu().numpy(), want, (end - start) % 16 == 0, f"attend [{start},{end}) ring={ring}")
 
 
+@pytest.mark.parametrize("nh,kvh,hd,end,start,ring", [(2, 2, 256, 300, 0, 0), (8, 1, 128, 520, 7, 0),
+                                                      (6, 2, 192, 200, 0, 0), (16, 1, 64, 96, 0, 0),
+                                                      (8, 2, 512, 8192, 0, 0),
+                                                      (4, 2, 256, 1100, 900, 512)])
+def test_attention_head_groups_and_long_windows(orc, nh, kvh, hd, end, start, ring):
+    """Query heads per KV head 1, 8, 3 and 16, and windows long enough to
+    stream the K and V caches through several shared-memory stages."""
+    rng = np.random.default_rng(nh * 131 + hd + end)
+    rows = 2
+    cap = ring or end
+    kc, ks, vt, vs = _caches(orc, rng, rows, cap, kvh, hd)
+    q = (rng.standard_normal((rows, nh * hd)) * 2).astype(np.float32)
+    out = torch.full((rows, nh * hd), float("nan"), device="cuda")
+    D.attend_q8(out, nh * hd, dev(q), nh * hd, dev(kc), cap * kvh * hd, dev(ks), cap, dev(vt),
+                vt.shape[1], dev(vs), cap, rows, nh, kvh, hd, start, end, ring)
+    torch.cuda.synchronize()
+    want = np.stack([orc.attend_q8(q[r], kc[r], ks[r], vt[r], vs[r], nh, kvh, hd, start, end, ring)
+                     for r in range(rows)])
+    same(out.cpu().numpy(), want, (end - start) % 16 == 0, f"attend G={nh // kvh} hd={hd}")
+
+
+def test_attention_caches_on_4_byte_boundaries(orc):
+    """K and V caches that start 4 bytes past a 16-byte boundary take the
+    4-byte copy path and give the same bits."""
+    rng = np.random.default_rng(7)
+    rows, nh, kvh, hd, n = 2, 8, 2, 256, 160
+    kc, ks, vt, vs = _caches(orc, rng, rows, n, kvh, hd)
+    kbuf = torch.zeros(kc.size + 16, dtype=torch.int8, device="cuda")
+    vbuf = torch.zeros(vt.size + 16, dtype=torch.int8, device="cuda")
+    kbuf[4:4 + kc.size] = dev(kc.reshape(-1))
+    vbuf[4:4 + vt.size] = dev(vt.reshape(-1))
+    q = (rng.standard_normal((rows, nh * hd)) * 2).astype(np.float32)
+    out = torch.full((rows, nh * hd), float("nan"), device="cuda")
+    D.attend_q8(out, nh * hd, dev(q), nh * hd, kbuf[4:], n * kvh * hd, dev(ks), n, vbuf[4:],
+                vt.shape[1], dev(vs), n, rows, nh, kvh, hd, 0, n, 0)
+    torch.cuda.synchronize()
+    want = np.stack([orc.attend_q8(q[r], kc[r], ks[r], vt[r], vs[r], nh, kvh, hd, 0, n, 0)
+                     for r in range(rows)])
+    same(out.cpu().numpy(), want, True, "attend, 4-byte aligned caches")
+
+
 def test_attention_rejects_bad_windows():
     from fastgemma_b200 import _lib
     z = torch.zeros(4096, device="cuda")
@@ -146,3 +187,7 @@ def test_attention_rejects_bad_windows():
         D.attend_q8(z, 256, z, 256, zi, 0, z, 0, zi, 0, z, 0, 1, 1, 1, 256, 0, 200, 128)
     with pytest.raises(_lib.FgmCudaError, match="head_dim"):
         D.attend_q8(z, 256, z, 256, zi, 0, z, 0, zi, 0, z, 0, 1, 1, 1, 96, 0, 16, 0)
+    with pytest.raises(_lib.FgmCudaError, match="aligned"):
+        D.attend_q8(z, 256, z, 256, zi[1:], 0, z, 0, zi, 0, z, 0, 1, 1, 1, 256, 0, 16, 0)
+    with pytest.raises(_lib.FgmCudaError, match="fit"):
+        D.attend_q8(z, 4096, z, 4096, zi, 0, z, 0, zi, 0, z, 0, 1, 32, 1, 64, 0, 16, 0)
