@@ -524,23 +524,19 @@ def bench_lm_head(args, dev, gen, world, rank):
                         f"scales are outside the fgm-kernels format)"}
 
 
-def bench_decode_chain(args, dev, gen, world):
-    """BASELINE config 3: one decode step of a Gemma-E2B-shaped stack for 8
-    sequences -- 30 layers (hidden 2048, 8 query heads and 2 KV heads of
-    dim 256, MLP 8192), every projection int4 q4g, then the int4 LM head
-    (262144 x 2048) and the token choice -- with all the operations between
-    the GEMMs (forward.rs:469-654): norms, per-head q/k/v norms, rope, int8
-    KV-cache writes, the int8-KV attention over `--chain-context` positions,
-    gelu_mul, residual adds, final softcap.  Random-init weights, synthetic
-    caches; one CUDA graph per step.  Each rank runs its own 8 sequences."""
+def build_decode_chain(dev, gen, T, L=30):
+    """The synthetic config-3 stack on `dev` (random-init weights and caches)
+    and its decode step; returns (step, weight bytes per step)."""
     import torch
     from fastgemma_b200 import _lib
     from fastgemma_b200 import device as D
-    L, M, H, NH, KVH, HD, FF = 30, M_DECODE, 2048, 8, 2, 256, 8192
-    T = args.chain_context
+    M, H, NH, KVH, HD, FF = M_DECODE, 2048, 8, 2, 256, 8192
     KVD = KVH * HD
-    shapes = [("q", H, NH * HD), ("k", H, KVD), ("v", H, KVD), ("o", NH * HD, H),
-              ("gate", H, FF), ("up", H, FF), ("down", FF, H)]
+    # k and v as one [k | v] weight, gate and up as one [gate | up] weight:
+    # config 1's projection shapes; each blob is the two weights' n-blocks
+    # back to back, so a loader builds it by concatenation
+    shapes = [("q", H, NH * HD), ("kv", H, 2 * KVD), ("o", NH * HD, H), ("gate_up", H, 2 * FF),
+              ("down", FF, H)]
 
     def q4(k, n):
         w = torch.randint(0, 256, (n * k // 2,), dtype=torch.uint8, device=dev, generator=gen)
@@ -569,62 +565,64 @@ def bench_decode_chain(args, dev, gen, world):
     pos = torch.full((M,), T - 1, dtype=torch.int32, device=dev)
     x = torch.randn((M, H), device=dev, generator=gen)
     f32 = lambda *shape: torch.empty(shape, device=dev)  # noqa: E731
-    h, q, k, v, attn, o = f32(M, H), f32(M, NH * HD), f32(M, KVD), f32(M, KVD), f32(M, NH * HD), \
-        f32(M, H)
-    gate, up, act, dn = f32(M, FF), f32(M, FF), f32(M, FF), f32(M, H)
+    q, kv, attn, o = f32(M, NH * HD), f32(M, 2 * KVD), f32(M, NH * HD), f32(M, H)
+    gu, dn = f32(M, 2 * FF), f32(M, H)
     logits = f32(M, LM_HEAD_N)
     pa = {K: D.packed_a(M, K, dev) for K in (H, FF)}
     qs = torch.empty(M, device=dev)
-    k8, v8 = (torch.empty((M, KVD), dtype=torch.int8, device=dev) for _ in range(2))
-    ksc, vsc = torch.empty(M, device=dev), torch.empty(M, device=dev)
     parts = _lib.lib().fgm_cuda_argmax_parts(LM_HEAD_N)
     avals = torch.empty((M, parts), device=dev)
     aidx = torch.empty((M, parts), dtype=torch.int32, device=dev)
     tok = torch.empty(M, dtype=torch.int32, device=dev)
-    slot = T - 1
 
-    def linear(src, K, N, wts, out):
-        D.prep_rows(src, K, qs, pa[K], M, K, 0)
-        D.gemm_q4g(M, N, K, pa[K], qs, wts[0], wts[1], GROUP, out)
+    x0 = x.clone()
+    stream = lambda: torch.cuda.current_stream().cuda_stream  # noqa: E731
 
     def step():
-        for lw in layers:
-            D.rmsnorm(h, x, lw["in"], M, H, 1e-6)
-            D.prep_rows(h, H, qs, pa[H], M, H, 0)
-            for name, out in (("q", q), ("k", k), ("v", v)):
-                D.gemm_q4g(M, out.shape[1], H, pa[H], qs, lw[name][0], lw[name][1], GROUP, out)
-            D.rmsnorm(q, q, lw["qn"], M * NH, HD, 1e-6)
-            D.rmsnorm(k, k, lw["kn"], M * KVH, HD, 1e-6)
-            D.rmsnorm(v, v, None, M * KVH, HD, 1e-6)
-            D.rope(q, NH * HD, M, NH, HD, inv_freq, pos)
-            D.rope(k, KVD, M, KVH, HD, inv_freq, pos)
-            D.quant_act(k, M, KVD, k8, ksc)
-            D.quant_act(v, M, KVD, v8, vsc)
-            lw["kc"][:, slot, :].copy_(k8)
-            lw["ks"][:, slot].copy_(ksc)
-            D.store_v_t(lw["vt"], lw["vt"].shape[1], v8, KVD, M, KVD, slot)
-            lw["vs"][:, slot].copy_(vsc)
+        # glue between the GEMMs runs fused per row: norm_prep = (post-norm,
+        # residual add,) pre-norm and prep; qkv_post = head norms, rope and
+        # the int8 K / V cache writes; gelu_mul_prep = activation and prep
+        x.copy_(x0)  # stands in for the embedding gather
+        D.norm_prep(x, None, None, layers[0]["in"], M, H, 1e-6, qs, pa[H])
+        for li, lw in enumerate(layers):
+            D.gemm_q4g(M, NH * HD, H, pa[H], qs, lw["q"][0], lw["q"][1], GROUP, q)
+            D.gemm_q4g(M, 2 * KVD, H, pa[H], qs, lw["kv"][0], lw["kv"][1], GROUP, kv)
+            D.qkv_post(q, kv, kv[:, KVD:], M, NH, KVH, HD, lw["qn"], lw["kn"], 1e-6, inv_freq, pos,
+                       0, lw["kc"], T * KVD, lw["ks"], T, lw["vt"], lw["vt"].shape[1], lw["vs"], T,
+                       kv_ld=2 * KVD)
             D.attend_q8(attn, NH * HD, q, NH * HD, lw["kc"], T * KVD, lw["ks"], T, lw["vt"],
                         lw["vt"].shape[1], lw["vs"], T, M, NH, KVH, HD, 0, T)
-            linear(attn, NH * HD, H, lw["o"], o)
-            D.rmsnorm(o, o, lw["pa"], M, H, 1e-6)
-            D.add(x, o)
-            D.rmsnorm(h, x, lw["pf"], M, H, 1e-6)
-            D.prep_rows(h, H, qs, pa[H], M, H, 0)
-            D.gemm_q4g(M, FF, H, pa[H], qs, lw["gate"][0], lw["gate"][1], GROUP, gate)
-            D.gemm_q4g(M, FF, H, pa[H], qs, lw["up"][0], lw["up"][1], GROUP, up)
-            D.gelu_mul(act, gate, up, M, FF)
-            linear(act, FF, H, lw["down"], dn)
-            D.rmsnorm(dn, dn, lw["pff"], M, H, 1e-6)
-            D.add(x, dn)
-        D.rmsnorm(h, x, final_norm, M, H, 1e-6)
-        linear(h, H, LM_HEAD_N, (lm_w, lm_s), logits)
+            D.prep_rows(attn, NH * HD, qs, pa[H], M, NH * HD, 0)
+            D.gemm_q4g(M, H, NH * HD, pa[H], qs, lw["o"][0], lw["o"][1], GROUP, o)
+            D.norm_prep(x, o, lw["pa"], lw["pf"], M, H, 1e-6, qs, pa[H])
+            D.gemm_q4g(M, 2 * FF, H, pa[H], qs, lw["gate_up"][0], lw["gate_up"][1], GROUP, gu)
+            D.gelu_mul_prep(gu, gu[:, FF:], M, FF, qs, pa[FF], ld=2 * FF)
+            D.gemm_q4g(M, H, FF, pa[FF], qs, lw["down"][0], lw["down"][1], GROUP, dn)
+            nxt = layers[li + 1]["in"] if li + 1 < L else final_norm
+            D.norm_prep(x, dn, lw["pff"], nxt, M, H, 1e-6, qs, pa[H])
+        D.gemm_q4g(M, LM_HEAD_N, H, pa[H], qs, lm_w, lm_s, GROUP, logits)
         D.softcap(logits, M, LM_HEAD_N, 30.0)
         _lib.call("fgm_cuda_argmax_partials", logits.data_ptr(), M, LM_HEAD_N, LM_HEAD_N, 0,
-                  avals.data_ptr(), aidx.data_ptr(), torch.cuda.current_stream().cuda_stream)
+                  avals.data_ptr(), aidx.data_ptr(), stream())
         _lib.call("fgm_cuda_argmax_merge", avals.data_ptr(), aidx.data_ptr(), M, parts,
-                  tok.data_ptr(), torch.cuda.current_stream().cuda_stream)
+                  tok.data_ptr(), stream())
+    wbytes = L * sum(sum(q4g_bytes(k_, n_)) for _, k_, n_ in shapes) + sum(q4g_bytes(H, LM_HEAD_N))
+    return step, wbytes
 
+
+def bench_decode_chain(args, dev, gen, world):
+    """BASELINE config 3: one decode step of a Gemma-E2B-shaped stack for 8
+    sequences -- 30 layers (hidden 2048, 8 query heads and 2 KV heads of
+    dim 256, MLP 8192), every projection int4 q4g, then the int4 LM head
+    (262144 x 2048) and the token choice -- with all the operations between
+    the GEMMs (forward.rs:469-654): norms, per-head q/k/v norms, rope, int8
+    KV-cache writes, the int8-KV attention over `--chain-context` positions,
+    gelu_mul, residual adds, final softcap.  Random-init weights, synthetic
+    caches; one CUDA graph per step.  Each rank runs its own 8 sequences."""
+    import torch
+    from fastgemma_b200 import _lib
+    L, M, T = 30, M_DECODE, args.chain_context
+    step, wbytes = build_decode_chain(dev, gen, T, L)
     side = torch.cuda.Stream(device=dev)
     lib = _lib.lib()
     with torch.cuda.stream(side):
@@ -648,7 +646,6 @@ def bench_decode_chain(args, dev, gen, world):
         e1.record(side)
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
-    wbytes = L * sum(sum(q4g_bytes(k_, n_)) for _, k_, n_ in shapes) + sum(q4g_bytes(H, LM_HEAD_N))
     del g
     return {"value": world * M / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
             "weight_gbs": world * wbytes / (ms * 1e-3) / 1e9, "steps": steps,
@@ -656,7 +653,9 @@ def bench_decode_chain(args, dev, gen, world):
             "workload": f"BASELINE config 3: 30 layers (hidden 2048, 8 q heads / 2 KV heads of "
                         f"256, MLP 8192, int4 g64 projections), {M} sequences at context {T}, "
                         f"norms, rope, int8 KV writes, int8-KV attention, gelu_mul, residuals, "
-                        f"int4 LM head 262144 x 2048, softcap, argmax; one CUDA graph per step"}
+                        f"int4 LM head 262144 x 2048, softcap, argmax; k|v and gate|up as one "
+                        f"weight each, the glue between GEMMs fused per row; one CUDA graph per "
+                        f"step"}
 
 
 def bench_prefill(args, dev, gen, world):

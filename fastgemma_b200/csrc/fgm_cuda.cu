@@ -1348,6 +1348,64 @@ int fgm_cuda_attend_q8(float *out, int out_ld, const float *q, int q_ld, const i
                    "attend launch");
 }
 
+int fgm_cuda_norm_prep(float *h, const float *proj, const float *w_post, const float *w_pre,
+                       int rows, int n, float eps, float *qs, int8_t *pa, void *stream) {
+  if (rows < 0 || n <= 0 || n % 64 != 0 || n > 49152)
+    return fail(FGM_CUDA_EINVAL, "norm_prep: rows=%d n=%d (need n %% 64 == 0, n <= 49152)", rows,
+                n);
+  if (rows == 0) return FGM_CUDA_OK;
+  if (!h || !qs || !pa) return fail(FGM_CUDA_EINVAL, "null pointer");
+  if ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(proj)) & 15)
+    return fail(FGM_CUDA_EINVAL, "norm_prep: h and proj must be 16-byte aligned");
+  return glue_done(launch_norm_prep(h, proj, w_post, w_pre, rows, n, eps, qs, pa, use_pdl(),
+                                    (cudaStream_t)stream),
+                   "norm_prep launch");
+}
+
+int fgm_cuda_gelu_mul_prep(const float *gate, const float *up, int ld, int rows, int n,
+                           float *act, float *qs, int8_t *pa, void *stream) {
+  if (rows < 0 || rows > 65520 || n <= 0 || n % 64 != 0 || n > 49152 || ld < n || ld % 4 != 0)
+    return fail(FGM_CUDA_EINVAL,
+                "gelu_mul_prep: rows=%d n=%d ld=%d (need n %% 64 == 0, n <= 49152, ld >= n, "
+                "ld %% 4 == 0)", rows, n, ld);
+  if (rows == 0) return FGM_CUDA_OK;
+  if (!gate || !up || !qs || !pa) return fail(FGM_CUDA_EINVAL, "null pointer");
+  if ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) |
+       reinterpret_cast<uintptr_t>(act)) & 15)
+    return fail(FGM_CUDA_EINVAL, "gelu_mul_prep: gate, up and act must be 16-byte aligned");
+  return glue_done(
+      launch_gelu_mul_prep(gate, up, ld, rows, n, act, qs, pa, use_pdl(), (cudaStream_t)stream),
+      "gelu_mul_prep launch");
+}
+
+int fgm_cuda_qkv_post(float *q, int q_ld, float *k, float *v, int kv_ld, int rows, int n_heads,
+                      int kv_heads, int head_dim, const float *q_norm, const float *k_norm, float eps,
+                      const float *inv_freq, const int *pos, int ring, int8_t *kc,
+                      size_t kc_stride, float *ks, size_t ks_stride, int8_t *vt, size_t vt_stride,
+                      float *vs, size_t vs_stride, void *stream) {
+  if (rows < 0 || n_heads <= 0 || kv_heads <= 0 || n_heads + 2 * kv_heads > 48 ||
+      head_dim <= 0 || head_dim % 4 != 0 || ring < 0 || q_ld < n_heads * head_dim ||
+      kv_ld < kv_heads * head_dim || q_ld % 4 != 0 || kv_ld % 4 != 0)
+    return fail(FGM_CUDA_EINVAL,
+                "qkv_post: rows=%d heads=%d kv_heads=%d head_dim=%d ring=%d q_ld=%d kv_ld=%d",
+                rows, n_heads, kv_heads, head_dim, ring, q_ld, kv_ld);
+  if (rows == 0) return FGM_CUDA_OK;
+  if (!q || !k || !v || !q_norm || !k_norm || !inv_freq || !pos || !kc || !ks || !vt || !vs)
+    return fail(FGM_CUDA_EINVAL, "null pointer");
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+       reinterpret_cast<uintptr_t>(v)) & 15)
+    return fail(FGM_CUDA_EINVAL, "qkv_post: q, k and v must be 16-byte aligned");
+  DevInfo *di = nullptr;
+  int rc = dev_info(&di);
+  if (rc) return rc;
+  QkvParams p{q, k, v, q_ld, kv_ld, n_heads, kv_heads, head_dim, q_norm, k_norm, eps, inv_freq,
+              pos, ring, kc, ks, vt, vs, kc_stride, ks_stride, vt_stride, vs_stride};
+  if (qkv_post_smem(p) > di->smem_optin)
+    return fail(FGM_CUDA_EINVAL, "qkv_post: %d heads of %d need too much shared memory",
+                n_heads + 2 * kv_heads, head_dim);
+  return glue_done(launch_qkv_post(p, rows, use_pdl(), (cudaStream_t)stream), "qkv_post launch");
+}
+
 // ------------------------------------------------ peer memory, fused gather
 int fgm_cuda_ipc_alloc(size_t bytes, void **dev_ptr) {
   if (!dev_ptr || !bytes) return fail(FGM_CUDA_EINVAL, "ipc_alloc: null pointer or zero size");

@@ -108,10 +108,34 @@ struct AttnParams {
   // in stages of kp slots and multiplies them in stages of vg groups; the
   // lane sums gather `win` positions at a time; 16-byte copies when vec16;
   // vgp: V stage storage in groups (vg rounded up to whole 32-slot steps)
-  int cluster, gchunk, kp, vg, vgp, win, vec16;
-  unsigned off_ks, off_k, off_v, off_e, off_win, off_w, off_acc;  // shared memory layout (bytes)
+  // one: the whole window fits one gather (see the kernel)
+  int cluster, gchunk, kp, vg, vgp, win, vec16, one;
+  unsigned off_ks, off_k, off_v, off_e, off_win, off_w, off_vsa, off_acc;  // shared memory (bytes)
   size_t smem;
 };
+// Fused row glue of the decode step (glue.cu).
+cudaError_t launch_norm_prep(float *h, const float *proj, const float *w_post, const float *w_pre,
+                             int m, int n, float eps, float *qs, int8_t *pa, bool pdl,
+                             cudaStream_t st);
+cudaError_t launch_gelu_mul_prep(const float *gate, const float *up, int ld, int m, int n,
+                                 float *act, float *qs, int8_t *pa, bool pdl, cudaStream_t st);
+struct QkvParams {
+  float *q, *k, *v;                 // rows q_ld (q) and kv_ld (k, v) floats apart
+  int q_ld, kv_ld;
+  int n_heads, kv_heads, head_dim;
+  const float *q_norm, *k_norm;     // [head_dim]
+  float eps;
+  const float *inv_freq;            // [head_dim / 2]
+  const int *pos;                   // [rows]
+  int ring;                         // 0: slot = pos, else pos % ring
+  int8_t *kc;
+  float *ks;
+  int8_t *vt;
+  float *vs;
+  size_t kc_stride, ks_stride, vt_stride, vs_stride;  // per row (elements)
+};
+size_t qkv_post_smem(const QkvParams &p);
+cudaError_t launch_qkv_post(const QkvParams &p, int rows, bool pdl, cudaStream_t st);
 // Fills the cluster split and the shared memory layout; false when the
 // window does not fit in smem_limit bytes.
 bool attend_layout(AttnParams &p, size_t smem_limit);

@@ -247,7 +247,14 @@ __device__ __forceinline__ uint32_t lds32(const void *p) {
 // (column 2h: high bytes of head h, 2h + 1: low bytes) and the int32
 // accumulators [2 GM][hd].  Row paddings keep the fragment loads free of
 // bank conflicts.
-template <int GM>
+//
+// ONE (the whole window fits one gather, the usual decode case): after the
+// gather every CTA holds all exponentials, so it computes the weight max and
+// all weight bytes itself and multiplies every slot against its own
+// head_dim / C output dimensions -- V staged as [group][its dims], results
+// stored directly -- which drops the weight-max exchange and the integer
+// atomics with their two cluster barriers.
+template <int GM, bool ONE>
 __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParams p) {
   constexpr int nt = kGlueThreads, nw = kGlueThreads / 32;
   constexpr int kTiles = (512 / 16) * ((2 * GM + 7) / 8) / nw;  // P.V tiles per warp, at most
@@ -283,6 +290,9 @@ __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParam
   const int8_t *vt = p.vt + (size_t)r * p.vt_stride + (size_t)kvh * hd * 4;
   const float *vs = p.vs + (size_t)r * p.vs_stride;
   const int full = n & ~15;
+  const int dper = hd / C, d0 = rank * dper;  // ONE: this CTA's output dimensions
+  const int vldo = dper * 4 + 32;             // ONE: bytes per V group row (padded)
+  float *vsa = reinterpret_cast<float *>(sm + p.off_vsa);  // ONE: V scales of all slots
 
   // window position held by cache slot s, or -1
   auto pos_of = [&](int s) -> int {
@@ -331,14 +341,37 @@ __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParam
     cp_async_commit();
   };
 
-  for (int i = tid; i < GM * 2 * hd; i += nt) acc[i] = 0;
+  // ONE: every slot group of this KV head, this CTA's dims
+  auto load_v_dims = [&]() {
+    const int per = dper * 4 / wdt;
+    const int8_t *src = vt + (size_t)(p.wbase / 4) * kvd * 4 + (size_t)d0 * 4;
+    for (int c = tid; c < (p.wslots / 4) * per; c += nt) {
+      const int g = c / per, piece = c - g * per;
+      int8_t *dst = vst + g * vldo + piece * wdt;
+      const int8_t *sp = src + (size_t)g * kvd * 4 + piece * wdt;
+      if (p.vec16)
+        cp_async16(dst, sp);
+      else
+        cp_async4(dst, sp);
+    }
+    cp_async_commit();
+  };
+
+  if constexpr (!ONE)
+    for (int i = tid; i < GM * 2 * hd; i += nt) acc[i] = 0;
   for (int j = tid; j < ns; j += nt)
     if (pos_of(S0 + j) >= 0) {
       cp_async4(ksm + j, ks + S0 + j);
       cp_async4(vsm + j, vs + S0 + j);
     }
+  if constexpr (ONE)
+    for (int s = tid; s < p.wslots; s += nt)
+      if (pos_of(p.wbase + s) >= 0) cp_async4(vsa + s, vs + p.wbase + s);
   load_k(0, min(ns, kp));  // commits the scales with the first K stage
-  load_v(0, min(ns / 4, vg));
+  if constexpr (ONE)
+    load_v_dims();
+  else
+    load_v(0, min(ns / 4, vg));
 
   // ---- Q per head: int8 with one scale (ops.c:412-431)
   for (int h = warp; h < G; h += nw) {
@@ -465,6 +498,8 @@ __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParam
         }
       }
       __syncthreads();
+      if constexpr (ONE)  // the last read of another CTA's shared memory
+        asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
       if (tid < G * 16)
         for (int u = w0 + ln; u < min(w0 + wn, full); u += 16)
           l = __fadd_rn(l, wbuf[h * win + u - w0]);
@@ -478,6 +513,104 @@ __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParam
       s_inv[tid] = __fdiv_rn(1.0f, sum);
     }
     __syncthreads();
+  }
+
+  if constexpr (ONE) {
+    // ---- weights of every slot, their max per head, then P.V against this
+    // CTA's dimensions (ops.c:560-625)
+    cp_async_wait<0>();  // V scales and V (a CTA without slots never waited)
+    __syncthreads();
+    {
+      float wl[GM];
+#pragma unroll
+      for (int h = 0; h < GM; h++) wl[h] = 0.0f;
+      for (int s = tid; s < p.wslots; s += nt) {
+        const int u = pos_of(p.wbase + s);
+        if (u < 0) continue;
+        const float vsv = vsa[s];
+#pragma unroll
+        for (int h = 0; h < GM; h++)
+          if (h < G) {
+            const float w = __fmul_rn(__fmul_rn(wbuf[h * win + u], s_inv[h]), vsv);
+            wl[h] = w > wl[h] ? w : wl[h];
+          }
+      }
+#pragma unroll
+      for (int h = 0; h < GM; h++) wl[h] = warp_max(wl[h]);
+      if (lane == 0)
+#pragma unroll
+        for (int h = 0; h < GM; h++) s_red[warp][h] = wl[h];
+    }
+    __syncthreads();
+    if (tid < G) {
+      float m = s_red[0][tid];
+      for (int w = 1; w < nw; w++) m = s_red[w][tid] > m ? s_red[w][tid] : m;
+      s_wmax[tid] = m;
+      s_wqs[tid] = __fdiv_rn(m, 65535.0f);
+      s_wqi[tid] = m > 0.0f ? __fdiv_rn(65535.0f, m) : 0.0f;
+    }
+    __syncthreads();
+    const int kpad = (p.wslots + 31) & ~31;
+    for (int s = tid; s < kpad; s += nt) {
+      const int u = s < p.wslots ? pos_of(p.wbase + s) : -1;
+#pragma unroll
+      for (int h = 0; h < GM; h++)
+        if (h < G) {
+          int iw = 0;
+          if (u >= 0 && s_wmax[h] > 0.0f) {
+            const float x = __fadd_rn(
+                __fmul_rn(__fmul_rn(__fmul_rn(wbuf[h * win + u], s_inv[h]), vsa[s]), s_wqi[h]),
+                0.5f);
+            iw = (int)x;
+            iw = iw > 65535 ? 65535 : (iw < 0 ? 0 : iw);
+          }
+          wst[(2 * h) * wld + s] = (uint8_t)(iw >> 8);
+          wst[(2 * h + 1) * wld + s] = (uint8_t)(iw & 255);
+        }
+    }
+    __syncthreads();
+    // tiles: 16 dims x 8 columns (head h: columns 2h, 2h + 1 = high, low
+    // bytes); the k steps of a tile split over the warps that share it,
+    // partial sums added in shared memory (integers: any order)
+    const int pm = dper >> 4, pn = (2 * G + 7) >> 3, tiles = pm * pn;
+    const int split = nw / tiles > 0 ? nw / tiles : 1, ksteps = kpad >> 5;
+    int *part = reinterpret_cast<int *>(kst);  // the K stage is free now
+    for (int tw = warp; tw < tiles * split; tw += nw) {
+      const int tile = tw % tiles, sp = tw / tiles;
+      const int m0 = (tile % pm) * 16, n0 = (tile / pm) * 8;
+      const int8_t *ar = vst + tig * vldo + (m0 + gid) * 4;
+      const uint8_t *br = wst + min(n0 + gid, 2 * G - 1) * wld + tig * 4;
+      int32_t d[4] = {0, 0, 0, 0};
+      for (int ks = sp; ks < ksteps; ks += split) {
+        const int8_t *a = ar + ks * 8 * vldo;
+        mma_s8u8_m16n8k32(d, lds32(a), lds32(a + 32), lds32(a + 4 * vldo),
+                          lds32(a + 4 * vldo + 32), lds32(br + ks * 32), lds32(br + ks * 32 + 16));
+      }
+#pragma unroll
+      for (int e = 0; e < 4; e++) part[(tw * 32 + lane) * 4 + e] = d[e];
+    }
+    __syncthreads();
+    for (int idx = tid; idx < tiles * 32; idx += nt) {
+      const int tile = idx >> 5, ln = idx & 31, g8 = ln >> 2, t4 = ln & 3;
+      const int m0 = (tile % pm) * 16, n0 = (tile / pm) * 8, h = (n0 >> 1) + t4;
+      int32_t d[4] = {0, 0, 0, 0};
+      for (int sp = 0; sp < split; sp++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) d[e] += part[((sp * tiles + tile) * 32 + ln) * 4 + e];
+      if (h < G) {
+#pragma unroll
+        for (int hr = 0; hr < 2; hr++) {  // rows g8 and g8 + 8: (high, low) in d[2hr], d[2hr+1]
+          const int i = d0 + m0 + g8 + hr * 8;
+          float o = 0.0f;
+          if (s_wmax[h] > 0.0f)
+            o = __fmul_rn((float)(int)(((uint32_t)d[2 * hr] << 8) + (uint32_t)d[2 * hr + 1]),
+                          s_wqs[h]);
+          p.out[(size_t)r * p.out_ld + (size_t)(kvh * G + h) * hd + i] = o;
+        }
+      }
+    }
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+    return;
   }
 
   // ---- weights w_t = e_t * inv * vs_t: their max per head over the window
@@ -569,8 +702,7 @@ __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParam
       }
     }
   }
-  // integer sums meet in the CTA that owns the dimension
-  const int dper = hd / C;
+  // integer sums meet in the CTA that owns the dimension (dims [d0, d0 + dper))
 #pragma unroll
   for (int q = 0; q < kTiles; q++) {
     const int tile = warp + q * nw;
@@ -596,6 +728,272 @@ __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParam
   }
 }
 
+// ------------------------------------------------------------ fused row ops
+// The decode step's glue between GEMMs merged per row so that each merge is
+// one launch; every value is computed by the same expressions as the
+// separate kernels above, so the results are bit-identical to running them
+// one after the other.
+
+// ops.c:59-92: 1 / sqrt(mean of squares + eps) of a row staged in shared
+// memory -- 16 lane sums in order, reduced, then the tail.  Called by all
+// threads of the CTA.
+__device__ float rms_inv(const float *xs, int n, float eps, float *lanes, float *s_val) {
+  const int full = n & ~15;
+  if (threadIdx.x < 16) {
+    float acc = 0.0f;
+    for (int i = threadIdx.x; i < full; i += 16) acc = __fmaf_rn(xs[i], xs[i], acc);
+    lanes[threadIdx.x] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float ss = reduce16(lanes);
+    for (int i = full; i < n; i++) ss = __fmaf_rn(xs[i], xs[i], ss);
+    *s_val = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+  }
+  __syncthreads();
+  return *s_val;
+}
+
+// Largest |x| over the CTA's values (each thread passes its own maximum).
+__device__ float block_amax(float mx, float *red) {
+  mx = warp_max(mx);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = 0.0f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); w++) mx = red[w] > mx ? red[w] : mx;
+  __syncthreads();  // red may be reused
+  return mx;
+}
+
+// The prep of a row staged in shared memory with no rotation (ops.c:293-314):
+// the symmetric int8 scale of its max (ops.c:181-204), then the row's 64-byte
+// pieces of the packed GEMM tiles.  k is a multiple of 64.
+__device__ void quant_pack_row(const float *xs, int k, int r, float *qs, int8_t *pa, float *red) {
+  float mx = 0.0f;
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    const float a = fabsf(xs[i]);
+    mx = a > mx ? a : mx;
+  }
+  mx = block_amax(mx, red);
+  const float s = mx == 0.0f ? 1.0f : __fdiv_rn(mx, 127.0f);
+  const float inv = __fdiv_rn(1.0f, s);
+  if (threadIdx.x == 0) qs[r] = s;
+  int8_t *row = pa + (size_t)(r / 16) * (k / kTileK) * kATile + (size_t)(r % 16) * 64;
+  for (int i = threadIdx.x * 4; i < k; i += blockDim.x * 4)
+    *reinterpret_cast<uint32_t *>(row + (size_t)(i / 64) * kATile + (i % 64)) =
+        q8_quad(*reinterpret_cast<const float4 *>(xs + i), inv);
+}
+
+// A packed row past the last real row of its 16-row tile: zeros.
+__device__ void zero_pack_row(int k, int r, int8_t *pa) {
+  int8_t *row = pa + (size_t)(r / 16) * (k / kTileK) * kATile + (size_t)(r % 16) * 64;
+  for (int i = threadIdx.x * 4; i < k; i += blockDim.x * 4)
+    *reinterpret_cast<uint32_t *>(row + (size_t)(i / 64) * kATile + (i % 64)) = 0u;
+}
+
+// forward.rs:625-640 + :476-480: when proj is given, h += rmsnorm(proj, w_post)
+// (ops.c:59-92 then ops.c:317-321); then the next GEMM's packed rows of
+// rmsnorm(h, w_pre).  One CTA per row, rows [m, 16-row tile end) zero-filled.
+// Rows go through shared memory whole (all loads in flight at once), h is
+// written back last.
+__global__ void __launch_bounds__(kGlueThreads) norm_prep_kernel(
+    float *__restrict__ h, const float *__restrict__ proj, const float *__restrict__ w_post,
+    const float *__restrict__ w_pre, int m, int n, float eps, float *__restrict__ qs,
+    int8_t *__restrict__ pa) {
+  extern __shared__ __align__(16) float xs[];  // [n] the row to normalise, [n] the residual
+  __shared__ float lanes[16], red[32], s_val;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int r = blockIdx.x, n4 = n >> 2;
+  if (r >= m) {
+    zero_pack_row(n, r, pa);
+    return;
+  }
+  float *hs = xs + n;
+  float4 *h4 = reinterpret_cast<float4 *>(h + (size_t)r * n);
+  const float4 *p4 = proj ? reinterpret_cast<const float4 *>(proj + (size_t)r * n) : nullptr;
+#pragma unroll 4
+  for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+    reinterpret_cast<float4 *>(hs)[i] = h4[i];
+    if (p4) reinterpret_cast<float4 *>(xs)[i] = p4[i];
+  }
+  __syncthreads();
+  if (proj) {
+    const float inv = rms_inv(xs, n, eps, lanes, &s_val);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const float t = w_post ? __fmul_rn(__fmul_rn(xs[i], inv), w_post[i]) : __fmul_rn(xs[i], inv);
+      hs[i] = __fadd_rn(hs[i], t);
+    }
+    __syncthreads();
+  }
+  const float inv = rms_inv(hs, n, eps, lanes, &s_val);
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    xs[i] = w_pre ? __fmul_rn(__fmul_rn(hs[i], inv), w_pre[i]) : __fmul_rn(hs[i], inv);
+  __syncthreads();
+  if (proj)
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) h4[i] = reinterpret_cast<float4 *>(hs)[i];
+  quant_pack_row(xs, n, r, qs, pa, red);
+}
+
+// ops.c:119-131 then the prep: the down projection's packed rows of
+// gelu(gate) * up, gate and up rows ld floats apart (optionally the f32
+// product too, rows of n).  A cluster of C CTAs per
+// row, each on n / C columns; the row's max meets through distributed
+// shared memory.
+__global__ void __launch_bounds__(kGlueThreads) gelu_mul_prep_kernel(
+    const float *__restrict__ gate, const float *__restrict__ up, int ld, int m, int n,
+    float *__restrict__ act, float *__restrict__ qs, int8_t *__restrict__ pa) {
+  cg::cluster_group cluster = cg::this_cluster();
+  extern __shared__ __align__(16) float xs[];
+  __shared__ float red[32], s_amax;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int C = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
+  const int r = blockIdx.y, w = n / C, c0 = rank * w;  // w: a multiple of 64
+  int8_t *row = pa + (size_t)(r / 16) * (n / kTileK) * kATile + (size_t)(r % 16) * 64;
+  if (r >= m) {  // the whole cluster is a padding row
+    for (int i = threadIdx.x * 4; i < w; i += blockDim.x * 4)
+      *reinterpret_cast<uint32_t *>(row + (size_t)((c0 + i) / 64) * kATile + ((c0 + i) % 64)) = 0u;
+    return;
+  }
+  const float4 *g4 = reinterpret_cast<const float4 *>(gate + (size_t)r * ld + c0);
+  const float4 *u4 = reinterpret_cast<const float4 *>(up + (size_t)r * ld + c0);
+  const int full = n & ~15;
+  float mx = 0.0f;
+#pragma unroll 2
+  for (int i = threadIdx.x; i < w / 4; i += blockDim.x) {
+    const float4 g = g4[i], u = u4[i];
+    const int c = c0 + 4 * i;
+    float4 v;
+    v.x = __fmul_rn(c < full ? gelu_lane(g.x) : gelu_tail(g.x), u.x);
+    v.y = __fmul_rn(c + 1 < full ? gelu_lane(g.y) : gelu_tail(g.y), u.y);
+    v.z = __fmul_rn(c + 2 < full ? gelu_lane(g.z) : gelu_tail(g.z), u.z);
+    v.w = __fmul_rn(c + 3 < full ? gelu_lane(g.w) : gelu_tail(g.w), u.w);
+    reinterpret_cast<float4 *>(xs)[i] = v;
+    const float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    mx = a > mx ? a : mx;
+  }
+  mx = block_amax(mx, red);
+  if (threadIdx.x == 0) s_amax = mx;
+  cluster.sync();
+  float v[8];
+#pragma unroll
+  for (int c = 0; c < 8; c++)
+    v[c] = c < C ? *cluster.map_shared_rank(&s_amax, c) : 0.0f;
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");  // done with the peers
+  mx = 0.0f;
+#pragma unroll
+  for (int c = 0; c < 8; c++) mx = v[c] > mx ? v[c] : mx;
+  const float s = mx == 0.0f ? 1.0f : __fdiv_rn(mx, 127.0f);
+  const float inv = __fdiv_rn(1.0f, s);
+  if (rank == 0 && threadIdx.x == 0) qs[r] = s;
+  for (int i = threadIdx.x; i < w / 4; i += blockDim.x) {
+    const float4 x = reinterpret_cast<const float4 *>(xs)[i];
+    const int c = c0 + 4 * i;
+    *reinterpret_cast<uint32_t *>(row + (size_t)(c / 64) * kATile + (c % 64)) = q8_quad(x, inv);
+    if (act) *reinterpret_cast<float4 *>(act + (size_t)r * n + c) = x;
+  }
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// forward.rs:482-545 for one row: rmsnorm of each query head (q_norm) and
+// key head (k_norm) then rope (ops.c:135-147), each value head without
+// scale; then the key and value rows quantised to int8 with one scale each
+// (ops.c:181-204) into the row's caches at slot pos (mod ring): K as a row
+// of the [slot][kv_heads * head_dim] cache, V into the slot-interleaved
+// layout (ops.c:653-660).  q, k and v keep the normalised (and rotated)
+// values, like the reference's buffers.
+__global__ void __launch_bounds__(kGlueThreads) qkv_post_kernel(const QkvParams p) {
+  extern __shared__ __align__(16) float xs[];  // q heads, k heads, v heads; then cos, sin
+  __shared__ float lanes[48][16], inv_h[48], red[32];
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int r = blockIdx.x, hd = p.head_dim, half = hd / 2;
+  const int nq = p.n_heads * hd, kvd = p.kv_heads * hd, heads = p.n_heads + 2 * p.kv_heads;
+  float *qr = p.q + (size_t)r * p.q_ld, *kr = p.k + (size_t)r * p.kv_ld,
+        *vr = p.v + (size_t)r * p.kv_ld;
+  float *cs = xs + nq + 2 * kvd, *sn = cs + half;
+  const int pos = p.pos[r];
+  {  // all loads in flight at once: q, k and v rows as float4
+    const int q4 = nq >> 2, k4 = kvd >> 2;
+    float4 *x4 = reinterpret_cast<float4 *>(xs);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < q4 + 2 * k4; i += blockDim.x)
+      x4[i] = i < q4 ? reinterpret_cast<const float4 *>(qr)[i]
+                     : (i < q4 + k4 ? reinterpret_cast<const float4 *>(kr)[i - q4]
+                                    : reinterpret_cast<const float4 *>(vr)[i - q4 - k4]);
+  }
+  for (int j = threadIdx.x; j < half; j += blockDim.x) {
+    const float a = __fmul_rn((float)pos, p.inv_freq[j]);
+    cs[j] = (float)cos((double)a);
+    sn[j] = (float)sin((double)a);
+  }
+  __syncthreads();
+  // per-head sums of squares: a half-warp per head, 16 lanes in order
+  for (int hh = threadIdx.x >> 4; hh < heads; hh += blockDim.x >> 4) {
+    const float *x = xs + hh * hd;
+    float acc = 0.0f;
+    for (int i = threadIdx.x & 15; i < hd; i += 16) acc = __fmaf_rn(x[i], x[i], acc);
+    lanes[hh][threadIdx.x & 15] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x < heads)
+    inv_h[threadIdx.x] = __fdiv_rn(
+        1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(reduce16(lanes[threadIdx.x]), (float)hd), p.eps)));
+  __syncthreads();
+  for (int i = threadIdx.x; i < nq + 2 * kvd; i += blockDim.x) {
+    const int hh = i / hd, d = i - hh * hd;
+    const float *w = hh < p.n_heads ? p.q_norm : (hh < p.n_heads + p.kv_heads ? p.k_norm : nullptr);
+    xs[i] = w ? __fmul_rn(__fmul_rn(xs[i], inv_h[hh]), w[d]) : __fmul_rn(xs[i], inv_h[hh]);
+  }
+  __syncthreads();
+  // rope on the query and key heads: pairs (j, j + half)
+  for (int idx = threadIdx.x; idx < (p.n_heads + p.kv_heads) * half; idx += blockDim.x) {
+    const int hh = idx / half, j = idx - hh * half;
+    float *x = xs + hh * hd;
+    const float lo = x[j], hi = x[j + half];
+    x[j] = __fmaf_rn(lo, cs[j], -__fmul_rn(hi, sn[j]));
+    x[j + half] = __fmaf_rn(hi, cs[j], __fmul_rn(lo, sn[j]));
+  }
+  __syncthreads();
+  {
+    const int q4 = nq >> 2, k4 = kvd >> 2;
+    const float4 *x4 = reinterpret_cast<const float4 *>(xs);
+    for (int i = threadIdx.x; i < q4 + 2 * k4; i += blockDim.x) {
+      if (i < q4)
+        reinterpret_cast<float4 *>(qr)[i] = x4[i];
+      else if (i < q4 + k4)
+        reinterpret_cast<float4 *>(kr)[i - q4] = x4[i];
+      else
+        reinterpret_cast<float4 *>(vr)[i - q4 - k4] = x4[i];
+    }
+  }
+  // int8 K and V rows with one scale each, into the caches
+  const int slot = p.ring ? pos % p.ring : pos;
+  for (int part = 0; part < 2; part++) {
+    const float *x = xs + nq + part * kvd;
+    float mx = 0.0f;
+    for (int i = threadIdx.x; i < kvd; i += blockDim.x) {
+      const float a = fabsf(x[i]);
+      mx = a > mx ? a : mx;
+    }
+    mx = block_amax(mx, red);
+    const float s = mx == 0.0f ? 1.0f : __fdiv_rn(mx, 127.0f);
+    const float inv = __fdiv_rn(1.0f, s);
+    if (part == 0) {
+      int8_t *dst = p.kc + (size_t)r * p.kc_stride + (size_t)slot * kvd;
+      for (int i = threadIdx.x; i < kvd; i += blockDim.x)
+        dst[i] = (int8_t)q8_x86(__fmul_rn(x[i], inv));
+      if (threadIdx.x == 0) p.ks[(size_t)r * p.ks_stride + slot] = s;
+    } else {
+      int8_t *dst = p.vt + (size_t)r * p.vt_stride + (size_t)(slot >> 2) * kvd * 4 + (slot & 3);
+      for (int i = threadIdx.x; i < kvd; i += blockDim.x)
+        dst[(size_t)i * 4] = (int8_t)q8_x86(__fmul_rn(x[i], inv));
+      if (threadIdx.x == 0) p.vs[(size_t)r * p.vs_stride + slot] = s;
+    }
+  }
+}
+
 template <class K, class... A>
 cudaError_t launch_pdl(K kern, dim3 grid, dim3 block, size_t smem, bool pdl, cudaStream_t st,
                        A... args) {
@@ -618,6 +1016,61 @@ unsigned grid_for(size_t n) {
 }
 
 }  // namespace
+
+cudaError_t launch_norm_prep(float *h, const float *proj, const float *w_post, const float *w_pre,
+                             int m, int n, float eps, float *qs, int8_t *pa, bool pdl,
+                             cudaStream_t st) {
+  const size_t smem = (size_t)n * 8;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(norm_prep_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_pdl(norm_prep_kernel, dim3((unsigned)((m + 15) & ~15)), dim3(kGlueThreads), smem,
+                    pdl, st, h, proj, w_post, w_pre, m, n, eps, qs, pa);
+}
+
+cudaError_t launch_gelu_mul_prep(const float *gate, const float *up, int ld, int m, int n,
+                                 float *act, float *qs, int8_t *pa, bool pdl, cudaStream_t st) {
+  int c = 8;
+  while ((n / 64) % c) c >>= 1;  // whole 64-column tiles per CTA
+  const size_t smem = (size_t)(n / c) * 4;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(gelu_mul_prep_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)c, (unsigned)((m + 15) & ~15));
+  cfg.blockDim = dim3(kGlueThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)c;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, gelu_mul_prep_kernel, gate, up, ld, m, n, act, qs, pa);
+}
+
+size_t qkv_post_smem(const QkvParams &p) {
+  return ((size_t)(p.n_heads + 2 * p.kv_heads) * p.head_dim + p.head_dim) * 4;
+}
+
+cudaError_t launch_qkv_post(const QkvParams &p, int rows, bool pdl, cudaStream_t st) {
+  const size_t smem = qkv_post_smem(p);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(qkv_post_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_pdl(qkv_post_kernel, dim3((unsigned)rows), dim3(kGlueThreads), smem, pdl, st, p);
+}
+
 
 cudaError_t launch_rmsnorm(float *out, const float *x, const float *w, int rows, int n, float eps,
                            bool pdl, cudaStream_t st) {
@@ -676,9 +1129,9 @@ int gm_of(const AttnParams &p) {
   return gm;
 }
 
-template <int GM>
+template <int GM, bool ONE>
 cudaError_t launch_attend_gm(const AttnParams &p, int rows, bool pdl, cudaStream_t st) {
-  cudaError_t e = cudaFuncSetAttribute(attend_q8_kernel<GM>,
+  cudaError_t e = cudaFuncSetAttribute(attend_q8_kernel<GM, ONE>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -695,7 +1148,7 @@ cudaError_t launch_attend_gm(const AttnParams &p, int rows, bool pdl, cudaStream
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, attend_q8_kernel<GM>, p);
+  return cudaLaunchKernelEx(&cfg, attend_q8_kernel<GM, ONE>, p);
 }
 
 }  // namespace
@@ -708,12 +1161,37 @@ bool attend_layout(AttnParams &p, size_t smem_limit) {
   p.cluster = c;
   p.gchunk = (p.wslots / 4 + c - 1) / c;
   const int cs = 4 * p.gchunk;
-  p.win = (4096 / gm) & ~15;
-  if (p.win > ((n + 15) & ~15)) p.win = (n + 15) & ~15;
+  const int win_max = (4096 / gm) & ~15;
+  p.win = win_max < ((n + 15) & ~15) ? win_max : ((n + 15) & ~15);
   const size_t kld = (size_t)hd + 16, vld = (size_t)hd * 4 + 32;
-  const size_t fixed = align16((size_t)gm * hd) + align16((size_t)2 * cs * 4) +
-                       align16((size_t)gm * cs * 4) + align16((size_t)gm * p.win * 4) +
-                       (size_t)gm * 2 * hd * 4 + 4096;  // + static shared memory
+  const size_t base = align16((size_t)gm * hd) + align16((size_t)2 * cs * 4) +
+                      align16((size_t)gm * cs * 4) + align16((size_t)gm * p.win * 4) +
+                      4096;  // + static shared memory
+  // single-window form: all V groups of this CTA's dims, all weight bytes,
+  // all V scales, the P.V partial sums in the K stage
+  p.one = ((n + 15) & ~15) <= win_max && (hd / c) % 16 == 0;
+  if (p.one) {
+    const int kpad = (p.wslots + 31) & ~31;
+    const int tiles = (hd / c / 16) * ((2 * (p.n_heads / p.kv_heads) + 7) / 8);
+    const size_t part = (size_t)(tiles > 8 ? tiles : 8) * 512;
+    p.kp = cs < kGlueThreads ? ((cs + 15) & ~15) : kGlueThreads;
+    size_t kbytes = align16((size_t)p.kp * kld);
+    if (kbytes < part) kbytes = align16(part);
+    p.vg = p.gchunk;
+    p.vgp = kpad / 4;
+    p.off_ks = align16((size_t)gm * hd);
+    p.off_k = p.off_ks + align16((size_t)2 * cs * 4);
+    p.off_v = p.off_k + (unsigned)kbytes;
+    p.off_e = p.off_v + align16((size_t)p.vgp * ((size_t)hd / c * 4 + 32));
+    p.off_win = p.off_e + align16((size_t)gm * cs * 4);
+    p.off_w = p.off_win + align16((size_t)gm * p.win * 4);
+    p.off_vsa = p.off_w + align16((size_t)2 * gm * (p.vgp * 4 + 16));
+    p.off_acc = p.off_vsa + align16((size_t)p.wslots * 4);
+    p.smem = p.off_acc;
+    if (p.smem + 4096 <= smem_limit) return true;
+    p.one = 0;
+  }
+  const size_t fixed = base + (size_t)gm * 2 * hd * 4;
   // smallest stages: 16 K rows, 8 V groups with their weight bytes
   const size_t kv_min = 16 * kld + 8 * vld + 2 * (size_t)gm * (32 + 16);
   if (fixed + kv_min > smem_limit) return false;
@@ -732,7 +1210,8 @@ bool attend_layout(AttnParams &p, size_t smem_limit) {
   p.off_e = p.off_v + align16((size_t)p.vgp * vld);
   p.off_win = p.off_e + align16((size_t)gm * cs * 4);
   p.off_w = p.off_win + align16((size_t)gm * p.win * 4);
-  p.off_acc = p.off_w + align16((size_t)2 * gm * (p.vgp * 4 + 16));
+  p.off_vsa = p.off_w + align16((size_t)2 * gm * (p.vgp * 4 + 16));
+  p.off_acc = p.off_vsa;
   p.smem = p.off_acc + (size_t)gm * 2 * hd * 4;
   return p.smem + 4096 <= smem_limit;
 }
@@ -740,12 +1219,17 @@ bool attend_layout(AttnParams &p, size_t smem_limit) {
 cudaError_t launch_attend_q8(const AttnParams &p, int rows, bool pdl, size_t smem_limit,
                              cudaStream_t st) {
   if (p.smem + 4096 > smem_limit) return cudaErrorInvalidConfiguration;
-  switch (gm_of(p)) {
-    case 1: return launch_attend_gm<1>(p, rows, pdl, st);
-    case 2: return launch_attend_gm<2>(p, rows, pdl, st);
-    case 4: return launch_attend_gm<4>(p, rows, pdl, st);
-    case 8: return launch_attend_gm<8>(p, rows, pdl, st);
-    case 16: return launch_attend_gm<16>(p, rows, pdl, st);
+  switch (gm_of(p) * 2 + (p.one ? 1 : 0)) {
+    case 2: return launch_attend_gm<1, false>(p, rows, pdl, st);
+    case 3: return launch_attend_gm<1, true>(p, rows, pdl, st);
+    case 4: return launch_attend_gm<2, false>(p, rows, pdl, st);
+    case 5: return launch_attend_gm<2, true>(p, rows, pdl, st);
+    case 8: return launch_attend_gm<4, false>(p, rows, pdl, st);
+    case 9: return launch_attend_gm<4, true>(p, rows, pdl, st);
+    case 16: return launch_attend_gm<8, false>(p, rows, pdl, st);
+    case 17: return launch_attend_gm<8, true>(p, rows, pdl, st);
+    case 32: return launch_attend_gm<16, false>(p, rows, pdl, st);
+    case 33: return launch_attend_gm<16, true>(p, rows, pdl, st);
     default: return cudaErrorInvalidConfiguration;
   }
 }

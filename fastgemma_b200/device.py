@@ -163,3 +163,28 @@ def attend_q8(out, out_ld, q, q_ld, kc, kc_stride, ks, ks_stride, vt, vt_stride,
     call("fgm_cuda_attend_q8", _p(out), out_ld, _p(q), q_ld, _p(kc), kc_stride, _p(ks), ks_stride,
          _p(vt), vt_stride, _p(vs), vs_stride, rows, n_heads, kv_heads, head_dim, start, end, ring,
          _s(stream))
+
+
+def norm_prep(h, proj, w_post, w_pre, rows, n, eps, qs, pa, stream=None):
+    """forward.rs:476-480, :625-654: h += rmsnorm(proj, w_post) (when proj is
+    given), then the packed rows of rmsnorm(h, w_pre)."""
+    call("fgm_cuda_norm_prep", _p(h), _p(proj), _p(w_post), _p(w_pre), rows, n, eps, _p(qs), _p(pa),
+         _s(stream))
+
+
+def gelu_mul_prep(gate, up, rows, n, qs, pa, act=None, ld=None, stream=None):
+    """forward.rs:641-643: packed rows of gelu(gate) * up (rows ld apart)."""
+    call("fgm_cuda_gelu_mul_prep", _p(gate), _p(up), n if ld is None else ld, rows, n, _p(act),
+         _p(qs), _p(pa), _s(stream))
+
+
+def qkv_post(q, k, v, rows, n_heads, kv_heads, head_dim, q_norm, k_norm, eps, inv_freq, pos, ring,
+             kc, kc_stride, ks, ks_stride, vt, vt_stride, vs, vs_stride, q_ld=None, kv_ld=None,
+             stream=None):
+    """forward.rs:482-545: head norms, rope, int8 K / V rows into the caches."""
+    q_ld = n_heads * head_dim if q_ld is None else q_ld
+    kv_ld = kv_heads * head_dim if kv_ld is None else kv_ld
+    call("fgm_cuda_qkv_post", _p(q), q_ld, _p(k), _p(v), kv_ld, rows, n_heads, kv_heads, head_dim,
+         _p(q_norm), _p(k_norm), eps, _p(inv_freq), _p(pos), ring, _p(kc), kc_stride, _p(ks),
+         ks_stride, _p(vt), vt_stride, _p(vs), vs_stride, _s(stream))
+

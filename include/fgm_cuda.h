@@ -289,12 +289,51 @@ int fgm_cuda_store_v_t(int8_t *vt, size_t vt_stride, const int8_t *src, int src_
  * int8 cache: K [slot][kv_heads*head_dim] with scales ks [slot], V in the
  * store_v_t layout (holding whole groups of four slots) with scales vs.
  * ring = 0: slot = position; ring > 0: slot = position % ring and the
- * window must not be longer than the ring.  head_dim % 64 == 0, <= 512;
- * the window needs 4 bytes of shared memory per position. */
+ * window must not be longer than the ring.  head_dim % 64 == 0, <= 512; at
+ * most 16 query heads per KV head; the caches and their row strides 4-byte
+ * aligned (16-byte aligned ones copy faster). */
 int fgm_cuda_attend_q8(float *out, int out_ld, const float *q, int q_ld, const int8_t *kc,
                        size_t kc_stride, const float *ks, size_t ks_stride, const int8_t *vt,
                        size_t vt_stride, const float *vs, size_t vs_stride, int rows, int n_heads,
                        int kv_heads, int head_dim, int start, int end, int ring, void *stream);
+
+/* ------------------------------------------- fused glue of a decode step
+ * Each entry is one launch for a run of reference operations between two
+ * GEMMs, bit-identical to calling the entries above one after the other.
+ *
+ * fgm_cuda_norm_prep (forward.rs:476-480, :625-654): when proj is not null,
+ * h += rmsnorm(proj, w_post) for each row (ops.c:59-92 then :317-321; h
+ * updated in place); then the packed int8 rows (and scales) of
+ * rmsnorm(h, w_pre) for the next GEMM, as fgm_cuda_prep_rows with hsz 0.
+ * Rows of n floats (n % 64 == 0, n <= 49152; h and proj 16-byte aligned);
+ * pa holds (rows rounded up to 16) x n bytes, the padding rows are
+ * zero-filled. */
+int fgm_cuda_norm_prep(float *h, const float *proj, const float *w_post, const float *w_pre,
+                       int rows, int n, float eps, float *qs, int8_t *pa, void *stream);
+
+/* fgm_cuda_gelu_mul_prep (forward.rs:641-643): the down projection's packed
+ * rows of gelu(gate) * up (ops.c:119-131 per row of n, n % 64 == 0; gate
+ * and up rows ld floats apart, so one fused [gate | up] GEMM output serves
+ * as both), and the f32 product in act [rows][n] when act is not null (all
+ * 16-byte aligned, ld % 4 == 0). */
+int fgm_cuda_gelu_mul_prep(const float *gate, const float *up, int ld, int rows, int n,
+                           float *act, float *qs, int8_t *pa, void *stream);
+
+/* fgm_cuda_qkv_post (forward.rs:482-545): for each row r, rmsnorm of every
+ * query head (q_norm) and key head (k_norm) followed by rope at pos[r]
+ * (ops.c:135-147), rmsnorm without scale of every value head, all in place
+ * in q (rows q_ld floats apart), k and v (rows kv_ld apart); then
+ * the key and value rows quantised to int8 with one scale each (ops.c:
+ * 181-204) into row r's caches at slot pos[r] (pos[r] % ring when ring >
+ * 0): kc + r*kc_stride [slot][kv_heads*head_dim], ks + r*ks_stride [slot],
+ * V into vt + r*vt_stride in the store_v_t layout, vs + r*vs_stride [slot].
+ * head_dim % 4 == 0, at most 48 heads in all, q, k and v 16-byte aligned,
+ * q_ld and kv_ld multiples of 4. */
+int fgm_cuda_qkv_post(float *q, int q_ld, float *k, float *v, int kv_ld, int rows, int n_heads,
+                      int kv_heads, int head_dim, const float *q_norm, const float *k_norm, float eps,
+                      const float *inv_freq, const int *pos, int ring, int8_t *kc,
+                      size_t kc_stride, float *ks, size_t ks_stride, int8_t *vt, size_t vt_stride,
+                      float *vs, size_t vs_stride, void *stream);
 
 /* ------------------------------------------------------------ row argmax
  * The token choice that follows the LM head (fgm-serve/src/engine.rs:75-83,

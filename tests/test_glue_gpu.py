@@ -191,3 +191,118 @@ def test_attention_rejects_bad_windows():
         D.attend_q8(z, 256, z, 256, zi[1:], 0, z, 0, zi, 0, z, 0, 1, 1, 1, 256, 0, 16, 0)
     with pytest.raises(_lib.FgmCudaError, match="fit"):
         D.attend_q8(z, 4096, z, 4096, zi, 0, z, 0, zi, 0, z, 0, 1, 32, 1, 64, 0, 16, 0)
+
+
+def _bits_equal(got, want, what):
+    got, want = np.asarray(got), np.asarray(want)
+    assert got.shape == want.shape, f"{what}: shape {got.shape} vs {want.shape}"
+    g = got.view(np.uint32) if got.dtype == np.float32 else got
+    w = want.view(np.uint32) if want.dtype == np.float32 else want
+    bad = g != w
+    assert not bad.any(), f"{what}: {int(bad.sum())} of {bad.size} differ"
+
+
+@pytest.mark.parametrize("rows,n,with_proj", [(5, 2048, True), (8, 2048, False), (3, 8192, True),
+                                              (17, 1024, True)])
+def test_norm_prep_against_oracle(orc, rows, n, with_proj):
+    """Post-norm + residual add + pre-norm + prep in one launch equals the
+    oracle's rmsnorm, add, rmsnorm and prep_rows: h, scales and packed rows
+    bit for bit, padding rows of the last 16-row tile zeroed."""
+    rng = np.random.default_rng(rows * 7 + n)
+    h = rng.standard_normal((rows, n)).astype(np.float32)
+    proj = (rng.standard_normal((rows, n)) * 3).astype(np.float32)
+    w_post = rng.uniform(0.5, 1.5, n).astype(np.float32)
+    w_pre = rng.uniform(0.5, 1.5, n).astype(np.float32)
+    eps = 1e-6
+    want_h = orc.add(h, orc.rmsnorm(proj, w_post, eps)) if with_proj else h
+    _, _, want_qs, want_pa = orc.prep_rows(orc.rmsnorm(want_h, w_pre, eps), rows, n, 0)
+    th = dev(h)
+    qs = torch.empty(rows, device="cuda")
+    pa = torch.full((want_pa.size,), 7, dtype=torch.int8, device="cuda")
+    D.norm_prep(th, dev(proj) if with_proj else None, dev(w_post), dev(w_pre), rows, n, eps, qs, pa)
+    torch.cuda.synchronize()
+    _bits_equal(th.cpu().numpy(), want_h, "h")
+    _bits_equal(qs.cpu().numpy(), want_qs, "scales")
+    _bits_equal(pa.cpu().numpy(), want_pa, "packed rows")
+
+
+@pytest.mark.parametrize("rows,n,fused", [(8, 8192, True), (3, 1024, False), (5, 192, True)])
+def test_gelu_mul_prep_against_oracle(orc, rows, n, fused):
+    """fused: gate and up are the two halves of one [gate | up] GEMM output."""
+    rng = np.random.default_rng(rows + n)
+    gate = (rng.standard_normal((rows, n)) * 2).astype(np.float32)
+    up = rng.standard_normal((rows, n)).astype(np.float32)
+    want_act = orc.gelu_mul(gate, up)
+    _, _, want_qs, want_pa = orc.prep_rows(want_act, rows, n, 0)
+    act = torch.empty((rows, n), device="cuda")
+    qs = torch.empty(rows, device="cuda")
+    pa = torch.full((want_pa.size,), 7, dtype=torch.int8, device="cuda")
+    if fused:
+        gu = dev(np.concatenate([gate, up], axis=1))
+        D.gelu_mul_prep(gu, gu[:, n:], rows, n, qs, pa, act=act, ld=2 * n)
+    else:
+        D.gelu_mul_prep(dev(gate), dev(up), rows, n, qs, pa, act=act)
+    torch.cuda.synchronize()
+    _bits_equal(act.cpu().numpy(), want_act, "act")
+    _bits_equal(qs.cpu().numpy(), want_qs, "scales")
+    _bits_equal(pa.cpu().numpy(), want_pa, "packed rows")
+
+
+@pytest.mark.parametrize("nh,kvh,hd,ring,fused", [(8, 2, 256, 0, True), (4, 1, 128, 64, False)])
+def test_qkv_post_equals_the_separate_kernels(orc, nh, kvh, hd, ring, fused):
+    """Head norms, rope and the int8 K / V cache writes in one launch equal
+    the separate glue kernels bit for bit (and the oracle's norms and rope
+    to the libm tolerance)."""
+    rng = np.random.default_rng(nh * hd + ring)
+    rows, kvd, cap, eps = 4, kvh * hd, 160, 1e-6
+    pos = np.array([5, 150, 77, 128], np.int32)
+    q = (rng.standard_normal((rows, nh * hd)) * 2).astype(np.float32)
+    k = (rng.standard_normal((rows, kvd)) * 2).astype(np.float32)
+    v = rng.standard_normal((rows, kvd)).astype(np.float32)
+    qn = rng.uniform(0.5, 1.5, hd).astype(np.float32)
+    kn = rng.uniform(0.5, 1.5, hd).astype(np.float32)
+    inv_freq = (1.0 / 10000.0 ** (np.arange(0, hd, 2) / hd)).astype(np.float32)
+    slots = ring or cap
+    vslots = (slots + 3) // 4 * 4
+
+    def caches():
+        return (torch.zeros((rows, slots, kvd), dtype=torch.int8, device="cuda"),
+                torch.zeros((rows, slots), device="cuda"),
+                torch.zeros((rows, vslots * kvd), dtype=torch.int8, device="cuda"),
+                torch.zeros((rows, slots), device="cuda"))
+
+    tq = dev(q)
+    if fused:  # k and v: the two halves of one [k | v] GEMM output
+        tkv = dev(np.concatenate([k, v], axis=1))
+        tk, tv = tkv[:, :kvd], tkv[:, kvd:]
+    else:
+        tk, tv = dev(k), dev(v)
+    kc, ks, vt, vs = caches()
+    tpos, tinv = dev(pos), dev(inv_freq)
+    D.qkv_post(tq, tk, tv, rows, nh, kvh, hd, dev(qn), dev(kn), eps, tinv, tpos, ring, kc,
+               slots * kvd, ks, slots, vt, vt.shape[1], vs, slots, kv_ld=2 * kvd if fused else kvd)
+    # the same steps one kernel at a time
+    rq, rk, rv = dev(q), dev(k), dev(v)
+    D.rmsnorm(rq, rq, dev(qn), rows * nh, hd, eps)
+    D.rmsnorm(rk, rk, dev(kn), rows * kvh, hd, eps)
+    D.rmsnorm(rv, rv, None, rows * kvh, hd, eps)
+    D.rope(rq, nh * hd, rows, nh, hd, tinv, tpos)
+    D.rope(rk, kvd, rows, kvh, hd, tinv, tpos)
+    k8, v8 = (torch.empty((rows, kvd), dtype=torch.int8, device="cuda") for _ in range(2))
+    ksc, vsc = torch.empty(rows, device="cuda"), torch.empty(rows, device="cuda")
+    D.quant_act(rk, rows, kvd, k8, ksc)
+    D.quant_act(rv, rows, kvd, v8, vsc)
+    rkc, rks, rvt, rvs = caches()
+    for r in range(rows):
+        sl = int(pos[r]) % ring if ring else int(pos[r])
+        rkc[r, sl] = k8[r]
+        rks[r, sl] = ksc[r]
+        rvs[r, sl] = vsc[r]
+        D.store_v_t(rvt[r:r + 1], rvt.shape[1], v8[r:r + 1], kvd, 1, kvd, sl)
+    torch.cuda.synchronize()
+    for got, want, what in ((tq, rq, "q"), (tk, rk, "k"), (tv, rv, "v"), (kc, rkc, "K cache"),
+                            (ks, rks, "K scales"), (vt, rvt, "V cache"), (vs, rvs, "V scales")):
+        _bits_equal(got.cpu().numpy(), want.cpu().numpy(), what)
+    oq = orc.rope(orc.rmsnorm(q.reshape(-1, hd), qn, eps).reshape(rows, -1)[0], nh, hd, inv_freq,
+                  int(pos[0]))
+    same(tq.cpu().numpy()[0], oq, False, "q against the oracle")
