@@ -588,8 +588,8 @@ def build_decode_chain(dev, gen, T, L=30):
             D.gemm_q4g(M, NH * HD, H, pa[H], qs, lw["q"][0], lw["q"][1], GROUP, q)
             D.gemm_q4g(M, 2 * KVD, H, pa[H], qs, lw["kv"][0], lw["kv"][1], GROUP, kv)
             D.qkv_post(q, kv, kv[:, KVD:], M, NH, KVH, HD, lw["qn"], lw["kn"], 1e-6, inv_freq, pos,
-                       0, lw["kc"], T * KVD, lw["ks"], T, lw["vt"], lw["vt"].shape[1], lw["vs"], T,
-                       kv_ld=2 * KVD)
+                       0, T, lw["kc"], T * KVD, lw["ks"], T, lw["vt"], lw["vt"].shape[1], lw["vs"],
+                       T, kv_ld=2 * KVD)
             D.attend_q8(attn, NH * HD, q, NH * HD, lw["kc"], T * KVD, lw["ks"], T, lw["vt"],
                         lw["vt"].shape[1], lw["vs"], T, M, NH, KVH, HD, 0, T)
             D.prep_rows(attn, NH * HD, qs, pa[H], M, NH * HD, 0)

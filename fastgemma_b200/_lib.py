@@ -62,8 +62,8 @@ SIGNATURES = {
                             _i, _i, _i, _p], _i),
     "fgm_cuda_norm_prep": ([_p, _p, _p, _p, _i, _i, C.c_float, _p, _p, _p], _i),
     "fgm_cuda_gelu_mul_prep": ([_p, _p, _i, _i, _i, _p, _p, _p, _p], _i),
-    "fgm_cuda_qkv_post": ([_p, _i, _p, _p, _i, _i, _i, _i, _i, _p, _p, C.c_float, _p, _p, _i, _p,
-                           _sz, _p, _sz, _p, _sz, _p, _sz, _p], _i),
+    "fgm_cuda_qkv_post": ([_p, _i, _p, _p, _i, _i, _i, _i, _i, _p, _p, C.c_float, _p, _p, _i, _i,
+                           _p, _sz, _p, _sz, _p, _sz, _p, _sz, _p], _i),
     "fgm_cuda_ipc_alloc": ([_sz, C.POINTER(_p)], _i),
     "fgm_cuda_ipc_free": ([_p], _i),
     "fgm_cuda_ipc_handle": ([_p, _p], _i),

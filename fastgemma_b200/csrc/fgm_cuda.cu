@@ -1312,6 +1312,13 @@ int fgm_cuda_attend_q8(float *out, int out_ld, const float *q, int q_ld, const i
     return fail(FGM_CUDA_EINVAL, "attend: out_ld=%d q_ld=%d < heads*head_dim", out_ld, q_ld);
   if (rows == 0) return FGM_CUDA_OK;
   if (!out || !q || !kc || !ks || !vt || !vs) return fail(FGM_CUDA_EINVAL, "null pointer");
+  {  // with several rows the strides bound each cache: the window must fit
+    const size_t slots = ring ? (size_t)ring : (size_t)end, kvd = (size_t)kv_heads * head_dim;
+    if (rows > 1 && (slots * kvd > kc_stride || slots > ks_stride || slots > vs_stride ||
+                     ((slots + 3) & ~(size_t)3) * kvd > vt_stride))
+      return fail(FGM_CUDA_EINVAL, "attend: row strides shorter than the %zu slots the window "
+                  "reads", slots);
+  }
   DevInfo *di = nullptr;
   int rc = dev_info(&di);
   if (rc) return rc;
@@ -1380,9 +1387,15 @@ int fgm_cuda_gelu_mul_prep(const float *gate, const float *up, int ld, int rows,
 
 int fgm_cuda_qkv_post(float *q, int q_ld, float *k, float *v, int kv_ld, int rows, int n_heads,
                       int kv_heads, int head_dim, const float *q_norm, const float *k_norm, float eps,
-                      const float *inv_freq, const int *pos, int ring, int8_t *kc,
+                      const float *inv_freq, const int *pos, int ring, int cap, int8_t *kc,
                       size_t kc_stride, float *ks, size_t ks_stride, int8_t *vt, size_t vt_stride,
                       float *vs, size_t vs_stride, void *stream) {
+  if (cap <= 0 || (ring > 0 && ring > cap))
+    return fail(FGM_CUDA_EINVAL, "qkv_post: cap=%d ring=%d (need 0 < ring <= cap)", cap, ring);
+  if (rows > 1 && ((size_t)cap * kv_heads * head_dim > kc_stride || (size_t)cap > ks_stride ||
+                   (size_t)cap > vs_stride ||
+                   (size_t)((cap + 3) & ~3) * kv_heads * head_dim > vt_stride))
+    return fail(FGM_CUDA_EINVAL, "qkv_post: row strides shorter than %d cache slots", cap);
   if (rows < 0 || n_heads <= 0 || kv_heads <= 0 || n_heads + 2 * kv_heads > 48 ||
       head_dim <= 0 || head_dim % 4 != 0 || ring < 0 || q_ld < n_heads * head_dim ||
       kv_ld < kv_heads * head_dim || q_ld % 4 != 0 || kv_ld % 4 != 0)
@@ -1399,7 +1412,7 @@ int fgm_cuda_qkv_post(float *q, int q_ld, float *k, float *v, int kv_ld, int row
   int rc = dev_info(&di);
   if (rc) return rc;
   QkvParams p{q, k, v, q_ld, kv_ld, n_heads, kv_heads, head_dim, q_norm, k_norm, eps, inv_freq,
-              pos, ring, kc, ks, vt, vs, kc_stride, ks_stride, vt_stride, vs_stride};
+              pos, ring, cap, kc, ks, vt, vs, kc_stride, ks_stride, vt_stride, vs_stride};
   if (qkv_post_smem(p) > di->smem_optin)
     return fail(FGM_CUDA_EINVAL, "qkv_post: %d heads of %d need too much shared memory",
                 n_heads + 2 * kv_heads, head_dim);

@@ -128,6 +128,7 @@ struct QkvParams {
   const float *inv_freq;            // [head_dim / 2]
   const int *pos;                   // [rows]
   int ring;                         // 0: slot = pos, else pos % ring
+  int cap;                          // cache slots per row
   int8_t *kc;
   float *ks;
   int8_t *vt;

@@ -80,6 +80,23 @@ __device__ __forceinline__ float reduce16(const float *a) {
   return __fadd_rn(__fadd_rn(t4[0], t4[2]), __fadd_rn(t4[1], t4[3]));
 }
 
+// One of the reference's 16 accumulator lanes over a row in shared memory:
+// acc = fmaf(x[i], x[i], acc) for i = lane, lane + 16, ... < full, in that
+// order.  Loads go out eight at a time so the chain waits on FMAs only.
+__device__ __forceinline__ float lane_sumsq(const float *x, int lane, int full) {
+  float acc = 0.0f;
+  int i = lane;
+  for (; i + 16 * 7 < full; i += 16 * 8) {
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) v[k] = x[i + 16 * k];
+#pragma unroll
+    for (int k = 0; k < 8; k++) acc = __fmaf_rn(v[k], v[k], acc);
+  }
+  for (; i < full; i += 16) acc = __fmaf_rn(x[i], x[i], acc);
+  return acc;
+}
+
 constexpr int kGlueThreads = 256;
 
 // ops.c:59-92, one row per CTA.  The row goes through shared memory; 16
@@ -98,9 +115,7 @@ __global__ void __launch_bounds__(kGlueThreads) rmsnorm_kernel(float *out, const
   __syncthreads();
   const int full = n & ~15;
   if (threadIdx.x < 16) {
-    float acc = 0.0f;
-    for (int i = threadIdx.x; i < full; i += 16) acc = __fmaf_rn(xs[i], xs[i], acc);
-    lanes[threadIdx.x] = acc;
+    lanes[threadIdx.x] = lane_sumsq(xs, threadIdx.x, full);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -610,8 +625,7 @@ __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParam
       }
     }
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-    return;
-  }
+  } else {
 
   // ---- weights w_t = e_t * inv * vs_t: their max per head over the window
   {
@@ -726,6 +740,7 @@ __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParam
                     s_wqs[h]);
     p.out[(size_t)r * p.out_ld + (size_t)(kvh * G + h) * hd + i] = o;
   }
+  }  // !ONE
 }
 
 // ------------------------------------------------------------ fused row ops
@@ -740,9 +755,7 @@ __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParam
 __device__ float rms_inv(const float *xs, int n, float eps, float *lanes, float *s_val) {
   const int full = n & ~15;
   if (threadIdx.x < 16) {
-    float acc = 0.0f;
-    for (int i = threadIdx.x; i < full; i += 16) acc = __fmaf_rn(xs[i], xs[i], acc);
-    lanes[threadIdx.x] = acc;
+    lanes[threadIdx.x] = lane_sumsq(xs, threadIdx.x, full);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -902,7 +915,8 @@ __global__ void __launch_bounds__(kGlueThreads) gelu_mul_prep_kernel(
 // (ops.c:181-204) into the row's caches at slot pos (mod ring): K as a row
 // of the [slot][kv_heads * head_dim] cache, V into the slot-interleaved
 // layout (ops.c:653-660).  q, k and v keep the normalised (and rotated)
-// values, like the reference's buffers.
+// values, like the reference's buffers.  A slot outside [0, cap) writes no
+// cache entry.
 __global__ void __launch_bounds__(kGlueThreads) qkv_post_kernel(const QkvParams p) {
   extern __shared__ __align__(16) float xs[];  // q heads, k heads, v heads; then cos, sin
   __shared__ float lanes[48][16], inv_h[48], red[32];
@@ -932,14 +946,15 @@ __global__ void __launch_bounds__(kGlueThreads) qkv_post_kernel(const QkvParams 
   // per-head sums of squares: a half-warp per head, 16 lanes in order
   for (int hh = threadIdx.x >> 4; hh < heads; hh += blockDim.x >> 4) {
     const float *x = xs + hh * hd;
-    float acc = 0.0f;
-    for (int i = threadIdx.x & 15; i < hd; i += 16) acc = __fmaf_rn(x[i], x[i], acc);
-    lanes[hh][threadIdx.x & 15] = acc;
+    lanes[hh][threadIdx.x & 15] = lane_sumsq(x, threadIdx.x & 15, hd & ~15);
   }
   __syncthreads();
-  if (threadIdx.x < heads)
-    inv_h[threadIdx.x] = __fdiv_rn(
-        1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(reduce16(lanes[threadIdx.x]), (float)hd), p.eps)));
+  if (threadIdx.x < heads) {  // ops.c:59-92: reduced lanes, then the tail past the last 16
+    const float *x = xs + threadIdx.x * hd;
+    float ss = reduce16(lanes[threadIdx.x]);
+    for (int i = hd & ~15; i < hd; i++) ss = __fmaf_rn(x[i], x[i], ss);
+    inv_h[threadIdx.x] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), p.eps)));
+  }
   __syncthreads();
   for (int i = threadIdx.x; i < nq + 2 * kvd; i += blockDim.x) {
     const int hh = i / hd, d = i - hh * hd;
@@ -970,6 +985,7 @@ __global__ void __launch_bounds__(kGlueThreads) qkv_post_kernel(const QkvParams 
   }
   // int8 K and V rows with one scale each, into the caches
   const int slot = p.ring ? pos % p.ring : pos;
+  if (slot < 0 || slot >= p.cap) return;  // no cache entry for this row (whole CTA)
   for (int part = 0; part < 2; part++) {
     const float *x = xs + nq + part * kvd;
     float mx = 0.0f;

@@ -179,12 +179,12 @@ def gelu_mul_prep(gate, up, rows, n, qs, pa, act=None, ld=None, stream=None):
 
 
 def qkv_post(q, k, v, rows, n_heads, kv_heads, head_dim, q_norm, k_norm, eps, inv_freq, pos, ring,
-             kc, kc_stride, ks, ks_stride, vt, vt_stride, vs, vs_stride, q_ld=None, kv_ld=None,
+             cap, kc, kc_stride, ks, ks_stride, vt, vt_stride, vs, vs_stride, q_ld=None, kv_ld=None,
              stream=None):
     """forward.rs:482-545: head norms, rope, int8 K / V rows into the caches."""
     q_ld = n_heads * head_dim if q_ld is None else q_ld
     kv_ld = kv_heads * head_dim if kv_ld is None else kv_ld
     call("fgm_cuda_qkv_post", _p(q), q_ld, _p(k), _p(v), kv_ld, rows, n_heads, kv_heads, head_dim,
-         _p(q_norm), _p(k_norm), eps, _p(inv_freq), _p(pos), ring, _p(kc), kc_stride, _p(ks),
+         _p(q_norm), _p(k_norm), eps, _p(inv_freq), _p(pos), ring, cap, _p(kc), kc_stride, _p(ks),
          ks_stride, _p(vt), vt_stride, _p(vs), vs_stride, _s(stream))
 

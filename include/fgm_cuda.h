@@ -327,11 +327,13 @@ int fgm_cuda_gelu_mul_prep(const float *gate, const float *up, int ld, int rows,
  * 181-204) into row r's caches at slot pos[r] (pos[r] % ring when ring >
  * 0): kc + r*kc_stride [slot][kv_heads*head_dim], ks + r*ks_stride [slot],
  * V into vt + r*vt_stride in the store_v_t layout, vs + r*vs_stride [slot].
+ * Each cache holds cap slots (0 < ring <= cap); a row whose slot falls
+ * outside [0, cap) writes no cache entry.
  * head_dim % 4 == 0, at most 48 heads in all, q, k and v 16-byte aligned,
  * q_ld and kv_ld multiples of 4. */
 int fgm_cuda_qkv_post(float *q, int q_ld, float *k, float *v, int kv_ld, int rows, int n_heads,
                       int kv_heads, int head_dim, const float *q_norm, const float *k_norm, float eps,
-                      const float *inv_freq, const int *pos, int ring, int8_t *kc,
+                      const float *inv_freq, const int *pos, int ring, int cap, int8_t *kc,
                       size_t kc_stride, float *ks, size_t ks_stride, int8_t *vt, size_t vt_stride,
                       float *vs, size_t vs_stride, void *stream);
 

@@ -248,7 +248,8 @@ def test_gelu_mul_prep_against_oracle(orc, rows, n, fused):
     _bits_equal(pa.cpu().numpy(), want_pa, "packed rows")
 
 
-@pytest.mark.parametrize("nh,kvh,hd,ring,fused", [(8, 2, 256, 0, True), (4, 1, 128, 64, False)])
+@pytest.mark.parametrize("nh,kvh,hd,ring,fused", [(8, 2, 256, 0, True), (4, 1, 128, 64, False),
+                                                  (8, 8, 72, 0, False)])
 def test_qkv_post_equals_the_separate_kernels(orc, nh, kvh, hd, ring, fused):
     """Head norms, rope and the int8 K / V cache writes in one launch equal
     the separate glue kernels bit for bit (and the oracle's norms and rope
@@ -279,8 +280,9 @@ def test_qkv_post_equals_the_separate_kernels(orc, nh, kvh, hd, ring, fused):
         tk, tv = dev(k), dev(v)
     kc, ks, vt, vs = caches()
     tpos, tinv = dev(pos), dev(inv_freq)
-    D.qkv_post(tq, tk, tv, rows, nh, kvh, hd, dev(qn), dev(kn), eps, tinv, tpos, ring, kc,
-               slots * kvd, ks, slots, vt, vt.shape[1], vs, slots, kv_ld=2 * kvd if fused else kvd)
+    D.qkv_post(tq, tk, tv, rows, nh, kvh, hd, dev(qn), dev(kn), eps, tinv, tpos, ring, slots,
+               kc, slots * kvd, ks, slots, vt, vt.shape[1], vs, slots,
+               kv_ld=2 * kvd if fused else kvd)
     # the same steps one kernel at a time
     rq, rk, rv = dev(q), dev(k), dev(v)
     D.rmsnorm(rq, rq, dev(qn), rows * nh, hd, eps)
@@ -306,3 +308,28 @@ def test_qkv_post_equals_the_separate_kernels(orc, nh, kvh, hd, ring, fused):
     oq = orc.rope(orc.rmsnorm(q.reshape(-1, hd), qn, eps).reshape(rows, -1)[0], nh, hd, inv_freq,
                   int(pos[0]))
     same(tq.cpu().numpy()[0], oq, False, "q against the oracle")
+
+
+def test_qkv_post_writes_no_cache_entry_outside_the_capacity():
+    """A row whose position falls outside its cache (no ring) keeps its q / k
+    / v results but writes no K / V entry; the other rows write theirs."""
+    rng = np.random.default_rng(3)
+    rows, nh, kvh, hd, cap = 2, 4, 1, 64, 8
+    kvd = kvh * hd
+    q = dev(rng.standard_normal((rows, nh * hd)).astype(np.float32))
+    k = dev(rng.standard_normal((rows, kvd)).astype(np.float32))
+    v = dev(rng.standard_normal((rows, kvd)).astype(np.float32))
+    ones = torch.ones(hd, device="cuda")
+    inv_freq = dev((1.0 / 10000.0 ** (np.arange(0, hd, 2) / hd)).astype(np.float32))
+    pos = dev(np.array([3, 8], np.int32))  # row 1: slot 8 of an 8-slot cache
+    kc = torch.zeros((rows, cap, kvd), dtype=torch.int8, device="cuda")
+    ks = torch.zeros((rows, cap), device="cuda")
+    vt = torch.zeros((rows, cap * kvd), dtype=torch.int8, device="cuda")
+    vs = torch.zeros((rows, cap), device="cuda")
+    D.qkv_post(q, k, v, rows, nh, kvh, hd, ones, ones, 1e-6, inv_freq, pos, 0, cap, kc, cap * kvd,
+               ks, cap, vt, cap * kvd, vs, cap)
+    torch.cuda.synchronize()
+    assert ks[0, 3].item() > 0 and vs[0, 3].item() > 0 and kc[0, 3].abs().sum().item() > 0
+    assert ks[1].abs().sum().item() == 0 and vs[1].abs().sum().item() == 0
+    assert kc[1].abs().sum().item() == 0 and vt[1].abs().sum().item() == 0
+    assert torch.isfinite(q).all() and k[1].abs().sum().item() > 0
