@@ -1357,13 +1357,14 @@ int fgm_cuda_attend_q8(float *out, int out_ld, const float *q, int q_ld, const i
 
 int fgm_cuda_norm_prep(float *h, const float *proj, const float *w_post, const float *w_pre,
                        int rows, int n, float eps, float *qs, int8_t *pa, void *stream) {
-  if (rows < 0 || n <= 0 || n % 64 != 0 || n > 49152)
-    return fail(FGM_CUDA_EINVAL, "norm_prep: rows=%d n=%d (need n %% 64 == 0, n <= 49152)", rows,
+  if (rows < 0 || n <= 0 || n % 64 != 0 || n > 12288)
+    return fail(FGM_CUDA_EINVAL, "norm_prep: rows=%d n=%d (need n %% 64 == 0, n <= 12288)", rows,
                 n);
   if (rows == 0) return FGM_CUDA_OK;
   if (!h || !qs || !pa) return fail(FGM_CUDA_EINVAL, "null pointer");
-  if ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(proj)) & 15)
-    return fail(FGM_CUDA_EINVAL, "norm_prep: h and proj must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(proj) |
+       reinterpret_cast<uintptr_t>(w_post) | reinterpret_cast<uintptr_t>(w_pre)) & 15)
+    return fail(FGM_CUDA_EINVAL, "norm_prep: h, proj and the weights must be 16-byte aligned");
   return glue_done(launch_norm_prep(h, proj, w_post, w_pre, rows, n, eps, qs, pa, use_pdl(),
                                     (cudaStream_t)stream),
                    "norm_prep launch");

@@ -813,7 +813,8 @@ __global__ void __launch_bounds__(kGlueThreads) norm_prep_kernel(
     float *__restrict__ h, const float *__restrict__ proj, const float *__restrict__ w_post,
     const float *__restrict__ w_pre, int m, int n, float eps, float *__restrict__ qs,
     int8_t *__restrict__ pa) {
-  extern __shared__ __align__(16) float xs[];  // [n] the row to normalise, [n] the residual
+  // shared memory: [n] the row to normalise, [n] the residual, [n] w_post, [n] w_pre
+  extern __shared__ __align__(16) float xs[];
   __shared__ float lanes[16], red[32], s_val;
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -822,26 +823,43 @@ __global__ void __launch_bounds__(kGlueThreads) norm_prep_kernel(
     zero_pack_row(n, r, pa);
     return;
   }
-  float *hs = xs + n;
+  float *hs = xs + n, *wa = xs + 2 * n, *wb = xs + 3 * n;
   float4 *h4 = reinterpret_cast<float4 *>(h + (size_t)r * n);
-  const float4 *p4 = proj ? reinterpret_cast<const float4 *>(proj + (size_t)r * n) : nullptr;
-#pragma unroll 4
-  for (int i = threadIdx.x; i < n4; i += blockDim.x) {
-    reinterpret_cast<float4 *>(hs)[i] = h4[i];
-    if (p4) reinterpret_cast<float4 *>(xs)[i] = p4[i];
+  const float4 *src[4] = {h4, proj ? reinterpret_cast<const float4 *>(proj + (size_t)r * n) : nullptr,
+                          proj ? reinterpret_cast<const float4 *>(w_post) : nullptr,
+                          reinterpret_cast<const float4 *>(w_pre)};
+  float4 *dst[4] = {reinterpret_cast<float4 *>(hs), reinterpret_cast<float4 *>(xs),
+                    reinterpret_cast<float4 *>(wa), reinterpret_cast<float4 *>(wb)};
+  // every load of a batch is issued before any shared store
+  for (int base = 0; base < n4; base += 2 * kGlueThreads) {
+    float4 v[4][2];
+#pragma unroll
+    for (int a = 0; a < 4; a++)
+#pragma unroll
+      for (int k = 0; k < 2; k++) {
+        const int i = base + k * kGlueThreads + threadIdx.x;
+        if (src[a] && i < n4) v[a][k] = src[a][i];
+      }
+#pragma unroll
+    for (int a = 0; a < 4; a++)
+#pragma unroll
+      for (int k = 0; k < 2; k++) {
+        const int i = base + k * kGlueThreads + threadIdx.x;
+        if (src[a] && i < n4) dst[a][i] = v[a][k];
+      }
   }
   __syncthreads();
   if (proj) {
     const float inv = rms_inv(xs, n, eps, lanes, &s_val);
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      const float t = w_post ? __fmul_rn(__fmul_rn(xs[i], inv), w_post[i]) : __fmul_rn(xs[i], inv);
+      const float t = w_post ? __fmul_rn(__fmul_rn(xs[i], inv), wa[i]) : __fmul_rn(xs[i], inv);
       hs[i] = __fadd_rn(hs[i], t);
     }
     __syncthreads();
   }
   const float inv = rms_inv(hs, n, eps, lanes, &s_val);
   for (int i = threadIdx.x; i < n; i += blockDim.x)
-    xs[i] = w_pre ? __fmul_rn(__fmul_rn(hs[i], inv), w_pre[i]) : __fmul_rn(hs[i], inv);
+    xs[i] = w_pre ? __fmul_rn(__fmul_rn(hs[i], inv), wb[i]) : __fmul_rn(hs[i], inv);
   __syncthreads();
   if (proj)
     for (int i = threadIdx.x; i < n4; i += blockDim.x) h4[i] = reinterpret_cast<float4 *>(hs)[i];
@@ -918,7 +936,8 @@ __global__ void __launch_bounds__(kGlueThreads) gelu_mul_prep_kernel(
 // values, like the reference's buffers.  A slot outside [0, cap) writes no
 // cache entry.
 __global__ void __launch_bounds__(kGlueThreads) qkv_post_kernel(const QkvParams p) {
-  extern __shared__ __align__(16) float xs[];  // q heads, k heads, v heads; then cos, sin
+  // shared memory: q heads, k heads, v heads; then cos, sin [hd / 2] each, q_norm, k_norm
+  extern __shared__ __align__(16) float xs[];
   __shared__ float lanes[48][16], inv_h[48], red[32];
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -926,21 +945,37 @@ __global__ void __launch_bounds__(kGlueThreads) qkv_post_kernel(const QkvParams 
   const int nq = p.n_heads * hd, kvd = p.kv_heads * hd, heads = p.n_heads + 2 * p.kv_heads;
   float *qr = p.q + (size_t)r * p.q_ld, *kr = p.k + (size_t)r * p.kv_ld,
         *vr = p.v + (size_t)r * p.kv_ld;
-  float *cs = xs + nq + 2 * kvd, *sn = cs + half;
+  float *cs = xs + nq + 2 * kvd, *sn = cs + half, *qn = sn + half, *kn = qn + hd;
   const int pos = p.pos[r];
-  {  // all loads in flight at once: q, k and v rows as float4
-    const int q4 = nq >> 2, k4 = kvd >> 2;
+  {  // q, k and v rows as float4, every load of a batch before any shared store
+    const int q4 = nq >> 2, k4 = kvd >> 2, tot = q4 + 2 * k4;
     float4 *x4 = reinterpret_cast<float4 *>(xs);
-#pragma unroll 4
-    for (int i = threadIdx.x; i < q4 + 2 * k4; i += blockDim.x)
-      x4[i] = i < q4 ? reinterpret_cast<const float4 *>(qr)[i]
-                     : (i < q4 + k4 ? reinterpret_cast<const float4 *>(kr)[i - q4]
-                                    : reinterpret_cast<const float4 *>(vr)[i - q4 - k4]);
+    for (int base = 0; base < tot; base += 4 * kGlueThreads) {
+      float4 v[4];
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const int i = base + k * kGlueThreads + threadIdx.x;
+        if (i < tot)
+          v[k] = i < q4 ? reinterpret_cast<const float4 *>(qr)[i]
+                        : (i < q4 + k4 ? reinterpret_cast<const float4 *>(kr)[i - q4]
+                                       : reinterpret_cast<const float4 *>(vr)[i - q4 - k4]);
+      }
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const int i = base + k * kGlueThreads + threadIdx.x;
+        if (i < tot) x4[i] = v[k];
+      }
+    }
   }
-  for (int j = threadIdx.x; j < half; j += blockDim.x) {
-    const float a = __fmul_rn((float)pos, p.inv_freq[j]);
-    cs[j] = (float)cos((double)a);
-    sn[j] = (float)sin((double)a);
+  for (int j = threadIdx.x; j < hd; j += blockDim.x) {
+    const float a = j < half ? __fmul_rn((float)pos, p.inv_freq[j]) : 0.0f;
+    const float wq = p.q_norm[j], wk = p.k_norm[j];
+    qn[j] = wq;
+    kn[j] = wk;
+    if (j < half) {
+      cs[j] = (float)cos((double)a);
+      sn[j] = (float)sin((double)a);
+    }
   }
   __syncthreads();
   // per-head sums of squares: a half-warp per head, 16 lanes in order
@@ -958,7 +993,7 @@ __global__ void __launch_bounds__(kGlueThreads) qkv_post_kernel(const QkvParams 
   __syncthreads();
   for (int i = threadIdx.x; i < nq + 2 * kvd; i += blockDim.x) {
     const int hh = i / hd, d = i - hh * hd;
-    const float *w = hh < p.n_heads ? p.q_norm : (hh < p.n_heads + p.kv_heads ? p.k_norm : nullptr);
+    const float *w = hh < p.n_heads ? qn : (hh < p.n_heads + p.kv_heads ? kn : nullptr);
     xs[i] = w ? __fmul_rn(__fmul_rn(xs[i], inv_h[hh]), w[d]) : __fmul_rn(xs[i], inv_h[hh]);
   }
   __syncthreads();
@@ -1036,7 +1071,7 @@ unsigned grid_for(size_t n) {
 cudaError_t launch_norm_prep(float *h, const float *proj, const float *w_post, const float *w_pre,
                              int m, int n, float eps, float *qs, int8_t *pa, bool pdl,
                              cudaStream_t st) {
-  const size_t smem = (size_t)n * 8;
+  const size_t smem = (size_t)n * 16;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(norm_prep_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -1074,7 +1109,7 @@ cudaError_t launch_gelu_mul_prep(const float *gate, const float *up, int ld, int
 }
 
 size_t qkv_post_smem(const QkvParams &p) {
-  return ((size_t)(p.n_heads + 2 * p.kv_heads) * p.head_dim + p.head_dim) * 4;
+  return ((size_t)(p.n_heads + 2 * p.kv_heads) * p.head_dim + 3 * (size_t)p.head_dim) * 4;
 }
 
 cudaError_t launch_qkv_post(const QkvParams &p, int rows, bool pdl, cudaStream_t st) {

@@ -305,7 +305,8 @@ int fgm_cuda_attend_q8(float *out, int out_ld, const float *q, int q_ld, const i
  * h += rmsnorm(proj, w_post) for each row (ops.c:59-92 then :317-321; h
  * updated in place); then the packed int8 rows (and scales) of
  * rmsnorm(h, w_pre) for the next GEMM, as fgm_cuda_prep_rows with hsz 0.
- * Rows of n floats (n % 64 == 0, n <= 49152; h and proj 16-byte aligned);
+ * Rows of n floats (n % 64 == 0, n <= 12288; h, proj and the norm weights
+ * 16-byte aligned);
  * pa holds (rows rounded up to 16) x n bytes, the padding rows are
  * zero-filled. */
 int fgm_cuda_norm_prep(float *h, const float *proj, const float *w_post, const float *w_pre,
