@@ -73,6 +73,9 @@ def parse():
     ap.add_argument("--no-lm-head", action="store_true")
     ap.add_argument("--warm", action="store_true",
                     help="each decode GEMM prefetches the next projection's weights into L2")
+    ap.add_argument("--profile-chain", action="store_true",
+                    help="only run the config-3 decode step eagerly: two warm-up steps, then one "
+                         "inside the NVTX range 'decode_chain' (for ncu launch lists)")
     ap.add_argument("--eager", action="store_true",
                     help="launch the step's kernels directly instead of replaying a CUDA graph "
                          "(same kernels, same order; used for ncu launch lists)")
@@ -267,6 +270,16 @@ def main():
 
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
+    if args.profile_chain:
+        step, _ = build_decode_chain(dev, gen, args.chain_context)
+        step()
+        step()
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("decode_chain")
+        step()
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        return
     L = args.layers
     # ---- decode stack: weights streamed from HBM every step
     layers = []

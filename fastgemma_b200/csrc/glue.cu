@@ -991,57 +991,67 @@ __global__ void __launch_bounds__(kGlueThreads) qkv_post_kernel(const QkvParams 
     inv_h[threadIdx.x] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), p.eps)));
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < nq + 2 * kvd; i += blockDim.x) {
-    const int hh = i / hd, d = i - hh * hd;
-    const float *w = hh < p.n_heads ? qn : (hh < p.n_heads + p.kv_heads ? kn : nullptr);
-    xs[i] = w ? __fmul_rn(__fmul_rn(xs[i], inv_h[hh]), w[d]) : __fmul_rn(xs[i], inv_h[hh]);
-  }
-  __syncthreads();
-  // rope on the query and key heads: pairs (j, j + half)
-  for (int idx = threadIdx.x; idx < (p.n_heads + p.kv_heads) * half; idx += blockDim.x) {
-    const int hh = idx / half, j = idx - hh * half;
+  // a warp per head: the norm, rope on query and key heads (pairs j, j +
+  // half), the result stored to the row and, for k and v, kept for the cache
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  float kmx = 0.0f, vmx = 0.0f;
+  for (int hh = warp; hh < heads; hh += nw) {
     float *x = xs + hh * hd;
-    const float lo = x[j], hi = x[j + half];
-    x[j] = __fmaf_rn(lo, cs[j], -__fmul_rn(hi, sn[j]));
-    x[j + half] = __fmaf_rn(hi, cs[j], __fmul_rn(lo, sn[j]));
-  }
-  __syncthreads();
-  {
-    const int q4 = nq >> 2, k4 = kvd >> 2;
-    const float4 *x4 = reinterpret_cast<const float4 *>(xs);
-    for (int i = threadIdx.x; i < q4 + 2 * k4; i += blockDim.x) {
-      if (i < q4)
-        reinterpret_cast<float4 *>(qr)[i] = x4[i];
-      else if (i < q4 + k4)
-        reinterpret_cast<float4 *>(kr)[i - q4] = x4[i];
-      else
-        reinterpret_cast<float4 *>(vr)[i - q4 - k4] = x4[i];
+    const float inv = inv_h[hh];
+    const bool is_q = hh < p.n_heads, is_v = hh >= p.n_heads + p.kv_heads;
+    const float *w = is_q ? qn : kn;
+    float *dst = is_q ? qr + (size_t)hh * hd
+                      : (is_v ? vr + (size_t)(hh - p.n_heads - p.kv_heads) * hd
+                              : kr + (size_t)(hh - p.n_heads) * hd);
+    if (is_v) {
+      for (int d = lane; d < hd; d += 32) {
+        const float y = __fmul_rn(x[d], inv);
+        x[d] = y;
+        dst[d] = y;
+        vmx = fabsf(y) > vmx ? fabsf(y) : vmx;
+      }
+    } else {
+      for (int j = lane; j < half; j += 32) {
+        const float lo = __fmul_rn(__fmul_rn(x[j], inv), w[j]);
+        const float hi = __fmul_rn(__fmul_rn(x[j + half], inv), w[j + half]);
+        const float rl = __fmaf_rn(lo, cs[j], -__fmul_rn(hi, sn[j]));
+        const float rh = __fmaf_rn(hi, cs[j], __fmul_rn(lo, sn[j]));
+        x[j] = rl;
+        x[j + half] = rh;
+        dst[j] = rl;
+        dst[j + half] = rh;
+        if (!is_q) kmx = fmaxf(kmx, fmaxf(fabsf(rl), fabsf(rh)));
+      }
     }
   }
-  // int8 K and V rows with one scale each, into the caches
+  // int8 K and V rows with one scale each (ops.c:181-204), into the caches
   const int slot = p.ring ? pos % p.ring : pos;
   if (slot < 0 || slot >= p.cap) return;  // no cache entry for this row (whole CTA)
-  for (int part = 0; part < 2; part++) {
-    const float *x = xs + nq + part * kvd;
-    float mx = 0.0f;
-    for (int i = threadIdx.x; i < kvd; i += blockDim.x) {
-      const float a = fabsf(x[i]);
-      mx = a > mx ? a : mx;
-    }
-    mx = block_amax(mx, red);
-    const float s = mx == 0.0f ? 1.0f : __fdiv_rn(mx, 127.0f);
-    const float inv = __fdiv_rn(1.0f, s);
-    if (part == 0) {
-      int8_t *dst = p.kc + (size_t)r * p.kc_stride + (size_t)slot * kvd;
-      for (int i = threadIdx.x; i < kvd; i += blockDim.x)
-        dst[i] = (int8_t)q8_x86(__fmul_rn(x[i], inv));
-      if (threadIdx.x == 0) p.ks[(size_t)r * p.ks_stride + slot] = s;
-    } else {
-      int8_t *dst = p.vt + (size_t)r * p.vt_stride + (size_t)(slot >> 2) * kvd * 4 + (slot & 3);
-      for (int i = threadIdx.x; i < kvd; i += blockDim.x)
-        dst[(size_t)i * 4] = (int8_t)q8_x86(__fmul_rn(x[i], inv));
-      if (threadIdx.x == 0) p.vs[(size_t)r * p.vs_stride + slot] = s;
-    }
+  kmx = warp_max(kmx);
+  vmx = warp_max(vmx);
+  if (lane == 0) {
+    red[warp] = kmx;
+    red[16 + warp] = vmx;
+  }
+  __syncthreads();
+  kmx = vmx = 0.0f;
+  for (int w = 0; w < nw; w++) {
+    kmx = red[w] > kmx ? red[w] : kmx;
+    vmx = red[16 + w] > vmx ? red[16 + w] : vmx;
+  }
+  const float ksc = kmx == 0.0f ? 1.0f : __fdiv_rn(kmx, 127.0f);
+  const float vsc = vmx == 0.0f ? 1.0f : __fdiv_rn(vmx, 127.0f);
+  const float kinv = __fdiv_rn(1.0f, ksc), vinv = __fdiv_rn(1.0f, vsc);
+  const float *xk = xs + nq, *xv = xs + nq + kvd;
+  int8_t *kd = p.kc + (size_t)r * p.kc_stride + (size_t)slot * kvd;
+  int8_t *vd = p.vt + (size_t)r * p.vt_stride + (size_t)(slot >> 2) * kvd * 4 + (slot & 3);
+  for (int i = threadIdx.x; i < kvd; i += blockDim.x) {
+    kd[i] = (int8_t)q8_x86(__fmul_rn(xk[i], kinv));
+    vd[(size_t)i * 4] = (int8_t)q8_x86(__fmul_rn(xv[i], vinv));
+  }
+  if (threadIdx.x == 0) {
+    p.ks[(size_t)r * p.ks_stride + slot] = ksc;
+    p.vs[(size_t)r * p.vs_stride + slot] = vsc;
   }
 }
 
