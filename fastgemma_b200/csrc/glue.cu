@@ -535,21 +535,29 @@ __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParam
     // CTA's dimensions (ops.c:560-625)
     cp_async_wait<0>();  // V scales and V (a CTA without slots never waited)
     __syncthreads();
+    // weights per (head, group of 4 slots) into wf (the K stage is free now);
+    // an empty slot weighs 0
+    const int kpad = (p.wslots + 31) & ~31, ngr = kpad >> 2;
+    float *wf = reinterpret_cast<float *>(kst);  // [G][kpad]
     {
       float wl[GM];
 #pragma unroll
       for (int h = 0; h < GM; h++) wl[h] = 0.0f;
-      for (int s = tid; s < p.wslots; s += nt) {
-        const int u = pos_of(p.wbase + s);
-        if (u < 0) continue;
-        const float vsv = vsa[s];
 #pragma unroll
-        for (int h = 0; h < GM; h++)
-          if (h < G) {
-            const float w = __fmul_rn(__fmul_rn(wbuf[h * win + u], s_inv[h]), vsv);
-            wl[h] = w > wl[h] ? w : wl[h];
+      for (int h = 0; h < GM; h++)
+        if (h < G)
+          for (int g = tid; g < ngr; g += nt) {
+            float w4[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+              const int sl = 4 * g + j;
+              const int u = sl < p.wslots ? pos_of(p.wbase + sl) : -1;
+              w4[j] = u < 0 ? 0.0f : __fmul_rn(__fmul_rn(wbuf[h * win + u], s_inv[h]), vsa[sl]);
+              wl[h] = w4[j] > wl[h] ? w4[j] : wl[h];
+            }
+            *reinterpret_cast<float4 *>(wf + h * kpad + 4 * g) =
+                make_float4(w4[0], w4[1], w4[2], w4[3]);
           }
-      }
 #pragma unroll
       for (int h = 0; h < GM; h++) wl[h] = warp_max(wl[h]);
       if (lane == 0)
@@ -565,24 +573,30 @@ __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParam
       s_wqi[tid] = m > 0.0f ? __fdiv_rn(65535.0f, m) : 0.0f;
     }
     __syncthreads();
-    const int kpad = (p.wslots + 31) & ~31;
-    for (int s = tid; s < kpad; s += nt) {
-      const int u = s < p.wslots ? pos_of(p.wbase + s) : -1;
+    // 16-bit weights of their max, high and low bytes packed four slots a word
 #pragma unroll
-      for (int h = 0; h < GM; h++)
-        if (h < G) {
-          int iw = 0;
-          if (u >= 0 && s_wmax[h] > 0.0f) {
-            const float x = __fadd_rn(
-                __fmul_rn(__fmul_rn(__fmul_rn(wbuf[h * win + u], s_inv[h]), vsa[s]), s_wqi[h]),
-                0.5f);
-            iw = (int)x;
-            iw = iw > 65535 ? 65535 : (iw < 0 ? 0 : iw);
+    for (int h = 0; h < GM; h++)
+      if (h < G) {
+        const bool live = s_wmax[h] > 0.0f;
+        const float wqi = s_wqi[h];
+        for (int g = tid; g < ngr; g += nt) {
+          const float4 w4 = *reinterpret_cast<const float4 *>(wf + h * kpad + 4 * g);
+          const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+          uint32_t hi = 0, lo = 0;
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            int iw = 0;
+            if (live) {
+              iw = (int)__fadd_rn(__fmul_rn(wv[j], wqi), 0.5f);
+              iw = iw > 65535 ? 65535 : (iw < 0 ? 0 : iw);
+            }
+            hi |= (uint32_t)(iw >> 8) << (8 * j);
+            lo |= (uint32_t)(iw & 255) << (8 * j);
           }
-          wst[(2 * h) * wld + s] = (uint8_t)(iw >> 8);
-          wst[(2 * h + 1) * wld + s] = (uint8_t)(iw & 255);
+          *reinterpret_cast<uint32_t *>(wst + (2 * h) * wld + 4 * g) = hi;
+          *reinterpret_cast<uint32_t *>(wst + (2 * h + 1) * wld + 4 * g) = lo;
         }
-    }
+      }
     __syncthreads();
     // tiles: 16 dims x 8 columns (head h: columns 2h, 2h + 1 = high, low
     // bytes); the k steps of a tile split over the warps that share it,
@@ -1238,6 +1252,7 @@ bool attend_layout(AttnParams &p, size_t smem_limit) {
     p.kp = cs < kGlueThreads ? ((cs + 15) & ~15) : kGlueThreads;
     size_t kbytes = align16((size_t)p.kp * kld);
     if (kbytes < part) kbytes = align16(part);
+    if (kbytes < (size_t)gm * kpad * 4) kbytes = align16((size_t)gm * kpad * 4);  // weights
     p.vg = p.gchunk;
     p.vgp = kpad / 4;
     p.off_ks = align16((size_t)gm * hd);
