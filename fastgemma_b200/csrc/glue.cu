@@ -357,20 +357,39 @@ __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParam
   };
 
   // ONE: every slot group of this KV head, this CTA's dims
-  auto load_v_dims = [&]() {
-    const int per = dper * 4 / wdt;
+  // by threads [t0, t0 + nthr); every thread commits (equal group counts)
+  auto load_v_dims = [&](int t0, int nthr) {
+    const int per = dper * 4 / wdt, t = tid - t0;
     const int8_t *src = vt + (size_t)(p.wbase / 4) * kvd * 4 + (size_t)d0 * 4;
-    for (int c = tid; c < (p.wslots / 4) * per; c += nt) {
-      const int g = c / per, piece = c - g * per;
-      int8_t *dst = vst + g * vldo + piece * wdt;
-      const int8_t *sp = src + (size_t)g * kvd * 4 + piece * wdt;
-      if (p.vec16)
-        cp_async16(dst, sp);
-      else
-        cp_async4(dst, sp);
+    if (t >= 0 && t < nthr) {
+      if (per <= nthr) {
+        const int gpp = nthr / per, piece = t % per;
+        if (t < gpp * per)
+          for (int g = t / per; g < p.wslots / 4; g += gpp) {
+            int8_t *dst = vst + g * vldo + piece * wdt;
+            const int8_t *sp = src + (size_t)g * kvd * 4 + piece * wdt;
+            if (p.vec16)
+              cp_async16(dst, sp);
+            else
+              cp_async4(dst, sp);
+          }
+      } else {
+        for (int g = 0; g < p.wslots / 4; g++)
+          for (int piece = t; piece < per; piece += nthr) {
+            int8_t *dst = vst + g * vldo + piece * wdt;
+            const int8_t *sp = src + (size_t)g * kvd * 4 + piece * wdt;
+            if (p.vec16)
+              cp_async16(dst, sp);
+            else
+              cp_async4(dst, sp);
+          }
+      }
     }
     cp_async_commit();
   };
+  // ONE: with fewer heads than warps the spare warps issue the V copies
+  // while the others quantise Q
+  const bool v_late = ONE && G < nw;
 
   if constexpr (!ONE)
     for (int i = tid; i < GM * 2 * hd; i += nt) acc[i] = 0;
@@ -383,10 +402,11 @@ __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParam
     for (int s = tid; s < p.wslots; s += nt)
       if (pos_of(p.wbase + s) >= 0) cp_async4(vsa + s, vs + p.wbase + s);
   load_k(0, min(ns, kp));  // commits the scales with the first K stage
-  if constexpr (ONE)
-    load_v_dims();
-  else
+  if constexpr (ONE) {
+    if (!v_late) load_v_dims(0, nt);
+  } else {
     load_v(0, min(ns / 4, vg));
+  }
 
   // ---- Q per head: int8 with one scale (ops.c:412-431)
   for (int h = warp; h < G; h += nw) {
@@ -409,6 +429,7 @@ __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParam
       }
     if (lane == 0) s_qscale[h] = __fdiv_rn(qamax, 127.0f);
   }
+  if (v_late) load_v_dims(G * 32, nt - G * 32);
 
   // ---- scores: exact int8 dots (ops.c:432-474), slots x heads on the
   // tensor cores; an empty slot scores -inf here and weighs 0 below
@@ -489,10 +510,11 @@ __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParam
       if (p.ring) s0 %= p.ring;
       s0 -= p.wbase;
       __syncthreads();
-      for (int i0 = 0; i0 < wn; i0 += 2 * nt) {
-        float v[2][GM];
+      constexpr int kB = GM <= 4 ? 4 : (GM <= 8 ? 2 : 1);  // positions a thread has in flight
+      for (int i0 = 0; i0 < wn; i0 += kB * nt) {
+        float v[kB][GM];
 #pragma unroll
-        for (int k = 0; k < 2; k++) {
+        for (int k = 0; k < kB; k++) {
           const int i = i0 + k * nt + tid;
           if (i < wn) {
             int s = s0 + i;
@@ -504,7 +526,7 @@ __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParam
           }
         }
 #pragma unroll
-        for (int k = 0; k < 2; k++) {
+        for (int k = 0; k < kB; k++) {
           const int i = i0 + k * nt + tid;
           if (i < wn)
 #pragma unroll
@@ -543,21 +565,29 @@ __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParam
       float wl[GM];
 #pragma unroll
       for (int h = 0; h < GM; h++) wl[h] = 0.0f;
+      for (int g = tid; g < ngr; g += nt) {
+        int u[4];
+        float vsv[4];
 #pragma unroll
-      for (int h = 0; h < GM; h++)
-        if (h < G)
-          for (int g = tid; g < ngr; g += nt) {
+        for (int j = 0; j < 4; j++) {
+          const int sl = 4 * g + j;
+          u[j] = sl < p.wslots ? pos_of(p.wbase + sl) : -1;
+          vsv[j] = u[j] < 0 ? 0.0f : vsa[sl];
+        }
+#pragma unroll
+        for (int h = 0; h < GM; h++)
+          if (h < G) {
             float w4[4];
 #pragma unroll
             for (int j = 0; j < 4; j++) {
-              const int sl = 4 * g + j;
-              const int u = sl < p.wslots ? pos_of(p.wbase + sl) : -1;
-              w4[j] = u < 0 ? 0.0f : __fmul_rn(__fmul_rn(wbuf[h * win + u], s_inv[h]), vsa[sl]);
+              w4[j] = u[j] < 0 ? 0.0f
+                               : __fmul_rn(__fmul_rn(wbuf[h * win + u[j]], s_inv[h]), vsv[j]);
               wl[h] = w4[j] > wl[h] ? w4[j] : wl[h];
             }
             *reinterpret_cast<float4 *>(wf + h * kpad + 4 * g) =
                 make_float4(w4[0], w4[1], w4[2], w4[3]);
           }
+      }
 #pragma unroll
       for (int h = 0; h < GM; h++) wl[h] = warp_max(wl[h]);
       if (lane == 0)
