@@ -545,11 +545,12 @@ def build_decode_chain(dev, gen, T, L=30):
     from fastgemma_b200 import device as D
     M, H, NH, KVH, HD, FF = M_DECODE, 2048, 8, 2, 256, 8192
     KVD = KVH * HD
-    # k and v as one [k | v] weight, gate and up as one [gate | up] weight:
-    # config 1's projection shapes; each blob is the two weights' n-blocks
-    # back to back, so a loader builds it by concatenation
-    shapes = [("q", H, NH * HD), ("kv", H, 2 * KVD), ("o", NH * HD, H), ("gate_up", H, 2 * FF),
-              ("down", FF, H)]
+    # q, k and v as one [q | k | v] weight, gate and up as one [gate | up]
+    # weight: each blob is the weights' n-blocks back to back, so a loader
+    # builds it by concatenation, and one GEMM serves the projections that
+    # share an input
+    QKV = NH * HD + 2 * KVD
+    shapes = [("qkv", H, QKV), ("o", NH * HD, H), ("gate_up", H, 2 * FF), ("down", FF, H)]
 
     def q4(k, n):
         w = torch.randint(0, 256, (n * k // 2,), dtype=torch.uint8, device=dev, generator=gen)
@@ -578,7 +579,8 @@ def build_decode_chain(dev, gen, T, L=30):
     pos = torch.full((M,), T - 1, dtype=torch.int32, device=dev)
     x = torch.randn((M, H), device=dev, generator=gen)
     f32 = lambda *shape: torch.empty(shape, device=dev)  # noqa: E731
-    q, kv, attn, o = f32(M, NH * HD), f32(M, 2 * KVD), f32(M, NH * HD), f32(M, H)
+    qkv, attn, o = f32(M, QKV), f32(M, NH * HD), f32(M, H)
+    q, k, v = qkv[:, :NH * HD], qkv[:, NH * HD:NH * HD + KVD], qkv[:, NH * HD + KVD:]
     gu, dn = f32(M, 2 * FF), f32(M, H)
     logits = f32(M, LM_HEAD_N)
     pa = {K: D.packed_a(M, K, dev) for K in (H, FF)}
@@ -598,12 +600,11 @@ def build_decode_chain(dev, gen, T, L=30):
         x.copy_(x0)  # stands in for the embedding gather
         D.norm_prep(x, None, None, layers[0]["in"], M, H, 1e-6, qs, pa[H])
         for li, lw in enumerate(layers):
-            D.gemm_q4g(M, NH * HD, H, pa[H], qs, lw["q"][0], lw["q"][1], GROUP, q)
-            D.gemm_q4g(M, 2 * KVD, H, pa[H], qs, lw["kv"][0], lw["kv"][1], GROUP, kv)
-            D.qkv_post(q, kv, kv[:, KVD:], M, NH, KVH, HD, lw["qn"], lw["kn"], 1e-6, inv_freq, pos,
-                       0, T, lw["kc"], T * KVD, lw["ks"], T, lw["vt"], lw["vt"].shape[1], lw["vs"],
-                       T, kv_ld=2 * KVD)
-            D.attend_q8(attn, NH * HD, q, NH * HD, lw["kc"], T * KVD, lw["ks"], T, lw["vt"],
+            D.gemm_q4g(M, QKV, H, pa[H], qs, lw["qkv"][0], lw["qkv"][1], GROUP, qkv)
+            D.qkv_post(q, k, v, M, NH, KVH, HD, lw["qn"], lw["kn"], 1e-6, inv_freq, pos, 0, T,
+                       lw["kc"], T * KVD, lw["ks"], T, lw["vt"], lw["vt"].shape[1], lw["vs"], T,
+                       q_ld=QKV, kv_ld=QKV)
+            D.attend_q8(attn, NH * HD, q, QKV, lw["kc"], T * KVD, lw["ks"], T, lw["vt"],
                         lw["vt"].shape[1], lw["vs"], T, M, NH, KVH, HD, 0, T)
             D.prep_rows(attn, NH * HD, qs, pa[H], M, NH * HD, 0)
             D.gemm_q4g(M, H, NH * HD, pa[H], qs, lw["o"][0], lw["o"][1], GROUP, o)
@@ -666,8 +667,8 @@ def bench_decode_chain(args, dev, gen, world):
             "workload": f"BASELINE config 3: 30 layers (hidden 2048, 8 q heads / 2 KV heads of "
                         f"256, MLP 8192, int4 g64 projections), {M} sequences at context {T}, "
                         f"norms, rope, int8 KV writes, int8-KV attention, gelu_mul, residuals, "
-                        f"int4 LM head 262144 x 2048, softcap, argmax; k|v and gate|up as one "
-                        f"weight each, the glue between GEMMs fused per row; one CUDA graph per "
+                        f"int4 LM head 262144 x 2048, softcap, argmax; q|k|v and gate|up as "
+                        f"one weight each, the glue between GEMMs fused per row; one CUDA graph per "
                         f"step"}
 
 
