@@ -511,6 +511,22 @@ __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParam
       s0 -= p.wbase;
       __syncthreads();
       constexpr int kB = GM <= 4 ? 4 : (GM <= 8 ? 2 : 1);  // positions a thread has in flight
+      if (!p.ring && (p.start & 3) == 0) {
+        // slots run with positions from a 4-aligned start: four positions are
+        // four slots of one owner, moved as one 16-byte load (any values past
+        // the window end are exponentials of empty slots, 0, never read)
+        for (int i = 4 * tid; i < wn; i += 4 * nt) {
+          const int sl = s0 + i, c = sl / cs;
+          const float *pe = cluster.map_shared_rank(ev, c) + (sl - c * cs);
+          float4 v[GM];
+#pragma unroll
+          for (int hh = 0; hh < GM; hh++)
+            if (hh < G) v[hh] = *reinterpret_cast<const float4 *>(pe + hh * cs);
+#pragma unroll
+          for (int hh = 0; hh < GM; hh++)
+            if (hh < G) *reinterpret_cast<float4 *>(wbuf + hh * win + i) = v[hh];
+        }
+      } else
       for (int i0 = 0; i0 < wn; i0 += kB * nt) {
         float v[kB][GM];
 #pragma unroll
