@@ -841,13 +841,18 @@ __device__ float block_amax(float mx, float *red) {
 // The prep of a row staged in shared memory with no rotation (ops.c:293-314):
 // the symmetric int8 scale of its max (ops.c:181-204), then the row's 64-byte
 // pieces of the packed GEMM tiles.  k is a multiple of 64.
-__device__ void quant_pack_row(const float *xs, int k, int r, float *qs, int8_t *pa, float *red) {
-  float mx = 0.0f;
-  for (int i = threadIdx.x; i < k; i += blockDim.x) {
-    const float a = fabsf(xs[i]);
-    mx = a > mx ? a : mx;
+// mx: this thread's max |x| over the values it wrote, or -1 to scan the row.
+__device__ void quant_pack_row(const float *xs, int k, int r, float *qs, int8_t *pa, float *red,
+                               float mx = -1.0f) {
+  if (mx < 0.0f) {
+    mx = 0.0f;
+    __syncthreads();
+    for (int i = threadIdx.x; i < k; i += blockDim.x) {
+      const float a = fabsf(xs[i]);
+      mx = a > mx ? a : mx;
+    }
   }
-  mx = block_amax(mx, red);
+  mx = block_amax(mx, red);  // its first barrier also publishes xs
   const float s = mx == 0.0f ? 1.0f : __fdiv_rn(mx, 127.0f);
   const float inv = __fdiv_rn(1.0f, s);
   if (threadIdx.x == 0) qs[r] = s;
@@ -918,12 +923,15 @@ __global__ void __launch_bounds__(kGlueThreads) norm_prep_kernel(
     __syncthreads();
   }
   const float inv = rms_inv(hs, n, eps, lanes, &s_val);
-  for (int i = threadIdx.x; i < n; i += blockDim.x)
-    xs[i] = w_pre ? __fmul_rn(__fmul_rn(hs[i], inv), wb[i]) : __fmul_rn(hs[i], inv);
-  __syncthreads();
+  float mx = 0.0f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float y = w_pre ? __fmul_rn(__fmul_rn(hs[i], inv), wb[i]) : __fmul_rn(hs[i], inv);
+    xs[i] = y;
+    mx = fabsf(y) > mx ? fabsf(y) : mx;
+  }
   if (proj)
     for (int i = threadIdx.x; i < n4; i += blockDim.x) h4[i] = reinterpret_cast<float4 *>(hs)[i];
-  quant_pack_row(xs, n, r, qs, pa, red);
+  quant_pack_row(xs, n, r, qs, pa, red, mx);
 }
 
 // ops.c:119-131 then the prep: the down projection's packed rows of
