@@ -266,9 +266,13 @@ __device__ __forceinline__ uint32_t lds32(const void *p) {
 // ONE (the whole window fits one gather, the usual decode case): after the
 // gather every CTA holds all exponentials, so it computes the weight max and
 // all weight bytes itself and multiplies every slot against its own
-// head_dim / C output dimensions -- V staged as [group][its dims], results
-// stored directly -- which drops the weight-max exchange and the integer
-// atomics with their two cluster barriers.
+// head_dim / C output dimensions -- V staged as [group][its dims + padding],
+// the V scales of all slots, the weights and then the P.V partial sums in
+// the K stage, results stored directly.  That drops the weight-max exchange
+// and the integer atomics; the last cluster barrier is split (arrive after
+// the gather, wait at exit) so that no CTA leaves while a peer may still
+// read its exponentials.  With fewer heads than warps, the spare warps issue
+// the V copies while the others quantise Q.
 template <int GM, bool ONE>
 __global__ void __launch_bounds__(kGlueThreads) attend_q8_kernel(const AttnParams p) {
   constexpr int nt = kGlueThreads, nw = kGlueThreads / 32;
