@@ -89,3 +89,48 @@ def test_availability_probe_reports_no_device_here():
     if torch.cuda.is_available():
         pytest.skip("a device is visible")
     assert _lib.lib().fgm_cuda_available() == 0
+
+
+# ---- decode-step glue: argument contracts checked on the host, no device
+_FAKE = 0x10000  # never dereferenced: every case below fails before any access
+
+
+def _err():
+    return _lib.lib().fgm_cuda_last_error().decode()
+
+
+@pytest.mark.parametrize("kw,frag", [
+    (dict(head_dim=96), "head_dim"), (dict(n_heads=6, kv_heads=4), "kv_heads"),
+    (dict(start=0, end=200, ring=128), "ring"), (dict(end=0), "positions"),
+    (dict(out_ld=100), "out_ld"), (dict(rows=2, kc_stride=64 * 256 - 1), "strides"),
+    (dict(rows=2, vt_stride=64 * 256 - 4), "strides")])
+def test_attention_contract(kw, frag):
+    a = dict(out_ld=256, q_ld=256, kc_stride=64 * 256, ks_stride=64, vt_stride=64 * 256,
+             vs_stride=64, rows=1, n_heads=1, kv_heads=1, head_dim=256, start=0, end=64, ring=0)
+    a.update(kw)
+    rc = _lib.lib().fgm_cuda_attend_q8(
+        _FAKE, a["out_ld"], _FAKE, a["q_ld"], _FAKE, a["kc_stride"], _FAKE, a["ks_stride"], _FAKE,
+        a["vt_stride"], _FAKE, a["vs_stride"], a["rows"], a["n_heads"], a["kv_heads"],
+        a["head_dim"], a["start"], a["end"], a["ring"], None)
+    assert rc == -1 and frag in _err(), _err()
+
+
+def test_fused_glue_contracts():
+    L = _lib.lib()
+    # norm_prep: n a multiple of 64, at most 12288
+    assert L.fgm_cuda_norm_prep(_FAKE, None, None, None, 2, 100, 1e-6, _FAKE, _FAKE, None) == -1
+    assert "n=100" in _err()
+    assert L.fgm_cuda_norm_prep(_FAKE, None, None, None, 2, 16384, 1e-6, _FAKE, _FAKE, None) == -1
+    # gelu_mul_prep: rows of gate / up at least n apart
+    assert L.fgm_cuda_gelu_mul_prep(_FAKE, _FAKE, 64, 2, 128, None, _FAKE, _FAKE, None) == -1
+    assert "ld=64" in _err()
+    # qkv_post: the ring must fit the cache, the row strides must hold it
+    args = [_FAKE, 2048, _FAKE, _FAKE, 512, 2, 8, 2, 256, _FAKE, _FAKE, 1e-6, _FAKE, _FAKE]
+    tail = [_FAKE, 1024 * 512, _FAKE, 1024, _FAKE, 1024 * 512, _FAKE, 1024, None]
+    assert L.fgm_cuda_qkv_post(*args, 2048, 1024, *tail) == -1 and "ring" in _err()
+    assert L.fgm_cuda_qkv_post(*args, 0, 2048, *tail) == -1 and "strides" in _err()
+    bad_ld = list(args)
+    bad_ld[1] = 1000
+    assert L.fgm_cuda_qkv_post(*bad_ld, 0, 1024, *tail) == -1 and "q_ld=1000" in _err()
+    # rows == 0 is a no-op that needs no device
+    assert L.fgm_cuda_norm_prep(_FAKE, None, None, None, 0, 2048, 1e-6, _FAKE, _FAKE, None) == 0
