@@ -98,6 +98,15 @@ class _Glue:
         self._f("softcap")(_ptr(x), x.size, C.c_float(cap))
         return x
 
+    def quant_act(self, x: np.ndarray):
+        """ops.c:181-204: rows to int8 with one scale each."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        rows, k = x.shape
+        q = np.empty((rows, k), np.int8)
+        s = np.empty(rows, np.float32)
+        self._f("quant_act")(_ptr(x), rows, k, _ptr(q), _ptr(s))
+        return q, s
+
     def store_v_t(self, vt, src, slot):
         src = np.ascontiguousarray(src, np.int8)
         self._f("store_v_t")(_ptr(vt), _ptr(src), src.size, slot)
@@ -178,14 +187,6 @@ class Oracle(_Glue):
         y = np.ascontiguousarray(x, dtype=np.float32).copy()
         self.lib.orc_fwht(_ptr(y), y.size, hsz)
         return y
-
-    def quant_act(self, x: np.ndarray):
-        x = np.ascontiguousarray(x, dtype=np.float32)
-        rows, k = x.shape
-        q = np.empty((rows, k), np.int8)
-        s = np.empty(rows, np.float32)
-        self.lib.orc_quant_act(_ptr(x), rows, k, _ptr(q), _ptr(s))
-        return q, s
 
     def pack_a(self, a: np.ndarray) -> np.ndarray:
         a = np.ascontiguousarray(a, dtype=np.int8)

@@ -251,3 +251,19 @@ def test_store_v_t_matches_reference_live(orc, ref):
         orc.store_v_t(a, src, slot)
         ref.store_v_t(b, src, slot)
     assert np.array_equal(a, b)
+
+
+def test_composed_decode_step_matches_the_reference(orc, ref):
+    """The toy decode step composed from the oracle's restatements equals the
+    same step composed from the reference's own kernels, bit for bit (GEMMs on
+    the reference's AMX or VNNI path): the step the GPU test checks the device
+    step against is the reference's step."""
+    import decode_step
+    if not ref.usable:
+        pytest.skip("host CPU has neither AMX nor AVX-512 VNNI")
+    inp = decode_step.make_inputs()
+    got = decode_step.compose(orc, inp)
+    want = decode_step.compose(ref, inp)
+    for g, w, what in zip(got, want, ("logits", "K cache", "K scales", "V cache", "V scales")):
+        assert np.array_equal(g.view(np.uint32) if g.dtype == np.float32 else g,
+                              w.view(np.uint32) if w.dtype == np.float32 else w), what
