@@ -1178,6 +1178,9 @@ int fgm_cuda_gemm_q8c_noalloc(int M, int N, int K, const int8_t *A, const float 
   rc = static_rows(&rows);
   if (rc) return rc;
   const cudaStream_t st = (cudaStream_t)stream;
+  // The repack must stay a plain launch (no programmatic dependent launch):
+  // the previous call's GEMM releases its dependents before it has read the
+  // buffer, so an early-started repack could overwrite rows still in use.
   const cudaError_t e = launch_packed_to_rows(A, rows, M, K, st);
   if (e != cudaSuccess) return cuda_fail(e, "activation repack");
   count_launch();

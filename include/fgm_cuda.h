@@ -220,7 +220,9 @@ int fgm_cuda_q8c_release(const int8_t *B);
  * kernel.  The first call on each device is set-up (it resolves the buffer's
  * address and the device's status word): make it before any stream capture.
  * One buffer per device: calls that overlap in time (different streams or
- * host threads) race on it; calls on one stream are ordered. */
+ * host threads) race on it; calls on one stream are ordered.  The buffer is
+ * a file-scope device array, so every device on which this library's kernels
+ * load holds its 4 MiB until the process exits. */
 int fgm_cuda_gemm_q8c_noalloc(int M, int N, int K, const int8_t *A, const float *a_scale,
                               const int8_t *B, const float *b_scale, float *C, int ldc,
                               int n0, int n1, void *stream);

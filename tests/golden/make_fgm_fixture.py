@@ -57,7 +57,8 @@ def weights(bits, n, k, group, seed):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("FGM_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("FGM_REFERENCE") or os.path.join(
+        os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))), "reference"))
     ap.add_argument("--out", default=os.path.join(HERE, "tiny.fgm"))
     args = ap.parse_args()
     fgm = _load(os.path.join(args.ref, "convert", "fgm.py"), "ref_fgm")

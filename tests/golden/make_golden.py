@@ -63,7 +63,8 @@ def pack_ref(ref, M, K, A):
 
 def main():
     ap_ = argparse.ArgumentParser()
-    ap_.add_argument("--ref", default="/root/reference")
+    ap_.add_argument("--ref", default=os.environ.get("FGM_REFERENCE") or os.path.join(
+        os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))), "reference"))
     args = ap_.parse_args()
     orc = Oracle()
     ref = Reference()
