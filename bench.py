@@ -71,6 +71,9 @@ def parse():
                     help="skip the full decode step (BASELINE config 3)")
     ap.add_argument("--chain-context", type=int, default=1024)
     ap.add_argument("--no-lm-head", action="store_true")
+    ap.add_argument("--no-config0", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the config-1 M x shape sweep")
+    ap.add_argument("--no-config4", action="store_true")
     ap.add_argument("--warm", action="store_true",
                     help="each decode GEMM prefetches the next projection's weights into L2")
     ap.add_argument("--profile-chain", action="store_true",
@@ -232,16 +235,23 @@ def cpu_reference_run(layers: int, seconds: float | None, steps: int | None, war
 def run_reference_arm(args, world, rank):
     if rank != 0:
         return
-    gbs, sec, info = cpu_reference_run(args.layers, None, args.steps, args.warmup)
+    # one step = the GPU arm's step: every layer of the stack once
+    gbs, sec, info = cpu_reference_run(args.layers, None, args.steps * args.layers,
+                                       args.warmup * args.layers)
+    sec *= args.layers
     line = {
         "metric": "decode W4A8 GEMM weight GB/s (M=8); prefill W8A8 GEMM int8 TOPS at M=256",
         "impl": "reference", "value": gbs, "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic",
-        "config": {"workload": "BASELINE config 1 at M=8 (decode projections q/kv/o/gate_up/"
-                               "down, int4 g64), one layer per step, reference CPU kernels",
-                   "l2": "12 layer copies rotated (383 MB) > host last-level cache"},
+        "config": {"workload": "BASELINE config 1 at M=8: q 2048x2048, kv 2048x512, o 2048x2048, "
+                               "gate_up 2048x16384, down 8192x2048 (KxN), int4 q4g group 64 f16 "
+                               f"scales, {args.layers} distinct layer copies, 4 preps + 5 GEMMs per "
+                               "layer (the GPU arm's step), reference CPU kernels",
+                   "weight_bytes_per_step": args.layers * sum(sum(q4g_bytes(K, N))
+                                                              for _, K, N in DECODE_SHAPES),
+                   "l2": f"{args.layers} layer copies (381 MB) > host last-level cache"},
         "cpu_baseline": dict(info, value=gbs, unit="GB/s"),
         "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -414,6 +424,9 @@ def main():
     achieved = alg / kmean / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                 "frac": achieved / hbm, "traffic": traffic, "peak_source": peak_src,
+                "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of one ncu "
+                                  "capture of this kernel and shape (profiles/"
+                                  "gemv_q4g_gate_up_M8.md), not measured in this run",
                 "kernel": "gemv_kernel<q4g, M<=8> gate/up 2048x16384",
                 "algorithmic_bytes_per_launch": alg, "mean_launch_us": kmean * 1e6,
                 "launches_timed": len(kdur) * L * R,
@@ -435,6 +448,11 @@ def main():
     prefill = None
     if not args.no_prefill:
         prefill = bench_prefill(args, dev, gen, world)
+
+    # ---- BASELINE config 0 (the metric's own shape), config 1 sweep, config 4
+    config0 = bench_config0(args, dev, gen, world) if not args.no_config0 else None
+    sweep = bench_config1_sweep(args, dev, gen, world) if not args.no_sweep else None
+    config4 = bench_config4(args, dev, world, rank) if not args.no_config4 else None
 
     # ---- e2e through the host-pointer C ABI
     e2e = None
@@ -466,6 +484,7 @@ def main():
             "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clk.summary(),
             "e2e": e2e, "prefill": prefill, "lm_head": lm_head, "decode_chain": chain,
+            "config0": config0, "config1_sweep": sweep, "config4": config4,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
@@ -475,66 +494,316 @@ def main():
         dist.destroy_process_group()
 
 
+def _timed(fn, steps, world, dev, stream=None, warm=3):
+    """Mean device ms of fn() over `steps` calls, CUDA events on `stream`
+    (torch's current stream when None), max over ranks."""
+    import torch
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st = stream or torch.cuda.current_stream()
+    e0.record(st)
+    for _ in range(steps):
+        fn()
+    e1.record(st)
+    torch.cuda.synchronize()
+    return max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
+
+
+def _all_ranks(flag: bool, world: int, dev) -> bool:
+    if world == 1:
+        return bool(flag)
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([1 if flag else 0], dtype=torch.int32, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item())
+
+
 def bench_lm_head(args, dev, gen, world, rank):
     """BASELINE config 3's LM head (int4, N = 262144, K = 2048, M = 8) split by
-    output columns over the ranks, logits all-gathered over NCCL."""
+    output columns over the ranks.  Every rank draws the same whole weight and
+    X (one seed), keeps its column shard, and -- outside the timed regions --
+    checks its gathered logits bit for bit against a whole-width GEMM of the
+    same inputs on its own GPU, for the fused path over three calls (both
+    double buffers) and for the NCCL path."""
     import torch
     from fastgemma_b200 import device as D
     from fastgemma_b200 import shard as S
     N, K, M = LM_HEAD_N, 2048, M_DECODE
+    g = torch.Generator(device=dev)
+    g.manual_seed(2718)  # the same weight and X on every rank
+    w_full = torch.randint(0, 256, (N * K // 2,), dtype=torch.uint8, device=dev, generator=g)
+    s_full = torch.empty((K // GROUP, N), dtype=torch.float32, device=dev).uniform_(
+        0.005, 0.02, generator=g).half()
+    x = torch.randn((M, K), dtype=torch.float32, device=dev, generator=g)
     nb0, nb1 = S.shard_nblocks(N // 16, world, rank)
     cols = (nb1 - nb0) * 16
-    w = torch.randint(0, 256, (cols * K // 2,), dtype=torch.uint8, device=dev, generator=gen)
-    s = torch.empty((K // GROUP, cols), dtype=torch.float32, device=dev).uniform_(
-        0.005, 0.02, generator=gen).half()
+    w = w_full[nb0 * 16 * K // 2:nb1 * 16 * K // 2].clone()
+    s = s_full[:, nb0 * 16:nb1 * 16].contiguous()
     sh = S.ColumnShardedGemm("q4g", None, None, N, K, GROUP, rank=rank, world=world, device=dev,
                              shard=(w, s))
-    x = torch.randn((M, K), dtype=torch.float32, device=dev, generator=gen)
     pa = D.packed_a(M, K, dev)
     qs = torch.empty(M, dtype=torch.float32, device=dev)
     D.prep_rows(x, K, qs, pa, M, K, 0)
     out = torch.empty((M, N), dtype=torch.float32, device=dev)
+    whole = torch.empty((M, N), dtype=torch.float32, device=dev)
+    D.gemm_q4g(M, N, K, pa, qs, w_full, s_full, GROUP, whole)  # the parity reference
     steps = max(10, args.steps // 4)
 
-    def timed(fn):
-        for _ in range(3):
-            fn()
-        torch.cuda.synchronize()
-        if world > 1:
-            import torch.distributed as dist
-            dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(steps):
-            fn()
-        e1.record()
-        torch.cuda.synchronize()
-        return max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
-
-    ms_gemm = timed(lambda: sh.local(M, pa, qs))
+    ms_gemm = _timed(lambda: sh.local(M, pa, qs), steps, world, dev)
     local = sh.local(M, pa, qs)
-    ms_gather = timed(lambda: sh.gather(local, out))
-    ms_nccl = timed(lambda: sh(M, pa, qs, out))
+    ms_gather = _timed(lambda: sh.gather(local, out), steps, world, dev)
+    ms_nccl = _timed(lambda: sh(M, pa, qs, out), steps, world, dev)
+    out.fill_(float("nan"))
+    sh(M, pa, qs, out)
+    torch.cuda.synchronize()
+    parity_nccl = bool(torch.equal(out.view(torch.int32), whole.view(torch.int32)))
     # the product path: GEMM + all-gather fused in one kernel per rank (NVLink stores)
     shf = S.ColumnShardedGemm("q4g", None, None, N, K, GROUP, rank=rank, world=world, device=dev,
                               shard=(w, s), fused=True, max_rows=M)
-    ms_step = timed(lambda: shf(M, pa, qs))
+    ms_step = _timed(lambda: shf(M, pa, qs), steps, world, dev)
+    parity_fused = True
+    for _ in range(3):  # consecutive calls alternate the two peer buffers
+        res = shf(M, pa, qs)
+        torch.cuda.synchronize()
+        parity_fused &= bool(torch.equal(res.view(torch.int32), whole.view(torch.int32)))
     # token choice (row argmax of the logits): on the fused path each rank
     # scans the gathered logits; on the NCCL path the ranks exchange only
     # per-row (value, index) pairs
-    ms_argmax = timed(lambda: shf.argmax(M, pa, qs))
+    ms_argmax = _timed(lambda: shf.argmax(M, pa, qs), steps, world, dev)
+    tok_ref = whole.argmax(dim=1).to(torch.int32)  # no NaN here: first maximum, as the scan
+    tok_f = shf.argmax(M, pa, qs)
     shf.close()
-    ms_argmax_pairs = timed(lambda: sh.argmax(M, pa, qs))
+    ms_argmax_pairs = _timed(lambda: sh.argmax(M, pa, qs), steps, world, dev)
+    tok_p = sh.argmax(M, pa, qs)
+    torch.cuda.synchronize()
+    parity_tok = bool(torch.equal(tok_f, tok_ref)) and bool(torch.equal(tok_p, tok_ref))
+    parity = _all_ranks(parity_nccl and parity_fused and parity_tok, world, dev)
     wbytes = sum(q4g_bytes(K, N))
     return {"value": wbytes / (ms_step * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms_step,
             "gemm_ms": ms_gemm, "nccl_gather_ms": ms_gather, "nccl_step_ms": ms_nccl,
             "argmax_step_ms": ms_argmax, "argmax_pairs_ms": ms_argmax_pairs,
-            "steps": steps,
+            "steps": steps, "cols_per_rank": cols,
+            "parity": parity,
+            "parity_detail": {"fused_3_calls": parity_fused, "nccl": parity_nccl,
+                              "tokens": parity_tok, "all_ranks": parity},
+            "parity_check": "outside the timed regions, every rank's gathered logits equal a "
+                            "whole-width gemm_q4g of the same weight and X on its own GPU, "
+                            "bit for bit; tokens equal the whole logits' row argmax",
             "workload": f"BASELINE config 3 LM head: int4 q4g {N}x{K} group {GROUP} f16 scales, "
                         f"M={M}, {world}-way output-column shards; value: one kernel per rank "
                         f"that also stores its columns into every peer's logits over NVLink; "
                         f"nccl_*: the same GEMM followed by an NCCL all-gather (group-32 f32 "
                         f"scales are outside the fgm-kernels format)"}
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except OSError:
+        return {}
+
+
+def int8_peak():
+    """(TOPS, source): dense int8 tensor peak.  The measured file holds bf16
+    only; int8 runs at twice the bf16 rate on this part, so twice the measured
+    bf16 burst figure (nominal dense int8: 4500 TOPS)."""
+    pk = _peaks()
+    if pk.get("bf16_tflops"):
+        return 2.0 * pk["bf16_tflops"], "2 x measured bf16 burst (MEASURED_PEAKS.json)"
+    return 2.0 * 1590.0, "2 x fallback bf16 1590 TFLOP/s"
+
+
+def hbm_peak():
+    pk = _peaks()
+    if pk.get("hbm_gbs"):
+        return pk["hbm_gbs"], "measured"
+    return 6650.0, "fallback"
+
+
+def tc_roofline(ops, bytes_, seconds, gpus=1):
+    """Roofline block of an int8 tensor-core GEMM step: achieved TOPS per GPU
+    against the int8 peak, and the attainable fraction min(1, AI / ridge)
+    with ridge = peak ops / HBM bytes per second."""
+    peak, src = int8_peak()
+    hbm, _ = hbm_peak()
+    ach = ops / seconds / 1e12 / gpus
+    ai = ops / bytes_
+    ridge = peak * 1e12 / (hbm * 1e9)
+    return {"bound": "tensor" if ai >= ridge else "hbm", "achieved": ach, "peak": peak,
+            "unit": "TOPS", "frac": ach / peak, "peak_source": src, "ops": ops,
+            "algorithmic_bytes": bytes_, "arith_intensity": ai, "ridge": ridge,
+            "attainable_frac": min(1.0, ai / ridge)}
+
+
+def bench_config0(args, dev, gen, world):
+    """one decode projection M=8, N=8192, K=2048, int4 g64,
+    as fastgemma's Gemm::run -- prep of f32 X then the GEMM -- over a chain of
+    32 distinct weight copies (285 MB > 2 x L2), one CUDA graph."""
+    import torch
+    from fastgemma_b200 import device as D
+    M, N, K, copies = M_DECODE, 8192, 2048, 32
+    wb, sb = q4g_bytes(K, N)
+    ws = [(torch.randint(0, 256, (wb,), dtype=torch.uint8, device=dev, generator=gen),
+           torch.empty((K // GROUP, N), device=dev).uniform_(0.005, 0.02, generator=gen).half())
+          for _ in range(copies)]
+    x = torch.randn((M, K), device=dev, generator=gen)
+    pa, qs = D.packed_a(M, K, dev), torch.empty(M, device=dev)
+    c = torch.empty((M, N), device=dev)
+    side = torch.cuda.Stream(device=dev)
+
+    def chain():
+        for w, s in ws:
+            D.prep_rows(x, K, qs, pa, M, K, 0)
+            D.gemm_q4g(M, N, K, pa, qs, w, s, GROUP, c)
+
+    with torch.cuda.stream(side):
+        chain()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        chain()
+    ms = _timed(g.replay, max(5, args.steps // 10), world, dev, stream=side)
+    del g
+    per_call = ms / copies
+    hbm, src = hbm_peak()
+    alg = wb + sb + M * K * 4 + M * N * 4
+    gbs = (wb + sb) / (per_call * 1e-3) / 1e9
+    return {"value": world * gbs, "unit": "GB/s", "us_per_call": per_call * 1e3,
+            "frac_hbm": (alg / (per_call * 1e-3) / 1e9) / hbm, "hbm_peak": hbm,
+            "peak_source": src, "algorithmic_bytes": alg,
+            "workload": f"BASELINE config 0: prep + int4 GEMM M={M} N={N} K={K} g{GROUP} f16 "
+                        f"scales, {copies} distinct weight copies per graph replay; value = "
+                        f"weight+scale bytes / time per call"}
+
+
+def bench_config1_sweep(args, dev, gen, world):
+    """BASELINE config 1 as fastgemma's gemm_bench sweeps it
+    (bench/kernels/gemm_bench.c:253-307): each (M, projection) timed alone
+    as back-to-back GEMMs over distinct weight copies (> 2 x L2 per shape),
+    M in {1, 2, 4, 8, 16}."""
+    import torch
+    from fastgemma_b200 import device as D
+    K_all = (2048, 8192)
+    out = {}
+    side = torch.cuda.Stream(device=dev)
+    hbm, _ = hbm_peak()
+    for name, K, N in DECODE_SHAPES:
+        wb, sb = q4g_bytes(K, N)
+        copies = max(4, min(128, -(-2 * 126 * 2 ** 20 // (wb + sb))))
+        ws = [(torch.randint(0, 256, (wb,), dtype=torch.uint8, device=dev, generator=gen),
+               torch.empty((K // GROUP, N), device=dev).uniform_(0.005, 0.02,
+                                                                 generator=gen).half())
+              for _ in range(copies)]
+        c = torch.empty((16, N), device=dev)
+        for M in (1, 2, 4, 8, 16):
+            x = torch.randn((M, K), device=dev, generator=gen)
+            pa, qs = D.packed_a(M, K, dev), torch.empty(M, device=dev)
+            D.prep_rows(x, K, qs, pa, M, K, 0)
+
+            def chain():
+                for w, s in ws:
+                    D.gemm_q4g(M, N, K, pa, qs, w, s, GROUP, c)
+
+            with torch.cuda.stream(side):
+                chain()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=side):
+                chain()
+            ms = _timed(g.replay, 5, world, dev, stream=side)
+            del g
+            us = ms * 1e3 / copies
+            alg = wb + sb + M * K + M * 4 + M * N * 4
+            out.setdefault(f"M{M}", {})[name] = {
+                "us": us, "weight_gbs": (wb + sb) / (us * 1e-6) / 1e9,
+                "frac_hbm": alg / (us * 1e-6) / 1e9 / hbm}
+        del ws
+    return {"unit": "us per GEMM / weight GB/s", "results": out,
+            "workload": "BASELINE config 1: int4 g64 GEMM alone (prep excluded), back to back "
+                        "over distinct weight copies (> 2 x L2 per shape), one CUDA graph; "
+                        "frac_hbm = algorithmic bytes / time / measured HBM"}
+
+
+def bench_config4(args, dev, world, rank):
+    """M in {256, 1024, 4096} x K=2048 x N=262144 int8
+    (the LM-head width), columns sharded over the ranks, NCCL all-gather of
+    each rank's column block.  GEMM-only and GEMM + gather are timed apart
+    and reported as whole-job int8 TOPS and per-GPU fraction of int8 peak;
+    outside the timed regions every rank checks the gathered output bit for
+    bit against a whole-width GEMM of the same inputs on its own GPU."""
+    import torch
+    import torch.distributed as dist
+    from fastgemma_b200 import device as D
+    from fastgemma_b200 import shard as S
+    N, K = LM_HEAD_N, 2048
+    g = torch.Generator(device=dev)
+    g.manual_seed(31337)  # same weight on every rank
+    w_full = torch.randint(-127, 128, (N * K,), dtype=torch.int8, device=dev, generator=g)
+    s_full = torch.empty(N, device=dev).uniform_(0.001, 0.01, generator=g)
+    nb0, nb1 = S.shard_nblocks(N // 16, world, rank)
+    cols = (nb1 - nb0) * 16
+    w = w_full[nb0 * 16 * K:nb1 * 16 * K].clone()
+    s = s_full[nb0 * 16:nb1 * 16].contiguous()
+    D.q8c_prepare(w, cols, K)
+    res = {}
+    steps = max(3, args.steps // 20)
+    for M in (256, 1024, 4096):
+        x = torch.randn((M, K), device=dev, generator=g)
+        qa = torch.empty((M, K), dtype=torch.int8, device=dev)
+        qs = torch.empty(M, device=dev)
+        pa = D.packed_a(M, K, dev)
+        D.prep_rows(x, K, qs, pa, M, K, 0, qa=qa)
+        local = torch.empty((M, cols), device=dev)
+        gathered = torch.empty((world, M, cols), device=dev)
+
+        def gemm():
+            D.gemm_q8c_rows(M, cols, K, qa, qs, w, s, local)
+
+        def gemm_gather():
+            gemm()
+            if world > 1:
+                dist.all_gather_into_tensor(gathered, local)
+
+        ms_gemm = _timed(gemm, steps, world, dev)
+        ms_all = _timed(gemm_gather, steps, world, dev)
+        # parity: whole-width GEMM of the same inputs on this GPU
+        D.q8c_prepare(w_full, N, K)
+        whole = torch.empty((M, N), device=dev)
+        D.gemm_q8c_rows(M, N, K, qa, qs, w_full, s_full, whole)
+        D.q8c_release(w_full)
+        gemm_gather()
+        torch.cuda.synchronize()
+        ok = True
+        for r, (a, b) in enumerate(S.shard_ranges(N // 16, world)):
+            src = gathered[r] if world > 1 else local
+            ok &= bool(torch.equal(src.view(torch.int32),
+                                   whole[:, a * 16:b * 16].contiguous().view(torch.int32)))
+        del whole
+        torch.cuda.empty_cache()
+        ops = 2.0 * M * N * K
+        bytes_ = N * K + N * 4 + world * (M * K + M * 4) + M * N * 4
+        res[f"M{M}"] = {
+            "gemm_ms": ms_gemm, "gemm_gather_ms": ms_all,
+            "gemm_tops": ops / (ms_gemm * 1e-3) / 1e12,
+            "gemm_gather_tops": ops / (ms_all * 1e-3) / 1e12,
+            "roofline_gemm": tc_roofline(ops, bytes_, ms_gemm * 1e-3, world),
+            "parity": _all_ranks(ok, world, dev)}
+        del local, gathered
+    D.q8c_release(w)
+    return {"unit": "TOPS (whole job)", "results": res, "n_gpus": world,
+            "cols_per_rank": cols,
+            "workload": f"BASELINE config 4: prep of X~N(0,1) then W8A8 GEMM M x K={K} x N={N}, "
+                        f"{world}-way output-column shards (one prepared int8 shard per rank), "
+                        f"gather = NCCL all_gather_into_tensor of the [M, N/{world}] blocks "
+                        f"(rank-major); roofline per GPU; parity: gathered blocks == a "
+                        f"whole-width GEMM on each rank's own GPU, bit for bit"}
 
 
 def build_decode_chain(dev, gen, T, L=30):
@@ -726,8 +995,13 @@ def bench_prefill(args, dev, gen, world):
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
     ops = copies * sum(2 * M_PREFILL * N * K for _, K, N in PREFILL_SHAPES)
+    # algorithmic bytes: int8 weights + scales, X f32 in, int8 X out of prep and
+    # back in, Y f32 out
+    bytes_ = copies * sum(N * K + N * 4 + M_PREFILL * K * 4 + 2 * M_PREFILL * K + M_PREFILL * N * 4
+                          for _, K, N in PREFILL_SHAPES)
     return {"value": world * ops / (ms * 1e-3) / 1e12, "unit": "TOPS", "ms_per_step": ms,
-            "steps": steps, "workload": f"BASELINE config 2: M=256 prep + W8A8 GEMM at "
+            "steps": steps, "roofline": tc_roofline(ops, bytes_, ms * 1e-3),
+            "workload": f"BASELINE config 2: M=256 prep + W8A8 GEMM at "
             f"2048x16384 and 8192x2048 (KxN), {copies} weight copies per step"}
 
 
