@@ -498,18 +498,20 @@ def _timed(fn, steps, world, dev, stream=None, warm=3):
     """Mean device ms of fn() over `steps` calls, CUDA events on `stream`
     (torch's current stream when None), max over ranks."""
     import torch
-    for _ in range(warm):
-        fn()
+    with torch.cuda.stream(stream or torch.cuda.current_stream()):
+        for _ in range(warm):
+            fn()
     torch.cuda.synchronize()
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     st = stream or torch.cuda.current_stream()
-    e0.record(st)
-    for _ in range(steps):
-        fn()
-    e1.record(st)
+    with torch.cuda.stream(st):  # fn launches (and graphs replay) on the timed stream
+        e0.record(st)
+        for _ in range(steps):
+            fn()
+        e1.record(st)
     torch.cuda.synchronize()
     return max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
 
@@ -994,6 +996,9 @@ def bench_prefill(args, dev, gen, world):
         e1.record(side)
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
+    for lw in ws:  # the tensor-core copies are keyed by the weights' addresses
+        for w, _ in lw.values():
+            D.q8c_release(w)
     ops = copies * sum(2 * M_PREFILL * N * K for _, K, N in PREFILL_SHAPES)
     # algorithmic bytes: int8 weights + scales, X f32 in, int8 X out of prep and
     # back in, Y f32 out
