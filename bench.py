@@ -74,6 +74,8 @@ def parse():
     ap.add_argument("--no-config0", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the config-1 M x shape sweep")
     ap.add_argument("--no-config4", action="store_true")
+    ap.add_argument("--no-per-call", action="store_true",
+                    help="skip the config-1 step timed as per-call launches")
     ap.add_argument("--warm", action="store_true",
                     help="each decode GEMM prefetches the next projection's weights into L2")
     ap.add_argument("--profile-chain", action="store_true",
@@ -304,72 +306,37 @@ def main():
         layers.append(lw)
     xs = [torch.randn((M_DECODE, K), dtype=torch.float32, device=dev, generator=gen)
           for K in (2048, 2048, 2048, 8192)]
-    pas = [D.packed_a(M_DECODE, x.shape[1], dev) for x in xs]
-    qss = [torch.empty(M_DECODE, dtype=torch.float32, device=dev) for _ in xs]
-    cs = {name: torch.empty((M_DECODE, N), dtype=torch.float32, device=dev)
-          for name, K, N in DECODE_SHAPES}
     wbytes_step = L * sum(sum(q4g_bytes(K, N)) for _, K, N in DECODE_SHAPES)
 
-    # the decode order of the projections; with --warm each GEMM warms L2 with
-    # the weights of the one after it (the last wraps to the next step's first)
-    order = [(l, name) for l in range(L) for name, _, _ in DECODE_SHAPES]
-
-    def step():
-        j = 0
-        for l in range(L):
-            for i, x in enumerate(xs):
-                D.prep_rows(x, x.shape[1], qss[i], pas[i], M_DECODE, x.shape[1], 0)
-            for name, K, N in DECODE_SHAPES:
-                w, s = layers[l][name]
-                i = DECODE_INPUT[name]
-                if not args.warm:
-                    D.gemm_q4g(M_DECODE, N, K, pas[i], qss[i], w, s, GROUP, cs[name])
-                else:
-                    nl, nname = order[(j + 1) % len(order)]
-                    D.gemm_q4g_warm(M_DECODE, N, K, pas[i], qss[i], w, s, GROUP, cs[name],
-                                    layers[nl][nname])
-                j += 1
-
-    def gate_up_only():  # the dominant kernel back to back over the L weight copies
-        i = DECODE_INPUT["gate_up"]
-        K, N = 2048, 16384
-        for l in range(L):
-            w, s = layers[l]["gate_up"]
-            D.gemm_q4g(M_DECODE, N, K, pas[i], qss[i], w, s, GROUP, cs["gate_up"])
-
+    # The step as ONE work-list launch: per layer the four preps (each into
+    # its own packed buffer) and the five GEMMs, each waiting inside the
+    # launch for the prep it reads; every (layer, projection) has its own
+    # output rows.
+    wl = D.WorkList()
+    outs = []
+    for l in range(L):
+        pidx = []
+        for x in xs:
+            K = x.shape[1]
+            pa, qs = D.packed_a(M_DECODE, K, dev), torch.empty(M_DECODE, device=dev)
+            pidx.append((wl.prep(x, K, K, pa, qs), pa, qs))
+        for name, K, N in DECODE_SHAPES:
+            w, s = layers[l][name]
+            ip, pa, qs = pidx[DECODE_INPUT[name]]
+            c = torch.empty((M_DECODE, N), dtype=torch.float32, device=dev)
+            wl.gemm_q4g(N, K, pa, qs, w, s, GROUP, c, deps=(ip,))
+            outs.append(c)
+    wl.build(M_DECODE)
     side = torch.cuda.Stream(device=dev)
-    with torch.cuda.stream(side):
-        c0 = lib.fgm_cuda_launch_count()
-        step()
-        launches_per_step = lib.fgm_cuda_launch_count() - c0
+
+    def run_step():
+        with torch.cuda.stream(side):
+            wl.run()
+
+    c0 = lib.fgm_cuda_launch_count()
+    run_step()
+    launches_per_step = lib.fgm_cuda_launch_count() - c0
     torch.cuda.synchronize()
-    if args.eager:
-        graph = tgraph = None
-
-        def run_step():
-            with torch.cuda.stream(side):
-                step()
-
-        def run_gate_up():
-            with torch.cuda.stream(side):
-                gate_up_only()
-    else:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=side):
-            step()
-        # the dominant kernel alone: L back-to-back launches over distinct weights
-        tgraph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(tgraph, stream=side):
-            gate_up_only()
-
-        def run_step():
-            with torch.cuda.stream(side):
-                graph.replay()
-
-        def run_gate_up():
-            with torch.cuda.stream(side):
-                tgraph.replay()
-
     for _ in range(max(args.warmup, 3)):
         run_step()
     torch.cuda.synchronize()
@@ -388,51 +355,41 @@ def main():
         torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / args.steps
     value = world * wbytes_step / (ms * 1e-3) / 1e9
+    from fastgemma_b200 import _lib as _L
+    _L.call("fgm_cuda_device_status")
 
-    # ---- roofline of the dominant kernel (gate/up q4g GEMM), CUDA events
-    # R replays of the L-launch chain per event pair: L*R launches back to back
-    # (inputs 12 x 17.9 MB > L2), so one host-side graph launch gap is spread
-    # over L*R kernels instead of L
-    kdur, R = [], 8
-    run_gate_up()
-    torch.cuda.synchronize()
-    for _ in range(3):
-        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        k0.record(side)
-        for _ in range(R):
-            run_gate_up()
-        k1.record(side)
-        torch.cuda.synchronize()
-        kdur.append(k0.elapsed_time(k1) * 1e-3 / (L * R))
-    K_, N_ = 2048, 16384
-    alg = sum(q4g_bytes(K_, N_)) + M_DECODE * K_ + M_DECODE * 4 + M_DECODE * N_ * 4
-    kmean = statistics.mean(kdur)
-    peaks = {}
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            peaks = json.load(f)
-    except OSError:
-        pass
-    hbm = peaks.get("hbm_gbs")
-    peak_src = "measured" if hbm else "fallback"
-    hbm = hbm or 6650.0
+    # ---- roofline of the dominant kernel: the work-list kernel is the whole
+    # step (one launch), so its launch duration is the step time above.
+    # Algorithmic bytes per launch: weights + scales, the preps' f32 rows in
+    # and packed rows + scales out, every GEMM's packed rows + scales in and
+    # f32 rows out.
+    M = M_DECODE
+    alg = wbytes_step + L * (sum(M * x.shape[1] * 4 + M * x.shape[1] + M * 4 for x in xs)
+                             + sum(M * K + M * 4 + M * N * 4 for _, K, N in DECODE_SHAPES))
+    hbm, peak_src = hbm_peak()
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
         with open(tpath) as f:
-            traffic = json.load(f).get("gemv_q4g_gate_up_M8")
-    achieved = alg / kmean / 1e9
+            traffic = json.load(f).get("worklist_config1_M8")
+    achieved = alg / (ms * 1e-3) / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                 "frac": achieved / hbm, "traffic": traffic, "peak_source": peak_src,
                 "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of one ncu "
-                                  "capture of this kernel and shape (profiles/"
-                                  "gemv_q4g_gate_up_M8.md), not measured in this run",
-                "kernel": "gemv_kernel<q4g, M<=8> gate/up 2048x16384",
-                "algorithmic_bytes_per_launch": alg, "mean_launch_us": kmean * 1e6,
-                "launches_timed": len(kdur) * L * R,
-                "timing": "CUDA events on the launching stream around "
-                          + (f"{R} passes of " if args.eager else f"{R} replays of a graph of ")
-                          + f"{L} back-to-back launches over distinct weight copies"}
+                                  "capture of this kernel on this list (profiles/"
+                                  "worklist_config1_M8.md), not measured in this run",
+                "kernel": f"worklist_kernel<MT=1>: {L} layers x (4 preps + 5 int4 GEMMs)",
+                "algorithmic_bytes_per_launch": alg, "mean_launch_us": ms * 1e3,
+                "launches_timed": args.steps,
+                "timing": "CUDA events on the launching stream around the timed steps "
+                          "(one launch per step)"}
+
+    # ---- the same step as one launch per prep and per GEMM (the per-call
+    # entries in a CUDA graph): what the list replaces
+    per_call = None
+    if not args.no_per_call:
+        per_call = bench_config1_per_call(args, dev, world, layers, xs, side)
+    del outs
 
     # ---- LM head, column-sharded over the ranks
     lm_head = None
@@ -479,8 +436,10 @@ def main():
                             f"scales, {L} distinct layer copies, 4 preps + 5 GEMMs per layer",
                 "weight_bytes_per_step": wbytes_step, "l2": "inputs larger than L2 "
                 f"({wbytes_step / 1e6:.0f} MB of weights per step > 2 x 126 MB)",
-                "graph": "eager launches (--eager)" if args.eager else "one CUDA graph per step", "parallelism": f"replicas x{world}"},
+                "launch": "one work-list kernel launch per step (fgm_cuda_worklist_run)",
+                "parallelism": f"replicas x{world}"},
             "roofline": roofline,
+            "config1_per_call": per_call,
             "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clk.summary(),
             "e2e": e2e, "prefill": prefill, "lm_head": lm_head, "decode_chain": chain,
@@ -488,9 +447,9 @@ def main():
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+    wl.close()
     if world > 1:
         dist.barrier()
-        del graph, tgraph
         dist.destroy_process_group()
 
 
@@ -524,6 +483,41 @@ def _all_ranks(flag: bool, world: int, dev) -> bool:
     t = torch.tensor([1 if flag else 0], dtype=torch.int32, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MIN)
     return bool(t.item())
+
+
+def bench_config1_per_call(args, dev, world, layers, xs, side):
+    """The config-1 step as separate launches: per layer four prep_rows and
+    five gemm_q4g calls (the per-call device entries), captured in one CUDA
+    graph -- the launch structure the work list replaces."""
+    import torch
+    from fastgemma_b200 import device as D
+    L, M = len(layers), M_DECODE
+    pas = [D.packed_a(M, x.shape[1], dev) for x in xs]
+    qss = [torch.empty(M, device=dev) for _ in xs]
+    cs = {name: torch.empty((M, N), device=dev) for name, K, N in DECODE_SHAPES}
+
+    def step():
+        for l in range(L):
+            for i, x in enumerate(xs):
+                D.prep_rows(x, x.shape[1], qss[i], pas[i], M, x.shape[1], 0)
+            for name, K, N in DECODE_SHAPES:
+                w, s = layers[l][name]
+                i = DECODE_INPUT[name]
+                D.gemm_q4g(M, N, K, pas[i], qss[i], w, s, GROUP, cs[name])
+
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        step()
+    ms = _timed(g.replay, max(5, args.steps // 2), world, dev, stream=side)
+    del g
+    wbytes = L * sum(sum(q4g_bytes(K, N)) for _, K, N in DECODE_SHAPES)
+    return {"value": world * wbytes / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms,
+            "launches_per_step": L * (len(xs) + len(DECODE_SHAPES)),
+            "workload": "the config-1 step as 108 launches (prep_rows + gemm_q4g per "
+                        "projection) in one CUDA graph"}
 
 
 def bench_lm_head(args, dev, gen, world, rank):

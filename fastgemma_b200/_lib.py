@@ -46,6 +46,9 @@ SIGNATURES = {
     "fgm_cuda_gemm_q8c_rows": ([_i, _i, _i, _p, _i, _p, _p, _p, _p, _i, _i, _i, _p], _i),
     "fgm_cuda_q8c_release": ([_p], _i),
     "fgm_cuda_gemm_q8c_noalloc": ([_i, _i, _i, _p, _p, _p, _p, _p, _i, _i, _i, _p], _i),
+    "fgm_cuda_worklist_create": ([_i, _p, _i, C.POINTER(_p)], _i),
+    "fgm_cuda_worklist_run": ([_p, _p], _i),
+    "fgm_cuda_worklist_destroy": ([_p], _i),
     "fgm_cuda_argmax_parts": ([_i], _i),
     "fgm_cuda_argmax_partials": ([_p, _i, _i, _i, _i, _p, _p, _p], _i),
     "fgm_cuda_argmax_merge": ([_p, _p, _i, _i, _p, _p], _i),

@@ -1187,6 +1187,57 @@ int fgm_cuda_gemm_q8c_noalloc(int M, int N, int K, const int8_t *A, const float 
   return run_q8c_tc(M, N, K, rows, K, a_scale, b_scale, map, C, ldc, 0, nullptr, n0, n1, st);
 }
 
+// ------------------------------------------------------- decode work list
+struct WorkList {
+  int dev = -1;
+  int n = 0;
+  WlPlan plan;
+  void *mem = nullptr;
+  WlParams params{};
+};
+
+static int check_work(int M, const fgm_cuda_work &w, int i, int n) {
+  for (int d : w.deps)
+    if (d != -1 && (d < 0 || d >= i))
+      return fail(FGM_CUDA_EINVAL, "work %d: dependency %d is not an earlier entry", i, d);
+  (void)n;
+  auto al = [](const void *p, unsigned a) { return ((uintptr_t)p & (a - 1)) == 0; };
+  if (w.kind == FGM_CUDA_WORK_PREP) {
+    if (w.K <= 0 || w.K % 128 != 0 || w.K > 65536)
+      return fail(FGM_CUDA_EINVAL, "work %d (prep): K=%d, need K %% 128 == 0", i, w.K);
+    if (w.lda < w.K || w.lda % 4 != 0)
+      return fail(FGM_CUDA_EINVAL, "work %d (prep): lda=%d, need lda >= K, lda %% 4 == 0", i,
+                  w.lda);
+    if (w.hsz < 0 || w.hsz > 128 || (w.hsz & (w.hsz - 1)) != 0 || (w.hsz > 0 && w.K % w.hsz))
+      return fail(FGM_CUDA_EINVAL, "work %d (prep): hsz=%d, need 0 or a power of two <= 128",
+                  i, w.hsz);
+    if (!w.src || !w.pa || !w.qs) return fail(FGM_CUDA_EINVAL, "work %d (prep): null pointer", i);
+    if (!al(w.src, 16) || !al(w.pa, 4) || !al(w.qs, 4))
+      return fail(FGM_CUDA_EINVAL, "work %d (prep): src must be 16-byte, pa and qs 4-byte aligned",
+                  i);
+    return FGM_CUDA_OK;
+  }
+  if (w.kind != FGM_CUDA_WORK_Q4G && w.kind != FGM_CUDA_WORK_Q8C)
+    return fail(FGM_CUDA_EINVAL, "work %d: kind %d", i, w.kind);
+  const bool q4 = w.kind == FGM_CUDA_WORK_Q4G;
+  if (w.K <= 0 || w.K % (q4 ? 512 : 256) != 0 || w.K > 16384)
+    return fail(FGM_CUDA_EINVAL, "work %d: K=%d, need K %% %d == 0 and K <= 16384", i, w.K,
+                q4 ? 512 : 256);
+  if (w.N <= 0 || w.N % 16 != 0) return fail(FGM_CUDA_EINVAL, "work %d: N=%d", i, w.N);
+  if (w.n0 < 0 || w.n1 <= w.n0 || w.n1 > w.N / 16)
+    return fail(FGM_CUDA_EINVAL, "work %d: n-blocks [%d, %d) of %d", i, w.n0, w.n1, w.N / 16);
+  if (w.ldc < w.n1 * 16) return fail(FGM_CUDA_EINVAL, "work %d: ldc=%d", i, w.ldc);
+  if (q4 && (w.group != 64 && w.group != 128 && w.group != 256 && w.group != 512))
+    return fail(FGM_CUDA_EINVAL, "work %d: group %d, need 64, 128, 256 or 512", i, w.group);
+  if (q4 && w.K % w.group) return fail(FGM_CUDA_EINVAL, "work %d: K %% group != 0", i);
+  if (!w.A || !w.a_scale || !w.B || !w.b_scale || !w.C)
+    return fail(FGM_CUDA_EINVAL, "work %d: null pointer", i);
+  if (!al(w.A, 16) || !al(w.B, 16) || !al(w.b_scale, 4))
+    return fail(FGM_CUDA_EINVAL, "work %d: A and B must be 16-byte, scales 4-byte aligned", i);
+  (void)M;
+  return FGM_CUDA_OK;
+}
+
 // ---------------------------------------------------------- row argmax
 int fgm_cuda_argmax_partials(const float *C, int M, int N, int ldc, int col0, float *vals,
                              int32_t *idx, void *stream) {
@@ -1202,6 +1253,124 @@ int fgm_cuda_argmax_partials(const float *C, int M, int N, int ldc, int col0, fl
 }
 
 int fgm_cuda_argmax_parts(int N) { return N > 0 ? argmax_chunk_count(N) : 0; }
+
+int fgm_cuda_worklist_create(int M, const fgm_cuda_work *w, int n, void **list) {
+  if (!list) return fail(FGM_CUDA_EINVAL, "worklist: null handle pointer");
+  *list = nullptr;
+  if (M < 1 || M > 16) return fail(FGM_CUDA_EINVAL, "worklist: M=%d, need 1 <= M <= 16", M);
+  if (n < 1 || n > 65536 || !w) return fail(FGM_CUDA_EINVAL, "worklist: %d entries", n);
+  int rc = FGM_CUDA_OK;
+  for (int i = 0; i < n; i++)
+    if ((rc = check_work(M, w[i], i, n))) return rc;
+  DevInfo *di = nullptr;
+  if ((rc = dev_info(&di))) return rc;
+  const int MT = M <= 8 ? 1 : 2;
+  std::vector<WlItem> items((size_t)n);
+  for (int i = 0; i < n; i++) {
+    const fgm_cuda_work &s = w[i];
+    WlItem &it = items[i];
+    memset(&it, 0, sizeof(it));
+    it.kind = s.kind == FGM_CUDA_WORK_Q4G ? kWlQ4 : (s.kind == FGM_CUDA_WORK_Q8C ? kWlQ8 : kWlPrep);
+    it.N = s.N;
+    it.K = s.K;
+    it.deps[0] = s.deps[0];
+    it.deps[1] = s.deps[1];
+    if (it.kind == kWlPrep) {
+      it.units = (M + 15) / 16 * 16;
+      it.lda = s.lda;
+      it.hsz = s.hsz;
+      it.src = s.src;
+      it.pa = s.pa;
+      it.qs = s.qs;
+      continue;
+    }
+    it.gk = it.kind == kWlQ4 ? s.group / 64 : 0;
+    it.nb0 = s.n0;
+    it.units = s.n1 - s.n0;
+    it.ldc = s.ldc;
+    it.c_col0 = 0;
+    it.B = static_cast<const uint8_t *>(s.B);
+    it.b_scale = s.b_scale;
+    it.a_scale = s.a_scale;
+    it.C = s.C;
+    if (!encode_packed_a_map(&it.amap, s.A, s.K, MT * 8))
+      return fail(FGM_CUDA_ERUNTIME, "worklist: cuTensorMapEncodeTiled failed for entry %d", i);
+  }
+  WorkList *wl = new WorkList();
+  const char *why = worklist_plan(wl->plan, items, M, di->sms, di->smem_optin);
+  if (why) {
+    delete wl;
+    return fail(FGM_CUDA_EINVAL, "worklist: %s", why);
+  }
+  // one device block: descriptors (64-byte aligned), segments, offsets, counters
+  const size_t o_items = 0, b_items = sizeof(WlItem) * (size_t)n;
+  const size_t o_segs = align256(o_items + b_items), b_segs = sizeof(WlSeg) * wl->plan.segs.size();
+  const size_t o_off = align256(o_segs + b_segs), b_off = sizeof(int) * wl->plan.seg_off.size();
+  const size_t o_cnt = align256(o_off + b_off), b_cnt = sizeof(unsigned) * ((size_t)n + 2);
+  const size_t total = o_cnt + b_cnt;
+  if (cudaMalloc(&wl->mem, total) != cudaSuccess) {
+    cudaGetLastError();
+    delete wl;
+    return fail(FGM_CUDA_ENOMEM, "worklist: cudaMalloc(%zu)", total);
+  }
+  char *d = static_cast<char *>(wl->mem);
+  cudaError_t e = cudaMemcpy(d + o_items, items.data(), b_items, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && b_segs)
+    e = cudaMemcpy(d + o_segs, wl->plan.segs.data(), b_segs, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(d + o_off, wl->plan.seg_off.data(), b_off, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(d + o_cnt, 0, b_cnt);
+  if (e != cudaSuccess) {
+    cudaFree(wl->mem);
+    delete wl;
+    return cuda_fail(e, "worklist upload");
+  }
+  cudaGetDevice(&wl->dev);
+  wl->n = n;
+  WlParams &p = wl->params;
+  p.items = reinterpret_cast<const WlItem *>(d + o_items);
+  p.n_items = n;
+  p.segs = reinterpret_cast<const WlSeg *>(d + o_segs);
+  p.seg_off = reinterpret_cast<const int *>(d + o_off);
+  p.done = reinterpret_cast<unsigned *>(d + o_cnt);
+  p.ctas_done = p.done + n;
+  p.abort = reinterpret_cast<int *>(p.done + n + 1);
+  p.err = di->err;
+  p.M = M;
+  p.stages = wl->plan.stages;
+  p.n_abuf = wl->plan.n_abuf;
+  p.abuf_bytes = wl->plan.abuf_bytes;
+  *list = wl;
+  return FGM_CUDA_OK;
+}
+
+int fgm_cuda_worklist_run(void *list, void *stream) {
+  if (!list) return fail(FGM_CUDA_EINVAL, "worklist: null handle");
+  WorkList *wl = static_cast<WorkList *>(list);
+  int dev = -1;
+  FGM_TRY(cudaGetDevice(&dev));
+  if (dev != wl->dev)
+    return fail(FGM_CUDA_EINVAL, "worklist: created on device %d, current device is %d", wl->dev,
+                dev);
+  const cudaError_t e = launch_worklist(wl->params, wl->plan, use_pdl(), (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "worklist launch");
+  count_launch();
+  return FGM_CUDA_OK;
+}
+
+int fgm_cuda_worklist_destroy(void *list) {
+  if (!list) return FGM_CUDA_OK;
+  WorkList *wl = static_cast<WorkList *>(list);
+  int cur = -1;
+  cudaGetDevice(&cur);
+  if (wl->dev >= 0) cudaSetDevice(wl->dev);
+  cudaDeviceSynchronize();
+  const cudaError_t e = cudaFree(wl->mem);
+  if (cur >= 0) cudaSetDevice(cur);
+  delete wl;
+  if (e != cudaSuccess) return cuda_fail(e, "worklist free");
+  return FGM_CUDA_OK;
+}
 
 int fgm_cuda_argmax_merge(const float *vals, const int32_t *idx, int M, int P, int32_t *out,
                           void *stream) {

@@ -3,6 +3,9 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <vector>
+
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace fgm {
@@ -172,6 +175,9 @@ namespace fgm {
 // Row-major [rows][ld] byte matrix as a 2-D TMA view, boxes of box_rows x 128
 // bytes with the 128-byte swizzle.
 bool encode_rows_map(CUtensorMap *map, const void *base, int rows, int K, int ld, int box_rows);
+// Tile-packed activations of one 16-row block as a 3-D TMA view, box of
+// `rows` rows x K/64 tiles, 64-byte swizzle (K <= 16384).
+bool encode_packed_a_map(CUtensorMap *map, const void *base, int K, int rows);
 // .fgm int8 tiles -> row-major [N][K] (the tensor-core weight operand).
 cudaError_t launch_q8c_rows(const int8_t *tiles, int8_t *rows, int N, int K, cudaStream_t st);
 // tile-packed activations -> row-major [M][K].
@@ -190,6 +196,53 @@ cudaError_t launch_argmax_partials(const float *C, int M, int N, int ldc, int co
                                    int *pi, bool pdl, cudaStream_t st);
 cudaError_t launch_argmax_merge(const float *pv, const int *pi, int M, int P, int *out, bool pdl,
                                 cudaStream_t st);
+
+// ------------------------------------------------------- decode work list
+// worklist.cu: many decode GEMMs and activation preps in one persistent
+// launch.  kind: kWlQ4 (int4 q4g GEMM), kWlQ8 (int8 q8c GEMM), kWlPrep (rows
+// of fgm_prep_rows into the packed layout).
+constexpr int kWlQ4 = 0, kWlQ8 = 1, kWlPrep = 2;
+struct WlItem {
+  CUtensorMap amap;        // GEMM: packed activations (encode_packed_a_map)
+  int kind, N, K, gk;      // gk: int4 scale group in 64-value tiles
+  int nb0, units;          // GEMM: first n-block and n-blocks; prep: rows (16 per block)
+  int ldc, c_col0;         // GEMM: C[m*ldc + n - c_col0]
+  int lda, hsz;            // prep: source row stride (floats), FWHT block
+  int deps[2];             // earlier items whose outputs this one reads (-1: none)
+  const uint8_t *B;        // GEMM weight tiles
+  const void *b_scale;     // f16 [K/group][N] (int4) or f32 [N] (int8)
+  const float *a_scale;    // GEMM: [M]
+  float *C;
+  const float *src;        // prep: f32 rows
+  int8_t *pa;              // prep: packed rows
+  float *qs;               // prep: row scales
+};
+struct WlSeg {             // units [u0, u1) of one item, handled by one CTA
+  int item, u0, u1;
+  int base;                // the CTA's units before this segment, mod the consumer warps
+  int kind, nst;           // item kind, 4 KB weight stages per unit
+};
+struct WlParams {
+  const WlItem *items;
+  int n_items;
+  const WlSeg *segs;       // every CTA's segments, back to back
+  const int *seg_off;      // CTA c: segs[seg_off[c], seg_off[c + 1])
+  unsigned *done;          // per item: units completed in this launch
+  unsigned *ctas_done;     // CTAs finished (the last one resets the counters)
+  int *abort;              // raised by a warp that gave up on a bounded wait
+  int *err;                // device status word
+  int M, stages, n_abuf, abuf_bytes;
+};
+struct WlPlan {
+  int M, MT, grid, stages, n_abuf, abuf_bytes;
+  size_t smem;
+  std::vector<WlSeg> segs;
+  std::vector<int> seg_off;
+};
+// Fills the schedule and launch geometry; returns an error text or nullptr.
+const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num_sms,
+                          size_t smem_optin);
+cudaError_t launch_worklist(const WlParams &p, const WlPlan &pl, bool pdl, cudaStream_t st);
 
 // Number of kernel launches issued by this library (instrumentation).
 void count_launch(int n = 1);

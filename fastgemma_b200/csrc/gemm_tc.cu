@@ -456,6 +456,23 @@ bool encode_rows_map(CUtensorMap *map, const void *base, int rows, int K, int ld
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Tile-packed activations [1][K/64][16][64] (M <= 16) as a 3-D TMA view
+// (64 bytes, 16 rows, K/64 tiles) read in one box of `rows` rows x every tile,
+// with the 64-byte swizzle: 16-byte chunk c of row r lands at chunk
+// c ^ ((r >> 1) & 3) of its 64-byte shared-memory row.
+bool encode_packed_a_map(CUtensorMap *map, const void *base, int K, int rows) {
+  auto enc = get_encode();
+  if (!enc || K % 64 != 0 || K / 64 > 256 || rows < 1 || rows > 16) return false;
+  const cuuint64_t dims[3] = {64, 16, (cuuint64_t)(K / 64)};
+  const cuuint64_t strides[2] = {64, 1024};
+  const cuuint32_t box[3] = {64, (cuuint32_t)rows, (cuuint32_t)(K / 64)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 cudaError_t launch_q8c_rows(const int8_t *tiles, int8_t *rows, int N, int K, cudaStream_t st) {
   const size_t words = (size_t)N * K / 4;
   q8c_tiles_to_rows<<<grid_for(words), 256, 0, st>>>(reinterpret_cast<const uint32_t *>(tiles),

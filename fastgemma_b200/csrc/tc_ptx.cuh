@@ -64,6 +64,16 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const void *tmap, uint64_
       : "memory");
 }
 
+// 3-D tiled TMA load into shared memory, completion counted on `bar`.
+__device__ __forceinline__ void tma_load_3d(void *dst, const void *tmap, uint64_t *bar, int c0,
+                                            int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void *tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }

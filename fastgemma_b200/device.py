@@ -6,6 +6,8 @@ for allocation and stream handles; the arithmetic is the library's.
 """
 from __future__ import annotations
 
+import ctypes as C
+
 import torch
 
 from ._lib import call
@@ -188,3 +190,74 @@ def qkv_post(q, k, v, rows, n_heads, kv_heads, head_dim, q_norm, k_norm, eps, in
          _p(q_norm), _p(k_norm), eps, _p(inv_freq), _p(pos), ring, cap, _p(kc), kc_stride, _p(ks),
          ks_stride, _p(vt), vt_stride, _p(vs), vs_stride, _s(stream))
 
+
+
+# ------------------------------------------------------- decode work list
+class _Work(C.Structure):
+    """fgm_cuda_work (include/fgm_cuda.h)."""
+    _fields_ = [("kind", C.c_int), ("N", C.c_int), ("K", C.c_int), ("group", C.c_int),
+                ("n0", C.c_int), ("n1", C.c_int), ("ldc", C.c_int), ("lda", C.c_int),
+                ("hsz", C.c_int), ("deps", C.c_int * 2),
+                ("A", C.c_void_p), ("a_scale", C.c_void_p), ("B", C.c_void_p),
+                ("b_scale", C.c_void_p), ("C", C.c_void_p), ("src", C.c_void_p),
+                ("pa", C.c_void_p), ("qs", C.c_void_p)]
+
+
+WORK_Q4G, WORK_Q8C, WORK_PREP = 0, 1, 2
+
+
+class WorkList:
+    """A decode step's projections as one persistent launch
+    (fgm_cuda_worklist_*).  Add entries in an order where every entry's
+    dependencies come first, then ``build(M)`` once and ``run()`` per step.
+    The tensors passed in must stay alive (and in place) as long as the list."""
+
+    def __init__(self):
+        self._items, self._keep, self.handle = [], [], None
+
+    def _add(self, w, deps, keep):
+        d = list(deps) + [-1, -1]
+        w.deps[0], w.deps[1] = d[0], d[1]
+        self._items.append(w)
+        self._keep.extend(keep)
+        return len(self._items) - 1
+
+    def prep(self, src, lda, K, pa, qs, hsz=0, deps=()):
+        """Rows [0, M) of src (f32) -> packed pa and scales qs (fgm_prep_rows)."""
+        w = _Work(kind=WORK_PREP, K=K, lda=lda, hsz=hsz, src=_p(src), pa=_p(pa), qs=_p(qs))
+        return self._add(w, deps, (src, pa, qs))
+
+    def gemm_q4g(self, N, K, A, a_scale, Bq, b_scale, group, C, ldc=None, n0=0, n1=None,
+                 deps=()):
+        n1 = N // 16 if n1 is None else n1
+        w = _Work(kind=WORK_Q4G, N=N, K=K, group=group, n0=n0, n1=n1,
+                  ldc=N if ldc is None else ldc, A=_p(A), a_scale=_p(a_scale), B=_p(Bq),
+                  b_scale=_p(b_scale), C=_p(C))
+        return self._add(w, deps, (A, a_scale, Bq, b_scale, C))
+
+    def gemm_q8c(self, N, K, A, a_scale, B, b_scale, C, ldc=None, n0=0, n1=None, deps=()):
+        n1 = N // 16 if n1 is None else n1
+        w = _Work(kind=WORK_Q8C, N=N, K=K, n0=n0, n1=n1, ldc=N if ldc is None else ldc,
+                  A=_p(A), a_scale=_p(a_scale), B=_p(B), b_scale=_p(b_scale), C=_p(C))
+        return self._add(w, deps, (A, a_scale, B, b_scale, C))
+
+    def build(self, M):
+        arr = (_Work * len(self._items))(*self._items)
+        h = C.c_void_p()
+        call("fgm_cuda_worklist_create", M, arr, len(self._items), C.byref(h))
+        self.handle = h
+        return self
+
+    def run(self, stream=None):
+        call("fgm_cuda_worklist_run", self.handle, _s(stream))
+
+    def close(self):
+        if self.handle is not None:
+            call("fgm_cuda_worklist_destroy", self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

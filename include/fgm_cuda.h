@@ -244,6 +244,63 @@ int fgm_cuda_gemm_q4g_acc(int M, int N, int K, const int8_t *A, const uint8_t *B
 int fgm_cuda_gemm_q8c_acc(int M, int N, int K, const int8_t *A, const int8_t *B,
                           int32_t *acc, int n0, int n1, void *stream);
 
+/* ------------------------------------------------------ decode work list
+ * A decode step's sequence of Gemm::run calls (fgm-core/src/forward.rs:128-158
+ * per projection, each a prep of its f32 input and an int4 or int8 GEMM) as
+ * ONE persistent kernel launch per run: every SM streams the weights of its
+ * share of every item through shared memory without stopping at item
+ * boundaries, and an item that reads another item's output waits on that
+ * item's completion counter (device-side, bounded) instead of a kernel
+ * boundary.  Each GEMM item computes exactly fgm_cuda_gemm_q4g /
+ * fgm_cuda_gemm_q8c over its column range, each prep item exactly
+ * fgm_cuda_prep_rows (rows [0, M), padding rows of the last 16-row block
+ * zeroed) -- bit-identical outputs.  No reference counterpart: the reference
+ * runs its projections one call at a time (pool.rs:126-145).
+ *
+ * A list is created once (validation, schedule, activation TMA descriptors,
+ * its device-side descriptors and counters: the only allocations) and run any
+ * number of times; every pointer in it stays fixed for the list's lifetime.
+ * Contract per entry (EINVAL otherwise), with 1 <= M <= 16 for the whole list:
+ *  - FGM_CUDA_WORK_Q4G / _Q8C: weight [N, K] in the .fgm layout, N % 16 == 0,
+ *    K % 512 == 0 (int4) or K % 256 == 0 (int8), K <= 16384; output columns
+ *    [n0*16, n1*16), 0 <= n0 < n1 <= N/16, C[m*ldc + n] with ldc >= n1*16;
+ *    int4 group in {64, 128, 256, 512} dividing K; A (tile-packed, one 16-row
+ *    block, zero padding rows) and B 16-byte aligned, scales 4-byte aligned.
+ *  - FGM_CUDA_WORK_PREP: f32 rows src[m*lda + k], K % 128 == 0, lda >= K,
+ *    lda % 4 == 0, src 16-byte aligned; hsz 0 or a power of two <= 128
+ *    dividing K (the FWHT block, ops.c:153-175); outputs pa (the packed 16-row
+ *    block, packed_a_len(M, K) bytes, 4-byte aligned) and qs [M].
+ *  - deps: up to two indices of EARLIER entries whose outputs this entry
+ *    reads (-1: none).  Inputs written before the run (earlier kernels on the
+ *    stream) need no entry.  Entries that write memory another entry reads or
+ *    writes must be ordered by deps; the kernel does not check it.
+ * Runs of one list must not overlap in time (they share its counters). */
+enum { FGM_CUDA_WORK_Q4G = 0, FGM_CUDA_WORK_Q8C = 1, FGM_CUDA_WORK_PREP = 2 };
+
+typedef struct fgm_cuda_work {
+  int kind;               /* FGM_CUDA_WORK_* */
+  int N, K, group;        /* GEMM: weight shape, int4 scale group; PREP: K = row length */
+  int n0, n1, ldc;        /* GEMM: output n-blocks [n0, n1), C row pitch */
+  int lda, hsz;           /* PREP: source row pitch (floats), FWHT block (0: none) */
+  int deps[2];            /* earlier entries this one waits for (-1: none) */
+  const int8_t *A;        /* GEMM: tile-packed activations */
+  const float *a_scale;   /* GEMM: [M] */
+  const void *B;          /* GEMM: weight blob (int4 q4g or int8 q8c) */
+  const void *b_scale;    /* GEMM: f16 [K/group][N] (int4) or f32 [N] (int8) */
+  float *C;               /* GEMM output */
+  const float *src;       /* PREP input rows */
+  int8_t *pa;             /* PREP: packed rows out */
+  float *qs;              /* PREP: row scales out */
+} fgm_cuda_work;
+
+/* Validate and schedule `n` entries for batch size M on the current device;
+ * *list receives the handle. */
+int fgm_cuda_worklist_create(int M, const fgm_cuda_work *items, int n, void **list);
+/* One launch of the whole list on `stream` (NULL: the default stream). */
+int fgm_cuda_worklist_run(void *list, void *stream);
+/* Free a list (waits for the device first). */
+int fgm_cuda_worklist_destroy(void *list);
+
 /* ------------------------------------------- decode-chain glue, attention
  * The operations between the GEMMs of the reference's decode forward pass
  * (fgm-core/src/forward.rs:469-654), on device buffers and a stream, as
