@@ -1306,7 +1306,8 @@ int fgm_cuda_worklist_create(int M, const fgm_cuda_work *w, int n, void **list) 
   const size_t o_items = 0, b_items = sizeof(WlItem) * (size_t)n;
   const size_t o_segs = align256(o_items + b_items), b_segs = sizeof(WlSeg) * wl->plan.segs.size();
   const size_t o_off = align256(o_segs + b_segs), b_off = sizeof(int) * wl->plan.seg_off.size();
-  const size_t o_cnt = align256(o_off + b_off), b_cnt = sizeof(unsigned) * ((size_t)n + 2);
+  const size_t o_un = align256(o_off + b_off), b_un = sizeof(int) * wl->plan.units.size();
+  const size_t o_cnt = align256(o_un + b_un), b_cnt = sizeof(unsigned) * ((size_t)n + 2);
   const size_t total = o_cnt + b_cnt;
   if (cudaMalloc(&wl->mem, total) != cudaSuccess) {
     cudaGetLastError();
@@ -1319,6 +1320,8 @@ int fgm_cuda_worklist_create(int M, const fgm_cuda_work *w, int n, void **list) 
     e = cudaMemcpy(d + o_segs, wl->plan.segs.data(), b_segs, cudaMemcpyHostToDevice);
   if (e == cudaSuccess)
     e = cudaMemcpy(d + o_off, wl->plan.seg_off.data(), b_off, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && b_un)
+    e = cudaMemcpy(d + o_un, wl->plan.units.data(), b_un, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemset(d + o_cnt, 0, b_cnt);
   if (e != cudaSuccess) {
     cudaFree(wl->mem);
@@ -1332,6 +1335,7 @@ int fgm_cuda_worklist_create(int M, const fgm_cuda_work *w, int n, void **list) 
   p.n_items = n;
   p.segs = reinterpret_cast<const WlSeg *>(d + o_segs);
   p.seg_off = reinterpret_cast<const int *>(d + o_off);
+  p.units = reinterpret_cast<const int *>(d + o_un);
   p.done = reinterpret_cast<unsigned *>(d + o_cnt);
   p.ctas_done = p.done + n;
   p.abort = reinterpret_cast<int *>(p.done + n + 1);

@@ -217,16 +217,17 @@ struct WlItem {
   int8_t *pa;              // prep: packed rows
   float *qs;               // prep: row scales
 };
-struct WlSeg {             // units [u0, u1) of one item, handled by one CTA
-  int item, u0, u1;
-  int base;                // the CTA's units before this segment, mod the consumer warps
-  int kind, nst;           // item kind, 4 KB weight stages per unit
+constexpr int kWlWarps = 8;  // consumer warps per CTA
+struct WlSeg {             // one CTA's share of one item
+  int item, kind, nst;     // item, its kind, 4 KB weight stages per unit
+  int ofs[kWlWarps + 1];   // consumer warp w takes units[ofs[w], ofs[w + 1])
 };
 struct WlParams {
   const WlItem *items;
   int n_items;
   const WlSeg *segs;       // every CTA's segments, back to back
   const int *seg_off;      // CTA c: segs[seg_off[c], seg_off[c + 1])
+  const int *units;        // unit indices (n-block or row inside the item) of every segment
   unsigned *done;          // per item: units completed in this launch
   unsigned *ctas_done;     // CTAs finished (the last one resets the counters)
   int *abort;              // raised by a warp that gave up on a bounded wait
@@ -238,6 +239,7 @@ struct WlPlan {
   size_t smem;
   std::vector<WlSeg> segs;
   std::vector<int> seg_off;
+  std::vector<int> units;
 };
 // Fills the schedule and launch geometry; returns an error text or nullptr.
 const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num_sms,

@@ -72,7 +72,6 @@ namespace {
 
 using namespace stream;
 
-constexpr int kWlWarps = 8;        // consumer warps per CTA
 constexpr int kWlStage = 4096;     // bytes per ring stage
 constexpr int kWlMaxStages = 8;
 constexpr uint64_t kWlLimitNs = 2000000000ull;
@@ -336,36 +335,62 @@ __device__ void prep_row(const WlItem &it, int r, int M, int lane) {
   if (lane == 0) it.qs[r] = s;
 }
 
-// -------------------------------------------------------- unit cursor
-// Position of a consumer warp in its own sequence of weight stages: segment
-// si of the CTA's list, this warp's j-th unit of that segment, stage st.
-struct Cur {
-  int si, j, st;
+// ------------------------------------------------------------ unit walk
+// A consumer warp's walk over the weight stages of its own units, item after
+// item: the segment's unit list, the stage inside the unit, and the item
+// fields it needs, loaded once per segment.
+struct Walk {
+  int si;                   // segment index (nseg: finished)
+  int e, e_end;             // this warp's unit entries [e, e_end) of the segment
+  int st, nst;              // stage inside the unit, stages per unit
+  int kind, nb0;
+  const uint8_t *B;
+  const uint8_t *bs;        // int4 scales (f16 rows of N)
+  int ubytes;               // weight bytes per unit (one n-block over all of K)
+  int nrow;                 // int4 scale bytes per group row (N * 2)
+  int rows_st;              // int4 scale group rows per stage (8 / gk)
+  int nb;                   // current n-block
 };
 
-__device__ __forceinline__ int first_of(const WlSeg &sg, int cw) {
-  int f = (cw - sg.base) % kWlWarps;
-  return f < 0 ? f + kWlWarps : f;
+__device__ __forceinline__ void walk_unit(Walk &k, const WlParams &p) {
+  k.nb = k.nb0 + __ldg(p.units + k.e);
 }
 
-__device__ __forceinline__ int count_of(const WlSeg &sg, int cw) {
-  const int n = sg.u1 - sg.u0 - first_of(sg, cw);
-  return n > 0 ? (n + kWlWarps - 1) / kWlWarps : 0;
+// Enter segment k.si or the first later one holding weight stages for warp cw.
+__device__ __forceinline__ void walk_enter(Walk &k, const WlParams &p, const WlSeg *segs, int nseg,
+                                           int cw) {
+  for (; k.si < nseg; k.si++) {
+    const WlSeg &sg = segs[k.si];
+    if (sg.kind == kWlPrep) continue;
+    const int e0 = sg.ofs[cw], e1 = sg.ofs[cw + 1];
+    if (e0 == e1) continue;
+    const WlItem &it = p.items[sg.item];
+    k.e = e0;
+    k.e_end = e1;
+    k.st = 0;
+    k.nst = sg.nst;
+    k.kind = sg.kind;
+    k.nb0 = it.nb0;
+    k.B = it.B;
+    k.bs = static_cast<const uint8_t *>(it.b_scale);
+    k.ubytes = it.K * (sg.kind == kWlQ4 ? 8 : 16);  // K/64 tiles of 512 or 1024 bytes
+    k.nrow = it.N * 2;
+    k.rows_st = sg.kind == kWlQ4 ? 8 / it.gk : 0;
+    walk_unit(k, p);
+    return;
+  }
 }
 
-// Move to the next segment (from si on) that holds weight stages for this warp.
-__device__ __forceinline__ void skip_to_gemm(Cur &c, const WlSeg *segs, int nseg, int cw) {
-  while (c.si < nseg && (segs[c.si].kind == kWlPrep || count_of(segs[c.si], cw) == 0)) c.si++;
-}
-
-__device__ __forceinline__ void advance(Cur &c, const WlSeg *segs, int nseg, int cw) {
-  const WlSeg &sg = segs[c.si];
-  if (++c.st < sg.nst) return;
-  c.st = 0;
-  if (++c.j < count_of(sg, cw)) return;
-  c.j = 0;
-  c.si++;
-  skip_to_gemm(c, segs, nseg, cw);
+__device__ __forceinline__ void walk_next(Walk &k, const WlParams &p, const WlSeg *segs, int nseg,
+                                          int cw) {
+  if (++k.st < k.nst) return;
+  k.st = 0;
+  if (++k.e < k.e_end) {
+    walk_unit(k, p);
+    return;
+  }
+  k.si++;
+  walk_enter(k, p, segs, nseg, cw);
 }
 
 template <int MT>
@@ -398,14 +423,15 @@ __global__ void __launch_bounds__((kWlWarps + 1) * 32, 1) worklist_kernel(const 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     pdl_wait();  // packed activations and their scales may come from earlier kernels
-    int g = 0, issued = 0;
+    int g = 0;  // GEMM segments staged so far; segment g uses buffer g % n_abuf
     bool ok = true;
     for (int si = 0; si < nseg && ok; si++) {
-      const WlSeg sg = segs[si];
+      const WlSeg &sg = segs[si];
       if (sg.kind == kWlPrep) continue;
       const WlItem &it = p.items[sg.item];
-      const int b = g % p.n_abuf, r = g / p.n_abuf;
-      if (r > 0) ok = wl_wait(&s_empty[b], (r - 1) & 1, p);  // every consumer left segment g - n_abuf
+      const int b = g % p.n_abuf;
+      if (g >= p.n_abuf)  // every consumer has left segment g - n_abuf, the buffer's last user
+        ok = wl_wait(&s_empty[b], (uint32_t)((g / p.n_abuf - 1) & 1), p);
       if (ok && lane == 0) ok = wl_wait_item(p, it.deps[0]) && wl_wait_item(p, it.deps[1]);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
@@ -416,13 +442,13 @@ __global__ void __launch_bounds__((kWlWarps + 1) * 32, 1) worklist_kernel(const 
         tc::mbar_expect_tx(&s_full[b], (uint32_t)(it.K / 64 * MT * 512));
         tc::tma_load_3d(smem + (size_t)b * p.abuf_bytes, &it.amap, &s_full[b], 0, 0, 0);
       }
-      issued = ++g;
+      g++;
     }
     if (!ok) {
       if (lane == 0) wl_fail(p, 5);
       // the last activation boxes requested may still be landing
-      for (int k = (issued > p.n_abuf ? issued - p.n_abuf : 0); k < issued; k++)
-        tc::mbar_wait(&s_full[k % p.n_abuf], (k / p.n_abuf) & 1);
+      for (int k = (g > p.n_abuf ? g - p.n_abuf : 0); k < g; k++)
+        tc::mbar_wait(&s_full[k % p.n_abuf], (uint32_t)((k / p.n_abuf) & 1));
     }
   } else {
     // ------------------------------------------------------------ consumers
@@ -430,75 +456,71 @@ __global__ void __launch_bounds__((kWlWarps + 1) * 32, 1) worklist_kernel(const 
     const WlLane L = make_lane(lane);
     const uint32_t ring = ring0 + (uint32_t)(cw * S * kWlStage);
     uint64_t *bars = s_ring[cw];
-    Cur ic{0, 0, 0}, sc{0, 0, 0};
-    skip_to_gemm(ic, segs, nseg, cw);
-    skip_to_gemm(sc, segs, nseg, cw);
-    int issued = 0, consumed = 0;
-    auto issue = [&]() {  // next weight stage at the issue cursor into its ring slot
-      const WlSeg &sg = segs[ic.si];
-      const WlItem &it = p.items[sg.item];
-      const int KB = it.K >> 6, T = it.kind == kWlQ4 ? 8 : 4, TB = it.kind == kWlQ4 ? 512 : 1024;
-      const int nb = it.nb0 + sg.u0 + first_of(sg, cw) + ic.j * kWlWarps;
-      const int slot = issued % S;
+    Walk iw{}, sw{};  // issue and scale walks
+    iw.si = sw.si = 0;
+    walk_enter(iw, p, segs, nseg, cw);
+    walk_enter(sw, p, segs, nseg, cw);
+    int islot = 0, inflight = 0;
+    auto issue = [&]() {  // the stage at the issue walk into ring slot islot
       if (lane == 0) {
-        tc::mbar_expect_tx(&bars[slot], kWlStage);
-        bulk_g2s(ring + slot * kWlStage, it.B + ((size_t)nb * KB + (size_t)ic.st * T) * TB,
-                 kWlStage, &bars[slot]);
+        tc::mbar_expect_tx(&bars[islot], kWlStage);
+        bulk_g2s(ring + islot * kWlStage,
+                 iw.B + (size_t)iw.nb * iw.ubytes + (size_t)iw.st * kWlStage, kWlStage,
+                 &bars[islot]);
       }
-      issued++;
-      advance(ic, segs, nseg, cw);
+      if (++islot == S) islot = 0;
+      inflight++;
+      walk_next(iw, p, segs, nseg, cw);
     };
-    // int4 scales of the stage at the scale cursor: lane l loads word l%8 of
-    // group rows glo + l/8 and glo + 4 + l/8 (16 columns of f16 = 8 words)
+    // int4 scales of the stage at the scale walk: lane l loads word l%8 of
+    // group rows r0 + l/8 and r0 + 4 + l/8 (16 columns of f16 = 8 words)
     auto scale_fetch = [&](uint32_t &r0, uint32_t &r1) {
       r0 = r1 = 0;
-      if (sc.si >= nseg) return;
-      const WlSeg &sg = segs[sc.si];
-      const WlItem &it = p.items[sg.item];
-      if (it.kind == kWlQ4) {
-        const int nb = it.nb0 + sg.u0 + first_of(sg, cw) + sc.j * kWlWarps;
-        const int glo = sc.st * 8 / it.gk, ng = 8 / it.gk;
-        const uint8_t *row = static_cast<const uint8_t *>(it.b_scale) +
-                             ((size_t)glo * it.N + (size_t)nb * 16) * 2 + (lane & 7) * 4;
+      if (sw.si >= nseg) return;
+      if (sw.kind == kWlQ4) {
+        const uint8_t *row = sw.bs + (size_t)(sw.st * sw.rows_st) * sw.nrow + (size_t)sw.nb * 32 +
+                             (lane & 7) * 4;
         const int q = lane >> 3;
-        if (q < ng) r0 = ldg_stream_u32(row + (size_t)q * it.N * 2);
-        if (q + 4 < ng) r1 = ldg_stream_u32(row + (size_t)(q + 4) * it.N * 2);
+        if (q < sw.rows_st) r0 = ldg_stream_u32(row + (size_t)q * sw.nrow);
+        if (q + 4 < sw.rows_st) r1 = ldg_stream_u32(row + (size_t)(q + 4) * sw.nrow);
       }
-      advance(sc, segs, nseg, cw);
+      walk_next(sw, p, segs, nseg, cw);
     };
 
     // the weights never come from earlier kernels: fill the ring first
-    while (issued < S && ic.si < nseg) issue();
+    while (inflight < S && iw.si < nseg) issue();
     uint32_t sa0, sa1, sb0, sb1;
     scale_fetch(sa0, sa1);
     scale_fetch(sb0, sb1);
     pdl_wait();  // prep sources and GEMM outputs are ordered after earlier kernels
 
     bool ok = true;
-    int g = 0;
+    int g = 0, cslot = 0;  // g: GEMM segments entered (segment g uses buffer g % n_abuf)
+    uint32_t cpar = 0;
     for (int si = 0; si < nseg && ok; si++) {
-      const WlSeg sg = segs[si];
+      const WlSeg &sg = segs[si];
+      const int e0 = sg.ofs[cw], e1 = sg.ofs[cw + 1];
       const WlItem &it = p.items[sg.item];
-      const int first = first_of(sg, cw), n_my = count_of(sg, cw);
       if (sg.kind == kWlPrep) {
-        if (n_my == 0) continue;
+        if (e0 == e1) continue;
         if (lane == 0) ok = wl_wait_item(p, it.deps[0]) && wl_wait_item(p, it.deps[1]);
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         if (!ok) break;
-        for (int j = 0; j < n_my; j++) prep_row(it, sg.u0 + first + j * kWlWarps, p.M, lane);
-        wl_signal(p, sg.item, (unsigned)n_my, lane);
+        for (int e = e0; e < e1; e++) prep_row(it, __ldg(p.units + e), p.M, lane);
+        wl_signal(p, sg.item, (unsigned)(e1 - e0), lane);
         continue;
       }
       const int b = g % p.n_abuf;
-      const uint32_t fpar = (uint32_t)((g / p.n_abuf) & 1);
-      g++;
-      ok = __all_sync(0xffffffffu, wl_wait(&s_full[b], fpar, p));
+      ok = __all_sync(0xffffffffu, wl_wait(&s_full[b], (uint32_t)((g / p.n_abuf) & 1), p));
       if (!ok) break;
       const uint32_t ab = abuf0 + (uint32_t)(b * p.abuf_bytes);
-      const bool q4 = it.kind == kWlQ4;
-      const int T = q4 ? 8 : 4;
-      for (int j = 0; j < n_my && ok; j++) {
-        const int nb = it.nb0 + sg.u0 + first + j * kWlWarps;
+      const bool q4 = sg.kind == kWlQ4;
+      const int gk = it.gk, nst = sg.nst, nb0 = it.nb0, ldc = it.ldc, c0 = it.c_col0;
+      float *C = it.C;
+      const float *b_scale8 = static_cast<const float *>(it.b_scale);
+      const uint32_t a_step = (uint32_t)((q4 ? 8 : 4) * MT * 512);  // activation bytes per stage
+      for (int e = e0; e < e1 && ok; e++) {
+        const int nb = nb0 + __ldg(p.units + e);
         float cf[MT][4];
         int32_t acc[MT][4];
 #pragma unroll
@@ -510,26 +532,29 @@ __global__ void __launch_bounds__((kWlWarps + 1) * 32, 1) worklist_kernel(const 
           }
         float bs0 = 0.0f, bs1 = 0.0f;  // int8 per-channel scales of columns g8, g8 + 8
         if (!q4) {
-          const float *bsp = static_cast<const float *>(it.b_scale) + nb * 16 + L.g8;
-          bs0 = bsp[0];
-          bs1 = bsp[8];
+          bs0 = __ldg(b_scale8 + nb * 16 + L.g8);
+          bs1 = __ldg(b_scale8 + nb * 16 + L.g8 + 8);
         }
-        for (int st = 0; st < sg.nst; st++) {
-          const uint32_t c0 = sa0, c1 = sa1;
+        uint32_t abs_ = ab;
+        for (int st = 0; st < nst; st++) {
+          const uint32_t s0 = sa0, s1 = sa1;
           sa0 = sb0;
           sa1 = sb1;
           scale_fetch(sb0, sb1);
-          const int slot = consumed % S;
-          ok = __all_sync(0xffffffffu, wl_wait(&bars[slot], (uint32_t)((consumed / S) & 1), p));
+          ok = __all_sync(0xffffffffu, wl_wait(&bars[cslot], cpar, p));
           if (!ok) break;
-          const uint32_t stg = ring + slot * kWlStage;
-          const uint32_t abs_ = ab + (uint32_t)(st * T * MT * 512);
-          if (q4) q4_stage_gk<MT>(it.gk, stg, abs_, L, c0, c1, cf);
+          const uint32_t stg = ring + cslot * kWlStage;
+          if (q4) q4_stage_gk<MT>(gk, stg, abs_, L, s0, s1, cf);
           else q8_stage<MT>(stg, abs_, L, acc);
+          abs_ += a_step;
           __syncwarp();
           fence_proxy_async_smem();  // this warp's reads of the slot precede its refill
-          consumed++;
-          if (ic.si < nseg) issue();
+          inflight--;
+          if (++cslot == S) {
+            cslot = 0;
+            cpar ^= 1u;
+          }
+          if (iw.si < nseg) issue();
         }
         if (!ok) break;
 #pragma unroll
@@ -540,7 +565,7 @@ __global__ void __launch_bounds__((kWlWarps + 1) * 32, 1) worklist_kernel(const 
             const int n = nb * 16 + L.g8 + (i >= 2 ? 8 : 0);
             if (m >= p.M) continue;
             const float as = s_as[b][m];
-            it.C[(size_t)m * it.ldc + (n - it.c_col0)] =
+            C[(size_t)m * ldc + (n - c0)] =
                 q4 ? __fmul_rn(cf[mt][i], as)
                    : __fmul_rn(__int2float_rn(acc[mt][i]), __fmul_rn(i < 2 ? bs0 : bs1, as));
           }
@@ -550,13 +575,19 @@ __global__ void __launch_bounds__((kWlWarps + 1) * 32, 1) worklist_kernel(const 
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
                                       tc::smem_u32(&s_empty[b]))
                                   : "memory");
-      if (n_my > 0) wl_signal(p, sg.item, (unsigned)n_my, lane);
+      if (e1 > e0) wl_signal(p, sg.item, (unsigned)(e1 - e0), lane);
+      g++;
     }
     if (!ok) {
       if (lane == 0) wl_fail(p, 5);
       // weight stages still in flight land before the CTA exits
-      for (int k = consumed; k < issued; k++)
-        tc::mbar_wait(&bars[k % S], (uint32_t)((k / S) & 1));
+      for (int k = 0; k < inflight; k++) {
+        tc::mbar_wait(&bars[cslot], cpar);
+        if (++cslot == S) {
+          cslot = 0;
+          cpar ^= 1u;
+        }
+      }
     }
   }
 
@@ -627,59 +658,96 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
       if (d >= 0) level[i] = std::max(level[i], level[d] + 1);
     nlev = std::max(nlev, level[i] + 1);
   }
-  // ---- segments per CTA, level by level
-  const int G = num_sms;
-  std::vector<std::vector<WlSeg>> cta(G);
-  std::vector<int> base(G, 0);
-  int rr = 0;  // round-robin position of prep rows
-  auto push = [&](int c, int item, int u0, int u1) {
-    const WlItem &it = items[item];
-    WlSeg sg{};
-    sg.item = item;
-    sg.u0 = u0;
-    sg.u1 = u1;
-    sg.base = base[c];
-    sg.kind = it.kind;
-    sg.nst = it.kind == kWlQ4 ? it.K / 512 : (it.kind == kWlQ8 ? it.K / 256 : 0);
-    base[c] = (base[c] + (u1 - u0)) % kWlWarps;
-    cta[c].push_back(sg);
+  // Cost of one unit in 4 KB weight stages (a prep row: two passes over its
+  // f32 source, which one warp reads at a fraction of the weight rate).
+  auto unit_cost = [&](const WlItem &it, int u) -> double {
+    if (it.kind == kWlQ4) return it.K / 512;
+    if (it.kind == kWlQ8) return it.K / 256;
+    return u < M ? 3.0 * it.K / 1024 : 1.0;
   };
+  // ---- each CTA's (item, unit range) pieces, level by level
+  const int G = num_sms;
+  struct Piece {
+    int item, u0, u1;
+  };
+  std::vector<std::vector<Piece>> cta(G);
+  std::vector<std::vector<int>> piece_level(G);
+  int rr = 0;  // round-robin position of prep rows
   for (int lv = 0; lv < nlev; lv++) {
-    // GEMM units of the level, flattened in list order, split by weight bytes
     double total = 0;
     for (int i = 0; i < n; i++)
-      if (level[i] == lv && items[i].kind != kWlPrep)
-        total += (double)items[i].units * (items[i].kind == kWlQ4 ? items[i].K / 512 : items[i].K / 256);
+      if (level[i] == lv && items[i].kind != kWlPrep) total += items[i].units * unit_cost(items[i], 0);
     double acc = 0;
     for (int i = 0; i < n; i++) {
       if (level[i] != lv) continue;
-      WlItem &it = items[i];
-      if (it.kind == kWlPrep) {
-        for (int u = 0; u < it.units; u++) {
-          push(rr % G, i, u, u + 1);
-          rr++;
+      const WlItem &it = items[i];
+      if (it.kind == kWlPrep) {  // rows round-robin over the CTAs
+        for (int u = 0; u < it.units; u++, rr++) {
+          cta[rr % G].push_back(Piece{i, u, u + 1});
+          piece_level[rr % G].push_back(lv);
         }
         continue;
       }
-      const double cost = it.kind == kWlQ4 ? it.K / 512 : it.K / 256;
+      // GEMM units: contiguous ranges of equal weight bytes
+      const double cost = unit_cost(it, 0);
       int u = 0;
       while (u < it.units) {
-        // the CTA whose share holds this unit's midpoint, and how far its share goes
         const int c = std::min(G - 1, (int)((acc + 0.5 * cost) * G / total));
         const double end = (double)(c + 1) * total / G;
         int u1 = u + 1;
         while (u1 < it.units && acc + (u1 - u + 0.5) * cost < end) u1++;
-        push(c, i, u, u1);
+        cta[c].push_back(Piece{i, u, u1});
+        piece_level[c].push_back(lv);
         acc += (u1 - u) * cost;
         u = u1;
       }
     }
   }
+  // ---- inside each CTA: units to consumer warps, level by level, costliest
+  // first to the least loaded warp (warps keep their units in list order)
   pl.seg_off.assign(G + 1, 0);
   pl.segs.clear();
+  pl.units.clear();
   for (int c = 0; c < G; c++) {
     pl.seg_off[c] = (int)pl.segs.size();
-    pl.segs.insert(pl.segs.end(), cta[c].begin(), cta[c].end());
+    const std::vector<Piece> &pc = cta[c];
+    std::vector<std::vector<std::vector<int>>> own(pc.size(),
+                                                   std::vector<std::vector<int>>(kWlWarps));
+    std::vector<double> load(kWlWarps, 0.0);
+    for (size_t a = 0; a < pc.size();) {
+      size_t z = a;
+      while (z < pc.size() && piece_level[c][z] == piece_level[c][a]) z++;
+      struct U {
+        double cost;
+        int piece, unit;
+      };
+      std::vector<U> us;
+      for (size_t q = a; q < z; q++)
+        for (int u = pc[q].u0; u < pc[q].u1; u++)
+          us.push_back(U{unit_cost(items[pc[q].item], u), (int)q, u});
+      std::stable_sort(us.begin(), us.end(), [](const U &x, const U &y) { return x.cost > y.cost; });
+      for (const U &x : us) {
+        const int w = (int)(std::min_element(load.begin(), load.end()) - load.begin());
+        load[w] += x.cost;
+        own[x.piece][w].push_back(x.unit);
+      }
+      a = z;
+    }
+    for (size_t q = 0; q < pc.size(); q++) {
+      const WlItem &it = items[pc[q].item];
+      WlSeg sg{};
+      sg.item = pc[q].item;
+      sg.kind = it.kind;
+      sg.nst = it.kind == kWlQ4 ? it.K / 512 : (it.kind == kWlQ8 ? it.K / 256 : 0);
+      for (int w = 0; w < kWlWarps; w++) {
+        std::vector<int> &v = own[q][w];
+        std::sort(v.begin(), v.end());
+        sg.ofs[w] = (int)pl.units.size();
+        pl.units.insert(pl.units.end(), v.begin(), v.end());
+      }
+      sg.ofs[kWlWarps] = (int)pl.units.size();
+      pl.segs.push_back(sg);
+    }
   }
   pl.seg_off[G] = (int)pl.segs.size();
   return nullptr;
