@@ -411,10 +411,13 @@ def main():
     sweep = bench_config1_sweep(args, dev, gen, world) if not args.no_sweep else None
     config4 = bench_config4(args, dev, world, rank) if not args.no_config4 else None
 
-    # ---- e2e through the host-pointer C ABI
-    e2e = None
+    # ---- e2e: host buffers in, host results out.  The headline goes through
+    # the work list (one call per step); the per-projection drop-in
+    # (fgm_linear_q4g_cuda, the reference's call structure) is reported beside it
+    e2e = e2e_per_call = None
     if not args.no_e2e:
-        e2e = bench_e2e(args, world, dev)
+        e2e = bench_e2e_list(args, world, dev, layers)
+        e2e_per_call = bench_e2e(args, world, dev)
 
     cpu = None
     if not args.no_cpu and rank == 0 and world == 1:
@@ -442,7 +445,7 @@ def main():
             "config1_per_call": per_call,
             "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clk.summary(),
-            "e2e": e2e, "prefill": prefill, "lm_head": lm_head, "decode_chain": chain,
+            "e2e": e2e, "e2e_per_call": e2e_per_call, "prefill": prefill, "lm_head": lm_head, "decode_chain": chain,
             "config0": config0, "config1_sweep": sweep, "config4": config4,
             "cpu_baseline": cpu,
         }
@@ -551,7 +554,25 @@ def bench_lm_head(args, dev, gen, world, rank):
     D.gemm_q4g(M, N, K, pa, qs, w_full, s_full, GROUP, whole)  # the parity reference
     steps = max(10, args.steps // 4)
 
-    ms_gemm = _timed(lambda: sh.local(M, pa, qs), steps, world, dev)
+    # launches replayed from CUDA graphs of R calls, so the host's launch rate
+    # does not set the pace (the fused call's arguments never change: the
+    # kernel counts its calls on the device)
+    R = 10
+    side = torch.cuda.Stream(device=dev)
+
+    def graphed(fn):
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            for _ in range(R):
+                fn()
+        return g
+
+    g_gemm = graphed(lambda: sh.local(M, pa, qs))
+    ms_gemm = _timed(g_gemm.replay, steps, world, dev, stream=side) / R
+    del g_gemm
     local = sh.local(M, pa, qs)
     ms_gather = _timed(lambda: sh.gather(local, out), steps, world, dev)
     ms_nccl = _timed(lambda: sh(M, pa, qs, out), steps, world, dev)
@@ -562,7 +583,13 @@ def bench_lm_head(args, dev, gen, world, rank):
     # the product path: GEMM + all-gather fused in one kernel per rank (NVLink stores)
     shf = S.ColumnShardedGemm("q4g", None, None, N, K, GROUP, rank=rank, world=world, device=dev,
                               shard=(w, s), fused=True, max_rows=M)
-    ms_step = _timed(lambda: shf(M, pa, qs), steps, world, dev)
+    g_fused = graphed(lambda: shf(M, pa, qs))  # R calls: the slots alternate on the device
+    ms_step = _timed(g_fused.replay, steps, world, dev, stream=side) / R
+    del g_fused
+    torch.cuda.synchronize()
+    shf._calls = R * (steps + 3) + 1  # the device counted every replayed call (+ the capture warm-up)
+    stamps = shf.peers.stamps(dev) if shf.peers is not None else None
+    ms_step_eager = _timed(lambda: shf(M, pa, qs), steps, world, dev)
     parity_fused = True
     for _ in range(3):  # consecutive calls alternate the two peer buffers
         res = shf(M, pa, qs)
@@ -581,7 +608,19 @@ def bench_lm_head(args, dev, gen, world, rank):
     parity_tok = bool(torch.equal(tok_f, tok_ref)) and bool(torch.equal(tok_p, tok_ref))
     parity = _all_ranks(parity_nccl and parity_fused and parity_tok, world, dev)
     wbytes = sum(q4g_bytes(K, N))
+    phases = None
+    if stamps is not None:  # this rank's last call: own work vs waiting for the others
+        t = torch.tensor([stamps["pushed"] - stamps["start"], stamps["arrived"] - stamps["pushed"]],
+                         dtype=torch.float64, device=dev)
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        phases = {"own_gemm_and_push_us_max": t[0].item() / 1e3,
+                  "wait_for_peers_us_max": t[1].item() / 1e3,
+                  "source": "%globaltimer stamps of each rank's last graph-replayed call, "
+                            "max over ranks"}
     return {"value": wbytes / (ms_step * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms_step,
+            "ms_per_step_eager": ms_step_eager, "phases": phases,
             "gemm_ms": ms_gemm, "nccl_gather_ms": ms_gather, "nccl_step_ms": ms_nccl,
             "argmax_step_ms": ms_argmax, "argmax_pairs_ms": ms_argmax_pairs,
             "steps": steps, "cols_per_rank": cols,
@@ -593,7 +632,9 @@ def bench_lm_head(args, dev, gen, world, rank):
                             "bit for bit; tokens equal the whole logits' row argmax",
             "workload": f"BASELINE config 3 LM head: int4 q4g {N}x{K} group {GROUP} f16 scales, "
                         f"M={M}, {world}-way output-column shards; value: one kernel per rank "
-                        f"that also stores its columns into every peer's logits over NVLink; "
+                        f"that also stores its columns into every peer's logits over NVLink, "
+                        f"{R} calls per CUDA graph replay (gemm_ms likewise; ms_per_step_eager: "
+                        f"one host launch per call); "
                         f"nccl_*: the same GEMM followed by an NCCL all-gather (group-32 f32 "
                         f"scales are outside the fgm-kernels format)"}
 
@@ -1002,6 +1043,84 @@ def bench_prefill(args, dev, gen, world):
             "steps": steps, "roofline": tc_roofline(ops, bytes_, ms * 1e-3),
             "workload": f"BASELINE config 2: M=256 prep + W8A8 GEMM at "
             f"2048x16384 and 8192x2048 (KxN), {copies} weight copies per step"}
+
+
+def bench_e2e_list(args, world, dev, layers):
+    """The config-1 step end to end with host buffers: each step copies the
+    four f32 input matrices from page-locked host memory to the device, runs
+    the work list once -- its GEMMs store their outputs straight into one
+    page-locked host buffer through its device mapping -- and waits for the
+    stream.  Host wall clock per step (fgm_cuda_worklist_run is the call).
+    Outside the timed region every output that reached the host is compared
+    bit for bit with the per-call entries (prep_rows + gemm_q4g)."""
+    import torch
+    from fastgemma_b200 import _lib
+    from fastgemma_b200 import device as D
+    L, M = len(layers), M_DECODE
+    Ks = (2048, 2048, 2048, 8192)
+    g = torch.Generator()
+    g.manual_seed(99)
+    xh = [torch.randn((M, K), generator=g).pin_memory() for K in Ks]
+    xd = [torch.empty((M, K), device=dev) for K in Ks]
+    out_cols = L * sum(N for _, _, N in DECODE_SHAPES)
+    ch = torch.empty((M * out_cols,), dtype=torch.float32).pin_memory()
+    wl = D.WorkList()
+    off = 0
+    for l in range(L):
+        pidx = []
+        for x in xd:
+            K = x.shape[1]
+            pa, qs = D.packed_a(M, K, dev), torch.empty(M, device=dev)
+            pidx.append((wl.prep(x, K, K, pa, qs), pa, qs))
+        for name, K, N in DECODE_SHAPES:
+            w, s = layers[l][name]
+            ip, pa, qs = pidx[DECODE_INPUT[name]]
+            c = ch[off:off + M * N].view(M, N)  # host rows, written by the kernel
+            off += M * N
+            wl.gemm_q4g(N, K, pa, qs, w, s, GROUP, c, deps=(ip,))
+    wl.build(M)
+    st = torch.cuda.Stream(device=dev)
+
+    def step():
+        with torch.cuda.stream(st):
+            for h, d in zip(xh, xd):
+                d.copy_(h, non_blocking=True)
+            wl.run(st)
+        st.synchronize()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    steps = max(10, args.steps)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    sec = max_over_ranks(time.perf_counter() - t0, world, dev) / steps
+    _lib.call("fgm_cuda_device_status")
+    parity, off = True, 0
+    pa_r = {K: D.packed_a(M, K, dev) for K in set(Ks)}
+    qs_r = torch.empty(M, device=dev)
+    ref = torch.empty((M, max(N for _, _, N in DECODE_SHAPES)), device=dev)
+    for l in range(L):
+        for name, K, N in DECODE_SHAPES:
+            x = xd[DECODE_INPUT[name]]
+            D.prep_rows(x, K, qs_r, pa_r[K], M, K, 0)
+            w, s_ = layers[l][name]
+            D.gemm_q4g(M, N, K, pa_r[K], qs_r, w, s_, GROUP, ref, ldc=ref.shape[1])
+            got = ch[off:off + M * N].view(M, N).to(dev)
+            parity &= bool(torch.equal(got.view(torch.int32),
+                                       ref[:, :N].contiguous().view(torch.int32)))
+            off += M * N
+    wl.close()
+    wbytes = L * sum(sum(q4g_bytes(K, N)) for _, K, N in DECODE_SHAPES)
+    return {"value": world * wbytes / sec / 1e9, "unit": "GB/s", "ms_per_step": sec * 1e3,
+            "h2d_bytes_per_step": sum(M * K * 4 for K in Ks),
+            "d2h_bytes_per_step": M * out_cols * 4, "steps": steps, "parity": parity,
+            "path": "fgm_cuda_worklist_run per step: 4 page-locked f32 inputs copied to the "
+                    "device, one work-list launch whose GEMMs store every output into "
+                    "page-locked host memory, stream synchronised; host wall clock"}
 
 
 def bench_e2e(args, world, dev):

@@ -72,8 +72,8 @@ SIGNATURES = {
     "fgm_cuda_ipc_handle": ([_p, _p], _i),
     "fgm_cuda_ipc_open": ([_p, C.POINTER(_p)], _i),
     "fgm_cuda_ipc_close": ([_p], _i),
-    "fgm_cuda_gemm_q4g_gather": ([_i, _i, _i, _p, _p, _p, _p, _i, _i, _i, _p, _p, _i, _i, _i,
-                                  C.c_ulonglong, _p], _i),
+    "fgm_cuda_gemm_q4g_gather": ([_i, _i, _i, _p, _p, _p, _p, _i, _i, _i, _p, _p, _i, _i, _sz,
+                                  _p], _i),
     "fgm_cuda_gemm_q4g_acc": ([_i, _i, _i, _p, _p, _i, _p, _i, _i, _p], _i),
     "fgm_cuda_gemm_q8c_acc": ([_i, _i, _i, _p, _p, _p, _i, _i, _p], _i),
 }

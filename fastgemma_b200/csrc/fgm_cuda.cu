@@ -1264,6 +1264,27 @@ int fgm_cuda_worklist_create(int M, const fgm_cuda_work *w, int n, void **list) 
     if ((rc = check_work(M, w[i], i, n))) return rc;
   DevInfo *di = nullptr;
   if ((rc = dev_info(&di))) return rc;
+  // Prep sources and GEMM outputs may live in page-locked host memory: the
+  // kernel reads and writes them through their device mapping.  Everything
+  // else (activations, weights, scales) must be device memory.
+  auto mapped = [&](const void *ptr, bool host_ok, const char *what, int i,
+                    const void **out) -> int {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(FGM_CUDA_EINVAL, "work %d: %s is not CUDA-accessible memory", i, what);
+    }
+    if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) {
+      *out = ptr;
+      return FGM_CUDA_OK;
+    }
+    if (a.type == cudaMemoryTypeHost && host_ok && a.devicePointer) {
+      *out = a.devicePointer;
+      return FGM_CUDA_OK;
+    }
+    return fail(FGM_CUDA_EINVAL, "work %d: %s must be device memory%s", i, what,
+                host_ok ? " or page-locked host memory" : "");
+  };
   const int MT = M <= 8 ? 1 : 2;
   std::vector<WlItem> items((size_t)n);
   for (int i = 0; i < n; i++) {
@@ -1279,9 +1300,13 @@ int fgm_cuda_worklist_create(int M, const fgm_cuda_work *w, int n, void **list) 
       it.units = (M + 15) / 16 * 16;
       it.lda = s.lda;
       it.hsz = s.hsz;
-      it.src = s.src;
-      it.pa = s.pa;
-      it.qs = s.qs;
+      const void *src = nullptr, *pa = nullptr, *qs = nullptr;
+      if ((rc = mapped(s.src, true, "src", i, &src)) || (rc = mapped(s.pa, false, "pa", i, &pa)) ||
+          (rc = mapped(s.qs, false, "qs", i, &qs)))
+        return rc;
+      it.src = static_cast<const float *>(src);
+      it.pa = static_cast<int8_t *>(const_cast<void *>(pa));
+      it.qs = static_cast<float *>(const_cast<void *>(qs));
       continue;
     }
     it.gk = it.kind == kWlQ4 ? s.group / 64 : 0;
@@ -1289,10 +1314,16 @@ int fgm_cuda_worklist_create(int M, const fgm_cuda_work *w, int n, void **list) 
     it.units = s.n1 - s.n0;
     it.ldc = s.ldc;
     it.c_col0 = 0;
-    it.B = static_cast<const uint8_t *>(s.B);
-    it.b_scale = s.b_scale;
-    it.a_scale = s.a_scale;
-    it.C = s.C;
+    const void *A = nullptr, *B = nullptr, *bs = nullptr, *as = nullptr, *Cp = nullptr;
+    if ((rc = mapped(s.A, false, "A", i, &A)) || (rc = mapped(s.B, false, "B", i, &B)) ||
+        (rc = mapped(s.b_scale, false, "b_scale", i, &bs)) ||
+        (rc = mapped(s.a_scale, false, "a_scale", i, &as)) ||
+        (rc = mapped(s.C, true, "C", i, &Cp)))
+      return rc;
+    it.B = static_cast<const uint8_t *>(B);
+    it.b_scale = bs;
+    it.a_scale = static_cast<const float *>(as);
+    it.C = static_cast<float *>(const_cast<void *>(Cp));
     if (!encode_packed_a_map(&it.amap, s.A, s.K, MT * 8))
       return fail(FGM_CUDA_ERUNTIME, "worklist: cuTensorMapEncodeTiled failed for entry %d", i);
   }
@@ -1650,7 +1681,7 @@ int fgm_cuda_ipc_close(void *dev_ptr) {
 int fgm_cuda_gemm_q4g_gather(int M, int N, int K, const int8_t *A, const float *a_scale,
                              const uint8_t *Bq, const uint16_t *b_scale, int group, int col0,
                              int ldc, void *const *out, unsigned long long *const *sig, int rank,
-                             int world, int slot, unsigned long long uses, void *stream) {
+                             int world, size_t slot_floats, void *stream) {
   int rc = check_gemm(M, N, K, N, 0, N / 16, group, true);
   if (rc) return rc;
   if (world < 1 || world > kMaxGatherRanks || rank < 0 || rank >= world)
@@ -1659,8 +1690,9 @@ int fgm_cuda_gemm_q4g_gather(int M, int N, int K, const int8_t *A, const float *
   if (M > 16) return fail(FGM_CUDA_EINVAL, "gather: M=%d > 16 (decode GEMM only)", M);
   if (col0 < 0 || col0 % 16 != 0 || ldc % 4 != 0 || col0 + N > ldc)
     return fail(FGM_CUDA_EINVAL, "gather: columns [%d, %d) of ldc=%d", col0, col0 + N, ldc);
-  if ((slot != 0 && slot != 1) || uses == 0)
-    return fail(FGM_CUDA_EINVAL, "gather: slot %d, uses %llu", slot, uses);
+  if (slot_floats < (size_t)M * ldc || slot_floats % 4 != 0)
+    return fail(FGM_CUDA_EINVAL, "gather: slot_floats=%zu < M*ldc or not a multiple of 4",
+                slot_floats);
   if (!out || !sig || !A || !a_scale || !Bq || !b_scale)
     return fail(FGM_CUDA_EINVAL, "null pointer");
   for (int q = 0; q < world; q++)
@@ -1685,8 +1717,7 @@ int fgm_cuda_gemm_q4g_gather(int M, int N, int K, const int8_t *A, const float *
   p.ldc = ldc;
   p.g.rank = rank;
   p.g.world = world;
-  p.g.slot = slot;
-  p.g.uses = uses;
+  p.g.slot_floats = slot_floats;
   for (int q = 0; q < world; q++) {
     p.g.out[q] = static_cast<float *>(out[q]);
     p.g.sig[q] = sig[q];

@@ -16,12 +16,22 @@ constexpr int kMaxGatherRanks = 8;
 // output buffer has the same [M][ldc] layout; this rank's finished columns
 // are also stored into each peer's buffer over NVLink, and system-scope
 // counters tell each rank when its buffer is complete.  world = 0: off.
+// Which of the two buffers a call uses, and how often that buffer was used
+// before, come from the rank's own call counter on the device, so a call's
+// launch parameters never change and the call can be replayed from a graph.
 struct GatherParams {
-  float *out[kMaxGatherRanks];               // each rank's output buffer for this call
-  unsigned long long *sig[kMaxGatherRanks];  // each rank's signal words (8 x u64)
-  int rank, world, slot;                     // slot: which of the double buffers
-  unsigned long long uses;                   // calls that used this slot so far, this one included
+  float *out[kMaxGatherRanks];               // each rank's double buffer (slot 0 at out[q])
+  unsigned long long *sig[kMaxGatherRanks];  // each rank's signal words (kGatherSigWords x u64)
+  size_t slot_floats;                        // floats between slot 0 and slot 1
+  int rank, world;
 };
+// Signal words of one rank (u64 each, zeroed once, never reset):
+//   [slot]     ranks whose last CTA finished pushing into this rank's buffer `slot`
+//   [2 + slot] ranks that started a call using `slot` (their buffer may be overwritten)
+//   [4 + slot] this rank's CTAs done pushing into `slot`
+//   [6]        calls this rank completed (slot = calls & 1)
+//   [8], [9], [10]  %globaltimer of the last call: CTA 0 start, own pushes done, all arrived
+constexpr int kGatherSigWords = 16;
 
 struct GemvParams {
   int M, N, K, group;       // group: int4 scale group; unused for int8

@@ -103,11 +103,7 @@ __device__ __forceinline__ void warm_next(const GemvParams &p, int lane) {
 }
 
 // ------------------------------------------------------ fused all-gather
-// Signal words of one rank (u64 each, zeroed once, never reset -- counts
-// grow by a known amount per call): [slot] = ranks whose last CTA finished
-// pushing into this rank's buffer `slot`; [2 + slot] = ranks that started a
-// call using `slot` (their buffer is free to overwrite); [4 + slot] = this
-// rank's CTAs done pushing.
+// Signal words: see GatherParams (counts grow by a known amount per call).
 __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *a) {
   unsigned long long v;
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
@@ -131,16 +127,28 @@ __device__ __forceinline__ void st_v4_global(float *p, float4 v) {
                : "memory");
 }
 
-// One 8-row block of n-block nb, already stored at p.C, copied to every
-// peer's buffer: lane = (row, 16-byte chunk), 64 contiguous bytes per row.
-__device__ __forceinline__ void push_rows(const GemvParams &p, int nb, int m0, int lane) {
+// One 8-row block of n-block nb, already stored at Cout (this rank's buffer
+// of the call's slot), copied to every peer's buffer: lane = (row, 16-byte
+// chunk), 64 contiguous bytes per row.
+__device__ __forceinline__ void push_rows(const GemvParams &p, float *Cout, int nb, int m0,
+                                          int lane) {
   const int m = m0 + (lane >> 2);
   if (m >= p.M) return;
   const size_t off = (size_t)m * p.ldc + (size_t)(nb * 16 - p.c_col0) + (lane & 3) * 4;
-  const float4 v = *reinterpret_cast<const float4 *>(p.C + off);
-  const size_t shift = (size_t)(p.C - p.g.out[p.g.rank]);
+  const float4 v = *reinterpret_cast<const float4 *>(Cout + off);
+  const size_t shift = (size_t)(Cout - p.g.out[p.g.rank]);
   for (int q = 0; q < p.g.world; q++)
     if (q != p.g.rank) st_v4_global(p.g.out[q] + shift + off, v);
+}
+
+// Before a warp's first push of a call: every rank has announced that its
+// buffer of this slot is free (bounded; false on time-out).
+__device__ __forceinline__ bool peers_free(const GemvParams &p, int slot, unsigned long long uses,
+                                           int lane) {
+  bool ok = true;
+  if (lane == 0)
+    ok = spin_until_geq(p.g.sig[p.g.rank] + 2 + slot, (unsigned long long)p.g.world * uses);
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
 // Per-lane constants shared by the stage routines.
@@ -390,6 +398,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     gemv_kernel(const GemvParams p, const GemvPlan pl) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_abort;
+  __shared__ int s_slot;                  // fused gather: this call's buffer
+  __shared__ unsigned long long s_uses;   // fused gather: calls that used it, this one included
   __shared__ float s_as[16];  // a_scale of the block's rows
   constexpr int TB = Geo<Q4>::TB;
   constexpr int T = Geo<Q4>::T;
@@ -504,18 +514,18 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
   }
   pdl_wait();  // activations and outputs are ordered after earlier kernels
   if (p.g.world > 0 && threadIdx.x == 0) {
+    // this call's slot from the rank's completed-call counter (the previous
+    // call finished before griddepcontrol.wait returned)
+    const unsigned long long c = ld_acquire_sys(p.g.sig[p.g.rank] + 6);
+    s_slot = (int)(c & 1);
+    s_uses = (c >> 1) + 1;
     if (blockIdx.x == 0 && blockIdx.y == 0) {
+      p.g.sig[p.g.rank][8] = tc::globaltimer_ns();
       // everything before this call on this stream is complete, including the
-      // readers of this slot's previous contents: tell every rank it may write
-      for (int q = 0; q < p.g.world; q++) atomicAdd_system(p.g.sig[q] + 2 + p.g.slot, 1ull);
-    }
-    // every rank's buffer must be free before this CTA pushes into it (the
-    // weight stream is already in flight meanwhile); units are pushed as they
-    // finish, after the block barrier that publishes s_abort
-    const unsigned long long need = (unsigned long long)p.g.world * p.g.uses;
-    if (!spin_until_geq(p.g.sig[p.g.rank] + 2 + p.g.slot, need)) {
-      s_abort = 1;
-      if (p.err) atomicExch(p.err, 3);
+      // readers of this slot's previous contents: tell every rank it may write.
+      // Each warp checks that every rank did the same just before its first
+      // push, so the weight stream and the first units do not wait for it.
+      for (int q = 0; q < p.g.world; q++) atomicAdd_system(p.g.sig[q] + 2 + s_slot, 1ull);
     }
   }
 
@@ -563,7 +573,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     for (int it = pre; it < prologue; it++) issue();
   }
   if (load_as) s_as[threadIdx.x] = as_v;
-  if (pl.a_bytes || !raw) __syncthreads();
+  if (pl.a_bytes || !raw || p.g.world > 0) __syncthreads();
+  const int gslot = p.g.world > 0 ? s_slot : 0;
+  const unsigned long long guses = p.g.world > 0 ? s_uses : 0;
+  float *const Cout = p.C + (size_t)gslot * p.g.slot_floats;  // this call's output buffer
+  bool pushed = false;  // this warp has checked that every peer's slot is free
 
   float cf[MT][4];
   int32_t gacc[MT][4];
@@ -666,17 +680,22 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
           if (raw) {
             p.acc[(size_t)m * p.N + n] = gacc[mt][i];
           } else if (Q4) {
-            p.C[(size_t)m * p.ldc + (n - p.c_col0)] = __fmul_rn(cf[mt][i], s_as[m - mb * 16]);
+            Cout[(size_t)m * p.ldc + (n - p.c_col0)] = __fmul_rn(cf[mt][i], s_as[m - mb * 16]);
           } else {
             const float bs = reinterpret_cast<const float *>(p.b_scale)[n];
-            p.C[(size_t)m * p.ldc + (n - p.c_col0)] =
+            Cout[(size_t)m * p.ldc + (n - p.c_col0)] =
                 __fmul_rn(__int2float_rn(gacc[mt][i]), __fmul_rn(bs, s_as[m - mb * 16]));
           }
         }
       if (p.g.world > 0 && !*reinterpret_cast<volatile int *>(&s_abort)) {
+        if (!pushed && !(pushed = peers_free(p, gslot, guses, lane))) {
+          s_abort = 1;
+          if (lane == 0 && p.err) atomicExch(p.err, 3);
+          continue;
+        }
         __syncwarp();  // this warp's stores of the unit are visible to its lanes
 #pragma unroll
-        for (int r0 = 0; r0 < MT * 8; r0 += 8) push_rows(p, nb, mb * 16 + r0, lane);
+        for (int r0 = 0; r0 < MT * 8; r0 += 8) push_rows(p, Cout, nb, mb * 16 + r0, lane);
       }
       continue;
     }
@@ -714,7 +733,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
         const size_t gstride = (size_t)MT * 8 * L.pr;
 #pragma unroll 8
         for (int g = 0; g < ng; g++) c = __fmaf_rn(xf[g * gstride], xs[g * 16], c);
-        p.C[(size_t)m * p.ldc + (n - p.c_col0)] = __fmul_rn(c, s_as[ml]);
+        Cout[(size_t)m * p.ldc + (n - p.c_col0)] = __fmul_rn(c, s_as[ml]);
       } else {
         const int32_t v = xsum[ml * 16 + nl];
         xsum[ml * 16 + nl] = 0;
@@ -723,14 +742,20 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
           p.acc[(size_t)m * p.N + n] = v;
         } else {
           const float bs = reinterpret_cast<const float *>(p.b_scale)[n];
-          p.C[(size_t)m * p.ldc + (n - p.c_col0)] =
+          Cout[(size_t)m * p.ldc + (n - p.c_col0)] =
               __fmul_rn(__int2float_rn(v), __fmul_rn(bs, s_as[ml]));
         }
       }
     }
     team_sync(team, P * 32);
-    if (p.g.world > 0 && part < MT && !*reinterpret_cast<volatile int *>(&s_abort))
-      push_rows(p, nb, mb * 16 + part * 8, lane);
+    if (p.g.world > 0 && part < MT && !*reinterpret_cast<volatile int *>(&s_abort)) {
+      if (!pushed && !(pushed = peers_free(p, gslot, guses, lane))) {
+        s_abort = 1;
+        if (lane == 0 && p.err) atomicExch(p.err, 3);
+      } else {
+        push_rows(p, Cout, nb, mb * 16 + part * 8, lane);
+      }
+    }
   }
 
   if (p.g.world > 0) {
@@ -738,16 +763,22 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     // the pushes, count this CTA, and let the rank's last CTA signal every
     // rank and wait until its own buffer holds all ranks' columns.
     const GatherParams &g = p.g;
-    const unsigned long long need = (unsigned long long)g.world * g.uses;
+    const unsigned long long need = (unsigned long long)g.world * guses;
     __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
-      const unsigned long long done = atomicAdd(g.sig[g.rank] + 4 + g.slot, 1ull) + 1;
-      if (done == g.uses * gridDim.x * gridDim.y) {  // this rank's last CTA
+      const unsigned long long done = atomicAdd(g.sig[g.rank] + 4 + gslot, 1ull) + 1;
+      if (done == guses * gridDim.x * gridDim.y) {  // this rank's last CTA
         __threadfence_system();
-        for (int q = 0; q < g.world; q++) atomicAdd_system(g.sig[q] + g.slot, 1ull);
+        g.sig[g.rank][9] = tc::globaltimer_ns();
+        for (int q = 0; q < g.world; q++) atomicAdd_system(g.sig[q] + gslot, 1ull);
         // the call completes when every rank's columns are in this buffer
-        if (!spin_until_geq(g.sig[g.rank] + g.slot, need) && p.err) atomicExch(p.err, 3);
+        if (!spin_until_geq(g.sig[g.rank] + gslot, need) && p.err) atomicExch(p.err, 3);
+        g.sig[g.rank][10] = tc::globaltimer_ns();
+        // the next call on this rank uses the other buffer (it reads this
+        // counter after griddepcontrol.wait, i.e. after this kernel completed)
+        __threadfence_system();
+        atomicAdd(g.sig[g.rank] + 6, 1ull);
       }
     }
   }

@@ -74,6 +74,9 @@ class _DeviceArray:
                                          "data": (ptr, False), "version": 3, "strides": None}
 
 
+SIG_BYTES = 128  # FGM_CUDA_GATHER_SIG_BYTES
+
+
 class PeerBuffers:
     """Every rank's double-buffered output [2][rows][N] f32 and signal words,
     allocated by the owner and opened by every peer (CUDA IPC, one node).
@@ -86,7 +89,7 @@ class PeerBuffers:
         self.slot_bytes = rows * N * 4
         out, sig = C.c_void_p(), C.c_void_p()
         call("fgm_cuda_ipc_alloc", 2 * self.slot_bytes, C.byref(out))
-        call("fgm_cuda_ipc_alloc", 64, C.byref(sig))
+        call("fgm_cuda_ipc_alloc", SIG_BYTES, C.byref(sig))
         self._own = (out.value, sig.value)
         h_out, h_sig = (C.c_ubyte * 64)(), (C.c_ubyte * 64)()
         call("fgm_cuda_ipc_handle", out, h_out)
@@ -114,6 +117,14 @@ class PeerBuffers:
     def view(self, slot: int, M: int, device) -> torch.Tensor:
         ptr = self.out[self.rank] + slot * self.slot_bytes
         return torch.as_tensor(_DeviceArray(ptr, (self.rows, self.N)), device=device)[:M]
+
+    def stamps(self, device) -> dict:
+        """%globaltimer stamps (ns) of this rank's last fused call: start, own
+        columns pushed, every rank's columns arrived; and its completed calls."""
+        w = torch.as_tensor(_DeviceArray(self.sig[self.rank], (SIG_BYTES // 8,), "<u8"),
+                            device=device).cpu().numpy()
+        return {"calls": int(w[6]), "start": int(w[8]), "pushed": int(w[9]),
+                "arrived": int(w[10])}
 
     def close(self):
         from ._lib import call
@@ -176,6 +187,7 @@ class ColumnShardedGemm:
         # them into every rank's output over NVLink (int4 decode GEMM only)
         self.peers = None
         self._calls = 0
+        self._args = None
         if fused:
             if kind != "q4g" or max_rows > 16:
                 raise ValueError("the fused gather covers the int4 decode GEMM (M <= 16)")
@@ -212,16 +224,17 @@ class ColumnShardedGemm:
         pb = self.peers
         if M > pb.rows:
             raise ValueError(f"M={M} > max_rows={pb.rows}")
-        slot, uses = self._calls & 1, self._calls // 2 + 1
+        slot = self._calls & 1  # the kernel counts the calls itself; this only picks the view
         self._calls += 1
-        outs = (C.c_void_p * self.world)(*[o + slot * pb.slot_bytes for o in pb.out])
-        sigs = (C.c_void_p * self.world)(*pb.sig)
+        if self._args is None:
+            self._args = ((C.c_void_p * self.world)(*pb.out), (C.c_void_p * self.world)(*pb.sig))
+        outs, sigs = self._args
         st = (stream or torch.cuda.current_stream(self.device)).cuda_stream
         A_p = A.data_ptr() if hasattr(A, "data_ptr") else A
         s_p = a_scale.data_ptr() if hasattr(a_scale, "data_ptr") else a_scale
         call("fgm_cuda_gemm_q4g_gather", M, self.cols, self.K, A_p, s_p, self.w.data_ptr(),
              self.s.data_ptr(), self.group, self.nb0 * 16, self.N, outs, sigs, self.rank,
-             self.world, slot, uses, st)
+             self.world, pb.slot_bytes // 4, st)
         return pb.view(slot, M, self.device)
 
     def argmax(self, M: int, A, a_scale, stream=None) -> torch.Tensor:

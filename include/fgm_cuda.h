@@ -270,6 +270,10 @@ int fgm_cuda_gemm_q8c_acc(int M, int N, int K, const int8_t *A, const int8_t *B,
  *    lda % 4 == 0, src 16-byte aligned; hsz 0 or a power of two <= 128
  *    dividing K (the FWHT block, ops.c:153-175); outputs pa (the packed 16-row
  *    block, packed_a_len(M, K) bytes, 4-byte aligned) and qs [M].
+ *  - Prep sources and GEMM outputs may be page-locked host memory (read and
+ *    written by the kernel through their device mapping, so one run moves a
+ *    step's inputs and results across the host link itself); every other
+ *    buffer must be device memory.  Pageable host memory is rejected.
  *  - deps: up to two indices of EARLIER entries whose outputs this entry
  *    reads (-1: none).  Inputs written before the run (earlier kernels on the
  *    stream) need no entry.  Entries that write memory another entry reads or
@@ -433,18 +437,25 @@ int fgm_cuda_ipc_close(void *dev_ptr);
 /* This rank's share of a column-sharded int4 decode GEMM with the all-gather
  * fused into it: Bq/b_scale hold this rank's N columns (a shard of the .fgm
  * blob), which land at columns [col0, col0 + N) of every rank's output
- * out[q] ([M][ldc] f32, M <= 16) -- locally and over NVLink into each peer.
- * sig[q] are the ranks' signal words (8 x u64, from fgm_cuda_ipc_alloc).
- * Collective: every rank calls with the same slot (0/1, double buffers) and
- * uses (calls so far with that slot, this one included).  When the kernel
- * completes on `stream`, out[rank] holds all ranks' columns; it stays valid
- * until the call after next.  Every cross-GPU wait is bounded (2 s, then
- * fgm_cuda_device_status reports FGM_CUDA_ETIMEOUT). */
+ * out[q] -- two buffers per rank, slot s at out[q] + s*slot_floats, each
+ * [M][ldc] f32 (M <= 16) -- locally and over NVLink into each peer.  sig[q]
+ * are the ranks' signal words (FGM_CUDA_GATHER_SIG_BYTES, zeroed, from
+ * fgm_cuda_ipc_alloc).  Collective: every rank makes the same sequence of
+ * calls; call c uses slot c % 2, counted on the device (a rank's own signal
+ * words hold its completed calls), so the arguments never change between
+ * calls and a sequence of calls can be replayed from a CUDA graph.  When the
+ * kernel completes on `stream`, slot c % 2 of out[rank] holds all ranks'
+ * columns; it stays valid until the call after next.  Words 8..10 of a rank's
+ * signal block hold %globaltimer stamps of its last call (start, own columns
+ * pushed, every rank's columns arrived).  Every cross-GPU wait is bounded
+ * (2 s, then fgm_cuda_device_status reports FGM_CUDA_ETIMEOUT; the ranks'
+ * counters may then disagree: make new buffers). */
+#define FGM_CUDA_GATHER_SIG_BYTES 128
 int fgm_cuda_gemm_q4g_gather(int M, int N, int K, const int8_t *A, const float *a_scale,
                              const uint8_t *Bq, const uint16_t *b_scale, int group,
                              int col0, int ldc, void *const *out,
                              unsigned long long *const *sig, int rank, int world,
-                             int slot, unsigned long long uses, void *stream);
+                             size_t slot_floats, void *stream);
 
 #ifdef __cplusplus
 }
