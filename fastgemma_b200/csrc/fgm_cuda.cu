@@ -1232,8 +1232,9 @@ static int check_work(int M, const fgm_cuda_work &w, int i, int n) {
   if (q4 && w.K % w.group) return fail(FGM_CUDA_EINVAL, "work %d: K %% group != 0", i);
   if (!w.A || !w.a_scale || !w.B || !w.b_scale || !w.C)
     return fail(FGM_CUDA_EINVAL, "work %d: null pointer", i);
-  if (!al(w.A, 16) || !al(w.B, 16) || !al(w.b_scale, 4))
-    return fail(FGM_CUDA_EINVAL, "work %d: A and B must be 16-byte, scales 4-byte aligned", i);
+  if (!al(w.A, 16) || !al(w.B, 16) || !al(w.b_scale, q4 ? 16 : 4))
+    return fail(FGM_CUDA_EINVAL, "work %d: A, B and int4 scales must be 16-byte aligned, int8 "
+                "scales 4-byte aligned", i);
   (void)M;
   return FGM_CUDA_OK;
 }
@@ -1372,9 +1373,9 @@ int fgm_cuda_worklist_create(int M, const fgm_cuda_work *w, int n, void **list) 
   p.abort = reinterpret_cast<int *>(p.done + n + 1);
   p.err = di->err;
   p.M = M;
+  p.warps = wl->plan.warps;
   p.stages = wl->plan.stages;
-  p.n_abuf = wl->plan.n_abuf;
-  p.abuf_bytes = wl->plan.abuf_bytes;
+  p.a_ring = wl->plan.a_ring;
   *list = wl;
   return FGM_CUDA_OK;
 }

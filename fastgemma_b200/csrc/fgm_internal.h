@@ -227,10 +227,10 @@ struct WlItem {
   int8_t *pa;              // prep: packed rows
   float *qs;               // prep: row scales
 };
-constexpr int kWlWarps = 8;  // consumer warps per CTA
-struct WlSeg {             // one CTA's share of one item
-  int item, kind, nst;     // item, its kind, 4 KB weight stages per unit
-  int ofs[kWlWarps + 1];   // consumer warp w takes units[ofs[w], ofs[w + 1])
+constexpr int kWlMaxWarps = 15;  // consumer warps per CTA, at most (16 warps with the producer)
+struct WlSeg {                 // one CTA's share of one item
+  int item, kind, nst;         // item, its kind, 4 KB weight stages per unit
+  int ofs[kWlMaxWarps + 1];    // consumer warp w takes units[ofs[w], ofs[w + 1])
 };
 struct WlParams {
   const WlItem *items;
@@ -242,10 +242,11 @@ struct WlParams {
   unsigned *ctas_done;     // CTAs finished (the last one resets the counters)
   int *abort;              // raised by a warp that gave up on a bounded wait
   int *err;                // device status word
-  int M, stages, n_abuf, abuf_bytes;
+  int M, warps, stages;    // consumer warps per CTA, weight ring stages per warp
+  int a_ring;              // bytes of the activation ring (segments staged FIFO)
 };
 struct WlPlan {
-  int M, MT, grid, stages, n_abuf, abuf_bytes;
+  int M, MT, grid, warps, stages, a_ring;
   size_t smem;
   std::vector<WlSeg> segs;
   std::vector<int> seg_off;

@@ -58,6 +58,8 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdlib>
+#include <type_traits>
 #include <cstring>
 #include <vector>
 
@@ -72,8 +74,11 @@ namespace {
 
 using namespace stream;
 
-constexpr int kWlStage = 4096;     // bytes per ring stage
+constexpr int kWlStageW = 4096;    // weight bytes per ring stage (8 int4 or 4 int8 tiles)
+constexpr int kWlStageS = 256;     // int4 scale rows of the stage (up to 8 groups x 32 bytes)
+constexpr int kWlStage = kWlStageW + kWlStageS;  // bytes per ring stage
 constexpr int kWlMaxStages = 8;
+constexpr int kWlASlots = 4;       // GEMM segments whose activations can be staged at once
 constexpr uint64_t kWlLimitNs = 2000000000ull;
 
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *a) {
@@ -131,6 +136,12 @@ __device__ __forceinline__ void wl_signal(const WlParams &p, int it, unsigned n,
   }
 }
 
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return v;
+}
+
 // Per-lane fragment constants.
 struct WlLane {
   int g8, tig;
@@ -163,9 +174,9 @@ __device__ __forceinline__ void load_b(uint32_t ab, int t, int mt, const WlLane 
 // One 4 KB stage of an int4 unit: 8 tiles, scale groups of GK tiles folded
 // into cf as they complete (the stage starts on a group boundary).
 template <int MT, int GK>
-__device__ __forceinline__ void q4_stage(uint32_t st, uint32_t ab, const WlLane &L, uint32_t sc0,
-                                         uint32_t sc1, float (&cf)[MT][4]) {
-  constexpr int CH = MT == 1 ? 8 : 4;  // tiles whose operands load together
+__device__ __forceinline__ void q4_stage(uint32_t st, uint32_t ab, const WlLane &L,
+                                         float (&cf)[MT][4]) {
+  constexpr int CH = MT == 1 ? 4 : 2;  // tiles whose operands load together
   int32_t gacc[MT][4];
 #pragma unroll
   for (int t0 = 0; t0 < 8; t0 += CH) {
@@ -198,14 +209,28 @@ __device__ __forceinline__ void q4_stage(uint32_t st, uint32_t ab, const WlLane 
         for (int i = 0; i < 4; i++)
           gacc[mt][i] = (t % GK == 0) ? ta[mt][i] : gacc[mt][i] + ta[mt][i];
       if ((t + 1) % GK != 0) continue;
-      const int lg = t / GK;  // group inside the stage
-      float s0, s1;
-      scale_pair(lg < 4 ? sc0 : sc1, (lg & 3) * 8, L.g8, s0, s1);
+      const int lg = t / GK;  // group inside the stage: its f16 scale row follows the tiles
+      const uint32_t srow = st + kWlStageW + lg * 32 + L.g8 * 2;
+      float s0 = f16_to_f32(lds16(srow)), s1 = f16_to_f32(lds16(srow + 16));
+      if (GK <= 4) {
+        // gacc is 16x the group sum (nibbles in the high half of each byte)
+        // and below 2^22 for groups up to 256: convert it as it is and take
+        // the 16 out of the scale instead -- (16 x)(s / 16) is x s exactly,
+        // so the fma rounds the reference's product once, as before
+        s0 = __fmul_rn(s0, 0.0625f);
+        s1 = __fmul_rn(s1, 0.0625f);
 #pragma unroll
-      for (int mt = 0; mt < MT; mt++)
+        for (int mt = 0; mt < MT; mt++)
 #pragma unroll
-        for (int i = 0; i < 4; i++)
-          cf[mt][i] = __fmaf_rn(i2f_exact(gacc[mt][i] >> 4), i < 2 ? s0 : s1, cf[mt][i]);
+          for (int i = 0; i < 4; i++)
+            cf[mt][i] = __fmaf_rn(i2f_exact(gacc[mt][i]), i < 2 ? s0 : s1, cf[mt][i]);
+      } else {
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+          for (int i = 0; i < 4; i++)
+            cf[mt][i] = __fmaf_rn(i2f_exact(gacc[mt][i] >> 4), i < 2 ? s0 : s1, cf[mt][i]);
+      }
     }
   }
 }
@@ -232,17 +257,6 @@ __device__ __forceinline__ void q8_stage(uint32_t st, uint32_t ab, const WlLane 
 #pragma unroll
       for (int i = 0; i < 4; i++) acc[mt][i] += ta[i];
     }
-  }
-}
-
-template <int MT>
-__device__ __forceinline__ void q4_stage_gk(int gk, uint32_t st, uint32_t ab, const WlLane &L,
-                                            uint32_t sc0, uint32_t sc1, float (&cf)[MT][4]) {
-  switch (gk) {
-    case 1: q4_stage<MT, 1>(st, ab, L, sc0, sc1, cf); break;
-    case 2: q4_stage<MT, 2>(st, ab, L, sc0, sc1, cf); break;
-    case 4: q4_stage<MT, 4>(st, ab, L, sc0, sc1, cf); break;
-    default: q4_stage<MT, 8>(st, ab, L, sc0, sc1, cf); break;
   }
 }
 
@@ -394,26 +408,28 @@ __device__ __forceinline__ void walk_next(Walk &k, const WlParams &p, const WlSe
 }
 
 template <int MT>
-__global__ void __launch_bounds__((kWlWarps + 1) * 32, 1) worklist_kernel(const WlParams p) {
+__global__ void __launch_bounds__((kWlMaxWarps + 1) * 32, 1) worklist_kernel(const WlParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  __shared__ uint64_t s_full[2], s_empty[2];
-  __shared__ uint64_t s_ring[kWlWarps][kWlMaxStages];
-  __shared__ float s_as[2][16];
+  __shared__ uint64_t s_full[kWlASlots], s_empty[kWlASlots];
+  __shared__ uint64_t s_ring[kWlMaxWarps][kWlMaxStages];
+  __shared__ float s_as[kWlASlots][16];
+  __shared__ uint32_t s_aoff[kWlASlots];
+  __shared__ int s_r0[kWlASlots], s_r1[kWlASlots];  // producer: regions of the last four segments
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const WlSeg *segs = p.segs + p.seg_off[blockIdx.x];
   const int nseg = p.seg_off[blockIdx.x + 1] - p.seg_off[blockIdx.x];
-  const int S = p.stages;
+  const int S = p.stages, W = p.warps;
   const uint32_t abuf0 = tc::smem_u32(smem);
-  const uint32_t ring0 = abuf0 + (uint32_t)(p.n_abuf * p.abuf_bytes);
+  const uint32_t ring0 = abuf0 + (uint32_t)p.a_ring;
 
   if (threadIdx.x == 0) {
-    for (int b = 0; b < 2; b++) {
+    for (int b = 0; b < kWlASlots; b++) {
       tc::mbar_init(&s_full[b], 1);
-      tc::mbar_init(&s_empty[b], kWlWarps);
+      tc::mbar_init(&s_empty[b], W);
     }
-    for (int w = 0; w < kWlWarps; w++)
+    for (int w = 0; w < W; w++)
       for (int s = 0; s < S; s++) tc::mbar_init(&s_ring[w][s], 1);
     tc::fence_mbar_init();
   }
@@ -422,80 +438,91 @@ __global__ void __launch_bounds__((kWlWarps + 1) * 32, 1) worklist_kernel(const 
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    // GEMM segment g stages its activations in slot g % 4 (barriers, scales)
+    // at a region of the activation ring allocated first in, first out; a
+    // region is reused once every consumer has left the segments holding it.
     pdl_wait();  // packed activations and their scales may come from earlier kernels
-    int g = 0;  // GEMM segments staged so far; segment g uses buffer g % n_abuf
+    int g = 0, head = 0;
     bool ok = true;
     for (int si = 0; si < nseg && ok; si++) {
       const WlSeg &sg = segs[si];
       if (sg.kind == kWlPrep) continue;
       const WlItem &it = p.items[sg.item];
-      const int b = g % p.n_abuf;
-      if (g >= p.n_abuf)  // every consumer has left segment g - n_abuf, the buffer's last user
-        ok = wl_wait(&s_empty[b], (uint32_t)((g / p.n_abuf - 1) & 1), p);
+      const int b = g & (kWlASlots - 1);
+      const int bytes = it.K / 64 * MT * 512;
+      const int sz = (bytes + 1023) & ~1023;
+      int off = head;
+      if (off + sz > p.a_ring) off = 0;
+      if (g >= kWlASlots)  // segment g - 4, the slot's last user, has been left
+        ok = wl_wait(&s_empty[b], (uint32_t)(((g >> 2) - 1) & 1), p);
+      for (int j = g - kWlASlots + 1; j < g && ok; j++) {  // younger segments in the region
+        if (j < 0) continue;
+        const int jb = j & (kWlASlots - 1);
+        if (s_r0[jb] < off + sz && off < s_r1[jb])
+          ok = wl_wait(&s_empty[jb], (uint32_t)((j >> 2) & 1), p);
+      }
       if (ok && lane == 0) ok = wl_wait_item(p, it.deps[0]) && wl_wait_item(p, it.deps[1]);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
-      fence_proxy_async_global();  // the activations may have been written in this launch
-      if (lane < 16) s_as[b][lane] = lane < p.M ? it.a_scale[lane] : 0.0f;
       __syncwarp();
       if (lane == 0) {
-        tc::mbar_expect_tx(&s_full[b], (uint32_t)(it.K / 64 * MT * 512));
-        tc::tma_load_3d(smem + (size_t)b * p.abuf_bytes, &it.amap, &s_full[b], 0, 0, 0);
+        s_r0[b] = off;
+        s_r1[b] = off + sz;
+      }
+      head = off + sz;
+      fence_proxy_async_global();  // the activations may have been written in this launch
+      if (lane < 16) s_as[b][lane] = lane < p.M ? it.a_scale[lane] : 0.0f;
+      if (lane == 0) s_aoff[b] = (uint32_t)off;
+      __syncwarp();
+      if (lane == 0) {
+        tc::mbar_expect_tx(&s_full[b], (uint32_t)bytes);
+        tc::tma_load_3d(smem + off, &it.amap, &s_full[b], 0, 0, 0);
       }
       g++;
     }
     if (!ok) {
       if (lane == 0) wl_fail(p, 5);
       // the last activation boxes requested may still be landing
-      for (int k = (g > p.n_abuf ? g - p.n_abuf : 0); k < g; k++)
-        tc::mbar_wait(&s_full[k % p.n_abuf], (uint32_t)((k / p.n_abuf) & 1));
+      for (int k = (g > kWlASlots ? g - kWlASlots : 0); k < g; k++)
+        tc::mbar_wait(&s_full[k & (kWlASlots - 1)], (uint32_t)((k >> 2) & 1));
     }
-  } else {
+  } else if (warp <= W) {
     // ------------------------------------------------------------ consumers
     const int cw = warp - 1;
     const WlLane L = make_lane(lane);
     const uint32_t ring = ring0 + (uint32_t)(cw * S * kWlStage);
     uint64_t *bars = s_ring[cw];
-    Walk iw{}, sw{};  // issue and scale walks
-    iw.si = sw.si = 0;
+    Walk iw{};  // the issue walk
+    iw.si = 0;
     walk_enter(iw, p, segs, nseg, cw);
-    walk_enter(sw, p, segs, nseg, cw);
     int islot = 0, inflight = 0;
-    auto issue = [&]() {  // the stage at the issue walk into ring slot islot
-      if (lane == 0) {
-        tc::mbar_expect_tx(&bars[islot], kWlStage);
-        bulk_g2s(ring + islot * kWlStage,
-                 iw.B + (size_t)iw.nb * iw.ubytes + (size_t)iw.st * kWlStage, kWlStage,
+    // The stage at the issue walk into ring slot islot: its weight tiles (one
+    // bulk copy) and, for int4, the f16 scale rows of its groups -- 16
+    // columns, 32 bytes each, one copy per row by lanes 0.. -- behind them.
+    auto issue = [&]() {
+      const uint32_t dst = ring + islot * kWlStage;
+      const int rows = iw.rows_st;
+      if (lane == 0)
+        tc::mbar_expect_tx(&bars[islot], (uint32_t)(kWlStageW + rows * 32));
+      __syncwarp();
+      if (lane == 0)
+        bulk_g2s(dst, iw.B + (size_t)iw.nb * iw.ubytes + (size_t)iw.st * kWlStageW, kWlStageW,
                  &bars[islot]);
-      }
+      if (lane < rows)
+        bulk_g2s(dst + kWlStageW + lane * 32,
+                 iw.bs + (size_t)(iw.st * rows + lane) * iw.nrow + (size_t)iw.nb * 32, 32,
+                 &bars[islot]);
       if (++islot == S) islot = 0;
       inflight++;
       walk_next(iw, p, segs, nseg, cw);
     };
-    // int4 scales of the stage at the scale walk: lane l loads word l%8 of
-    // group rows r0 + l/8 and r0 + 4 + l/8 (16 columns of f16 = 8 words)
-    auto scale_fetch = [&](uint32_t &r0, uint32_t &r1) {
-      r0 = r1 = 0;
-      if (sw.si >= nseg) return;
-      if (sw.kind == kWlQ4) {
-        const uint8_t *row = sw.bs + (size_t)(sw.st * sw.rows_st) * sw.nrow + (size_t)sw.nb * 32 +
-                             (lane & 7) * 4;
-        const int q = lane >> 3;
-        if (q < sw.rows_st) r0 = ldg_stream_u32(row + (size_t)q * sw.nrow);
-        if (q + 4 < sw.rows_st) r1 = ldg_stream_u32(row + (size_t)(q + 4) * sw.nrow);
-      }
-      walk_next(sw, p, segs, nseg, cw);
-    };
 
     // the weights never come from earlier kernels: fill the ring first
     while (inflight < S && iw.si < nseg) issue();
-    uint32_t sa0, sa1, sb0, sb1;
-    scale_fetch(sa0, sa1);
-    scale_fetch(sb0, sb1);
     pdl_wait();  // prep sources and GEMM outputs are ordered after earlier kernels
 
     bool ok = true;
-    int g = 0, cslot = 0;  // g: GEMM segments entered (segment g uses buffer g % n_abuf)
+    int g = 0, cslot = 0;  // g: GEMM segments entered (segment g uses activation slot g % 4)
     uint32_t cpar = 0;
     for (int si = 0; si < nseg && ok; si++) {
       const WlSeg &sg = segs[si];
@@ -510,66 +537,73 @@ __global__ void __launch_bounds__((kWlWarps + 1) * 32, 1) worklist_kernel(const 
         wl_signal(p, sg.item, (unsigned)(e1 - e0), lane);
         continue;
       }
-      const int b = g % p.n_abuf;
-      ok = __all_sync(0xffffffffu, wl_wait(&s_full[b], (uint32_t)((g / p.n_abuf) & 1), p));
+      const int b = g & (kWlASlots - 1);
+      ok = __all_sync(0xffffffffu, wl_wait(&s_full[b], (uint32_t)((g >> 2) & 1), p));
       if (!ok) break;
-      const uint32_t ab = abuf0 + (uint32_t)(b * p.abuf_bytes);
-      const bool q4 = sg.kind == kWlQ4;
-      const int gk = it.gk, nst = sg.nst, nb0 = it.nb0, ldc = it.ldc, c0 = it.c_col0;
+      const uint32_t ab = abuf0 + s_aoff[b];
+      const int nst = sg.nst, nb0 = it.nb0, ldc = it.ldc, c0 = it.c_col0;
       float *C = it.C;
       const float *b_scale8 = static_cast<const float *>(it.b_scale);
-      const uint32_t a_step = (uint32_t)((q4 ? 8 : 4) * MT * 512);  // activation bytes per stage
-      for (int e = e0; e < e1 && ok; e++) {
-        const int nb = nb0 + __ldg(p.units + e);
-        float cf[MT][4];
-        int32_t acc[MT][4];
+      // The units of this segment, one code path per weight format and int4
+      // scale group (each keeps its own registers; the format is fixed for
+      // the whole segment).  KIND: 0 int8, else the int4 group in tiles.
+      auto units = [&](auto kind_tag) {
+        constexpr int KIND = decltype(kind_tag)::value;
+        constexpr bool Q4 = KIND != 0;
+        constexpr uint32_t a_step = (Q4 ? 8 : 4) * MT * 512;  // activation bytes per stage
+        for (int e = e0; e < e1 && ok; e++) {
+          const int nb = nb0 + __ldg(p.units + e);
+          float cf[MT][4];
+          int32_t acc[MT][4];
 #pragma unroll
-        for (int mt = 0; mt < MT; mt++)
+          for (int mt = 0; mt < MT; mt++)
 #pragma unroll
-          for (int i = 0; i < 4; i++) {
-            cf[mt][i] = 0.0f;
-            acc[mt][i] = 0;
+            for (int i = 0; i < 4; i++) {
+              cf[mt][i] = 0.0f;
+              acc[mt][i] = 0;
+            }
+          float bs0 = 0.0f, bs1 = 0.0f;  // int8 per-channel scales of columns g8, g8 + 8
+          if (!Q4) {
+            bs0 = __ldg(b_scale8 + nb * 16 + L.g8);
+            bs1 = __ldg(b_scale8 + nb * 16 + L.g8 + 8);
           }
-        float bs0 = 0.0f, bs1 = 0.0f;  // int8 per-channel scales of columns g8, g8 + 8
-        if (!q4) {
-          bs0 = __ldg(b_scale8 + nb * 16 + L.g8);
-          bs1 = __ldg(b_scale8 + nb * 16 + L.g8 + 8);
-        }
-        uint32_t abs_ = ab;
-        for (int st = 0; st < nst; st++) {
-          const uint32_t s0 = sa0, s1 = sa1;
-          sa0 = sb0;
-          sa1 = sb1;
-          scale_fetch(sb0, sb1);
-          ok = __all_sync(0xffffffffu, wl_wait(&bars[cslot], cpar, p));
+          uint32_t abs_ = ab;
+          for (int st = 0; st < nst; st++) {
+            ok = __all_sync(0xffffffffu, wl_wait(&bars[cslot], cpar, p));
+            if (!ok) break;
+            const uint32_t stg = ring + cslot * kWlStage;
+            if constexpr (Q4) q4_stage<MT, (Q4 ? KIND : 1)>(stg, abs_, L, cf);
+            else q8_stage<MT>(stg, abs_, L, acc);
+            abs_ += a_step;
+            __syncwarp();
+            fence_proxy_async_smem();  // this warp's reads of the slot precede its refill
+            inflight--;
+            if (++cslot == S) {
+              cslot = 0;
+              cpar ^= 1u;
+            }
+            if (iw.si < nseg) issue();
+          }
           if (!ok) break;
-          const uint32_t stg = ring + cslot * kWlStage;
-          if (q4) q4_stage_gk<MT>(gk, stg, abs_, L, s0, s1, cf);
-          else q8_stage<MT>(stg, abs_, L, acc);
-          abs_ += a_step;
-          __syncwarp();
-          fence_proxy_async_smem();  // this warp's reads of the slot precede its refill
-          inflight--;
-          if (++cslot == S) {
-            cslot = 0;
-            cpar ^= 1u;
-          }
-          if (iw.si < nseg) issue();
+#pragma unroll
+          for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+              const int m = mt * 8 + 2 * L.tig + (i & 1);
+              const int n = nb * 16 + L.g8 + (i >= 2 ? 8 : 0);
+              if (m >= p.M) continue;
+              const float as = s_as[b][m];
+              C[(size_t)m * ldc + (n - c0)] =
+                  Q4 ? __fmul_rn(cf[mt][i], as)
+                     : __fmul_rn(__int2float_rn(acc[mt][i]), __fmul_rn(i < 2 ? bs0 : bs1, as));
+            }
         }
-        if (!ok) break;
-#pragma unroll
-        for (int mt = 0; mt < MT; mt++)
-#pragma unroll
-          for (int i = 0; i < 4; i++) {
-            const int m = mt * 8 + 2 * L.tig + (i & 1);
-            const int n = nb * 16 + L.g8 + (i >= 2 ? 8 : 0);
-            if (m >= p.M) continue;
-            const float as = s_as[b][m];
-            C[(size_t)m * ldc + (n - c0)] =
-                q4 ? __fmul_rn(cf[mt][i], as)
-                   : __fmul_rn(__int2float_rn(acc[mt][i]), __fmul_rn(i < 2 ? bs0 : bs1, as));
-          }
-      }
+      };
+      if (sg.kind == kWlQ8) units(std::integral_constant<int, 0>{});
+      else if (it.gk == 1) units(std::integral_constant<int, 1>{});
+      else if (it.gk == 2) units(std::integral_constant<int, 2>{});
+      else if (it.gk == 4) units(std::integral_constant<int, 4>{});
+      else units(std::integral_constant<int, 8>{});
       if (!ok) break;
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
@@ -609,11 +643,9 @@ __global__ void __launch_bounds__((kWlWarps + 1) * 32, 1) worklist_kernel(const 
 }  // namespace
 
 // ======================================================================= host
-size_t worklist_smem(int n_abuf, int abuf_bytes, int stages) {
-  return 1024 + (size_t)n_abuf * abuf_bytes + (size_t)kWlWarps * stages * kWlStage;
+static size_t worklist_smem(int a_ring, int warps, int stages) {
+  return 1024 + (size_t)a_ring + (size_t)warps * stages * kWlStage;
 }
-
-int worklist_consumers() { return kWlWarps; }
 
 static int wl_static_smem(int MT) {
   cudaFuncAttributes a{};
@@ -632,23 +664,33 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
   pl.M = M;
   pl.MT = M <= 8 ? 1 : 2;
   pl.grid = num_sms;
-  // ---- shared memory: activation buffers and the weight rings
-  int max_kb = 0;
+  // ---- shared memory: the activation ring and the consumers' weight rings.
+  // The most consumer warps (latency hiding) whose two-stage rings leave the
+  // activation ring room for the widest segment; FGM_CUDA_WORKLIST_WARPS
+  // (8, 12 or 15) overrides the choice.
+  int max_seg = 1024;
   for (const WlItem &it : items)
-    if (it.kind != kWlPrep) max_kb = std::max(max_kb, it.K / 64);
-  pl.abuf_bytes = std::max(1024, (pl.MT * 512 * max_kb + 1023) / 1024 * 1024);
+    if (it.kind != kWlPrep) max_seg = std::max(max_seg, (it.K / 64 * pl.MT * 512 + 1023) & ~1023);
   const size_t limit = smem_optin + 1024 - (size_t)wl_static_smem(pl.MT) - 256;
-  pl.n_abuf = 0;
-  for (int nb = 2; nb >= 1 && !pl.n_abuf; nb--) {
-    for (int s = kWlMaxStages; s >= (nb == 2 ? 3 : 2); s--)
-      if (worklist_smem(nb, pl.abuf_bytes, s) <= limit) {
-        pl.n_abuf = nb;
-        pl.stages = s;
-        break;
-      }
+  int want = 0;
+  if (const char *e = getenv("FGM_CUDA_WORKLIST_WARPS")) want = atoi(e);
+  pl.warps = 0;
+  for (int w : {15, 12, 8}) {
+    if (want && w != want) continue;
+    const size_t rings = (size_t)w * 2 * kWlStage;
+    if (1024 + rings + (size_t)max_seg > limit) continue;
+    pl.warps = w;
+    pl.stages = 2;
+    // deeper rings while the activation ring still holds two widest segments
+    while (pl.stages < kWlMaxStages &&
+           1024 + (size_t)w * (pl.stages + 1) * kWlStage + 2 * (size_t)max_seg <= limit)
+      pl.stages++;
+    pl.a_ring = (int)((limit - 1024 - (size_t)w * pl.stages * kWlStage) & ~(size_t)1023);
+    break;
   }
-  if (!pl.n_abuf) return "the activations of the widest item do not fit in shared memory";
-  pl.smem = worklist_smem(pl.n_abuf, pl.abuf_bytes, pl.stages);
+  if (!pl.warps) return "the activations of the widest item do not fit in shared memory";
+  pl.smem = worklist_smem(pl.a_ring, pl.warps, pl.stages);
+  const int W = pl.warps;
 
   // ---- levels: one more than the deepest dependency
   std::vector<int> level(n, 0);
@@ -712,8 +754,8 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
     pl.seg_off[c] = (int)pl.segs.size();
     const std::vector<Piece> &pc = cta[c];
     std::vector<std::vector<std::vector<int>>> own(pc.size(),
-                                                   std::vector<std::vector<int>>(kWlWarps));
-    std::vector<double> load(kWlWarps, 0.0);
+                                                   std::vector<std::vector<int>>(W));
+    std::vector<double> load(W, 0.0);
     for (size_t a = 0; a < pc.size();) {
       size_t z = a;
       while (z < pc.size() && piece_level[c][z] == piece_level[c][a]) z++;
@@ -739,13 +781,13 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
       sg.item = pc[q].item;
       sg.kind = it.kind;
       sg.nst = it.kind == kWlQ4 ? it.K / 512 : (it.kind == kWlQ8 ? it.K / 256 : 0);
-      for (int w = 0; w < kWlWarps; w++) {
+      for (int w = 0; w < W; w++) {
         std::vector<int> &v = own[q][w];
         std::sort(v.begin(), v.end());
         sg.ofs[w] = (int)pl.units.size();
         pl.units.insert(pl.units.end(), v.begin(), v.end());
       }
-      sg.ofs[kWlWarps] = (int)pl.units.size();
+      for (int w = W; w <= kWlMaxWarps; w++) sg.ofs[w] = (int)pl.units.size();
       pl.segs.push_back(sg);
     }
   }
@@ -756,7 +798,7 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
 cudaError_t launch_worklist(const WlParams &p, const WlPlan &pl, bool pdl, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.grid);
-  cfg.blockDim = dim3((kWlWarps + 1) * 32);
+  cfg.blockDim = dim3((pl.warps + 1) * 32);
   cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

@@ -265,7 +265,8 @@ int fgm_cuda_gemm_q8c_acc(int M, int N, int K, const int8_t *A, const int8_t *B,
  *    K % 512 == 0 (int4) or K % 256 == 0 (int8), K <= 16384; output columns
  *    [n0*16, n1*16), 0 <= n0 < n1 <= N/16, C[m*ldc + n] with ldc >= n1*16;
  *    int4 group in {64, 128, 256, 512} dividing K; A (tile-packed, one 16-row
- *    block, zero padding rows) and B 16-byte aligned, scales 4-byte aligned.
+ *    block, zero padding rows), B and int4 scales 16-byte aligned, int8
+ *    scales 4-byte aligned.
  *  - FGM_CUDA_WORK_PREP: f32 rows src[m*lda + k], K % 128 == 0, lda >= K,
  *    lda % 4 == 0, src 16-byte aligned; hsz 0 or a power of two <= 128
  *    dividing K (the FWHT block, ops.c:153-175); outputs pa (the packed 16-row
