@@ -349,6 +349,81 @@ __device__ void prep_row(const WlItem &it, int r, int M, int lane) {
   if (lane == 0) it.qs[r] = s;
 }
 
+// ------------------------------------------------------------- prologue
+// The preps that depend on nothing in the list (inputs written before the
+// run) do not wait inside the persistent kernel: one launch ahead of it
+// prepares all their rows at once, a CTA of 8 warps per row, each warp a
+// 1/8 of the row held in registers, the row maximum met in shared memory --
+// one memory round trip per row instead of a warp's serial passes.  The
+// persistent kernel follows with programmatic dependent launch; its weight
+// rings fill while this runs, its activation staging waits for it.
+constexpr int kProWarps = 8;
+constexpr int kProChunks = 8;  // 128-value chunks a warp holds in registers
+
+__global__ void __launch_bounds__(kProWarps * 32) worklist_prologue(const WlParams p) {
+  __shared__ float red[kProWarps];
+  pdl_launch_dependents();
+  pdl_wait();  // the sources may come from earlier kernels
+  const int job = p.pro_jobs[blockIdx.x];
+  const WlItem &it = p.items[job >> 4];
+  const int r = job & 15, K = it.K, KB = K >> 6, nch = K >> 7;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // this warp's chunks [c0, c1): the row in kProWarps equal parts
+  const int c0 = (int)((long)nch * warp / kProWarps), c1 = (int)((long)nch * (warp + 1) / kProWarps);
+  int8_t *pa_row = it.pa + (size_t)(r & 15) * 64;
+  if (r >= p.M) {  // zero padding of the tile block
+    for (int c = c0; c < c1; c++) {
+      const int kk = c * 128 + lane * 4;
+      *reinterpret_cast<uint32_t *>(pa_row + (size_t)(kk >> 6) * kATile + (kk & 63)) = 0u;
+    }
+    return;
+  }
+  const float *src = it.src + (size_t)r * it.lda + lane * 4;
+  const bool held = c1 - c0 <= kProChunks;  // the whole part fits in registers: one load
+  float4 v[kProChunks];
+  float mx = 0.0f;
+  for (int b0 = c0; b0 < c1; b0 += kProChunks) {
+#pragma unroll
+    for (int u = 0; u < kProChunks; u++)
+      if (b0 + u < c1) v[u] = *reinterpret_cast<const float4 *>(src + (b0 + u) * 128);
+#pragma unroll
+    for (int u = 0; u < kProChunks; u++) {
+      if (b0 + u >= c1) continue;
+      v[u] = fwht128(v[u], it.hsz, lane);
+      const float a0 = fabsf(v[u].x), a1 = fabsf(v[u].y), a2 = fabsf(v[u].z), a3 = fabsf(v[u].w);
+      mx = a0 > mx ? a0 : mx;
+      mx = a1 > mx ? a1 : mx;
+      mx = a2 > mx ? a2 : mx;
+      mx = a3 > mx ? a3 : mx;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, mx, o);
+    mx = u > mx ? u : mx;
+  }
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kProWarps; w++) mx = red[w] > mx ? red[w] : mx;
+  const float s = (mx == 0.0f) ? 1.0f : __fdiv_rn(mx, 127.0f);
+  const float inv = __fdiv_rn(1.0f, s);
+  if (threadIdx.x == 0) it.qs[r] = s;
+  for (int b0 = c0; b0 < c1; b0 += kProChunks) {
+#pragma unroll
+    for (int u = 0; u < kProChunks; u++) {
+      if (b0 + u >= c1) continue;
+      float4 x = v[u];
+      if (!held) x = fwht128(*reinterpret_cast<const float4 *>(src + (b0 + u) * 128), it.hsz, lane);
+      const int kk = (b0 + u) * 128 + lane * 4;
+      *reinterpret_cast<uint32_t *>(pa_row + (size_t)(kk >> 6) * kATile + (kk & 63)) =
+          q8_quad(x, inv);
+    }
+  }
+  (void)KB;
+}
+
 // ------------------------------------------------------------ unit walk
 // A consumer warp's walk over the weight stages of its own units, item after
 // item: the segment's unit list, the stage inside the unit, and the item
@@ -692,6 +767,19 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
   pl.smem = worklist_smem(pl.a_ring, pl.warps, pl.stages);
   const int W = pl.warps;
 
+  // ---- preps that depend on nothing run in the prologue launch; entries
+  // that read them wait for that launch (kernel order), not for a counter
+  std::vector<char> pro(n, 0);
+  pl.pro_jobs.clear();
+  for (int i = 0; i < n; i++) {
+    WlItem &it = items[i];
+    if (it.kind != kWlPrep || it.deps[0] >= 0 || it.deps[1] >= 0) continue;
+    pro[i] = 1;
+    for (int r = 0; r < it.units; r++) pl.pro_jobs.push_back(i * 16 + r);
+  }
+  for (int i = 0; i < n; i++)
+    for (int &d : items[i].deps)
+      if (d >= 0 && pro[d]) d = -1;
   // ---- levels: one more than the deepest dependency
   std::vector<int> level(n, 0);
   int nlev = 0;
@@ -721,7 +809,7 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
       if (level[i] == lv && items[i].kind != kWlPrep) total += items[i].units * unit_cost(items[i], 0);
     double acc = 0;
     for (int i = 0; i < n; i++) {
-      if (level[i] != lv) continue;
+      if (level[i] != lv || pro[i]) continue;
       const WlItem &it = items[i];
       if (it.kind == kWlPrep) {  // rows round-robin over the CTAs
         for (int u = 0; u < it.units; u++, rr++) {
@@ -796,6 +884,19 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
 }
 
 cudaError_t launch_worklist(const WlParams &p, const WlPlan &pl, bool pdl, cudaStream_t st) {
+  if (p.n_pro > 0) {
+    cudaLaunchConfig_t pc = {};
+    pc.gridDim = dim3(p.n_pro);
+    pc.blockDim = dim3(kProWarps * 32);
+    pc.stream = st;
+    cudaLaunchAttribute pa[1];
+    pa[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pa[0].val.programmaticStreamSerializationAllowed = 1;
+    pc.attrs = pa;
+    pc.numAttrs = pdl ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&pc, worklist_prologue, p);
+    if (e != cudaSuccess) return e;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.grid);
   cfg.blockDim = dim3((pl.warps + 1) * 32);
