@@ -1325,7 +1325,8 @@ int fgm_cuda_worklist_create(int M, const fgm_cuda_work *w, int n, void **list) 
     it.b_scale = bs;
     it.a_scale = static_cast<const float *>(as);
     it.C = static_cast<float *>(const_cast<void *>(Cp));
-    if (!encode_packed_a_map(&it.amap, s.A, s.K, MT * 8))
+    if (!encode_packed_a_map(&it.amap, s.A, s.K, MT * 8) ||
+        (it.kind == kWlQ4 && !encode_scale_map(&it.smap, bs, s.K / s.group, s.N, 8 / it.gk)))
       return fail(FGM_CUDA_ERUNTIME, "worklist: cuTensorMapEncodeTiled failed for entry %d", i);
   }
   WorkList *wl = new WorkList();
@@ -1338,8 +1339,7 @@ int fgm_cuda_worklist_create(int M, const fgm_cuda_work *w, int n, void **list) 
   const size_t o_items = 0, b_items = sizeof(WlItem) * (size_t)n;
   const size_t o_segs = align256(o_items + b_items), b_segs = sizeof(WlSeg) * wl->plan.segs.size();
   const size_t o_off = align256(o_segs + b_segs), b_off = sizeof(int) * wl->plan.seg_off.size();
-  const size_t o_un = align256(o_off + b_off), b_un = sizeof(int) * wl->plan.units.size();
-  const size_t o_pj = align256(o_un + b_un), b_pj = sizeof(int) * wl->plan.pro_jobs.size();
+  const size_t o_pj = align256(o_off + b_off), b_pj = sizeof(int) * wl->plan.pro_jobs.size();
   const size_t o_cnt = align256(o_pj + b_pj), b_cnt = sizeof(unsigned) * ((size_t)n + 2);
   const size_t total = o_cnt + b_cnt;
   if (cudaMalloc(&wl->mem, total) != cudaSuccess) {
@@ -1353,8 +1353,6 @@ int fgm_cuda_worklist_create(int M, const fgm_cuda_work *w, int n, void **list) 
     e = cudaMemcpy(d + o_segs, wl->plan.segs.data(), b_segs, cudaMemcpyHostToDevice);
   if (e == cudaSuccess)
     e = cudaMemcpy(d + o_off, wl->plan.seg_off.data(), b_off, cudaMemcpyHostToDevice);
-  if (e == cudaSuccess && b_un)
-    e = cudaMemcpy(d + o_un, wl->plan.units.data(), b_un, cudaMemcpyHostToDevice);
   if (e == cudaSuccess && b_pj)
     e = cudaMemcpy(d + o_pj, wl->plan.pro_jobs.data(), b_pj, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemset(d + o_cnt, 0, b_cnt);
@@ -1370,7 +1368,6 @@ int fgm_cuda_worklist_create(int M, const fgm_cuda_work *w, int n, void **list) 
   p.n_items = n;
   p.segs = reinterpret_cast<const WlSeg *>(d + o_segs);
   p.seg_off = reinterpret_cast<const int *>(d + o_off);
-  p.units = reinterpret_cast<const int *>(d + o_un);
   p.pro_jobs = reinterpret_cast<const int *>(d + o_pj);
   p.n_pro = (int)wl->plan.pro_jobs.size();
   p.done = reinterpret_cast<unsigned *>(d + o_cnt);

@@ -188,6 +188,8 @@ bool encode_rows_map(CUtensorMap *map, const void *base, int rows, int K, int ld
 // Tile-packed activations of one 16-row block as a 3-D TMA view, box of
 // `rows` rows x K/64 tiles, 64-byte swizzle (K <= 16384).
 bool encode_packed_a_map(CUtensorMap *map, const void *base, int K, int rows);
+// int4 group scales f16 [groups][N] as a 2-D TMA view, box 16 columns x rows.
+bool encode_scale_map(CUtensorMap *map, const void *base, int groups, int N, int rows);
 // .fgm int8 tiles -> row-major [N][K] (the tensor-core weight operand).
 cudaError_t launch_q8c_rows(const int8_t *tiles, int8_t *rows, int N, int K, cudaStream_t st);
 // tile-packed activations -> row-major [M][K].
@@ -214,11 +216,13 @@ cudaError_t launch_argmax_merge(const float *pv, const int *pi, int M, int P, in
 constexpr int kWlQ4 = 0, kWlQ8 = 1, kWlPrep = 2;
 struct WlItem {
   CUtensorMap amap;        // GEMM: packed activations (encode_packed_a_map)
+  CUtensorMap smap;        // int4 GEMM: the group scales (encode_scale_map)
   int kind, N, K, gk;      // gk: int4 scale group in 64-value tiles
   int nb0, units;          // GEMM: first n-block and n-blocks; prep: rows (16 per block)
   int ldc, c_col0;         // GEMM: C[m*ldc + n - c_col0]
   int lda, hsz;            // prep: source row stride (floats), FWHT block
   int deps[2];             // earlier items whose outputs this one reads (-1: none)
+  int waited;              // some item of the list waits for this one (publish its completion)
   const uint8_t *B;        // GEMM weight tiles
   const void *b_scale;     // f16 [K/group][N] (int4) or f32 [N] (int8)
   const float *a_scale;    // GEMM: [M]
@@ -230,14 +234,14 @@ struct WlItem {
 constexpr int kWlMaxWarps = 15;  // consumer warps per CTA, at most (16 warps with the producer)
 struct WlSeg {                 // one CTA's share of one item
   int item, kind, nst;         // item, its kind, 4 KB weight stages per unit
-  int ofs[kWlMaxWarps + 1];    // consumer warp w takes units[ofs[w], ofs[w + 1])
+  int ub, nu;                  // its units: [ub, ub + nu) of the item (n-blocks or rows)
+  int gseq;                    // GEMM segments of the CTA before this one (activation slot)
 };
 struct WlParams {
   const WlItem *items;
   int n_items;
   const WlSeg *segs;       // every CTA's segments, back to back
   const int *seg_off;      // CTA c: segs[seg_off[c], seg_off[c + 1])
-  const int *units;        // unit indices (n-block or row inside the item) of every segment
   unsigned *done;          // per item: units completed in this launch
   unsigned *ctas_done;     // CTAs finished (the last one resets the counters)
   int *abort;              // raised by a warp that gave up on a bounded wait
@@ -252,7 +256,6 @@ struct WlPlan {
   size_t smem;
   std::vector<WlSeg> segs;
   std::vector<int> seg_off;
-  std::vector<int> units;
   std::vector<int> pro_jobs;
 };
 // Fills the schedule and launch geometry; returns an error text or nullptr.

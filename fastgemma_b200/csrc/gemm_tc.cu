@@ -473,6 +473,20 @@ bool encode_packed_a_map(CUtensorMap *map, const void *base, int K, int rows) {
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// int4 group scales f16 [groups][N] as a 2-D TMA view, boxes of 16 columns x
+// `rows` group rows (one 32-byte row per group), no swizzle.
+bool encode_scale_map(CUtensorMap *map, const void *base, int groups, int N, int rows) {
+  auto enc = get_encode();
+  if (!enc || N % 16 != 0 || rows < 1 || rows > 8) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)groups};
+  const cuuint64_t strides[1] = {(cuuint64_t)N * 2};
+  const cuuint32_t box[2] = {16, (cuuint32_t)rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 cudaError_t launch_q8c_rows(const int8_t *tiles, int8_t *rows, int N, int K, cudaStream_t st) {
   const size_t words = (size_t)N * K / 4;
   q8c_tiles_to_rows<<<grid_for(words), 256, 0, st>>>(reinterpret_cast<const uint32_t *>(tiles),

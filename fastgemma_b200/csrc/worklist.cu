@@ -136,6 +136,16 @@ __device__ __forceinline__ void wl_signal(const WlParams &p, int it, unsigned n,
   }
 }
 
+// 2-D TMA load to a shared-memory address given as a 32-bit shared pointer.
+__device__ __forceinline__ void tma_load_2d_u32(uint32_t dst, const void *tmap, uint64_t *bar,
+                                                int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(tmap), "r"(tc::smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
 __device__ __forceinline__ uint32_t lds16(uint32_t a) {
   unsigned short v;
   asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
@@ -175,7 +185,7 @@ __device__ __forceinline__ void load_b(uint32_t ab, int t, int mt, const WlLane 
 // into cf as they complete (the stage starts on a group boundary).
 template <int MT, int GK>
 __device__ __forceinline__ void q4_stage(uint32_t st, uint32_t ab, const WlLane &L,
-                                         float (&cf)[MT][4]) {
+                                         float2 (&cf)[MT][2]) {
   constexpr int CH = MT == 1 ? 4 : 2;  // tiles whose operands load together
   int32_t gacc[MT][4];
 #pragma unroll
@@ -211,25 +221,29 @@ __device__ __forceinline__ void q4_stage(uint32_t st, uint32_t ab, const WlLane 
       if ((t + 1) % GK != 0) continue;
       const int lg = t / GK;  // group inside the stage: its f16 scale row follows the tiles
       const uint32_t srow = st + kWlStageW + lg * 32 + L.g8 * 2;
-      float s0 = f16_to_f32(lds16(srow)), s1 = f16_to_f32(lds16(srow + 16));
-      if (GK <= 4) {
-        // gacc is 16x the group sum (nibbles in the high half of each byte)
-        // and below 2^22 for groups up to 256: convert it as it is and take
-        // the 16 out of the scale instead -- (16 x)(s / 16) is x s exactly,
-        // so the fma rounds the reference's product once, as before
-        s0 = __fmul_rn(s0, 0.0625f);
-        s1 = __fmul_rn(s1, 0.0625f);
+      const float s0 = f16_to_f32(lds16(srow)), s1 = f16_to_f32(lds16(srow + 16));
+      const float2 sp0 = make_float2(s0, s0), sp1 = make_float2(s1, s1);
 #pragma unroll
-        for (int mt = 0; mt < MT; mt++)
-#pragma unroll
-          for (int i = 0; i < 4; i++)
-            cf[mt][i] = __fmaf_rn(i2f_exact(gacc[mt][i]), i < 2 ? s0 : s1, cf[mt][i]);
-      } else {
-#pragma unroll
-        for (int mt = 0; mt < MT; mt++)
-#pragma unroll
-          for (int i = 0; i < 4; i++)
-            cf[mt][i] = __fmaf_rn(i2f_exact(gacc[mt][i] >> 4), i < 2 ? s0 : s1, cf[mt][i]);
+      for (int mt = 0; mt < MT; mt++) {
+        // the group sums as exact floats, two per instruction, then the
+        // reference's fma into the running sums (each lane rounded alone)
+        float2 f01, f23;
+        if (GK <= 4) {
+          // gacc = 16 x the group sum, |sum| <= 2^18 for groups up to 256:
+          // added to the bit pattern of 1.5 * 2^19 (ulp 1/16) it gives
+          // 1.5 * 2^19 + sum exactly, no shift needed
+          f01 = __fadd2_rn(make_float2(__int_as_float(gacc[mt][0] + 0x49400000),
+                                       __int_as_float(gacc[mt][1] + 0x49400000)),
+                           make_float2(-786432.0f, -786432.0f));
+          f23 = __fadd2_rn(make_float2(__int_as_float(gacc[mt][2] + 0x49400000),
+                                       __int_as_float(gacc[mt][3] + 0x49400000)),
+                           make_float2(-786432.0f, -786432.0f));
+        } else {
+          f01 = make_float2(i2f_exact(gacc[mt][0] >> 4), i2f_exact(gacc[mt][1] >> 4));
+          f23 = make_float2(i2f_exact(gacc[mt][2] >> 4), i2f_exact(gacc[mt][3] >> 4));
+        }
+        cf[mt][0] = __ffma2_rn(f01, sp0, cf[mt][0]);
+        cf[mt][1] = __ffma2_rn(f23, sp1, cf[mt][1]);
       }
     }
   }
@@ -424,62 +438,46 @@ __global__ void __launch_bounds__(kProWarps * 32) worklist_prologue(const WlPara
   (void)KB;
 }
 
-// ------------------------------------------------------------ unit walk
-// A consumer warp's walk over the weight stages of its own units, item after
-// item: the segment's unit list, the stage inside the unit, and the item
-// fields it needs, loaded once per segment.
-struct Walk {
-  int si;                   // segment index (nseg: finished)
-  int e, e_end;             // this warp's unit entries [e, e_end) of the segment
-  int st, nst;              // stage inside the unit, stages per unit
-  int kind, nb0;
-  const uint8_t *B;
-  const uint8_t *bs;        // int4 scales (f16 rows of N)
-  int ubytes;               // weight bytes per unit (one n-block over all of K)
-  int nrow;                 // int4 scale bytes per group row (N * 2)
-  int rows_st;              // int4 scale group rows per stage (8 / gk)
-  int nb;                   // current n-block
+// ------------------------------------------------------------ unit queue
+// The consumer warps of a CTA take the units of its segments, in list order,
+// from one shared counter at the moment their weight rings need them (a warp
+// that runs ahead takes more), and remember them in a small queue of their
+// own for the compute side.  Taking units in list order keeps the segments in
+// order: a warp finishes its units of segment g before any later unit.
+constexpr int kWlFifo = 16;  // units a warp may hold ahead of its compute (> stages + 1)
+
+struct Issue {            // the issue side of a consumer warp
+  int j, total;           // next CTA-local unit index taken; the CTA's units
+  int si, seg_end;        // segment of unit j, and the CTA-local index past it
+  int st, nst;            // stage of the current unit, stages per unit
+  int nb;                 // current n-block
+  const uint8_t *B;       // weights of the current segment's item
+  const CUtensorMap *smap;  // its int4 scale view
+  int ubytes, rows_st, nb0, kind;
+  bool live;              // a unit with weight stages is current
+  bool loaded;            // the fields above belong to segment si
 };
 
-__device__ __forceinline__ void walk_unit(Walk &k, const WlParams &p) {
-  k.nb = k.nb0 + __ldg(p.units + k.e);
-}
-
-// Enter segment k.si or the first later one holding weight stages for warp cw.
-__device__ __forceinline__ void walk_enter(Walk &k, const WlParams &p, const WlSeg *segs, int nseg,
-                                           int cw) {
-  for (; k.si < nseg; k.si++) {
-    const WlSeg &sg = segs[k.si];
-    if (sg.kind == kWlPrep) continue;
-    const int e0 = sg.ofs[cw], e1 = sg.ofs[cw + 1];
-    if (e0 == e1) continue;
-    const WlItem &it = p.items[sg.item];
-    k.e = e0;
-    k.e_end = e1;
-    k.st = 0;
-    k.nst = sg.nst;
-    k.kind = sg.kind;
-    k.nb0 = it.nb0;
-    k.B = it.B;
-    k.bs = static_cast<const uint8_t *>(it.b_scale);
-    k.ubytes = it.K * (sg.kind == kWlQ4 ? 8 : 16);  // K/64 tiles of 512 or 1024 bytes
-    k.nrow = it.N * 2;
-    k.rows_st = sg.kind == kWlQ4 ? 8 / it.gk : 0;
-    walk_unit(k, p);
-    return;
+// Segment index and item fields for CTA-local unit j (segments advance monotonically).
+__device__ __forceinline__ void issue_seg(Issue &q, const WlParams &p, const WlSeg *segs,
+                                          int nseg, int &seg_lo) {
+  if (q.j < q.seg_end && q.loaded) return;  // same segment: the cached fields hold
+  while (q.si < nseg && q.j >= q.seg_end) {
+    seg_lo = q.seg_end;
+    q.si++;
+    if (q.si < nseg) q.seg_end += segs[q.si].nu;
   }
-}
-
-__device__ __forceinline__ void walk_next(Walk &k, const WlParams &p, const WlSeg *segs, int nseg,
-                                          int cw) {
-  if (++k.st < k.nst) return;
-  k.st = 0;
-  if (++k.e < k.e_end) {
-    walk_unit(k, p);
-    return;
-  }
-  k.si++;
-  walk_enter(k, p, segs, nseg, cw);
+  if (q.si >= nseg) return;
+  const WlSeg &sg = segs[q.si];
+  const WlItem &it = p.items[sg.item];
+  q.nst = sg.nst;
+  q.B = it.B;
+  q.smap = &it.smap;
+  q.ubytes = it.K * (sg.kind == kWlQ4 ? 8 : 16);  // K/64 tiles of 512 or 1024 bytes
+  q.rows_st = sg.kind == kWlQ4 ? 8 / it.gk : 0;
+  q.nb0 = it.nb0 + sg.ub;  // n-block of the segment's first unit
+  q.kind = sg.kind;
+  q.loaded = true;
 }
 
 template <int MT>
@@ -490,6 +488,9 @@ __global__ void __launch_bounds__((kWlMaxWarps + 1) * 32, 1) worklist_kernel(con
   __shared__ float s_as[kWlASlots][16];
   __shared__ uint32_t s_aoff[kWlASlots];
   __shared__ int s_r0[kWlASlots], s_r1[kWlASlots];  // producer: regions of the last four segments
+  __shared__ int s_grab;                            // next CTA-local unit to hand out
+  __shared__ int s_left[kWlASlots];                 // units of a GEMM segment still unfinished
+  __shared__ int s_fifo[kWlMaxWarps][kWlFifo];      // each warp's taken units, in order
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -502,11 +503,19 @@ __global__ void __launch_bounds__((kWlMaxWarps + 1) * 32, 1) worklist_kernel(con
   if (threadIdx.x == 0) {
     for (int b = 0; b < kWlASlots; b++) {
       tc::mbar_init(&s_full[b], 1);
-      tc::mbar_init(&s_empty[b], W);
+      tc::mbar_init(&s_empty[b], 1);  // the warp finishing a segment's last unit arrives
     }
     for (int w = 0; w < W; w++)
       for (int s = 0; s < S; s++) tc::mbar_init(&s_ring[w][s], 1);
     tc::fence_mbar_init();
+    s_grab = 0;
+  }
+  // unfinished units per activation slot, for the first four GEMM segments
+  if (threadIdx.x < kWlASlots) {
+    int left = 0;
+    for (int si = 0; si < nseg; si++)
+      if (segs[si].kind != kWlPrep && segs[si].gseq == (int)threadIdx.x) left = segs[si].nu;
+    s_left[threadIdx.x] = left;
   }
   __syncthreads();
   pdl_launch_dependents();
@@ -515,7 +524,7 @@ __global__ void __launch_bounds__((kWlMaxWarps + 1) * 32, 1) worklist_kernel(con
     // ------------------------------------------------------------ producer
     // GEMM segment g stages its activations in slot g % 4 (barriers, scales)
     // at a region of the activation ring allocated first in, first out; a
-    // region is reused once every consumer has left the segments holding it.
+    // region is reused once every unit of the segments holding it is done.
     pdl_wait();  // packed activations and their scales may come from earlier kernels
     int g = 0, head = 0;
     bool ok = true;
@@ -528,7 +537,7 @@ __global__ void __launch_bounds__((kWlMaxWarps + 1) * 32, 1) worklist_kernel(con
       const int sz = (bytes + 1023) & ~1023;
       int off = head;
       if (off + sz > p.a_ring) off = 0;
-      if (g >= kWlASlots)  // segment g - 4, the slot's last user, has been left
+      if (g >= kWlASlots)  // segment g - 4, the slot's last user, is done
         ok = wl_wait(&s_empty[b], (uint32_t)(((g >> 2) - 1) & 1), p);
       for (int j = g - kWlASlots + 1; j < g && ok; j++) {  // younger segments in the region
         if (j < 0) continue;
@@ -543,6 +552,7 @@ __global__ void __launch_bounds__((kWlMaxWarps + 1) * 32, 1) worklist_kernel(con
       if (lane == 0) {
         s_r0[b] = off;
         s_r1[b] = off + sz;
+        if (g >= kWlASlots) s_left[b] = sg.nu;  // the slot's previous segment is done
       }
       head = off + sz;
       fence_proxy_async_global();  // the activations may have been written in this launch
@@ -567,125 +577,180 @@ __global__ void __launch_bounds__((kWlMaxWarps + 1) * 32, 1) worklist_kernel(con
     const WlLane L = make_lane(lane);
     const uint32_t ring = ring0 + (uint32_t)(cw * S * kWlStage);
     uint64_t *bars = s_ring[cw];
-    Walk iw{};  // the issue walk
-    iw.si = 0;
-    walk_enter(iw, p, segs, nseg, cw);
-    int islot = 0, inflight = 0;
-    // The stage at the issue walk into ring slot islot: its weight tiles (one
-    // bulk copy) and, for int4, the f16 scale rows of its groups -- 16
-    // columns, 32 bytes each, one copy per row by lanes 0.. -- behind them.
+    int *fifo = s_fifo[cw];
+    int total = 0;
+    for (int si = 0; si < nseg; si++) total += segs[si].nu;
+    Issue q{};
+    q.total = total;
+    q.si = 0;
+    q.seg_end = nseg ? segs[0].nu : 0;
+    int seg_lo = 0, fpush = 0, fpop = 0, islot = 0, inflight = 0;
+    bool exhausted = false;  // every unit of the CTA has been taken
+    // Take the next unit for this warp and push it on its queue (the caller
+    // checked there is room); units without weight stages (prep rows) are
+    // only queued.
+    auto take = [&]() {
+      int j = 0;
+      if (lane == 0) j = atomicAdd(&s_grab, 1);
+      j = __shfl_sync(0xffffffffu, j, 0);
+      if (j >= total) {
+        exhausted = true;
+        q.live = false;
+        return;
+      }
+      q.j = j;
+      issue_seg(q, p, segs, nseg, seg_lo);
+      if (lane == 0) fifo[fpush & (kWlFifo - 1)] = j;
+      fpush++;
+      q.st = 0;
+      q.live = q.kind != kWlPrep;
+      if (q.live) q.nb = q.nb0 + (j - seg_lo);
+    };
+    // Make a unit with weight stages current on the issue side, taking units
+    // while the queue has room.
+    auto refill = [&]() {
+      while (!q.live && !exhausted && fpush - fpop < kWlFifo - 1) take();
+    };
+    auto next_live = [&]() {
+      q.live = false;
+      refill();
+    };
+    // The stage at the issue side into ring slot islot: its weight tiles (one
+    // bulk copy) and, for int4, the f16 scale rows of its groups (one 2-D
+    // TMA box of 16 columns x the stage's groups) behind them.
     auto issue = [&]() {
       const uint32_t dst = ring + islot * kWlStage;
-      const int rows = iw.rows_st;
-      if (lane == 0)
+      if (lane == 0) {
+        const int rows = q.rows_st;
         tc::mbar_expect_tx(&bars[islot], (uint32_t)(kWlStageW + rows * 32));
-      __syncwarp();
-      if (lane == 0)
-        bulk_g2s(dst, iw.B + (size_t)iw.nb * iw.ubytes + (size_t)iw.st * kWlStageW, kWlStageW,
+        bulk_g2s(dst, q.B + (size_t)q.nb * q.ubytes + (size_t)q.st * kWlStageW, kWlStageW,
                  &bars[islot]);
-      if (lane < rows)
-        bulk_g2s(dst + kWlStageW + lane * 32,
-                 iw.bs + (size_t)(iw.st * rows + lane) * iw.nrow + (size_t)iw.nb * 32, 32,
-                 &bars[islot]);
+        if (rows)
+          tma_load_2d_u32(dst + kWlStageW, q.smap, &bars[islot], q.nb * 16, q.st * rows);
+      }
       if (++islot == S) islot = 0;
       inflight++;
-      walk_next(iw, p, segs, nseg, cw);
+      if (++q.st == q.nst) next_live();
     };
+    auto can_issue = [&]() { return q.live; };
 
     // the weights never come from earlier kernels: fill the ring first
-    while (inflight < S && iw.si < nseg) issue();
+    refill();
+    while (inflight < S && can_issue()) issue();
     pdl_wait();  // prep sources and GEMM outputs are ordered after earlier kernels
 
     bool ok = true;
-    int g = 0, cslot = 0;  // g: GEMM segments entered (segment g uses activation slot g % 4)
+    int cseg = 0, cseg_lo = 0, cseg_end = nseg ? segs[0].nu : 0;  // compute side's segment
+    int cslot = 0;
     uint32_t cpar = 0;
-    for (int si = 0; si < nseg && ok; si++) {
-      const WlSeg &sg = segs[si];
-      const int e0 = sg.ofs[cw], e1 = sg.ofs[cw + 1];
+    while (ok) {
+      if (fpop == fpush) {  // nothing taken: take more
+        if (exhausted) break;
+        refill();
+        while (inflight < S && can_issue()) issue();
+        continue;
+      }
+      const int j = fifo[fpop & (kWlFifo - 1)];
+      fpop++;
+      refill();  // there is room again
+      while (j >= cseg_end) {
+        cseg_lo = cseg_end;
+        cseg++;
+        cseg_end += segs[cseg].nu;
+      }
+      const WlSeg &sg = segs[cseg];
       const WlItem &it = p.items[sg.item];
+      const int unit = sg.ub + (j - cseg_lo);
       if (sg.kind == kWlPrep) {
-        if (e0 == e1) continue;
         if (lane == 0) ok = wl_wait_item(p, it.deps[0]) && wl_wait_item(p, it.deps[1]);
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         if (!ok) break;
-        for (int e = e0; e < e1; e++) prep_row(it, __ldg(p.units + e), p.M, lane);
-        wl_signal(p, sg.item, (unsigned)(e1 - e0), lane);
+        prep_row(it, unit, p.M, lane);
+        if (it.waited) wl_signal(p, sg.item, 1u, lane);
         continue;
       }
-      const int b = g & (kWlASlots - 1);
-      ok = __all_sync(0xffffffffu, wl_wait(&s_full[b], (uint32_t)((g >> 2) & 1), p));
+      const int b = sg.gseq & (kWlASlots - 1);
+      ok = __all_sync(0xffffffffu, wl_wait(&s_full[b], (uint32_t)((sg.gseq >> 2) & 1), p));
       if (!ok) break;
       const uint32_t ab = abuf0 + s_aoff[b];
-      const int nst = sg.nst, nb0 = it.nb0, ldc = it.ldc, c0 = it.c_col0;
+      const int nst = sg.nst, ldc = it.ldc, c0 = it.c_col0;
+      const int nb = it.nb0 + unit;
       float *C = it.C;
       const float *b_scale8 = static_cast<const float *>(it.b_scale);
-      // The units of this segment, one code path per weight format and int4
-      // scale group (each keeps its own registers; the format is fixed for
-      // the whole segment).  KIND: 0 int8, else the int4 group in tiles.
-      auto units = [&](auto kind_tag) {
+      // one code path per weight format and int4 scale group
+      auto run = [&](auto kind_tag) {
         constexpr int KIND = decltype(kind_tag)::value;
         constexpr bool Q4 = KIND != 0;
         constexpr uint32_t a_step = (Q4 ? 8 : 4) * MT * 512;  // activation bytes per stage
-        for (int e = e0; e < e1 && ok; e++) {
-          const int nb = nb0 + __ldg(p.units + e);
-          float cf[MT][4];
-          int32_t acc[MT][4];
+        float2 cf[MT][2];  // running int4 sums: values (i = 0, 1) and (i = 2, 3)
+        int32_t acc[MT][4];
 #pragma unroll
-          for (int mt = 0; mt < MT; mt++)
+        for (int mt = 0; mt < MT; mt++) {
+          cf[mt][0] = cf[mt][1] = make_float2(0.0f, 0.0f);
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-              cf[mt][i] = 0.0f;
-              acc[mt][i] = 0;
-            }
-          float bs0 = 0.0f, bs1 = 0.0f;  // int8 per-channel scales of columns g8, g8 + 8
-          if (!Q4) {
-            bs0 = __ldg(b_scale8 + nb * 16 + L.g8);
-            bs1 = __ldg(b_scale8 + nb * 16 + L.g8 + 8);
-          }
-          uint32_t abs_ = ab;
-          for (int st = 0; st < nst; st++) {
-            ok = __all_sync(0xffffffffu, wl_wait(&bars[cslot], cpar, p));
-            if (!ok) break;
-            const uint32_t stg = ring + cslot * kWlStage;
-            if constexpr (Q4) q4_stage<MT, (Q4 ? KIND : 1)>(stg, abs_, L, cf);
-            else q8_stage<MT>(stg, abs_, L, acc);
-            abs_ += a_step;
-            __syncwarp();
-            fence_proxy_async_smem();  // this warp's reads of the slot precede its refill
-            inflight--;
-            if (++cslot == S) {
-              cslot = 0;
-              cpar ^= 1u;
-            }
-            if (iw.si < nseg) issue();
-          }
-          if (!ok) break;
-#pragma unroll
-          for (int mt = 0; mt < MT; mt++)
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-              const int m = mt * 8 + 2 * L.tig + (i & 1);
-              const int n = nb * 16 + L.g8 + (i >= 2 ? 8 : 0);
-              if (m >= p.M) continue;
-              const float as = s_as[b][m];
-              C[(size_t)m * ldc + (n - c0)] =
-                  Q4 ? __fmul_rn(cf[mt][i], as)
-                     : __fmul_rn(__int2float_rn(acc[mt][i]), __fmul_rn(i < 2 ? bs0 : bs1, as));
-            }
+          for (int i = 0; i < 4; i++) acc[mt][i] = 0;
         }
+        float bs0 = 0.0f, bs1 = 0.0f;  // int8 per-channel scales of columns g8, g8 + 8
+        if (!Q4) {
+          bs0 = __ldg(b_scale8 + nb * 16 + L.g8);
+          bs1 = __ldg(b_scale8 + nb * 16 + L.g8 + 8);
+        }
+        uint32_t abs_ = ab;
+        for (int st = 0; st < nst; st++) {
+          ok = __all_sync(0xffffffffu, wl_wait(&bars[cslot], cpar, p));
+          if (!ok) return;
+          const uint32_t stg = ring + cslot * kWlStage;
+          if constexpr (Q4) q4_stage<MT, (Q4 ? KIND : 1)>(stg, abs_, L, cf);
+          else q8_stage<MT>(stg, abs_, L, acc);
+          abs_ += a_step;
+          __syncwarp();
+          fence_proxy_async_smem();  // this warp's reads of the slot precede its refill
+          inflight--;
+          if (++cslot == S) {
+            cslot = 0;
+            cpar ^= 1u;
+          }
+          if (can_issue()) issue();
+        }
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            const int m = mt * 8 + 2 * L.tig + (i & 1);
+            const int n = nb * 16 + L.g8 + (i >= 2 ? 8 : 0);
+            if (m >= p.M) continue;
+            const float as = s_as[b][m];
+            const float2 c2 = cf[mt][i >> 1];
+            C[(size_t)m * ldc + (n - c0)] =
+                Q4 ? __fmul_rn((i & 1) ? c2.y : c2.x, as)
+                   : __fmul_rn(__int2float_rn(acc[mt][i]), __fmul_rn(i < 2 ? bs0 : bs1, as));
+          }
       };
-      if (sg.kind == kWlQ8) units(std::integral_constant<int, 0>{});
-      else if (it.gk == 1) units(std::integral_constant<int, 1>{});
-      else if (it.gk == 2) units(std::integral_constant<int, 2>{});
-      else if (it.gk == 4) units(std::integral_constant<int, 4>{});
-      else units(std::integral_constant<int, 8>{});
+      if (sg.kind == kWlQ8) run(std::integral_constant<int, 0>{});
+      else if (it.gk == 1) run(std::integral_constant<int, 1>{});
+      else if (it.gk == 2) run(std::integral_constant<int, 2>{});
+      else if (it.gk == 4) run(std::integral_constant<int, 4>{});
+      else run(std::integral_constant<int, 8>{});
       if (!ok) break;
+      // This unit is done.  The warp that finishes the segment's last unit
+      // releases its activation region; if another item waits for this one,
+      // every unit's outputs are made visible first and the segment is
+      // published.
+      const bool waited = it.waited != 0;
       __syncwarp();
-      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
-                                      tc::smem_u32(&s_empty[b]))
-                                  : "memory");
-      if (e1 > e0) wl_signal(p, sg.item, (unsigned)(e1 - e0), lane);
-      g++;
+      if (lane == 0) {
+        if (waited) __threadfence();
+        if (atomicAdd(&s_left[b], -1) == 1) {
+          if (waited) {
+            __threadfence();
+            atomicAdd(p.done + sg.item, (unsigned)sg.nu);
+          }
+          asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(&s_empty[b]))
+                       : "memory");
+        }
+      }
+      // keep the ring full when the queue was the limit
+      while (inflight < S && can_issue()) issue();
     }
     if (!ok) {
       if (lane == 0) wl_fail(p, 5);
@@ -765,7 +830,6 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
   }
   if (!pl.warps) return "the activations of the widest item do not fit in shared memory";
   pl.smem = worklist_smem(pl.a_ring, pl.warps, pl.stages);
-  const int W = pl.warps;
 
   // ---- preps that depend on nothing run in the prologue launch; entries
   // that read them wait for that launch (kernel order), not for a counter
@@ -780,6 +844,10 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
   for (int i = 0; i < n; i++)
     for (int &d : items[i].deps)
       if (d >= 0 && pro[d]) d = -1;
+  for (WlItem &it : items) it.waited = 0;
+  for (const WlItem &it : items)
+    for (int d : it.deps)
+      if (d >= 0) items[d].waited = 1;
   // ---- levels: one more than the deepest dependency
   std::vector<int> level(n, 0);
   int nlev = 0;
@@ -801,7 +869,6 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
     int item, u0, u1;
   };
   std::vector<std::vector<Piece>> cta(G);
-  std::vector<std::vector<int>> piece_level(G);
   int rr = 0;  // round-robin position of prep rows
   for (int lv = 0; lv < nlev; lv++) {
     double total = 0;
@@ -814,7 +881,6 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
       if (it.kind == kWlPrep) {  // rows round-robin over the CTAs
         for (int u = 0; u < it.units; u++, rr++) {
           cta[rr % G].push_back(Piece{i, u, u + 1});
-          piece_level[rr % G].push_back(lv);
         }
         continue;
       }
@@ -827,55 +893,27 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
         int u1 = u + 1;
         while (u1 < it.units && acc + (u1 - u + 0.5) * cost < end) u1++;
         cta[c].push_back(Piece{i, u, u1});
-        piece_level[c].push_back(lv);
         acc += (u1 - u) * cost;
         u = u1;
       }
     }
   }
-  // ---- inside each CTA: units to consumer warps, level by level, costliest
-  // first to the least loaded warp (warps keep their units in list order)
+  // ---- each CTA's segments in order; its consumer warps take the units
+  // from a shared counter while running
   pl.seg_off.assign(G + 1, 0);
   pl.segs.clear();
-  pl.units.clear();
   for (int c = 0; c < G; c++) {
     pl.seg_off[c] = (int)pl.segs.size();
-    const std::vector<Piece> &pc = cta[c];
-    std::vector<std::vector<std::vector<int>>> own(pc.size(),
-                                                   std::vector<std::vector<int>>(W));
-    std::vector<double> load(W, 0.0);
-    for (size_t a = 0; a < pc.size();) {
-      size_t z = a;
-      while (z < pc.size() && piece_level[c][z] == piece_level[c][a]) z++;
-      struct U {
-        double cost;
-        int piece, unit;
-      };
-      std::vector<U> us;
-      for (size_t q = a; q < z; q++)
-        for (int u = pc[q].u0; u < pc[q].u1; u++)
-          us.push_back(U{unit_cost(items[pc[q].item], u), (int)q, u});
-      std::stable_sort(us.begin(), us.end(), [](const U &x, const U &y) { return x.cost > y.cost; });
-      for (const U &x : us) {
-        const int w = (int)(std::min_element(load.begin(), load.end()) - load.begin());
-        load[w] += x.cost;
-        own[x.piece][w].push_back(x.unit);
-      }
-      a = z;
-    }
-    for (size_t q = 0; q < pc.size(); q++) {
-      const WlItem &it = items[pc[q].item];
+    int gseq = 0;
+    for (const Piece &pc : cta[c]) {
+      const WlItem &it = items[pc.item];
       WlSeg sg{};
-      sg.item = pc[q].item;
+      sg.item = pc.item;
       sg.kind = it.kind;
       sg.nst = it.kind == kWlQ4 ? it.K / 512 : (it.kind == kWlQ8 ? it.K / 256 : 0);
-      for (int w = 0; w < W; w++) {
-        std::vector<int> &v = own[q][w];
-        std::sort(v.begin(), v.end());
-        sg.ofs[w] = (int)pl.units.size();
-        pl.units.insert(pl.units.end(), v.begin(), v.end());
-      }
-      for (int w = W; w <= kWlMaxWarps; w++) sg.ofs[w] = (int)pl.units.size();
+      sg.ub = pc.u0;
+      sg.nu = pc.u1 - pc.u0;
+      sg.gseq = it.kind == kWlPrep ? -1 : gseq++;
       pl.segs.push_back(sg);
     }
   }
