@@ -1348,6 +1348,9 @@ int fgm_cuda_worklist_create(int M, const fgm_cuda_work *w, int n, void **list) 
     return fail(FGM_CUDA_ENOMEM, "worklist: cudaMalloc(%zu)", total);
   }
   char *d = static_cast<char *>(wl->mem);
+  for (WlSeg &sg : wl->plan.segs)  // each segment's view of its item's scales, on the device
+    if (sg.kind == kWlQ4)
+      sg.smap = &reinterpret_cast<const WlItem *>(d + o_items)[sg.item].smap;
   cudaError_t e = cudaMemcpy(d + o_items, items.data(), b_items, cudaMemcpyHostToDevice);
   if (e == cudaSuccess && b_segs)
     e = cudaMemcpy(d + o_segs, wl->plan.segs.data(), b_segs, cudaMemcpyHostToDevice);

@@ -236,6 +236,15 @@ struct WlSeg {                 // one CTA's share of one item
   int item, kind, nst;         // item, its kind, 4 KB weight stages per unit
   int ub, nu;                  // its units: [ub, ub + nu) of the item (n-blocks or rows)
   int gseq;                    // GEMM segments of the CTA before this one (activation slot)
+  // the item's fields a unit needs, copied here so one descriptor read
+  // serves a unit (no dependent lookup of the item)
+  int nb_base;                 // n-block of unit ub
+  int ldc, c_col0, gk, waited;
+  int ubytes, rows_st;         // weight bytes per unit, int4 scale rows per stage
+  float *C;
+  const void *b_scale;
+  const uint8_t *B;
+  const CUtensorMap *smap;     // device address of the item's scale view
 };
 struct WlParams {
   const WlItem *items;

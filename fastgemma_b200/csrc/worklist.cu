@@ -469,13 +469,12 @@ __device__ __forceinline__ void issue_seg(Issue &q, const WlParams &p, const WlS
   }
   if (q.si >= nseg) return;
   const WlSeg &sg = segs[q.si];
-  const WlItem &it = p.items[sg.item];
   q.nst = sg.nst;
-  q.B = it.B;
-  q.smap = &it.smap;
-  q.ubytes = it.K * (sg.kind == kWlQ4 ? 8 : 16);  // K/64 tiles of 512 or 1024 bytes
-  q.rows_st = sg.kind == kWlQ4 ? 8 / it.gk : 0;
-  q.nb0 = it.nb0 + sg.ub;  // n-block of the segment's first unit
+  q.B = sg.B;
+  q.smap = sg.smap;
+  q.ubytes = sg.ubytes;
+  q.rows_st = sg.rows_st;
+  q.nb0 = sg.nb_base;  // n-block of the segment's first unit
   q.kind = sg.kind;
   q.loaded = true;
 }
@@ -500,23 +499,17 @@ __global__ void __launch_bounds__((kWlMaxWarps + 1) * 32, 1) worklist_kernel(con
   const uint32_t abuf0 = tc::smem_u32(smem);
   const uint32_t ring0 = abuf0 + (uint32_t)p.a_ring;
 
-  if (threadIdx.x == 0) {
-    for (int b = 0; b < kWlASlots; b++) {
-      tc::mbar_init(&s_full[b], 1);
-      tc::mbar_init(&s_empty[b], 1);  // the warp finishing a segment's last unit arrives
-    }
-    for (int w = 0; w < W; w++)
-      for (int s = 0; s < S; s++) tc::mbar_init(&s_ring[w][s], 1);
+  // barriers: one thread each (the ring's W x S, then the slots' full and empty)
+  if ((int)threadIdx.x < W * S) {
+    tc::mbar_init(&s_ring[threadIdx.x / S][threadIdx.x % S], 1);
     tc::fence_mbar_init();
-    s_grab = 0;
+  } else if ((int)threadIdx.x < W * S + kWlASlots) {
+    const int b = threadIdx.x - W * S;
+    tc::mbar_init(&s_full[b], 1);
+    tc::mbar_init(&s_empty[b], 1);  // the warp finishing a segment's last unit arrives
+    tc::fence_mbar_init();
   }
-  // unfinished units per activation slot, for the first four GEMM segments
-  if (threadIdx.x < kWlASlots) {
-    int left = 0;
-    for (int si = 0; si < nseg; si++)
-      if (segs[si].kind != kWlPrep && segs[si].gseq == (int)threadIdx.x) left = segs[si].nu;
-    s_left[threadIdx.x] = left;
-  }
+  if (threadIdx.x == 0) s_grab = 0;
   __syncthreads();
   pdl_launch_dependents();
 
@@ -552,7 +545,8 @@ __global__ void __launch_bounds__((kWlMaxWarps + 1) * 32, 1) worklist_kernel(con
       if (lane == 0) {
         s_r0[b] = off;
         s_r1[b] = off + sz;
-        if (g >= kWlASlots) s_left[b] = sg.nu;  // the slot's previous segment is done
+        s_left[b] = sg.nu;  // the slot's previous segment is done; seen by its units
+                            // through the full barrier this lane arms below
       }
       head = off + sz;
       fence_proxy_async_global();  // the activations may have been written in this launch
@@ -659,24 +653,24 @@ __global__ void __launch_bounds__((kWlMaxWarps + 1) * 32, 1) worklist_kernel(con
         cseg_end += segs[cseg].nu;
       }
       const WlSeg &sg = segs[cseg];
-      const WlItem &it = p.items[sg.item];
-      const int unit = sg.ub + (j - cseg_lo);
-      if (sg.kind == kWlPrep) {
+      const int kind = sg.kind;
+      if (kind == kWlPrep) {
+        const WlItem &it = p.items[sg.item];
         if (lane == 0) ok = wl_wait_item(p, it.deps[0]) && wl_wait_item(p, it.deps[1]);
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         if (!ok) break;
-        prep_row(it, unit, p.M, lane);
+        prep_row(it, sg.ub + (j - cseg_lo), p.M, lane);
         if (it.waited) wl_signal(p, sg.item, 1u, lane);
         continue;
       }
-      const int b = sg.gseq & (kWlASlots - 1);
-      ok = __all_sync(0xffffffffu, wl_wait(&s_full[b], (uint32_t)((sg.gseq >> 2) & 1), p));
+      const int gseq = sg.gseq, nst = sg.nst, ldc = sg.ldc, c0 = sg.c_col0, gk = sg.gk;
+      const int nb = sg.nb_base + (j - cseg_lo);
+      float *C = sg.C;
+      const float *b_scale8 = static_cast<const float *>(sg.b_scale);
+      const int b = gseq & (kWlASlots - 1);
+      ok = __all_sync(0xffffffffu, wl_wait(&s_full[b], (uint32_t)((gseq >> 2) & 1), p));
       if (!ok) break;
       const uint32_t ab = abuf0 + s_aoff[b];
-      const int nst = sg.nst, ldc = it.ldc, c0 = it.c_col0;
-      const int nb = it.nb0 + unit;
-      float *C = it.C;
-      const float *b_scale8 = static_cast<const float *>(it.b_scale);
       // one code path per weight format and int4 scale group
       auto run = [&](auto kind_tag) {
         constexpr int KIND = decltype(kind_tag)::value;
@@ -726,24 +720,24 @@ __global__ void __launch_bounds__((kWlMaxWarps + 1) * 32, 1) worklist_kernel(con
                    : __fmul_rn(__int2float_rn(acc[mt][i]), __fmul_rn(i < 2 ? bs0 : bs1, as));
           }
       };
-      if (sg.kind == kWlQ8) run(std::integral_constant<int, 0>{});
-      else if (it.gk == 1) run(std::integral_constant<int, 1>{});
-      else if (it.gk == 2) run(std::integral_constant<int, 2>{});
-      else if (it.gk == 4) run(std::integral_constant<int, 4>{});
+      if (kind == kWlQ8) run(std::integral_constant<int, 0>{});
+      else if (gk == 1) run(std::integral_constant<int, 1>{});
+      else if (gk == 2) run(std::integral_constant<int, 2>{});
+      else if (gk == 4) run(std::integral_constant<int, 4>{});
       else run(std::integral_constant<int, 8>{});
       if (!ok) break;
       // This unit is done.  The warp that finishes the segment's last unit
       // releases its activation region; if another item waits for this one,
       // every unit's outputs are made visible first and the segment is
       // published.
-      const bool waited = it.waited != 0;
+      const bool waited = sg.waited != 0;
       __syncwarp();
       if (lane == 0) {
         if (waited) __threadfence();
         if (atomicAdd(&s_left[b], -1) == 1) {
           if (waited) {
             __threadfence();
-            atomicAdd(p.done + sg.item, (unsigned)sg.nu);
+            atomicAdd(p.done + segs[cseg].item, (unsigned)segs[cseg].nu);
           }
           asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(&s_empty[b]))
                        : "memory");
@@ -858,9 +852,12 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
   }
   // Cost of one unit in 4 KB weight stages (a prep row: two passes over its
   // f32 source, which one warp reads at a fraction of the weight rate).
+  // Cost of one unit in 4 KB weight stages: its stages plus a fixed cost per
+  // unit (taking it, its epilogue) measured at about one and a half stages;
+  // a prep row: two passes over its f32 source.
   auto unit_cost = [&](const WlItem &it, int u) -> double {
-    if (it.kind == kWlQ4) return it.K / 512;
-    if (it.kind == kWlQ8) return it.K / 256;
+    if (it.kind == kWlQ4) return it.K / 512 + 1.5;
+    if (it.kind == kWlQ8) return it.K / 256 + 1.5;
     return u < M ? 3.0 * it.K / 1024 : 1.0;
   };
   // ---- each CTA's (item, unit range) pieces, level by level
@@ -871,6 +868,8 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
   std::vector<std::vector<Piece>> cta(G);
   int rr = 0;  // round-robin position of prep rows
   for (int lv = 0; lv < nlev; lv++) {
+    std::vector<size_t> first(G);  // where this level's pieces start in each CTA's list
+    for (int c = 0; c < G; c++) first[c] = cta[c].size();
     double total = 0;
     for (int i = 0; i < n; i++)
       if (level[i] == lv && items[i].kind != kWlPrep) total += items[i].units * unit_cost(items[i], 0);
@@ -897,6 +896,16 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
         u = u1;
       }
     }
+    // Inside a level the items are independent: each CTA takes its prep rows
+    // first, then its GEMM units from the largest to the smallest, so the
+    // end of the level is made of small units that every warp can share
+    // (a few large units at the end would run on a few warps alone).
+    for (int c = 0; c < G; c++)
+      std::stable_sort(cta[c].begin() + first[c], cta[c].end(), [&](const Piece &x, const Piece &y) {
+        const double cx = items[x.item].kind == kWlPrep ? 1e30 : unit_cost(items[x.item], 0);
+        const double cy = items[y.item].kind == kWlPrep ? 1e30 : unit_cost(items[y.item], 0);
+        return cx > cy;
+      });
   }
   // ---- each CTA's segments in order; its consumer warps take the units
   // from a shared counter while running
@@ -914,6 +923,19 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
       sg.ub = pc.u0;
       sg.nu = pc.u1 - pc.u0;
       sg.gseq = it.kind == kWlPrep ? -1 : gseq++;
+      if (it.kind != kWlPrep) {
+        sg.nb_base = it.nb0 + pc.u0;
+        sg.ldc = it.ldc;
+        sg.c_col0 = it.c_col0;
+        sg.gk = it.gk;
+        sg.waited = it.waited;
+        sg.ubytes = it.K * (it.kind == kWlQ4 ? 8 : 16);  // K/64 tiles of 512 or 1024 bytes
+        sg.rows_st = it.kind == kWlQ4 ? 8 / it.gk : 0;
+        sg.C = it.C;
+        sg.b_scale = it.b_scale;
+        sg.B = it.B;
+        sg.smap = nullptr;  // set once the descriptors' device address is known
+      }
       pl.segs.push_back(sg);
     }
   }
