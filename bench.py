@@ -679,10 +679,17 @@ def tc_roofline(ops, bytes_, seconds, gpus=1):
             "attainable_frac": min(1.0, ai / ridge)}
 
 
+def _list_ms(wl, steps, world, dev, stream):
+    """Mean device ms of one work-list run (CUDA events on `stream`)."""
+    return _timed(lambda: wl.run(stream), steps, world, dev, stream=stream)
+
+
 def bench_config0(args, dev, gen, world):
     """one decode projection M=8, N=8192, K=2048, int4 g64,
-    as fastgemma's Gemm::run -- prep of f32 X then the GEMM -- over a chain of
-    32 distinct weight copies (285 MB > 2 x L2), one CUDA graph."""
+    as fastgemma's Gemm::run -- prep of f32 X then the GEMM -- for 32
+    distinct weight copies (285 MB > 2 x L2).  The value runs the 32 (prep,
+    GEMM) pairs as one work-list launch; the same pairs as per-call entries
+    in one CUDA graph are reported beside it."""
     import torch
     from fastgemma_b200 import device as D
     M, N, K, copies = M_DECODE, 8192, 2048, 32
@@ -691,9 +698,27 @@ def bench_config0(args, dev, gen, world):
            torch.empty((K // GROUP, N), device=dev).uniform_(0.005, 0.02, generator=gen).half())
           for _ in range(copies)]
     x = torch.randn((M, K), device=dev, generator=gen)
+    side = torch.cuda.Stream(device=dev)
+    hbm, src = hbm_peak()
+    alg = wb + sb + M * K * 4 + M * N * 4
+
+    # one work-list launch: per copy its own prep (into its own packed rows)
+    # and the GEMM that waits for it
+    wl = D.WorkList()
+    outs = []
+    for w, s in ws:
+        pa, qs = D.packed_a(M, K, dev), torch.empty(M, device=dev)
+        ip = wl.prep(x, K, K, pa, qs)
+        c = torch.empty((M, N), device=dev)
+        wl.gemm_q4g(N, K, pa, qs, w, s, GROUP, c, deps=(ip,))
+        outs.append(c)
+    wl.build(M)
+    ms_list = _list_ms(wl, max(20, args.steps // 4), world, dev, side)
+    list_call = ms_list / copies
+
+    # the same pairs as per-call entries, one CUDA graph
     pa, qs = D.packed_a(M, K, dev), torch.empty(M, device=dev)
     c = torch.empty((M, N), device=dev)
-    side = torch.cuda.Stream(device=dev)
 
     def chain():
         for w, s in ws:
@@ -703,31 +728,38 @@ def bench_config0(args, dev, gen, world):
     with torch.cuda.stream(side):
         chain()
     torch.cuda.synchronize()
+    # parity: the list's last copy equals the per-call entry's output bit for bit
+    parity = bool(torch.equal(outs[-1].view(torch.int32), c.view(torch.int32)))
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=side):
         chain()
     ms = _timed(g.replay, max(5, args.steps // 10), world, dev, stream=side)
     del g
+    wl.close()
     per_call = ms / copies
-    hbm, src = hbm_peak()
-    alg = wb + sb + M * K * 4 + M * N * 4
-    gbs = (wb + sb) / (per_call * 1e-3) / 1e9
-    return {"value": world * gbs, "unit": "GB/s", "us_per_call": per_call * 1e3,
-            "frac_hbm": (alg / (per_call * 1e-3) / 1e9) / hbm, "hbm_peak": hbm,
-            "peak_source": src, "algorithmic_bytes": alg,
+    gbs = (wb + sb) / (list_call * 1e-3) / 1e9
+    return {"value": world * gbs, "unit": "GB/s", "us_per_call": list_call * 1e3,
+            "frac_hbm": (alg / (list_call * 1e-3) / 1e9) / hbm, "hbm_peak": hbm,
+            "peak_source": src, "algorithmic_bytes": alg, "parity_vs_per_call": parity,
+            "per_call": {"us_per_call": per_call * 1e3,
+                         "weight_gbs": (wb + sb) / (per_call * 1e-3) / 1e9,
+                         "frac_hbm": (alg / (per_call * 1e-3) / 1e9) / hbm,
+                         "path": "prep_rows + gemm_q4g per copy, one CUDA graph"},
             "workload": f"BASELINE config 0: prep + int4 GEMM M={M} N={N} K={K} g{GROUP} f16 "
-                        f"scales, {copies} distinct weight copies per graph replay; value = "
-                        f"weight+scale bytes / time per call"}
+                        f"scales, {copies} distinct weight copies per step as one work-list "
+                        f"launch (each copy its own prep and output rows); value = weight+"
+                        f"scale bytes / (step time / {copies})"}
 
 
 def bench_config1_sweep(args, dev, gen, world):
     """BASELINE config 1 as fastgemma's gemm_bench sweeps it
     (bench/kernels/gemm_bench.c:253-307): each (M, projection) timed alone
-    as back-to-back GEMMs over distinct weight copies (> 2 x L2 per shape),
-    M in {1, 2, 4, 8, 16}."""
+    over distinct weight copies (> 2 x L2 per shape), M in {1, 2, 4, 8, 16},
+    prep excluded.  Two forms: the copies' GEMMs as one work-list launch
+    (reading rows packed before the run), and the per-call entry back to
+    back in one CUDA graph."""
     import torch
     from fastgemma_b200 import device as D
-    K_all = (2048, 8192)
     out = {}
     side = torch.cuda.Stream(device=dev)
     hbm, _ = hbm_peak()
@@ -739,10 +771,19 @@ def bench_config1_sweep(args, dev, gen, world):
                                                                  generator=gen).half())
               for _ in range(copies)]
         c = torch.empty((16, N), device=dev)
+        cs = torch.empty((copies, 16, N), device=dev)
         for M in (1, 2, 4, 8, 16):
             x = torch.randn((M, K), device=dev, generator=gen)
             pa, qs = D.packed_a(M, K, dev), torch.empty(M, device=dev)
             D.prep_rows(x, K, qs, pa, M, K, 0)
+            alg = wb + sb + M * K + M * 4 + M * N * 4
+
+            wl = D.WorkList()
+            for i, (w, s) in enumerate(ws):
+                wl.gemm_q4g(N, K, pa, qs, w, s, GROUP, cs[i])
+            wl.build(M)
+            us_list = _list_ms(wl, 20, world, dev, side) * 1e3 / copies
+            wl.close()
 
             def chain():
                 for w, s in ws:
@@ -757,15 +798,17 @@ def bench_config1_sweep(args, dev, gen, world):
             ms = _timed(g.replay, 5, world, dev, stream=side)
             del g
             us = ms * 1e3 / copies
-            alg = wb + sb + M * K + M * 4 + M * N * 4
             out.setdefault(f"M{M}", {})[name] = {
-                "us": us, "weight_gbs": (wb + sb) / (us * 1e-6) / 1e9,
-                "frac_hbm": alg / (us * 1e-6) / 1e9 / hbm}
-        del ws
+                "us": us_list, "weight_gbs": (wb + sb) / (us_list * 1e-6) / 1e9,
+                "frac_hbm": alg / (us_list * 1e-6) / 1e9 / hbm,
+                "per_call_us": us, "per_call_frac_hbm": alg / (us * 1e-6) / 1e9 / hbm}
+        del ws, cs
     return {"unit": "us per GEMM / weight GB/s", "results": out,
-            "workload": "BASELINE config 1: int4 g64 GEMM alone (prep excluded), back to back "
-                        "over distinct weight copies (> 2 x L2 per shape), one CUDA graph; "
-                        "frac_hbm = algorithmic bytes / time / measured HBM"}
+            "workload": "BASELINE config 1: int4 g64 GEMM alone (prep excluded) over distinct "
+                        "weight copies (> 2 x L2 per shape); us/frac_hbm: the copies as one "
+                        "work-list launch, us per GEMM = step / copies; per_call_*: "
+                        "gemm_q4g back to back in one CUDA graph; frac_hbm = algorithmic "
+                        "bytes / time / measured HBM"}
 
 
 def bench_config4(args, dev, world, rank):
@@ -883,6 +926,8 @@ def build_decode_chain(dev, gen, T, L=30):
     final_norm = norm(H)
     inv_freq = (1.0 / (10000.0 ** (torch.arange(0, HD, 2, device=dev, dtype=torch.float32) / HD)))
     pos = torch.full((M,), T - 1, dtype=torch.int32, device=dev)
+    # rope's cos / sin: the host libm table the reference computes per position
+    rope_cs = torch.from_numpy(D.rope_table(T, HD, inv_freq.cpu().numpy())).to(dev)
     x = torch.randn((M, H), device=dev, generator=gen)
     f32 = lambda *shape: torch.empty(shape, device=dev)  # noqa: E731
     qkv, attn, o = f32(M, QKV), f32(M, NH * HD), f32(M, H)
@@ -909,7 +954,7 @@ def build_decode_chain(dev, gen, T, L=30):
             D.gemm_q4g(M, QKV, H, pa[H], qs, lw["qkv"][0], lw["qkv"][1], GROUP, qkv)
             D.qkv_post(q, k, v, M, NH, KVH, HD, lw["qn"], lw["kn"], 1e-6, inv_freq, pos, 0, T,
                        lw["kc"], T * KVD, lw["ks"], T, lw["vt"], lw["vt"].shape[1], lw["vs"], T,
-                       q_ld=QKV, kv_ld=QKV)
+                       q_ld=QKV, kv_ld=QKV, cs=rope_cs)
             D.attend_q8(attn, NH * HD, q, QKV, lw["kc"], T * KVD, lw["ks"], T, lw["vt"],
                         lw["vt"].shape[1], lw["vs"], T, M, NH, KVH, HD, 0, T)
             D.prep_rows(attn, NH * HD, qs, pa[H], M, NH * HD, 0)

@@ -59,6 +59,8 @@ SIGNATURES = {
     "fgm_cuda_scale": ([_p, C.c_float, _sz, _p], _i),
     "fgm_cuda_softcap": ([_p, _i, _i, C.c_float, _p], _i),
     "fgm_cuda_rope": ([_p, _i, _i, _i, _i, _p, _p, _p], _i),
+    "fgm_cuda_rope_table": ([_p, _i, _i, _p], _i),
+    "fgm_cuda_rope_cs": ([_p, _i, _i, _i, _i, _p, _p, _i, _p, _p], _i),
     "fgm_cuda_quant_act": ([_p, _i, _i, _p, _p, _p], _i),
     "fgm_cuda_store_v_t": ([_p, _sz, _p, _i, _i, _i, _i, _p], _i),
     "fgm_cuda_attend_q8": ([_p, _i, _p, _i, _p, _sz, _p, _sz, _p, _sz, _p, _sz, _i, _i, _i, _i,
@@ -67,6 +69,8 @@ SIGNATURES = {
     "fgm_cuda_gelu_mul_prep": ([_p, _p, _i, _i, _i, _p, _p, _p, _p], _i),
     "fgm_cuda_qkv_post": ([_p, _i, _p, _p, _i, _i, _i, _i, _i, _p, _p, C.c_float, _p, _p, _i, _i,
                            _p, _sz, _p, _sz, _p, _sz, _p, _sz, _p], _i),
+    "fgm_cuda_qkv_post_cs": ([_p, _i, _p, _p, _i, _i, _i, _i, _i, _p, _p, C.c_float, _p, _p, _i,
+                              _p, _i, _i, _p, _sz, _p, _sz, _p, _sz, _p, _sz, _p], _i),
     "fgm_cuda_ipc_alloc": ([_sz, C.POINTER(_p)], _i),
     "fgm_cuda_ipc_free": ([_p], _i),
     "fgm_cuda_ipc_handle": ([_p, _p], _i),

@@ -1484,16 +1484,39 @@ int fgm_cuda_softcap(float *x, int rows, int n, float cap, void *stream) {
                    "softcap launch");
 }
 
+int fgm_cuda_rope_table(float *cs, int positions, int head_dim, const float *inv_freq) {
+  if (positions < 0 || head_dim <= 0 || head_dim % 2)
+    return fail(FGM_CUDA_EINVAL, "rope_table: positions=%d head_dim=%d", positions, head_dim);
+  if (positions == 0) return FGM_CUDA_OK;
+  if (!cs || !inv_freq) return fail(FGM_CUDA_EINVAL, "null pointer");
+  const int h = head_dim / 2;
+  for (int p = 0; p < positions; p++)  // ops.c:137-139, this host's libm
+    for (int j = 0; j < h; j++) {
+      const float a = (float)p * inv_freq[j];
+      cs[(size_t)p * head_dim + j] = cosf(a);
+      cs[(size_t)p * head_dim + h + j] = sinf(a);
+    }
+  return FGM_CUDA_OK;
+}
+
+int fgm_cuda_rope_cs(float *x, int x_ld, int rows, int n_heads, int head_dim,
+                     const float *inv_freq, const float *cs, int positions, const int *pos,
+                     void *stream) {
+  if (rows < 0 || n_heads <= 0 || head_dim <= 0 || head_dim % 2 || x_ld < n_heads * head_dim ||
+      positions < 0)
+    return fail(FGM_CUDA_EINVAL, "rope: rows=%d heads=%d head_dim=%d x_ld=%d positions=%d", rows,
+                n_heads, head_dim, x_ld, positions);
+  if (rows == 0) return FGM_CUDA_OK;
+  if (!x || !inv_freq || !pos || (positions > 0 && !cs))
+    return fail(FGM_CUDA_EINVAL, "null pointer");
+  return glue_done(launch_rope(x, x_ld, rows, n_heads, head_dim, inv_freq, cs, positions, pos,
+                               glue_pdl(), (cudaStream_t)stream),
+                   "rope launch");
+}
+
 int fgm_cuda_rope(float *x, int x_ld, int rows, int n_heads, int head_dim, const float *inv_freq,
                   const int *pos, void *stream) {
-  if (rows < 0 || n_heads <= 0 || head_dim <= 0 || head_dim % 2 || x_ld < n_heads * head_dim)
-    return fail(FGM_CUDA_EINVAL, "rope: rows=%d heads=%d head_dim=%d x_ld=%d", rows, n_heads,
-                head_dim, x_ld);
-  if (rows == 0) return FGM_CUDA_OK;
-  if (!x || !inv_freq || !pos) return fail(FGM_CUDA_EINVAL, "null pointer");
-  return glue_done(launch_rope(x, x_ld, rows, n_heads, head_dim, inv_freq, pos, glue_pdl(),
-                               (cudaStream_t)stream),
-                   "rope launch");
+  return fgm_cuda_rope_cs(x, x_ld, rows, n_heads, head_dim, inv_freq, nullptr, 0, pos, stream);
 }
 
 int fgm_cuda_quant_act(const float *x, int rows, int k, int8_t *q, float *scale, void *stream) {
@@ -1611,6 +1634,20 @@ int fgm_cuda_qkv_post(float *q, int q_ld, float *k, float *v, int kv_ld, int row
                       const float *inv_freq, const int *pos, int ring, int cap, int8_t *kc,
                       size_t kc_stride, float *ks, size_t ks_stride, int8_t *vt, size_t vt_stride,
                       float *vs, size_t vs_stride, void *stream) {
+  return fgm_cuda_qkv_post_cs(q, q_ld, k, v, kv_ld, rows, n_heads, kv_heads, head_dim, q_norm,
+                              k_norm, eps, inv_freq, nullptr, 0, pos, ring, cap, kc, kc_stride, ks,
+                              ks_stride, vt, vt_stride, vs, vs_stride, stream);
+}
+
+int fgm_cuda_qkv_post_cs(float *q, int q_ld, float *k, float *v, int kv_ld, int rows,
+                         int n_heads, int kv_heads, int head_dim, const float *q_norm,
+                         const float *k_norm, float eps, const float *inv_freq, const float *cs,
+                         int positions, const int *pos, int ring, int cap, int8_t *kc,
+                         size_t kc_stride, float *ks, size_t ks_stride, int8_t *vt,
+                         size_t vt_stride, float *vs, size_t vs_stride, void *stream) {
+  if (positions < 0 || (positions > 0 && !cs))
+    return fail(FGM_CUDA_EINVAL, "qkv_post: rope table of %d positions at %p", positions,
+                (const void *)cs);
   if (cap <= 0 || (ring > 0 && ring > cap))
     return fail(FGM_CUDA_EINVAL, "qkv_post: cap=%d ring=%d (need 0 < ring <= cap)", cap, ring);
   if (rows > 1 && ((size_t)cap * kv_heads * head_dim > kc_stride || (size_t)cap > ks_stride ||
@@ -1633,7 +1670,8 @@ int fgm_cuda_qkv_post(float *q, int q_ld, float *k, float *v, int kv_ld, int row
   int rc = dev_info(&di);
   if (rc) return rc;
   QkvParams p{q, k, v, q_ld, kv_ld, n_heads, kv_heads, head_dim, q_norm, k_norm, eps, inv_freq,
-              pos, ring, cap, kc, ks, vt, vs, kc_stride, ks_stride, vt_stride, vs_stride};
+              pos, ring, cap, kc, ks, vt, vs, kc_stride, ks_stride, vt_stride, vs_stride,
+              positions > 0 ? cs : nullptr, positions};
   if (qkv_post_smem(p) > di->smem_optin)
     return fail(FGM_CUDA_EINVAL, "qkv_post: %d heads of %d need too much shared memory",
                 n_heads + 2 * kv_heads, head_dim);

@@ -101,7 +101,8 @@ cudaError_t launch_elementwise(float *a, const float *b, float s, size_t n, int 
                                cudaStream_t st);
 cudaError_t launch_softcap(float *x, int rows, int n, float cap, bool pdl, cudaStream_t st);
 cudaError_t launch_rope(float *x, int x_ld, int rows, int n_heads, int head_dim,
-                        const float *inv_freq, const int *pos, bool pdl, cudaStream_t st);
+                        const float *inv_freq, const float *tab, int positions, const int *pos,
+                        bool pdl, cudaStream_t st);
 cudaError_t launch_store_v_t(int8_t *vt, size_t vt_stride, const int8_t *src, int src_ld, int rows,
                              int n, int slot, bool pdl, cudaStream_t st);
 struct AttnParams {
@@ -147,6 +148,8 @@ struct QkvParams {
   int8_t *vt;
   float *vs;
   size_t kc_stride, ks_stride, vt_stride, vs_stride;  // per row (elements)
+  const float *rope_tab;            // host-computed cos | sin per position, or null
+  int rope_positions;               // positions in rope_tab
 };
 size_t qkv_post_smem(const QkvParams &p);
 cudaError_t launch_qkv_post(const QkvParams &p, int rows, bool pdl, cudaStream_t st);

@@ -169,10 +169,27 @@ __global__ void softcap_kernel(float *x, int n, size_t total, float cap) {
   }
 }
 
+// Rope's cos and sin of angle pos * inv_freq[j]: from the caller's host
+// table (cs[pos][head_dim]: cos in [0, half), sin in [half, 2 half), the
+// reference's own libm values) when the position is inside it, else
+// evaluated in double precision and rounded once.
+__device__ __forceinline__ void rope_cs(const float *inv_freq, const float *tab, int positions,
+                                        int half, int pos, int j, float &c, float &s) {
+  if (tab && pos >= 0 && pos < positions) {
+    const float *t = tab + (size_t)pos * 2 * half;
+    c = t[j];
+    s = t[half + j];
+  } else {
+    const float a = __fmul_rn((float)pos, inv_freq[j]);
+    c = (float)cos((double)a);
+    s = (float)sin((double)a);
+  }
+}
+
 // ops.c:135-147 for `rows` rows (row r at x + r*x_ld, position pos[r]).  The
 // reference's build fuses each product pair into one rounding.
 __global__ void rope_kernel(float *x, int x_ld, int n_heads, int head_dim, const float *inv_freq,
-                            const int *pos) {
+                            const float *tab, int positions, const int *pos) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int h = head_dim / 2, r = blockIdx.y;
@@ -180,8 +197,8 @@ __global__ void rope_kernel(float *x, int x_ld, int n_heads, int head_dim, const
   for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < n_heads * h;
        idx += gridDim.x * blockDim.x) {
     const int hh = idx / h, j = idx % h;
-    const float a = __fmul_rn((float)pos[r], inv_freq[j]);
-    const float c = (float)cos((double)a), s = (float)sin((double)a);
+    float c, s;
+    rope_cs(inv_freq, tab, positions, h, pos[r], j, c, s);
     float *p = xr + (size_t)hh * head_dim;
     const float lo = p[j], hi = p[j + h];
     p[j] = __fmaf_rn(lo, c, -__fmul_rn(hi, s));
@@ -1040,14 +1057,10 @@ __global__ void __launch_bounds__(kGlueThreads) qkv_post_kernel(const QkvParams 
     }
   }
   for (int j = threadIdx.x; j < hd; j += blockDim.x) {
-    const float a = j < half ? __fmul_rn((float)pos, p.inv_freq[j]) : 0.0f;
     const float wq = p.q_norm[j], wk = p.k_norm[j];
     qn[j] = wq;
     kn[j] = wk;
-    if (j < half) {
-      cs[j] = (float)cos((double)a);
-      sn[j] = (float)sin((double)a);
-    }
+    if (j < half) rope_cs(p.inv_freq, p.rope_tab, p.rope_positions, half, pos, j, cs[j], sn[j]);
   }
   __syncthreads();
   // per-head sums of squares: a half-warp per head, 16 lanes in order
@@ -1237,11 +1250,12 @@ cudaError_t launch_softcap(float *x, int rows, int n, float cap, bool pdl, cudaS
 }
 
 cudaError_t launch_rope(float *x, int x_ld, int rows, int n_heads, int head_dim,
-                        const float *inv_freq, const int *pos, bool pdl, cudaStream_t st) {
+                        const float *inv_freq, const float *tab, int positions, const int *pos,
+                        bool pdl, cudaStream_t st) {
   const int pairs = n_heads * (head_dim / 2);
   const unsigned gx = (unsigned)((pairs + kGlueThreads - 1) / kGlueThreads);
   return launch_pdl(rope_kernel, dim3(gx, rows), dim3(kGlueThreads), 0, pdl, st, x, x_ld, n_heads,
-                    head_dim, inv_freq, pos);
+                    head_dim, inv_freq, tab, positions, pos);
 }
 
 cudaError_t launch_store_v_t(int8_t *vt, size_t vt_stride, const int8_t *src, int src_ld, int rows,

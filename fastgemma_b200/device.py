@@ -144,9 +144,26 @@ def softcap(x, rows, n, cap, stream=None):
     call("fgm_cuda_softcap", _p(x), rows, n, cap, _s(stream))
 
 
-def rope(x, x_ld, rows, n_heads, head_dim, inv_freq, pos, stream=None):
-    """ops.c:135-147 in place; pos: int32 device tensor [rows]."""
-    call("fgm_cuda_rope", _p(x), x_ld, rows, n_heads, head_dim, _p(inv_freq), _p(pos), _s(stream))
+def rope(x, x_ld, rows, n_heads, head_dim, inv_freq, pos, cs=None, stream=None):
+    """ops.c:135-147 in place; pos: int32 device tensor [rows]; cs: a device
+    copy of rope_table(...) (the reference's libm cos / sin), else the device
+    evaluates them."""
+    if cs is None:
+        call("fgm_cuda_rope", _p(x), x_ld, rows, n_heads, head_dim, _p(inv_freq), _p(pos),
+             _s(stream))
+    else:
+        call("fgm_cuda_rope_cs", _p(x), x_ld, rows, n_heads, head_dim, _p(inv_freq), _p(cs),
+             cs.shape[0], _p(pos), _s(stream))
+
+
+def rope_table(positions, head_dim, inv_freq):
+    """Host [positions][head_dim] f32: cosf | sinf of (float)p * inv_freq[j]
+    (ops.c:137-139) from this host's libm; inv_freq: numpy f32 [head_dim/2]."""
+    import numpy as np
+    inv = np.ascontiguousarray(inv_freq, dtype=np.float32)
+    out = np.empty((positions, head_dim), np.float32)
+    call("fgm_cuda_rope_table", out.ctypes.data, positions, head_dim, inv.ctypes.data)
+    return out
 
 
 def quant_act(x, rows, k, q, scale, stream=None):
@@ -182,12 +199,14 @@ def gelu_mul_prep(gate, up, rows, n, qs, pa, act=None, ld=None, stream=None):
 
 def qkv_post(q, k, v, rows, n_heads, kv_heads, head_dim, q_norm, k_norm, eps, inv_freq, pos, ring,
              cap, kc, kc_stride, ks, ks_stride, vt, vt_stride, vs, vs_stride, q_ld=None, kv_ld=None,
-             stream=None):
-    """forward.rs:482-545: head norms, rope, int8 K / V rows into the caches."""
+             cs=None, stream=None):
+    """forward.rs:482-545: head norms, rope, int8 K / V rows into the caches
+    (cs: a device copy of rope_table(...), as for rope)."""
     q_ld = n_heads * head_dim if q_ld is None else q_ld
     kv_ld = kv_heads * head_dim if kv_ld is None else kv_ld
-    call("fgm_cuda_qkv_post", _p(q), q_ld, _p(k), _p(v), kv_ld, rows, n_heads, kv_heads, head_dim,
-         _p(q_norm), _p(k_norm), eps, _p(inv_freq), _p(pos), ring, cap, _p(kc), kc_stride, _p(ks),
+    call("fgm_cuda_qkv_post_cs", _p(q), q_ld, _p(k), _p(v), kv_ld, rows, n_heads, kv_heads,
+         head_dim, _p(q_norm), _p(k_norm), eps, _p(inv_freq), _p(cs),
+         0 if cs is None else cs.shape[0], _p(pos), ring, cap, _p(kc), kc_stride, _p(ks),
          ks_stride, _p(vt), vt_stride, _p(vs), vs_stride, _s(stream))
 
 

@@ -337,6 +337,19 @@ int fgm_cuda_softcap(float *x, int rows, int n, float cap, void *stream);
 int fgm_cuda_rope(float *x, int x_ld, int rows, int n_heads, int head_dim, const float *inv_freq,
                   const int *pos, void *stream);
 
+/* Rope bit-identical to the reference: its cos / sin are this host's libm
+ * cosf / sinf of (float)pos * inv_freq[j] (ops.c:137-139), which the device
+ * cannot reproduce call for call.  fgm_cuda_rope_table fills, on the host
+ * (no device work), cs[p * head_dim + j] = cosf and cs[p * head_dim +
+ * head_dim/2 + j] = sinf for positions p in [0, positions) and j <
+ * head_dim/2.  Copied to the device, the table feeds fgm_cuda_rope_cs and
+ * fgm_cuda_qkv_post_cs; a row whose position lies outside [0, positions)
+ * falls back to the device evaluation of fgm_cuda_rope. */
+int fgm_cuda_rope_table(float *cs, int positions, int head_dim, const float *inv_freq);
+int fgm_cuda_rope_cs(float *x, int x_ld, int rows, int n_heads, int head_dim,
+                     const float *inv_freq, const float *cs, int positions, const int *pos,
+                     void *stream);
+
 /* ops.c:181-204, :641-644 (fgm_quant_act, fgm_quant_kv): rows of k f32 to
  * int8 with one scale per row (k % 64 == 0). */
 int fgm_cuda_quant_act(const float *x, int rows, int k, int8_t *q, float *scale, void *stream);
@@ -401,6 +414,14 @@ int fgm_cuda_qkv_post(float *q, int q_ld, float *k, float *v, int kv_ld, int row
                       const float *inv_freq, const int *pos, int ring, int cap, int8_t *kc,
                       size_t kc_stride, float *ks, size_t ks_stride, int8_t *vt, size_t vt_stride,
                       float *vs, size_t vs_stride, void *stream);
+/* fgm_cuda_qkv_post with rope's cos / sin from a device copy of
+ * fgm_cuda_rope_table (positions entries; see fgm_cuda_rope_cs). */
+int fgm_cuda_qkv_post_cs(float *q, int q_ld, float *k, float *v, int kv_ld, int rows,
+                         int n_heads, int kv_heads, int head_dim, const float *q_norm,
+                         const float *k_norm, float eps, const float *inv_freq, const float *cs,
+                         int positions, const int *pos, int ring, int cap, int8_t *kc,
+                         size_t kc_stride, float *ks, size_t ks_stride, int8_t *vt,
+                         size_t vt_stride, float *vs, size_t vs_stride, void *stream);
 
 /* ------------------------------------------------------------ row argmax
  * The token choice that follows the LM head (fgm-serve/src/engine.rs:75-83,

@@ -6,7 +6,7 @@ composed oracle step to the reference and by the GPU test that checks the
 device step against it."""
 import numpy as np
 
-DIMS = dict(M=3, H=256, NH=4, KVH=2, HD=64, FF=512, T=40, L=2, V=1024, G=64, eps=1e-6)
+DIMS = dict(M=3, H=256, NH=4, KVH=2, HD=64, FF=512, T=48, L=2, V=1024, G=64, eps=1e-6)
 
 
 def make_inputs(seed=11):

@@ -78,6 +78,15 @@ def test_rope_rows_with_their_positions(orc):
     torch.cuda.synchronize()
     want = np.stack([orc.rope(x[r], nh, hd, inv, int(pos[r])) for r in range(rows)])
     same(xd.cpu().numpy(), want, False, "rope")
+    # with the host's libm table: bit for bit (position 4095 lies outside the
+    # table and takes the device evaluation)
+    cs = dev(D.rope_table(1024, hd, inv))
+    xd = dev(x)
+    D.rope(xd, nh * hd, rows, nh, hd, dev(inv), dev(pos), cs=cs)
+    torch.cuda.synchronize()
+    got = xd.cpu().numpy()
+    same(got[:3], want[:3], True, "rope with the cos / sin table")
+    same(got[3:], want[3:], False, "rope past the table")
 
 
 def test_quant_act_and_store_v_t(orc):
@@ -308,6 +317,19 @@ def test_qkv_post_equals_the_separate_kernels(orc, nh, kvh, hd, ring, fused):
     oq = orc.rope(orc.rmsnorm(q.reshape(-1, hd), qn, eps).reshape(rows, -1)[0], nh, hd, inv_freq,
                   int(pos[0]))
     same(tq.cpu().numpy()[0], oq, False, "q against the oracle")
+    # rope's cos / sin from the host's libm table: q and k of every row equal
+    # the oracle's norms and rope bit for bit where the head norm has no
+    # scalar tail (head_dim % 16 == 0)
+    cs = dev(D.rope_table(cap, hd, inv_freq))
+    tq, tk, tv = dev(q), dev(k), dev(v)
+    kc, ks, vt, vs = caches()
+    D.qkv_post(tq, tk, tv, rows, nh, kvh, hd, dev(qn), dev(kn), eps, tinv, tpos, ring, slots,
+               kc, slots * kvd, ks, slots, vt, vt.shape[1], vs, slots, cs=cs)
+    torch.cuda.synchronize()
+    for got, x, n, w, what in ((tq, q, nh, qn, "q"), (tk, k, kvh, kn, "k")):
+        want = np.stack([orc.rope(orc.rmsnorm(x[r].reshape(-1, hd), w, eps).reshape(-1), n, hd,
+                                  inv_freq, int(pos[r])) for r in range(rows)])
+        same(got.cpu().numpy(), want, hd % 16 == 0, f"{what} with the table against the oracle")
 
 
 def test_qkv_post_writes_no_cache_entry_outside_the_capacity():
@@ -341,9 +363,11 @@ def test_decode_step_matches_the_oracle_end_to_end(orc):
     norm_prep, [gate|up] GEMM, gelu_mul_prep, down GEMM, norm_prep; then the
     LM head and softcap) against the same step composed from the oracle's
     restatements (pinned to the reference's own composed step in
-    test_oracle.py).  Rope's cos / sin are libm in the reference, so values
-    may move by a rounding and the int8 steps after it can turn that into
-    small differences: logits to a tolerance, tokens exactly."""
+    test_oracle.py).  Rope's cos / sin come from the host's libm table
+    (fgm_cuda_rope_table, what the reference calls per position) and every
+    row length and the attention window are multiples of 16 (no libm
+    tails), so the logits, tokens and the cache entries written are equal
+    bit for bit."""
     import decode_step
     d = decode_step.DIMS
     M, H, NH, KVH, HD, FF, T, L, V, G64, eps = (d[k] for k in
@@ -357,6 +381,7 @@ def test_decode_step_matches_the_oracle_end_to_end(orc):
     dl = [{k: ((t(v[0]), t(v[1])) if isinstance(v, tuple) else t(v)) for k, v in lw.items()}
           for lw in inp["layers"]]
     tx, tinv = t(inp["x"]), t(inp["inv_freq"])
+    cs = t(D.rope_table(T, HD, inp["inv_freq"]))
     tpos = torch.full((M,), pos, dtype=torch.int32, device="cuda")
     tkc, tks, tvt, tvs = t(inp["kc"]), t(inp["ks"]), t(inp["vt"]), t(inp["vs"])
     qs = torch.empty(M, device="cuda")
@@ -370,7 +395,7 @@ def test_decode_step_matches_the_oracle_end_to_end(orc):
         D.gemm_q4g(M, QKV, H, pa[H], qs, lw["qkv"][0], lw["qkv"][1], G64, qkv)
         D.qkv_post(qkv[:, :QD], qkv[:, QD:QD + KVD], qkv[:, QD + KVD:], M, NH, KVH, HD, lw["qn"],
                    lw["kn"], eps, tinv, tpos, 0, T, tkc[li], T * KVD, tks[li], T, tvt[li],
-                   vslots * KVD, tvs[li], T, q_ld=QKV, kv_ld=QKV)
+                   vslots * KVD, tvs[li], T, q_ld=QKV, kv_ld=QKV, cs=cs)
         D.attend_q8(attn, QD, qkv, QKV, tkc[li], T * KVD, tks[li], T, tvt[li], vslots * KVD,
                     tvs[li], T, M, NH, KVH, HD, 0, T)
         D.prep_rows(attn, QD, qs, pa[H], M, QD, 0)
@@ -385,8 +410,9 @@ def test_decode_step_matches_the_oracle_end_to_end(orc):
     D.softcap(logits, M, V, 30.0)
     torch.cuda.synchronize()
     got = logits.cpu().numpy()
-    assert np.allclose(got, want, rtol=0, atol=0.05), f"max |diff| {np.abs(got - want).max()}"
+    bad = got.view(np.uint32) != want.view(np.uint32)
+    assert not bad.any(), f"{int(bad.sum())} logits differ, max |diff| {np.abs(got - want).max()}"
     assert np.array_equal(orc.argmax_rows(got), want_tok)
     got_ks = tks.cpu().numpy()
     assert np.array_equal(got_ks[:, :, :pos], inp["ks"][:, :, :pos])  # old slots untouched
-    assert np.allclose(got_ks[:, :, pos], want_ks[:, :, pos], rtol=1e-2)
+    assert np.array_equal(got_ks.view(np.uint32), want_ks.view(np.uint32))

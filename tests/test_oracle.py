@@ -267,3 +267,24 @@ def test_composed_decode_step_matches_the_reference(orc, ref):
     for g, w, what in zip(got, want, ("logits", "K cache", "K scales", "V cache", "V scales")):
         assert np.array_equal(g.view(np.uint32) if g.dtype == np.float32 else g,
                               w.view(np.uint32) if w.dtype == np.float32 else w), what
+
+
+@pytest.mark.parametrize("hd", [64, 256])
+def test_rope_table_holds_the_references_cos_and_sin(orc, hd):
+    """fgm_cuda_rope_table (host code of the CUDA library, no device work)
+    against the cos / sin the oracle's rope applies (a unit vector [1 | 0]
+    rotates to [cos | sin] exactly), and against the reference's own
+    fgm_rope where it is built."""
+    import fastgemma_b200.device as D
+    from oracle.oracle import load_reference
+    inv = (1.0 / (10000 ** (np.arange(0, hd, 2) / hd))).astype(np.float32)
+    inv[-4:] = 0.0
+    positions = 600
+    tab = D.rope_table(positions, hd, inv)
+    unit = np.concatenate([np.ones(hd // 2), np.zeros(hd // 2)]).astype(np.float32)
+    ref = load_reference()
+    for p in list(range(0, positions, 37)) + [positions - 1]:
+        want = orc.rope(unit, 1, hd, inv, p)
+        assert np.array_equal(tab[p].view(np.uint32), want.view(np.uint32)), p
+        if ref is not None:
+            assert np.array_equal(tab[p].view(np.uint32), ref.rope(unit, 1, hd, inv, p).view(np.uint32))
