@@ -179,6 +179,7 @@ struct TcParams {
   int tma_store;          // write C through TMA stores (set by the launcher)
   int splits;             // K split across a cluster of this many CTAs (set by the launcher)
   int out_v4;             // C rows 16-byte aligned: vector stores allowed (set by the launcher)
+  int m_fast;             // grid x walks the M tiles, y the N tiles (set by the launcher)
 };
 
 }  // namespace fgm

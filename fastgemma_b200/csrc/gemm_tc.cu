@@ -110,8 +110,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KS = (p.K + kTcBK - 1) / kTcBK;
-  const int m0 = blockIdx.y * BM;
-  const int n0 = p.nb0 * 16 + blockIdx.x * NB;
+  // tile coordinates: with m_fast the CTAs that run together share their
+  // weight tile (B streams from HBM once; the activations stay in L2)
+  const int tile_n = p.m_fast ? blockIdx.y : blockIdx.x;
+  const int m0 = (p.m_fast ? blockIdx.x : blockIdx.y) * BM;
+  const int n0 = p.nb0 * 16 + tile_n * NB;
   // K slice of this CTA: the cluster's CTAs split the tile's K range evenly
   const int splits = p.splits, z = splits > 1 ? (int)tc::cluster_ctarank() : 0;
   const int ks0 = (int)((long)KS * z / splits), ks1 = (int)((long)KS * (z + 1) / splits);
@@ -295,7 +298,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncthreads();
           if (threadIdx.x == 0) {
-            const int col0 = blockIdx.x * NB;  // relative to the output map's origin
+            const int col0 = tile_n * NB;  // relative to the output map's origin
             for (int half = 0; half < 2; half++)
               for (int b2 = 0; b2 < 2; b2++) {
                 const int b = half * 4 + cb * 2 + b2;  // 32-column block of the tile
@@ -314,7 +317,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     if (threadIdx.x == 0 && ok && !s_fail) {
       if constexpr (NB == 128) {  // (256-wide tiles stored theirs pass by pass)
-        const int col0 = blockIdx.x * NB;  // relative to the output map's origin
+        const int col0 = tile_n * NB;  // relative to the output map's origin
         for (int b = 0; b < NB / 32; b++)
           if (p.nb0 * 16 + col0 + b * 32 < p.n_end)
             tc::tma_store_2d(&tmC, smem + (size_t)b * (BM * 128), col0 + b * 32, m0);
@@ -620,8 +623,9 @@ cudaError_t launch_tc_h(const TcParams &p, const CUtensorMap &tmA, const CUtenso
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int ncols = p.n_end - p.nb0 * 16;
+  const unsigned nt = (unsigned)((ncols + NB - 1) / NB), mt = (unsigned)((p.M + 128 * H - 1) / (128 * H));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((ncols + NB - 1) / NB, (p.M + 128 * H - 1) / (128 * H), p.splits);
+  cfg.gridDim = p.m_fast ? dim3(mt, nt, p.splits) : dim3(nt, mt, p.splits);
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -651,6 +655,9 @@ cudaError_t launch_q8c_tc(const TcParams &p_in, int lda, const CUtensorMap &tmB,
   if (c.smem + kTcStaticReserve > smem_limit) return cudaErrorInvalidConfiguration;
   p.stages = c.stages;
   p.splits = c.splits;
+  // M tiles fastest when there are several and no K split: a wave's CTAs then
+  // share weight tiles instead of each streaming its own
+  p.m_fast = c.splits == 1 && p.M > 128 * c.H;
   const int BM = 128 * c.H;
   CUtensorMap tmA, tmC;
   if (!encode_rows_map(&tmA, p.A, p.M, p.K, lda, BM)) return cudaErrorInvalidValue;
