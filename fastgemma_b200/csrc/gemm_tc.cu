@@ -393,6 +393,212 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
+// ------------------------------------------------- persistent 128 x 256 tiles
+// For outputs with more 128 x 256 tiles than SMs: one CTA per SM walks the
+// tiles (M tiles fastest, so the CTAs running together share weight tiles)
+// with two int32 accumulators in tensor memory (2 x 256 of the 512 columns),
+// so one tile's epilogue overlaps the next tile's MMAs.  Warp 0 (one lane)
+// streams the A / B stages of every tile through the ring; warp 1 (one lane)
+// issues the MMAs of tile i into accumulator i % 2 once the epilogue has
+// drained that accumulator (tile i - 2) and commits it; warps 4-7 drain an
+// accumulator (warp w: TMEM lanes 32(w%4)..), scale it and write the tile
+// through two 16 KB staging buffers of 32 columns with TMA stores.  Each
+// staging buffer is rewritten only after the store that last read it is
+// done reading.  Every wait is bounded; a warp that gives up raises the
+// flag, and the producer lets the loads it issued land before the CTA ends.
+constexpr int kTpStage = 128 * kTcBK + 256 * kTcBK;  // A 128 rows + B 256 rows
+constexpr int kTpOut = 128 * 128;                    // 32 f32 columns x 128 rows
+
+__device__ __forceinline__ void epi_sync() {  // the four epilogue warps
+  asm volatile("bar.sync 2, 128;" ::: "memory");
+}
+
+// True on every epilogue thread when any of them passes true.
+__device__ __forceinline__ bool epi_any(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 2, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v)
+      : "memory");
+  return r != 0;
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    q8c_tc_persistent(const __grid_constant__ CUtensorMap tmA,
+                      const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmC, const TcParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int S = p.stages;
+  uint8_t *stage_out = smem + (size_t)S * kTpStage;  // 2 x kTpOut
+  uint64_t *full = reinterpret_cast<uint64_t *>(stage_out + 2 * kTpOut);
+  uint64_t *empty = full + S;
+  uint64_t *tfull = empty + S;   // [2] accumulator b holds a finished tile
+  uint64_t *tempty = tfull + 2;  // [2] accumulator b is drained (4 epilogue warps arrive)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+  __shared__ int s_fail;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KS = (p.K + kTcBK - 1) / kTcBK;
+  const int ncols = p.n_end - p.nb0 * 16;
+  const int mt = (p.M + 127) / 128, nt = (ncols + 255) / 256;
+  const int tiles = mt * nt;
+
+  if (threadIdx.x == 0) {
+    s_fail = 0;
+    for (int s = 0; s < S; s++) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      tc::mbar_init(&tfull[b], 1);
+      tc::mbar_init(&tempty[b], 4);
+    }
+    tc::fence_mbar_init();
+    tc::prefetch_tmap(&tmA);
+    tc::prefetch_tmap(&tmB);
+    tc::prefetch_tmap(&tmC);
+  }
+  if (warp == 2) {
+    tc::tmem_alloc(tmem_slot, 512);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  if (warp == 0) {  // ------------------------------------------------ producer
+    if (lane == 0) {
+      asm volatile("griddepcontrol.wait;" ::: "memory");  // activations from earlier kernels
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int m0 = (t % mt) * 128, n0 = p.nb0 * 16 + (t / mt) * 256;
+        for (int k = 0; k < KS; k++, it++) {
+          const int s = (int)(it % S);
+          if (!tc::mbar_wait(&empty[s], ((it / S) & 1) ^ 1)) {
+            ok = false;
+            break;
+          }
+          uint8_t *sa = smem + (size_t)s * kTpStage;
+          tc::mbar_expect_tx(&full[s], kTpStage);
+          tc::tma_load_2d(sa, &tmA, &full[s], k * kTcBK, m0);
+          tc::tma_load_2d(sa + 128 * kTcBK, &tmB, &full[s], k * kTcBK, n0);
+          tc::tma_load_2d(sa + 256 * kTcBK, &tmB, &full[s], k * kTcBK, n0 + 128);
+        }
+      }
+      if (!ok) {
+        s_fail = 1;
+        // the last loads issued land before the CTA can end
+        for (uint32_t j = it > (uint32_t)S ? it - S : 0; j < it; j++)
+          tc::mbar_wait(&full[j % S], (j / S) & 1, 100000000ull);
+      }
+    }
+  } else if (warp == 1) {  // ------------------------------------------ MMA
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_i8(128, 256);
+      uint32_t it = 0, i = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, i++) {
+        const uint32_t b = i & 1;
+        if (!tc::mbar_wait(&tempty[b], ((i >> 1) & 1) ^ 1)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        for (int k = 0; k < KS; k++, it++) {
+          const int s = (int)(it % S);
+          if (!tc::mbar_wait(&full[s], (it / S) & 1)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const uint32_t sa = tc::smem_u32(smem + (size_t)s * kTpStage);
+          const uint32_t sb = sa + 128 * kTcBK;
+#pragma unroll
+          for (int j = 0; j < kTcBK / 32; j++)
+            tc::mma_i8(tmem + b * 256, tc::sdesc_sw128(sa + j * 32), tc::sdesc_sw128(sb + j * 32),
+                       idesc, (k | j) != 0);
+          tc::mma_commit(&empty[s]);
+        }
+        if (ok) tc::mma_commit(&tfull[b]);
+      }
+      if (!ok) s_fail = 1;
+    }
+  } else if (warp >= 4) {  // ------------------------------------- epilogue
+    const int q = warp & 3, ml = q * 32 + lane, et = threadIdx.x - 128;
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // a_scale from earlier kernels
+    uint32_t i = 0, sb = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, i++) {
+      const uint32_t b = i & 1;
+      const int m0 = (t % mt) * 128, tn = t / mt, n0 = p.nb0 * 16 + tn * 256;
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(&tfull[b], (i >> 1) & 1));
+      // the four warps agree before any of them leaves the named barriers
+      if (epi_any(!ok)) {
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      const int m = m0 + ml;
+      const float as = (p.a_scale && m < p.M) ? p.a_scale[m] : 0.0f;
+#pragma unroll 1
+      for (int c = 0; c < 8; c++) {  // 32-column chunks
+        uint32_t v[32];
+        tc::tmem_ld_x32(tmem + ((uint32_t)(q * 32) << 16) + b * 256 + c * 32, v);
+        tc::tmem_wait_ld();
+        if (c == 7) {  // the accumulator is free for tile i + 2
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&tempty[b]);
+        }
+        const int nc = n0 + c * 32;
+        if (nc >= p.n_end) continue;  // past the last column (uniform over the warps)
+        float bs[32];
+#pragma unroll
+        for (int e = 0; e < 32; e++) bs[e] = nc + e < p.n_end ? __ldg(p.b_scale + nc + e) : 0.0f;
+        // staging buffer sb % 2 (sb counts the stores issued): free once the
+        // store before the latest one has read it
+        if (et == 0) tc::bulk_wait_read_1();
+        epi_sync();
+        uint8_t *rowp = stage_out + (size_t)(sb & 1) * kTpOut + (size_t)ml * 128;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          float o[4];
+#pragma unroll
+          for (int e = 0; e < 4; e++)
+            o[e] = __fmul_rn(__int2float_rn((int32_t)v[j * 4 + e]), __fmul_rn(bs[j * 4 + e], as));
+          *reinterpret_cast<float4 *>(rowp + ((j ^ (ml & 7)) << 4)) =
+              make_float4(o[0], o[1], o[2], o[3]);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        epi_sync();
+        if (et == 0) {
+          tc::tma_store_2d(&tmC, stage_out + (size_t)(sb & 1) * kTpOut, tn * 256 + c * 32, m0);
+          tc::bulk_commit();
+        }
+        sb++;
+      }
+    }
+    if (!ok) s_fail = 1;
+    if (et == 0) tc::bulk_wait_all();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (s_fail && threadIdx.x == 0 && p.err) atomicExch(p.err, 2);
+  if (warp == 2) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
 // .fgm int8 tiles -> row-major [N][K]: output word (n, k/4) reads tile word
 // (k%64/4, n%16) of tile (n/16, k/64).
 __global__ void q8c_tiles_to_rows(const uint32_t *__restrict__ src, uint32_t *__restrict__ dst,
@@ -616,6 +822,57 @@ static bool encode_out_map(CUtensorMap *map, void *base, int rows, int cols, siz
              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+size_t tp_smem_bytes(int stages) {
+  return (size_t)stages * kTpStage + 2 * (size_t)kTpOut + (size_t)(2 * stages + 4) * 8 + 16 + 1024;
+}
+
+// The persistent kernel when it applies (128 x 256 tiles, no K split, TMA
+// stores, more tiles than SMs); false: use the one-tile-per-CTA kernel.
+// FGM_CUDA_TC_PERSISTENT=0 turns it off.
+static bool launch_tc_persistent(const TcParams &p, const CUtensorMap &tmA, const CUtensorMap &tmB,
+                                 const CUtensorMap &tmC, int num_sms, size_t smem_limit, bool pdl,
+                                 cudaStream_t st, cudaError_t *err) {
+  static const int enabled = [] {
+    const char *e = getenv("FGM_CUDA_TC_PERSISTENT");
+    return e ? atoi(e) : 1;
+  }();
+  const int ncols = p.n_end - p.nb0 * 16;
+  const long tiles = (long)((p.M + 127) / 128) * ((ncols + 255) / 256);
+  if (!enabled || p.splits != 1 || !p.tma_store || p.acc || tiles <= num_sms) return false;
+  int stages = 6;
+  static const size_t stat = [] {  // the kernel's static shared memory
+    cudaFuncAttributes a{};
+    if (cudaFuncGetAttributes(&a, q8c_tc_persistent) != cudaSuccess) {
+      cudaGetLastError();
+      return (size_t)4096;
+    }
+    return (size_t)a.sharedSizeBytes;
+  }();
+  // smem_limit is the opt-in size less 1 KB of headroom for static shared
+  // memory; the static size is counted exactly here instead
+  const size_t optin = smem_limit + 1024;
+  while (stages > 2 && tp_smem_bytes(stages) + stat > optin) stages--;
+  const size_t smem = tp_smem_bytes(stages);
+  if (smem + stat > optin) return false;
+  TcParams q = p;
+  q.stages = stages;
+  *err = cudaFuncSetAttribute(q8c_tc_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)smem);
+  if (*err != cudaSuccess) return true;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(tiles < num_sms ? tiles : num_sms));
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  *err = cudaLaunchKernelEx(&cfg, q8c_tc_persistent, tmA, tmB, tmC, q);
+  return true;
+}
+
 template <int H, int NB>
 cudaError_t launch_tc_h(const TcParams &p, const CUtensorMap &tmA, const CUtensorMap &tmB,
                         const CUtensorMap &tmC, size_t smem, bool pdl, cudaStream_t st) {
@@ -667,7 +924,11 @@ cudaError_t launch_q8c_tc(const TcParams &p_in, int lda, const CUtensorMap &tmB,
   p.tma_store = !p.acc && p.out_v4 && p.splits == 1 &&
                 encode_out_map(&tmC, origin, p.M, p.n_end - p.nb0 * 16, (size_t)p.ldc * 4, BM);
   if (!p.tma_store) memset(&tmC, 0, sizeof(tmC));
-  if (c.NB == 256) return launch_tc_h<1, 256>(p, tmA, tmB, tmC, c.smem, pdl, st);
+  if (c.NB == 256) {
+    cudaError_t e = cudaSuccess;
+    if (launch_tc_persistent(p, tmA, tmB, tmC, num_sms, smem_limit, pdl, st, &e)) return e;
+    return launch_tc_h<1, 256>(p, tmA, tmB, tmC, c.smem, pdl, st);
+  }
   return c.H == 2 ? launch_tc_h<2, kTcBN>(p, tmA, tmB, tmC, c.smem, pdl, st)
                   : launch_tc_h<1, kTcBN>(p, tmA, tmB, tmC, c.smem, pdl, st);
 }

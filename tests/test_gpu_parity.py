@@ -546,10 +546,16 @@ def test_launch_counter_counts_kernels():
                                              (300, 2048, 384, 0, 24, 16), (1024, 2048, 256, 8, 16, 16),
                                              (256, 8192, 256, 4, 12, 3), (130, 4096, 1024, 0, 64, 5),
                                              (256, 16384, 2048, 0, 128, 16),
-                                             (256, 2048, 6144, 0, 384, 16)])
+                                             (256, 2048, 6144, 0, 384, 16),
+                                             # more 128 x 256 tiles than SMs: the persistent
+                                             # kernel (153 tiles, the last 192 columns wide;
+                                             # 150 tiles from n-block 8)
+                                             (384, 512, 12992, 0, 812, 16),
+                                             (200, 768, 19456, 8, 1208, 4)])
 def test_q8c_tensor_core_bit_exact(orc, M, K, N, n0, n1, cpad):
     """M >= 64 with a prepared weight runs tcgen05.mma kind::i8 (K split over a
-    cluster when the output has few tiles); f32 outputs and int32
+    cluster when the output has few tiles, one persistent CTA per SM with two
+    tensor-memory accumulators when it has many); f32 outputs and int32
     accumulators must match the reference arithmetic exactly, with aligned
     and unaligned output rows (ldc = N + cpad)."""
     rng = np.random.default_rng(M * 31 + K + N)
