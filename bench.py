@@ -283,7 +283,7 @@ def main():
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
     if args.profile_chain:
-        step, _ = build_decode_chain(dev, gen, args.chain_context)
+        step, _, _ = build_decode_chain(dev, gen, args.chain_context)
         step()
         step()
         torch.cuda.synchronize()
@@ -886,9 +886,15 @@ def bench_config4(args, dev, world, rank):
                         f"whole-width GEMM on each rank's own GPU, bit for bit"}
 
 
-def build_decode_chain(dev, gen, T, L=30):
+def build_decode_chain(dev, gen, T, L=30, world=1, rank=0):
     """The synthetic config-3 stack on `dev` (random-init weights and caches)
-    and its decode step; returns (step, weight bytes per step)."""
+    and its decode step; returns (step, weight bytes per step, extras).
+    With world > 1 the layers are replicated and the LM head is
+    column-sharded over the ranks: each rank's fused GEMM + NVLink gather
+    (fgm_cuda_gemm_q4g_gather) leaves every rank the whole logits, which
+    each rank softcaps and scans as at one GPU.  The fused call alternates
+    two output slots, counted on the device, so a graph replays the step
+    in pairs (extras["calls_per_cycle"] = 2)."""
     import torch
     from fastgemma_b200 import _lib
     from fastgemma_b200 import device as D
@@ -923,6 +929,16 @@ def build_decode_chain(dev, gen, T, L=30):
         lw["vs"] = torch.empty((M, T), device=dev).uniform_(0.001, 0.02, generator=gen)
         layers.append(lw)
     lm_w, lm_s = q4(H, LM_HEAD_N)
+    sh = None
+    if world > 1:  # this rank's column shard of the LM head (n-blocks [nb0, nb1))
+        from fastgemma_b200 import shard as S
+        nb0, nb1 = S.shard_ranges(LM_HEAD_N // 16, world)[rank]
+        kb = H // 64
+        w_sh = lm_w[nb0 * kb * 512:nb1 * kb * 512].clone()
+        s_sh = lm_s[:, nb0 * 16:nb1 * 16].contiguous()
+        sh = S.ColumnShardedGemm("q4g", None, None, LM_HEAD_N, H, GROUP, rank=rank, world=world,
+                                 device=dev, shard=(w_sh, s_sh), fused=True, max_rows=M)
+    last = {}
     final_norm = norm(H)
     inv_freq = (1.0 / (10000.0 ** (torch.arange(0, HD, 2, device=dev, dtype=torch.float32) / HD)))
     pos = torch.full((M,), T - 1, dtype=torch.int32, device=dev)
@@ -965,14 +981,36 @@ def build_decode_chain(dev, gen, T, L=30):
             D.gemm_q4g(M, H, FF, pa[FF], qs, lw["down"][0], lw["down"][1], GROUP, dn)
             nxt = layers[li + 1]["in"] if li + 1 < L else final_norm
             D.norm_prep(x, dn, lw["pff"], nxt, M, H, 1e-6, qs, pa[H])
-        D.gemm_q4g(M, LM_HEAD_N, H, pa[H], qs, lm_w, lm_s, GROUP, logits)
-        D.softcap(logits, M, LM_HEAD_N, 30.0)
-        _lib.call("fgm_cuda_argmax_partials", logits.data_ptr(), M, LM_HEAD_N, LM_HEAD_N, 0,
+        if sh is None:
+            D.gemm_q4g(M, LM_HEAD_N, H, pa[H], qs, lm_w, lm_s, GROUP, logits)
+            lg = logits
+        else:  # this rank's columns, gathered from every rank over NVLink
+            lg = sh.fused_call(M, pa[H], qs, stream=torch.cuda.current_stream())
+        D.softcap(lg, M, LM_HEAD_N, 30.0)
+        _lib.call("fgm_cuda_argmax_partials", lg.data_ptr(), M, LM_HEAD_N, LM_HEAD_N, 0,
                   avals.data_ptr(), aidx.data_ptr(), stream())
         _lib.call("fgm_cuda_argmax_merge", avals.data_ptr(), aidx.data_ptr(), M, parts,
                   tok.data_ptr(), stream())
-    wbytes = L * sum(sum(q4g_bytes(k_, n_)) for _, k_, n_ in shapes) + sum(q4g_bytes(H, LM_HEAD_N))
-    return step, wbytes
+        last["logits"] = lg
+
+    def whole_tokens():
+        """The step's LM head as one whole-width GEMM on this rank from the
+        same final packed rows, softcapped and scanned: (logits, tokens)."""
+        D.gemm_q4g(M, LM_HEAD_N, H, pa[H], qs, lm_w, lm_s, GROUP, logits)
+        D.softcap(logits, M, LM_HEAD_N, 30.0)
+        wt = torch.empty(M, dtype=torch.int32, device=dev)
+        _lib.call("fgm_cuda_argmax_partials", logits.data_ptr(), M, LM_HEAD_N, LM_HEAD_N, 0,
+                  avals.data_ptr(), aidx.data_ptr(), stream())
+        _lib.call("fgm_cuda_argmax_merge", avals.data_ptr(), aidx.data_ptr(), M, parts,
+                  wt.data_ptr(), stream())
+        return logits, wt
+
+    # per-rank weight bytes of one step (the LM head's share only)
+    lm_bytes = sum(q4g_bytes(H, LM_HEAD_N)) * (1.0 if sh is None else sh.cols / LM_HEAD_N)
+    wbytes = L * sum(sum(q4g_bytes(k_, n_)) for _, k_, n_ in shapes) + lm_bytes
+    extras = {"tok": tok, "last": last, "whole_tokens": whole_tokens, "shard": sh,
+              "calls_per_cycle": 1 if sh is None else 2}
+    return step, wbytes, extras
 
 
 def bench_decode_chain(args, dev, gen, world):
@@ -983,44 +1021,78 @@ def bench_decode_chain(args, dev, gen, world):
     the GEMMs (forward.rs:469-654): norms, per-head q/k/v norms, rope, int8
     KV-cache writes, the int8-KV attention over `--chain-context` positions,
     gelu_mul, residual adds, final softcap.  Random-init weights, synthetic
-    caches; one CUDA graph per step.  Each rank runs its own 8 sequences."""
+    caches.  At N > 1 GPUs the step is ONE step across the N ranks: the 30
+    layers are replicated (every rank holds the same seeded model and rows)
+    and the LM head is column-sharded, fused with its NVLink gather; the
+    tokens then equal those of one GPU, which the line reports for
+    comparison.  The graph holds `calls_per_cycle` steps (two when the fused
+    gather alternates its slots)."""
     import torch
     from fastgemma_b200 import _lib
     L, M, T = 30, M_DECODE, args.chain_context
-    step, wbytes = build_decode_chain(dev, gen, T, L)
+    rank = torch.distributed.get_rank() if world > 1 else 0
+    cgen = torch.Generator(device=dev)
+    cgen.manual_seed(4321)  # the same model and rows on every rank
+    step, wbytes, ex = build_decode_chain(dev, cgen, T, L, world=world, rank=rank)
+    per = ex["calls_per_cycle"]
     side = torch.cuda.Stream(device=dev)
     lib = _lib.lib()
     with torch.cuda.stream(side):
         c0 = lib.fgm_cuda_launch_count()
         step()
         ours = lib.fgm_cuda_launch_count() - c0
+        for _ in range(2 * per - 1):  # an even number of fused calls before the graph
+            step()
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=side):
-        step()
+        for _ in range(per):
+            step()
     with torch.cuda.stream(side):
         for _ in range(3):
             g.replay()
     torch.cuda.synchronize()
-    steps = max(5, args.steps // 10)
+    cycles = max(5, args.steps // 10)
+    if world > 1:
+        torch.distributed.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(side):
         e0.record(side)
-        for _ in range(steps):
+        for _ in range(cycles):
             g.replay()
         e1.record(side)
     torch.cuda.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / (cycles * per)
+    # outside the timed region: the last step's tokens against the whole-width
+    # LM head of the same final rows on this rank (logits bit for bit too)
+    tokens = ex["tok"].cpu().tolist()
+    got_logits = ex["last"]["logits"].clone()
+    with torch.cuda.stream(side):
+        whole, wt = ex["whole_tokens"]()
+    torch.cuda.synchronize()
+    same = bool(torch.equal(got_logits.view(torch.int32), whole.view(torch.int32))
+                and wt.cpu().tolist() == tokens)
+    parity = _all_ranks(same, world, dev)
     del g
-    return {"value": world * M / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
-            "weight_gbs": world * wbytes / (ms * 1e-3) / 1e9, "steps": steps,
-            "library_launches_per_step": ours, "context": T,
+    if ex["shard"] is not None:
+        ex["shard"].close()
+    return {"value": M / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+            "weight_gbs_per_gpu": wbytes / (ms * 1e-3) / 1e9, "steps": cycles * per,
+            "library_launches_per_step": ours, "context": T, "tokens": tokens,
+            "parity": parity,
+            "parity_check": "outside the timed region, every rank's LM-head logits of the last "
+                            "step (after softcap) and its tokens equal a whole-width gemm_q4g "
+                            "of the same final rows on that rank, bit for bit",
+            "parallelism": ("one GPU" if world == 1 else
+                            f"one step across {world} GPUs: layers replicated, LM head "
+                            f"column-sharded {world} ways with the fused NVLink gather"),
             "workload": f"BASELINE config 3: 30 layers (hidden 2048, 8 q heads / 2 KV heads of "
                         f"256, MLP 8192, int4 g64 projections), {M} sequences at context {T}, "
-                        f"norms, rope, int8 KV writes, int8-KV attention, gelu_mul, residuals, "
-                        f"int4 LM head 262144 x 2048, softcap, argmax; q|k|v and gate|up as "
-                        f"one weight each, the glue between GEMMs fused per row; one CUDA graph per "
-                        f"step"}
+                        f"norms, rope (host libm cos/sin table), int8 KV writes, int8-KV "
+                        f"attention, gelu_mul, residuals, int4 LM head 262144 x 2048, softcap, "
+                        f"argmax; q|k|v and gate|up as one weight each, the glue between GEMMs "
+                        f"fused per row; the same seeded model on every rank; one CUDA graph of "
+                        f"{per} step(s) replayed"}
 
 
 def bench_prefill(args, dev, gen, world):
