@@ -74,6 +74,8 @@ def parse():
     ap.add_argument("--no-config0", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the config-1 M x shape sweep")
     ap.add_argument("--no-config4", action="store_true")
+    ap.add_argument("--config4-ms", default="256,1024,4096",
+                    help="config-4 row counts (comma-separated)")
     ap.add_argument("--no-per-call", action="store_true",
                     help="skip the config-1 step timed as per-call launches")
     ap.add_argument("--warm", action="store_true",
@@ -834,7 +836,7 @@ def bench_config4(args, dev, world, rank):
     D.q8c_prepare(w, cols, K)
     res = {}
     steps = max(3, args.steps // 20)
-    for M in (256, 1024, 4096):
+    for M in (int(v) for v in args.config4_ms.split(",")):
         x = torch.randn((M, K), device=dev, generator=g)
         qa = torch.empty((M, K), dtype=torch.int8, device=dev)
         qs = torch.empty(M, device=dev)
