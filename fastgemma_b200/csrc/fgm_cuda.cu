@@ -1339,8 +1339,9 @@ int fgm_cuda_worklist_create(int M, const fgm_cuda_work *w, int n, void **list) 
   const size_t o_items = 0, b_items = sizeof(WlItem) * (size_t)n;
   const size_t o_segs = align256(o_items + b_items), b_segs = sizeof(WlSeg) * wl->plan.segs.size();
   const size_t o_off = align256(o_segs + b_segs), b_off = sizeof(int) * wl->plan.seg_off.size();
-  const size_t o_pj = align256(o_off + b_off), b_pj = sizeof(int) * wl->plan.pro_jobs.size();
-  const size_t o_cnt = align256(o_pj + b_pj), b_cnt = sizeof(unsigned) * ((size_t)n + 2);
+  const size_t o_cr = align256(o_off + b_off), b_cr = sizeof(int) * wl->plan.crows.size();
+  const size_t o_co = align256(o_cr + b_cr), b_co = sizeof(int) * wl->plan.crow_off.size();
+  const size_t o_cnt = align256(o_co + b_co), b_cnt = sizeof(unsigned) * ((size_t)n + 2);
   const size_t total = o_cnt + b_cnt;
   if (cudaMalloc(&wl->mem, total) != cudaSuccess) {
     cudaGetLastError();
@@ -1356,8 +1357,10 @@ int fgm_cuda_worklist_create(int M, const fgm_cuda_work *w, int n, void **list) 
     e = cudaMemcpy(d + o_segs, wl->plan.segs.data(), b_segs, cudaMemcpyHostToDevice);
   if (e == cudaSuccess)
     e = cudaMemcpy(d + o_off, wl->plan.seg_off.data(), b_off, cudaMemcpyHostToDevice);
-  if (e == cudaSuccess && b_pj)
-    e = cudaMemcpy(d + o_pj, wl->plan.pro_jobs.data(), b_pj, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && b_cr)
+    e = cudaMemcpy(d + o_cr, wl->plan.crows.data(), b_cr, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(d + o_co, wl->plan.crow_off.data(), b_co, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemset(d + o_cnt, 0, b_cnt);
   if (e != cudaSuccess) {
     cudaFree(wl->mem);
@@ -1371,8 +1374,8 @@ int fgm_cuda_worklist_create(int M, const fgm_cuda_work *w, int n, void **list) 
   p.n_items = n;
   p.segs = reinterpret_cast<const WlSeg *>(d + o_segs);
   p.seg_off = reinterpret_cast<const int *>(d + o_off);
-  p.pro_jobs = reinterpret_cast<const int *>(d + o_pj);
-  p.n_pro = (int)wl->plan.pro_jobs.size();
+  p.crows = reinterpret_cast<const int *>(d + o_cr);
+  p.crow_off = reinterpret_cast<const int *>(d + o_co);
   p.done = reinterpret_cast<unsigned *>(d + o_cnt);
   p.ctas_done = p.done + n;
   p.abort = reinterpret_cast<int *>(p.done + n + 1);
@@ -1395,7 +1398,7 @@ int fgm_cuda_worklist_run(void *list, void *stream) {
                 dev);
   const cudaError_t e = launch_worklist(wl->params, wl->plan, use_pdl(), (cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_fail(e, "worklist launch");
-  count_launch(wl->params.n_pro ? 2 : 1);
+  count_launch();
   return FGM_CUDA_OK;
 }
 

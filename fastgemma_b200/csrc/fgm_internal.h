@@ -261,15 +261,15 @@ struct WlParams {
   int *err;                // device status word
   int M, warps, stages;    // consumer warps per CTA, weight ring stages per warp
   int a_ring;              // bytes of the activation ring (segments staged FIFO)
-  const int *pro_jobs;     // prologue: rows of the preps that depend on nothing (item*16 + row)
-  int n_pro;
+  const int *crows;        // rows of the preps that depend on nothing (item*16 + row):
+  const int *crow_off;     // CTA c prepares crows[crow_off[c], crow_off[c + 1]) first
 };
 struct WlPlan {
   int M, MT, grid, warps, stages, a_ring;
   size_t smem;
   std::vector<WlSeg> segs;
   std::vector<int> seg_off;
-  std::vector<int> pro_jobs;
+  std::vector<int> crows, crow_off;
 };
 // Fills the schedule and launch geometry; returns an error text or nullptr.
 const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num_sms,

@@ -58,6 +58,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <functional>
 #include <cstdlib>
 #include <type_traits>
 #include <cstring>
@@ -363,79 +364,152 @@ __device__ void prep_row(const WlItem &it, int r, int M, int lane) {
   if (lane == 0) it.qs[r] = s;
 }
 
-// ------------------------------------------------------------- prologue
-// The preps that depend on nothing in the list (inputs written before the
-// run) do not wait inside the persistent kernel: one launch ahead of it
-// prepares all their rows at once, a CTA of 8 warps per row, each warp a
-// 1/8 of the row held in registers, the row maximum met in shared memory --
-// one memory round trip per row instead of a warp's serial passes.  The
-// persistent kernel follows with programmatic dependent launch; its weight
-// rings fill while this runs, its activation staging waits for it.
-constexpr int kProWarps = 8;
-constexpr int kProChunks = 8;  // 128-value chunks a warp holds in registers
+// ------------------------------------------------------- cooperative rows
+// The preps that depend on nothing in the list (their inputs were written
+// before the run) are prepared at the start of the run by every CTA's
+// consumer warps together: the host deals their real rows (rows past M are
+// never read by the list's GEMMs) to the CTAs by cost, each CTA a few rows.
+// The consumer warps first fill their weight rings (the weights never come
+// from earlier kernels, so they stream while a previous launch finishes),
+// then walk the (row, 128-value chunk) pairs of the CTA's rows with a
+// stride of one warp each: a first pass keeps each row's largest |x| in
+// shared memory, a second pass quantises.  The CTA then publishes its rows.
+constexpr int kCoopRows = 16;  // rows a CTA may hold
+constexpr int kCoopBatch = 8;  // chunks a warp loads together (its first batch stays held)
 
-__global__ void __launch_bounds__(kProWarps * 32) worklist_prologue(const WlParams p) {
-  __shared__ float red[kProWarps];
-  pdl_launch_dependents();
-  pdl_wait();  // the sources may come from earlier kernels
-  const int job = p.pro_jobs[blockIdx.x];
-  const WlItem &it = p.items[job >> 4];
-  const int r = job & 15, K = it.K, KB = K >> 6, nch = K >> 7;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // this warp's chunks [c0, c1): the row in kProWarps equal parts
-  const int c0 = (int)((long)nch * warp / kProWarps), c1 = (int)((long)nch * (warp + 1) / kProWarps);
-  int8_t *pa_row = it.pa + (size_t)(r & 15) * 64;
-  if (r >= p.M) {  // zero padding of the tile block
-    for (int c = c0; c < c1; c++) {
-      const int kk = c * 128 + lane * 4;
-      *reinterpret_cast<uint32_t *>(pa_row + (size_t)(kk >> 6) * kATile + (kk & 63)) = 0u;
+struct CoopRow {
+  const float *src;   // the row's f32 values
+  int8_t *pa_row;     // its row of the packed tile block
+  float *qs;          // its scale
+  int item, hsz;      // the prep entry, its FWHT block
+  unsigned pub;       // units it publishes (row 0 also counts the padding rows)
+};
+
+__device__ __forceinline__ void consumers_sync(int W) {
+  asm volatile("bar.sync 1, %0;" ::"r"(W * 32) : "memory");
+}
+
+// Descriptors of the CTA's rows [k0, k0 + nr) into shared memory (one warp,
+// lane k: row k0 + k), the rows' chunk offsets and cleared maxima.
+__device__ __forceinline__ void coop_fetch(const WlParams &p, int k0, int nr, int lane, int M,
+                                           CoopRow *rows, int *cstart, unsigned *rmax) {
+  int nch = 0;
+  if (lane < nr) {
+    const int job = p.crows[k0 + lane];
+    const WlItem &it = p.items[job >> 4];
+    const int r = job & 15;
+    CoopRow cr;
+    cr.src = it.src + (size_t)r * it.lda;
+    cr.pa_row = it.pa + (size_t)r * 64;  // one 16-row tile block (M <= 16)
+    cr.qs = it.qs + r;
+    cr.item = job >> 4;
+    cr.hsz = it.hsz;
+    cr.pub = 1u + (r == 0 ? (unsigned)(it.units - M) : 0u);
+    rows[lane] = cr;
+    rmax[lane] = 0u;
+    nch = it.K >> 7;
+  }
+  // exclusive prefix of the chunk counts
+  int incl = nch;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane < nr) cstart[lane + 1] = incl;
+  if (lane == 0) cstart[0] = 0;
+}
+
+__device__ __forceinline__ int coop_row_of(const int *cstart, int nr, int id) {
+  int k = 0;
+  while (k + 1 < nr && cstart[k + 1] <= id) k++;
+  return k;
+}
+
+// Load the warp's batch starting at chunk id b0 (stride W) of the CTA's rows.
+__device__ __forceinline__ void coop_load(const CoopRow *rows, const int *cstart, int nr, int T,
+                                          int b0, int W, int lane, float4 (&v)[kCoopBatch],
+                                          int (&kk)[kCoopBatch], int (&cc)[kCoopBatch]) {
+#pragma unroll
+  for (int u = 0; u < kCoopBatch; u++) {
+    const int id = b0 + u * W;
+    kk[u] = -1;
+    if (id < T) {
+      const int k = coop_row_of(cstart, nr, id);
+      cc[u] = id - cstart[k];
+      v[u] = *reinterpret_cast<const float4 *>(rows[k].src + cc[u] * 128 + lane * 4);
+      kk[u] = k;
     }
-    return;
   }
-  const float *src = it.src + (size_t)r * it.lda + lane * 4;
-  const bool held = c1 - c0 <= kProChunks;  // the whole part fits in registers: one load
-  float4 v[kProChunks];
-  float mx = 0.0f;
-  for (int b0 = c0; b0 < c1; b0 += kProChunks) {
+}
+
+__device__ __forceinline__ void coop_max(const CoopRow *rows, unsigned *rmax, int lane,
+                                         const float4 (&v)[kCoopBatch],
+                                         const int (&kk)[kCoopBatch]) {
 #pragma unroll
-    for (int u = 0; u < kProChunks; u++)
-      if (b0 + u < c1) v[u] = *reinterpret_cast<const float4 *>(src + (b0 + u) * 128);
+  for (int u = 0; u < kCoopBatch; u++) {
+    if (kk[u] < 0) continue;  // warp-uniform
+    const float4 x = fwht128(v[u], rows[kk[u]].hsz, lane);
+    float m = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
 #pragma unroll
-    for (int u = 0; u < kProChunks; u++) {
-      if (b0 + u >= c1) continue;
-      v[u] = fwht128(v[u], it.hsz, lane);
-      const float a0 = fabsf(v[u].x), a1 = fabsf(v[u].y), a2 = fabsf(v[u].z), a3 = fabsf(v[u].w);
-      mx = a0 > mx ? a0 : mx;
-      mx = a1 > mx ? a1 : mx;
-      mx = a2 > mx ? a2 : mx;
-      mx = a3 > mx ? a3 : mx;
-    }
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    // |x| >= 0 orders as its bits; a NaN maximum (every lane NaN) is
+    // skipped, as the per-row prep's comparisons skip NaNs
+    if (lane == 0 && m == m) atomicMax(&rmax[kk[u]], __float_as_uint(m));
   }
+}
+
+__device__ __forceinline__ void coop_quant(const CoopRow *rows, const unsigned *rmax, int lane,
+                                           const float4 (&v)[kCoopBatch],
+                                           const int (&kk)[kCoopBatch],
+                                           const int (&cc)[kCoopBatch]) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float u = __shfl_xor_sync(0xffffffffu, mx, o);
-    mx = u > mx ? u : mx;
+  for (int u = 0; u < kCoopBatch; u++) {
+    if (kk[u] < 0) continue;
+    const CoopRow &cr = rows[kk[u]];
+    const float m = __uint_as_float(rmax[kk[u]]);
+    const float sc = (m == 0.0f) ? 1.0f : __fdiv_rn(m, 127.0f);
+    const int kq = cc[u] * 128 + lane * 4;
+    *reinterpret_cast<uint32_t *>(cr.pa_row + (size_t)(kq >> 6) * kATile + (kq & 63)) =
+        q8_quad(fwht128(v[u], cr.hsz, lane), __fdiv_rn(1.0f, sc));
   }
-  if (lane == 0) red[warp] = mx;
-  __syncthreads();
-  mx = 0.0f;
-#pragma unroll
-  for (int w = 0; w < kProWarps; w++) mx = red[w] > mx ? red[w] : mx;
-  const float s = (mx == 0.0f) ? 1.0f : __fdiv_rn(mx, 127.0f);
-  const float inv = __fdiv_rn(1.0f, s);
-  if (threadIdx.x == 0) it.qs[r] = s;
-  for (int b0 = c0; b0 < c1; b0 += kProChunks) {
-#pragma unroll
-    for (int u = 0; u < kProChunks; u++) {
-      if (b0 + u >= c1) continue;
-      float4 x = v[u];
-      if (!held) x = fwht128(*reinterpret_cast<const float4 *>(src + (b0 + u) * 128), it.hsz, lane);
-      const int kk = (b0 + u) * 128 + lane * 4;
-      *reinterpret_cast<uint32_t *>(pa_row + (size_t)(kk >> 6) * kATile + (kk & 63)) =
-          q8_quad(x, inv);
-    }
+}
+
+// The CTA's rows, by every consumer warp (cw of W); publishes them.  The
+// warp's first batch of chunks stays in registers across the barrier, so a
+// CTA with at most kCoopBatch chunks per warp reads its rows once.
+__device__ void coop_rows(const WlParams &p, int cw, int W, int lane, int nr, const CoopRow *rows,
+                          const int *cstart, unsigned *rmax) {
+  const int T = cstart[nr];
+  float4 h[kCoopBatch];
+  int hk[kCoopBatch], hc[kCoopBatch];
+  // pass 1: each row's largest |x| after the rotation
+  coop_load(rows, cstart, nr, T, cw, W, lane, h, hk, hc);
+  for (int b0 = cw + kCoopBatch * W; b0 < T; b0 += kCoopBatch * W) {
+    float4 v[kCoopBatch];
+    int kk[kCoopBatch], cc[kCoopBatch];
+    coop_load(rows, cstart, nr, T, b0, W, lane, v, kk, cc);
+    coop_max(rows, rmax, lane, v, kk);
   }
-  (void)KB;
+  coop_max(rows, rmax, lane, h, hk);
+  consumers_sync(W);
+  // pass 2: quantise (the held batch from registers, later ones from L2)
+  coop_quant(rows, rmax, lane, h, hk, hc);
+  for (int b0 = cw + kCoopBatch * W; b0 < T; b0 += kCoopBatch * W) {
+    float4 v[kCoopBatch];
+    int kk[kCoopBatch], cc[kCoopBatch];
+    coop_load(rows, cstart, nr, T, b0, W, lane, v, kk, cc);
+    coop_quant(rows, rmax, lane, v, kk, cc);
+  }
+  if (cw == 0 && lane < nr) {
+    const float m = __uint_as_float(rmax[lane]);
+    *rows[lane].qs = (m == 0.0f) ? 1.0f : __fdiv_rn(m, 127.0f);
+  }
+  // publish: the packed rows are read by TMA loads (async proxy) in other CTAs
+  fence_proxy_async_global();
+  __threadfence();
+  consumers_sync(W);
+  if (cw == 0 && lane < nr) atomicAdd(p.done + rows[lane].item, rows[lane].pub);
 }
 
 // ------------------------------------------------------------ unit queue
@@ -490,6 +564,9 @@ __global__ void __launch_bounds__((kWlMaxWarps + 1) * 32, 1) worklist_kernel(con
   __shared__ int s_grab;                            // next CTA-local unit to hand out
   __shared__ int s_left[kWlASlots];                 // units of a GEMM segment still unfinished
   __shared__ int s_fifo[kWlMaxWarps][kWlFifo];      // each warp's taken units, in order
+  __shared__ CoopRow s_crow[kCoopRows];              // cooperative rows: their descriptors,
+  __shared__ int s_cstart[kCoopRows + 1];            // first chunk of each,
+  __shared__ unsigned s_rmax[kCoopRows];             // largest |x| of each (as bits)
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -516,8 +593,8 @@ __global__ void __launch_bounds__((kWlMaxWarps + 1) * 32, 1) worklist_kernel(con
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     // GEMM segment g stages its activations in slot g % 4 (barriers, scales)
-    // at a region of the activation ring allocated first in, first out; a
-    // region is reused once every unit of the segments holding it is done.
+    // at a region of the activation ring; a region is reused once every unit
+    // of the segments holding it is done.
     pdl_wait();  // packed activations and their scales may come from earlier kernels
     int g = 0, head = 0;
     bool ok = true;
@@ -528,16 +605,40 @@ __global__ void __launch_bounds__((kWlMaxWarps + 1) * 32, 1) worklist_kernel(con
       const int b = g & (kWlASlots - 1);
       const int bytes = it.K / 64 * MT * 512;
       const int sz = (bytes + 1023) & ~1023;
-      int off = head;
-      if (off + sz > p.a_ring) off = 0;
       if (g >= kWlASlots)  // segment g - 4, the slot's last user, is done
         ok = wl_wait(&s_empty[b], (uint32_t)(((g >> 2) - 1) & 1), p);
-      for (int j = g - kWlASlots + 1; j < g && ok; j++) {  // younger segments in the region
-        if (j < 0) continue;
-        const int jb = j & (kWlASlots - 1);
-        if (s_r0[jb] < off + sz && off < s_r1[jb])
-          ok = wl_wait(&s_empty[jb], (uint32_t)((j >> 2) & 1), p);
+      // The region: the first of the head, the ring start or the end of a
+      // live younger segment's region where the block fits without touching
+      // a region still in use (a large block held by a long segment does not
+      // hold up the small ones behind it).  Lane 0 decides.
+      int off = -1;
+      if (ok && lane == 0) {
+        const uint64_t t0 = tc::globaltimer_ns();
+        while (off < 0) {
+          int cand[kWlASlots + 1];
+          int nc = 0;
+          cand[nc++] = head;
+          cand[nc++] = 0;
+          for (int j = g - kWlASlots + 1; j < g; j++)
+            if (j >= 0) cand[nc++] = s_r1[j & (kWlASlots - 1)];
+          for (int k = 0; k < nc && off < 0; k++) {
+            const int x = cand[k];
+            if (x + sz > p.a_ring) continue;
+            bool fit = true;
+            for (int j = g - kWlASlots + 1; j < g && fit; j++) {
+              if (j < 0) continue;
+              const int jb = j & (kWlASlots - 1);
+              if (s_r0[jb] < x + sz && x < s_r1[jb] &&
+                  !tc::mbar_try_wait(&s_empty[jb], (uint32_t)((j >> 2) & 1)))
+                fit = false;
+            }
+            if (fit) off = x;
+          }
+          if (off < 0 && (ld_volatile(p.abort) || tc::globaltimer_ns() - t0 > kWlLimitNs)) break;
+        }
+        ok = off >= 0;
       }
+      off = __shfl_sync(0xffffffffu, off, 0);
       if (ok && lane == 0) ok = wl_wait_item(p, it.deps[0]) && wl_wait_item(p, it.deps[1]);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
@@ -628,10 +729,18 @@ __global__ void __launch_bounds__((kWlMaxWarps + 1) * 32, 1) worklist_kernel(con
     };
     auto can_issue = [&]() { return q.live; };
 
-    // the weights never come from earlier kernels: fill the ring first
+    // the weights never come from earlier kernels: fill the ring first, then
+    // this CTA's share of the dependency-free preps' rows (their descriptors
+    // are list data, fetched before waiting for the previous kernel)
     refill();
     while (inflight < S && can_issue()) issue();
+    const int ck0 = p.crow_off[blockIdx.x], cnr = p.crow_off[blockIdx.x + 1] - ck0;
+    if (cw == 0 && cnr > 0) coop_fetch(p, ck0, cnr, lane, p.M, s_crow, s_cstart, s_rmax);
     pdl_wait();  // prep sources and GEMM outputs are ordered after earlier kernels
+    if (cnr > 0) {
+      consumers_sync(W);
+      coop_rows(p, cw, W, lane, cnr, s_crow, s_cstart, s_rmax);
+    }
 
     bool ok = true;
     int cseg = 0, cseg_lo = 0, cseg_end = nseg ? segs[0].nu : 0;  // compute side's segment
@@ -800,19 +909,27 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
   pl.grid = num_sms;
   // ---- shared memory: the activation ring and the consumers' weight rings.
   // The most consumer warps (latency hiding) whose two-stage rings leave the
-  // activation ring room for the widest segment; FGM_CUDA_WORKLIST_WARPS
-  // (8, 12 or 15) overrides the choice.
-  int max_seg = 1024;
+  // activation ring room for the widest segment and two of the narrowest (a
+  // CTA holding a wide block keeps staging the blocks behind it), else for
+  // the widest alone; FGM_CUDA_WORKLIST_WARPS (8..15) overrides the choice.
+  int max_seg = 1024, min_seg = 1 << 30;
   for (const WlItem &it : items)
-    if (it.kind != kWlPrep) max_seg = std::max(max_seg, (it.K / 64 * pl.MT * 512 + 1023) & ~1023);
+    if (it.kind != kWlPrep) {
+      const int sz = (it.K / 64 * pl.MT * 512 + 1023) & ~1023;
+      max_seg = std::max(max_seg, sz);
+      min_seg = std::min(min_seg, sz);
+    }
+  if (min_seg > max_seg) min_seg = max_seg;
   const size_t limit = smem_optin + 1024 - (size_t)wl_static_smem(pl.MT) - 256;
   int want = 0;
   if (const char *e = getenv("FGM_CUDA_WORKLIST_WARPS")) want = atoi(e);
   pl.warps = 0;
-  for (int w : {15, 12, 8}) {
+  for (int pass = 0; pass < 2 && !pl.warps; pass++)
+  for (int w = kWlMaxWarps; w >= 8; w--) {
     if (want && w != want) continue;
     const size_t rings = (size_t)w * 2 * kWlStage;
-    if (1024 + rings + (size_t)max_seg > limit) continue;
+    const size_t need = (size_t)max_seg + (pass == 0 && max_seg > min_seg ? 2 * (size_t)min_seg : 0);
+    if (1024 + rings + need > limit) continue;
     pl.warps = w;
     pl.stages = 2;
     // deeper rings while the activation ring still holds two widest segments
@@ -825,19 +942,42 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
   if (!pl.warps) return "the activations of the widest item do not fit in shared memory";
   pl.smem = worklist_smem(pl.a_ring, pl.warps, pl.stages);
 
-  // ---- preps that depend on nothing run in the prologue launch; entries
-  // that read them wait for that launch (kernel order), not for a counter
+  // ---- preps that depend on nothing: their real rows go to the CTAs,
+  // longest rows first to the least loaded CTA (at most kCoopRows each);
+  // every CTA's consumer warps prepare its rows at the start of the run and
+  // the entries that read them wait for their counters.  Rows past M are
+  // not written (the list's GEMMs read rows [0, M) only).
   std::vector<char> pro(n, 0);
-  pl.pro_jobs.clear();
-  for (int i = 0; i < n; i++) {
-    WlItem &it = items[i];
-    if (it.kind != kWlPrep || it.deps[0] >= 0 || it.deps[1] >= 0) continue;
-    pro[i] = 1;
-    for (int r = 0; r < it.units; r++) pl.pro_jobs.push_back(i * 16 + r);
+  {
+    std::vector<std::pair<int, int>> jobs;  // (K, item*16 + row)
+    for (int i = 0; i < n; i++) {
+      const WlItem &it = items[i];
+      if (it.kind != kWlPrep || it.deps[0] >= 0 || it.deps[1] >= 0) continue;
+      if ((long)jobs.size() + M > (long)kCoopRows * num_sms) break;  // the rest run as units
+      pro[i] = 1;
+      for (int r = 0; r < M; r++) jobs.push_back({it.K, i * 16 + r});
+    }
+    std::stable_sort(jobs.begin(), jobs.end(),
+                     [](const std::pair<int, int> &a, const std::pair<int, int> &b) {
+                       return a.first > b.first;
+                     });
+    std::vector<long> load(num_sms, 0);
+    std::vector<std::vector<int>> rows(num_sms);
+    for (const auto &j : jobs) {
+      int best = -1;
+      for (int c = 0; c < num_sms; c++)
+        if ((int)rows[c].size() < kCoopRows && (best < 0 || load[c] < load[best])) best = c;
+      rows[best].push_back(j.second);
+      load[best] += j.first;
+    }
+    pl.crows.clear();
+    pl.crow_off.assign(num_sms + 1, 0);
+    for (int c = 0; c < num_sms; c++) {
+      pl.crow_off[c] = (int)pl.crows.size();
+      pl.crows.insert(pl.crows.end(), rows[c].begin(), rows[c].end());
+    }
+    pl.crow_off[num_sms] = (int)pl.crows.size();
   }
-  for (int i = 0; i < n; i++)
-    for (int &d : items[i].deps)
-      if (d >= 0 && pro[d]) d = -1;
   for (WlItem &it : items) it.waited = 0;
   for (const WlItem &it : items)
     for (int d : it.deps)
@@ -870,27 +1010,74 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
   for (int lv = 0; lv < nlev; lv++) {
     std::vector<size_t> first(G);  // where this level's pieces start in each CTA's list
     for (int c = 0; c < G; c++) first[c] = cta[c].size();
-    double total = 0;
+    for (int i = 0; i < n; i++) {  // prep rows round-robin over the CTAs
+      if (level[i] != lv || pro[i] || items[i].kind != kWlPrep) continue;
+      for (int u = 0; u < items[i].units; u++, rr++) cta[rr % G].push_back(Piece{i, u, u + 1});
+    }
+    // GEMM units.  Items whose units cost more than twice the level's
+    // cheapest units ("large": e.g. the K=8192 down projections) each get a
+    // set of CTAs of their own, filling about half of each CTA's share, so
+    // no CTA holds two large activation blocks or ends on large units alone;
+    // the other items' units then fill every CTA's remaining share in
+    // contiguous ranges, in list order.  (Inside each CTA the large units go
+    // first, see below.)
+    double total = 0, cheapest = 1e30;
     for (int i = 0; i < n; i++)
-      if (level[i] == lv && items[i].kind != kWlPrep) total += items[i].units * unit_cost(items[i], 0);
-    double acc = 0;
-    for (int i = 0; i < n; i++) {
-      if (level[i] != lv || pro[i]) continue;
-      const WlItem &it = items[i];
-      if (it.kind == kWlPrep) {  // rows round-robin over the CTAs
-        for (int u = 0; u < it.units; u++, rr++) {
-          cta[rr % G].push_back(Piece{i, u, u + 1});
-        }
-        continue;
+      if (level[i] == lv && !pro[i] && items[i].kind != kWlPrep) {
+        total += items[i].units * unit_cost(items[i], 0);
+        cheapest = std::min(cheapest, unit_cost(items[i], 0));
       }
-      // GEMM units: contiguous ranges of equal weight bytes
+    const double share = total / G;
+    std::vector<double> have(G, 0.0);
+    std::vector<char> placed(n, 0);
+    int next = 0;  // first CTA without a large item
+    for (int i = 0; i < n; i++) {
+      const WlItem &it = items[i];
+      if (level[i] != lv || pro[i] || it.kind == kWlPrep) continue;
+      const double cost = unit_cost(it, 0);
+      if (cost <= 2 * cheapest) continue;
+      int k = (int)std::lround(it.units * cost / (0.5 * share));
+      k = std::max(1, std::min(k, it.units));
+      if (next + k > G) break;  // out of CTAs: the rest are dealt like the others
+      for (int j = 0; j < k; j++) {
+        const int u0 = (int)((long)it.units * j / k), u1 = (int)((long)it.units * (j + 1) / k);
+        if (u1 > u0) cta[next + j].push_back(Piece{i, u0, u1});
+        have[next + j] += (u1 - u0) * cost;
+      }
+      next += k;
+      placed[i] = 1;
+    }
+    std::vector<double> room_end(G + 1, 0.0);  // prefix of the CTAs' remaining shares
+    for (int c = 0; c < G; c++) room_end[c + 1] = room_end[c] + std::max(0.0, share - have[c]);
+    double rest = 0;  // the other items' cost, spread over the remaining shares
+    for (int i = 0; i < n; i++)
+      if (level[i] == lv && !pro[i] && items[i].kind != kWlPrep && !placed[i])
+        rest += items[i].units * unit_cost(items[i], 0);
+    if (room_end[G] <= 0)  // no room left anywhere: spread evenly
+      for (int c = 0; c < G; c++) room_end[c + 1] = room_end[c] + 1.0;
+    const double scale = rest > 0 ? room_end[G] / rest : 1.0;
+    // the largest items first: the CTAs holding a large item's block (they
+    // come first) then fill their room from one range of a big item, and
+    // the many small items go where the activation ring has room for them
+    std::vector<int> order;
+    for (int i = 0; i < n; i++)
+      if (level[i] == lv && !pro[i] && items[i].kind != kWlPrep && !placed[i]) order.push_back(i);
+    std::stable_sort(order.begin(), order.end(), [&](int x, int y) {
+      return items[x].units * unit_cost(items[x], 0) > items[y].units * unit_cost(items[y], 0);
+    });
+    double acc = 0;
+    for (int i : order) {
+      const WlItem &it = items[i];
       const double cost = unit_cost(it, 0);
       int u = 0;
       while (u < it.units) {
-        const int c = std::min(G - 1, (int)((acc + 0.5 * cost) * G / total));
-        const double end = (double)(c + 1) * total / G;
+        // the CTA whose remaining share holds the middle of this unit
+        const double mid = (acc + 0.5 * cost) * scale;
+        int c = (int)(std::upper_bound(room_end.begin() + 1, room_end.end(), mid) -
+                      (room_end.begin() + 1));
+        c = std::min(c, G - 1);
         int u1 = u + 1;
-        while (u1 < it.units && acc + (u1 - u + 0.5) * cost < end) u1++;
+        while (u1 < it.units && (acc + (u1 - u + 0.5) * cost) * scale < room_end[c + 1]) u1++;
         cta[c].push_back(Piece{i, u, u1});
         acc += (u1 - u) * cost;
         u = u1;
@@ -944,19 +1131,6 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
 }
 
 cudaError_t launch_worklist(const WlParams &p, const WlPlan &pl, bool pdl, cudaStream_t st) {
-  if (p.n_pro > 0) {
-    cudaLaunchConfig_t pc = {};
-    pc.gridDim = dim3(p.n_pro);
-    pc.blockDim = dim3(kProWarps * 32);
-    pc.stream = st;
-    cudaLaunchAttribute pa[1];
-    pa[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    pa[0].val.programmaticStreamSerializationAllowed = 1;
-    pc.attrs = pa;
-    pc.numAttrs = pdl ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&pc, worklist_prologue, p);
-    if (e != cudaSuccess) return e;
-  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.grid);
   cfg.blockDim = dim3((pl.warps + 1) * 32);

@@ -253,8 +253,12 @@ int fgm_cuda_gemm_q8c_acc(int M, int N, int K, const int8_t *A, const int8_t *B,
  * item's completion counter (device-side, bounded) instead of a kernel
  * boundary.  Each GEMM item computes exactly fgm_cuda_gemm_q4g /
  * fgm_cuda_gemm_q8c over its column range, each prep item exactly
- * fgm_cuda_prep_rows (rows [0, M), padding rows of the last 16-row block
- * zeroed) -- bit-identical outputs.  No reference counterpart: the reference
+ * fgm_cuda_prep_rows over rows [0, M) -- bit-identical outputs.  (A prep
+ * that depends on no other entry leaves the padding rows of its 16-row
+ * block as they are; in the list's GEMMs padding rows reach only outputs
+ * that are not stored.)  The preps that depend on no entry are prepared at
+ * the start of the run by all SMs together, after each SM has started its
+ * weight stream.  No reference counterpart: the reference
  * runs its projections one call at a time (pool.rs:126-145).
  *
  * A list is created once (validation, schedule, activation TMA descriptors,
@@ -265,7 +269,7 @@ int fgm_cuda_gemm_q8c_acc(int M, int N, int K, const int8_t *A, const int8_t *B,
  *    K % 512 == 0 (int4) or K % 256 == 0 (int8), K <= 16384; output columns
  *    [n0*16, n1*16), 0 <= n0 < n1 <= N/16, C[m*ldc + n] with ldc >= n1*16;
  *    int4 group in {64, 128, 256, 512} dividing K; A (tile-packed, one 16-row
- *    block, zero padding rows), B and int4 scales 16-byte aligned, int8
+ *    block; rows past M reach no stored output), B and int4 scales 16-byte aligned, int8
  *    scales 4-byte aligned.
  *  - FGM_CUDA_WORK_PREP: f32 rows src[m*lda + k], K % 128 == 0, lda >= K,
  *    lda % 4 == 0, src 16-byte aligned; hsz 0 or a power of two <= 128
