@@ -911,7 +911,7 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
   // The most consumer warps (latency hiding) whose two-stage rings leave the
   // activation ring room for the widest segment and two of the narrowest (a
   // CTA holding a wide block keeps staging the blocks behind it), else for
-  // the widest alone; FGM_CUDA_WORKLIST_WARPS (8..15) overrides the choice.
+  // the widest alone; FGM_CUDA_WORKLIST_WARPS (8..15) caps the count.
   int max_seg = 1024, min_seg = 1 << 30;
   for (const WlItem &it : items)
     if (it.kind != kWlPrep) {
@@ -926,7 +926,7 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
   pl.warps = 0;
   for (int pass = 0; pass < 2 && !pl.warps; pass++)
   for (int w = kWlMaxWarps; w >= 8; w--) {
-    if (want && w != want) continue;
+    if (want && w > want) continue;
     const size_t rings = (size_t)w * 2 * kWlStage;
     const size_t need = (size_t)max_seg + (pass == 0 && max_seg > min_seg ? 2 * (size_t)min_seg : 0);
     if (1024 + rings + need > limit) continue;
