@@ -1339,8 +1339,8 @@ int fgm_cuda_worklist_create(int M, const fgm_cuda_work *w, int n, void **list) 
   const size_t o_items = 0, b_items = sizeof(WlItem) * (size_t)n;
   const size_t o_segs = align256(o_items + b_items), b_segs = sizeof(WlSeg) * wl->plan.segs.size();
   const size_t o_off = align256(o_segs + b_segs), b_off = sizeof(int) * wl->plan.seg_off.size();
-  const size_t o_cr = align256(o_off + b_off), b_cr = sizeof(int) * wl->plan.crows.size();
-  const size_t o_co = align256(o_cr + b_cr), b_co = sizeof(int) * wl->plan.crow_off.size();
+  const size_t o_cr = align256(o_off + b_off), b_cr = sizeof(WlCoopRow) * wl->plan.coop.size();
+  const size_t o_co = align256(o_cr + b_cr), b_co = sizeof(int) * wl->plan.coop_n.size();
   const size_t o_cnt = align256(o_co + b_co), b_cnt = sizeof(unsigned) * ((size_t)n + 2);
   const size_t total = o_cnt + b_cnt;
   if (cudaMalloc(&wl->mem, total) != cudaSuccess) {
@@ -1358,9 +1358,9 @@ int fgm_cuda_worklist_create(int M, const fgm_cuda_work *w, int n, void **list) 
   if (e == cudaSuccess)
     e = cudaMemcpy(d + o_off, wl->plan.seg_off.data(), b_off, cudaMemcpyHostToDevice);
   if (e == cudaSuccess && b_cr)
-    e = cudaMemcpy(d + o_cr, wl->plan.crows.data(), b_cr, cudaMemcpyHostToDevice);
+    e = cudaMemcpy(d + o_cr, wl->plan.coop.data(), b_cr, cudaMemcpyHostToDevice);
   if (e == cudaSuccess)
-    e = cudaMemcpy(d + o_co, wl->plan.crow_off.data(), b_co, cudaMemcpyHostToDevice);
+    e = cudaMemcpy(d + o_co, wl->plan.coop_n.data(), b_co, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemset(d + o_cnt, 0, b_cnt);
   if (e != cudaSuccess) {
     cudaFree(wl->mem);
@@ -1374,8 +1374,8 @@ int fgm_cuda_worklist_create(int M, const fgm_cuda_work *w, int n, void **list) 
   p.n_items = n;
   p.segs = reinterpret_cast<const WlSeg *>(d + o_segs);
   p.seg_off = reinterpret_cast<const int *>(d + o_off);
-  p.crows = reinterpret_cast<const int *>(d + o_cr);
-  p.crow_off = reinterpret_cast<const int *>(d + o_co);
+  p.coop = reinterpret_cast<const WlCoopRow *>(d + o_cr);
+  p.coop_n = reinterpret_cast<const int *>(d + o_co);
   p.done = reinterpret_cast<unsigned *>(d + o_cnt);
   p.ctas_done = p.done + n;
   p.abort = reinterpret_cast<int *>(p.done + n + 1);

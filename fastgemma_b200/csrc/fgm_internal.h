@@ -250,6 +250,18 @@ struct WlSeg {                 // one CTA's share of one item
   const uint8_t *B;
   const CUtensorMap *smap;     // device address of the item's scale view
 };
+// One row of a dependency-free prep, prepared at the start of a run by the
+// CTA it is dealt to (built on the host: one load fetches it).
+struct WlCoopRow {
+  const float *src;   // the row's f32 values
+  int8_t *pa_row;     // its row of the packed tile block
+  float *qs;          // its scale
+  int item, hsz;      // the prep entry, its FWHT block
+  unsigned pub;       // units it publishes (row 0 also counts the padding rows)
+  int nch;            // 128-value chunks
+};
+constexpr int kWlCoopRows = 16;  // rows a CTA may hold
+
 struct WlParams {
   const WlItem *items;
   int n_items;
@@ -261,15 +273,16 @@ struct WlParams {
   int *err;                // device status word
   int M, warps, stages;    // consumer warps per CTA, weight ring stages per warp
   int a_ring;              // bytes of the activation ring (segments staged FIFO)
-  const int *crows;        // rows of the preps that depend on nothing (item*16 + row):
-  const int *crow_off;     // CTA c prepares crows[crow_off[c], crow_off[c + 1]) first
+  const WlCoopRow *coop;   // CTA c's dependency-free prep rows: coop[c*kWlCoopRows + k],
+  const int *coop_n;       // k < coop_n[c], prepared at the start of the run
 };
 struct WlPlan {
   int M, MT, grid, warps, stages, a_ring;
   size_t smem;
   std::vector<WlSeg> segs;
   std::vector<int> seg_off;
-  std::vector<int> crows, crow_off;
+  std::vector<WlCoopRow> coop;  // [grid][kWlCoopRows]
+  std::vector<int> coop_n;
 };
 // Fills the schedule and launch geometry; returns an error text or nullptr.
 const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num_sms,

@@ -374,40 +374,24 @@ __device__ void prep_row(const WlItem &it, int r, int M, int lane) {
 // then walk the (row, 128-value chunk) pairs of the CTA's rows with a
 // stride of one warp each: a first pass keeps each row's largest |x| in
 // shared memory, a second pass quantises.  The CTA then publishes its rows.
-constexpr int kCoopRows = 16;  // rows a CTA may hold
+constexpr int kCoopRows = kWlCoopRows;
 constexpr int kCoopBatch = 8;  // chunks a warp loads together (its first batch stays held)
-
-struct CoopRow {
-  const float *src;   // the row's f32 values
-  int8_t *pa_row;     // its row of the packed tile block
-  float *qs;          // its scale
-  int item, hsz;      // the prep entry, its FWHT block
-  unsigned pub;       // units it publishes (row 0 also counts the padding rows)
-};
+using CoopRow = WlCoopRow;
 
 __device__ __forceinline__ void consumers_sync(int W) {
   asm volatile("bar.sync 1, %0;" ::"r"(W * 32) : "memory");
 }
 
-// Descriptors of the CTA's rows [k0, k0 + nr) into shared memory (one warp,
-// lane k: row k0 + k), the rows' chunk offsets and cleared maxima.
-__device__ __forceinline__ void coop_fetch(const WlParams &p, int k0, int nr, int lane, int M,
-                                           CoopRow *rows, int *cstart, unsigned *rmax) {
+// The CTA's row descriptors into shared memory (one warp, lane k: row k;
+// one load each), the rows' chunk offsets and cleared maxima.
+__device__ __forceinline__ void coop_fetch(const WlParams &p, int nr, int lane, CoopRow *rows,
+                                           int *cstart, unsigned *rmax) {
   int nch = 0;
   if (lane < nr) {
-    const int job = p.crows[k0 + lane];
-    const WlItem &it = p.items[job >> 4];
-    const int r = job & 15;
-    CoopRow cr;
-    cr.src = it.src + (size_t)r * it.lda;
-    cr.pa_row = it.pa + (size_t)r * 64;  // one 16-row tile block (M <= 16)
-    cr.qs = it.qs + r;
-    cr.item = job >> 4;
-    cr.hsz = it.hsz;
-    cr.pub = 1u + (r == 0 ? (unsigned)(it.units - M) : 0u);
+    const CoopRow cr = p.coop[(size_t)blockIdx.x * kCoopRows + lane];
     rows[lane] = cr;
     rmax[lane] = 0u;
-    nch = it.K >> 7;
+    nch = cr.nch;
   }
   // exclusive prefix of the chunk counts
   int incl = nch;
@@ -475,16 +459,22 @@ __device__ __forceinline__ void coop_quant(const CoopRow *rows, const unsigned *
   }
 }
 
-// The CTA's rows, by every consumer warp (cw of W); publishes them.  The
-// warp's first batch of chunks stays in registers across the barrier, so a
-// CTA with at most kCoopBatch chunks per warp reads its rows once.
+// The CTA's rows, by every consumer warp (cw of W), in two calls: coop_first
+// issues the warp's first batch of chunks (held in registers until the end);
+// coop_rows, called once the weight rings are out, walks the rest, meets the
+// row maxima, quantises and publishes.  A CTA with at most kCoopBatch chunks
+// per warp reads its rows once.
+__device__ __forceinline__ void coop_first(int cw, int W, int lane, int nr, const CoopRow *rows,
+                                           const int *cstart, float4 (&h)[kCoopBatch],
+                                           int (&hk)[kCoopBatch], int (&hc)[kCoopBatch]) {
+  coop_load(rows, cstart, nr, cstart[nr], cw, W, lane, h, hk, hc);
+}
+
 __device__ void coop_rows(const WlParams &p, int cw, int W, int lane, int nr, const CoopRow *rows,
-                          const int *cstart, unsigned *rmax) {
+                          const int *cstart, unsigned *rmax, const float4 (&h)[kCoopBatch],
+                          const int (&hk)[kCoopBatch], const int (&hc)[kCoopBatch]) {
   const int T = cstart[nr];
-  float4 h[kCoopBatch];
-  int hk[kCoopBatch], hc[kCoopBatch];
   // pass 1: each row's largest |x| after the rotation
-  coop_load(rows, cstart, nr, T, cw, W, lane, h, hk, hc);
   for (int b0 = cw + kCoopBatch * W; b0 < T; b0 += kCoopBatch * W) {
     float4 v[kCoopBatch];
     int kk[kCoopBatch], cc[kCoopBatch];
@@ -595,6 +585,12 @@ __global__ void __launch_bounds__((kWlMaxWarps + 1) * 32, 1) worklist_kernel(con
     // GEMM segment g stages its activations in slot g % 4 (barriers, scales)
     // at a region of the activation ring; a region is reused once every unit
     // of the segments holding it is done.
+    // The entries' descriptors and the segments' activation maps are list
+    // data: prefetched while the previous kernel finishes.
+    for (size_t o = (size_t)lane * 128; o < (size_t)p.n_items * sizeof(WlItem); o += 32 * 128)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char *>(p.items) + o));
+    for (int si = lane; si < nseg; si += 32)
+      if (segs[si].kind != kWlPrep) tc::prefetch_tmap(&p.items[segs[si].item].amap);
     pdl_wait();  // packed activations and their scales may come from earlier kernels
     int g = 0, head = 0;
     bool ok = true;
@@ -732,15 +728,22 @@ __global__ void __launch_bounds__((kWlMaxWarps + 1) * 32, 1) worklist_kernel(con
     // the weights never come from earlier kernels: fill the ring first, then
     // this CTA's share of the dependency-free preps' rows (their descriptors
     // are list data, fetched before waiting for the previous kernel)
+    // This CTA's share of the dependency-free preps' rows: their descriptors
+    // (list data), then -- once earlier kernels are done -- the rows' loads,
+    // ahead of the weight rings in the memory queues; the weights then
+    // stream while the rows are quantised.
+    const int cnr = p.coop_n[blockIdx.x];
+    if (cw == 0 && cnr > 0) coop_fetch(p, cnr, lane, s_crow, s_cstart, s_rmax);
+    pdl_wait();  // prep sources and GEMM outputs are ordered after earlier kernels
+    float4 ch[kCoopBatch];
+    int chk[kCoopBatch], chc[kCoopBatch];
+    if (cnr > 0) {
+      consumers_sync(W);  // the descriptors
+      coop_first(cw, W, lane, cnr, s_crow, s_cstart, ch, chk, chc);
+    }
     refill();
     while (inflight < S && can_issue()) issue();
-    const int ck0 = p.crow_off[blockIdx.x], cnr = p.crow_off[blockIdx.x + 1] - ck0;
-    if (cw == 0 && cnr > 0) coop_fetch(p, ck0, cnr, lane, p.M, s_crow, s_cstart, s_rmax);
-    pdl_wait();  // prep sources and GEMM outputs are ordered after earlier kernels
-    if (cnr > 0) {
-      consumers_sync(W);
-      coop_rows(p, cw, W, lane, cnr, s_crow, s_cstart, s_rmax);
-    }
+    if (cnr > 0) coop_rows(p, cw, W, lane, cnr, s_crow, s_cstart, s_rmax, ch, chk, chc);
 
     bool ok = true;
     int cseg = 0, cseg_lo = 0, cseg_end = nseg ? segs[0].nu : 0;  // compute side's segment
@@ -970,13 +973,23 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
       rows[best].push_back(j.second);
       load[best] += j.first;
     }
-    pl.crows.clear();
-    pl.crow_off.assign(num_sms + 1, 0);
+    pl.coop.assign((size_t)num_sms * kCoopRows, WlCoopRow{});
+    pl.coop_n.assign(num_sms, 0);
     for (int c = 0; c < num_sms; c++) {
-      pl.crow_off[c] = (int)pl.crows.size();
-      pl.crows.insert(pl.crows.end(), rows[c].begin(), rows[c].end());
+      pl.coop_n[c] = (int)rows[c].size();
+      for (int k = 0; k < (int)rows[c].size(); k++) {
+        const int job = rows[c][k], r = job & 15;
+        const WlItem &it = items[job >> 4];
+        WlCoopRow &cr = pl.coop[(size_t)c * kCoopRows + k];
+        cr.src = it.src + (size_t)r * it.lda;
+        cr.pa_row = it.pa + (size_t)r * 64;  // one 16-row tile block (M <= 16)
+        cr.qs = it.qs + r;
+        cr.item = job >> 4;
+        cr.hsz = it.hsz;
+        cr.pub = 1u + (r == 0 ? (unsigned)(it.units - M) : 0u);
+        cr.nch = it.K >> 7;
+      }
     }
-    pl.crow_off[num_sms] = (int)pl.crows.size();
   }
   for (WlItem &it : items) it.waited = 0;
   for (const WlItem &it : items)
