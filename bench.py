@@ -236,6 +236,15 @@ def cpu_reference_run(layers: int, seconds: float | None, steps: int | None, war
     return gbs, el / n, info
 
 
+def step_config(L):
+    """The step both arms time (identical in both lines)."""
+    return {"workload": "BASELINE config 1 at M=8: q 2048x2048, kv 2048x512, o 2048x2048, "
+                        "gate_up 2048x16384, down 8192x2048 (KxN), int4 q4g group 64 f16 "
+                        f"scales, {L} distinct layer copies, 4 preps + 5 GEMMs per layer",
+            "weight_bytes_per_step": L * sum(sum(q4g_bytes(K, N)) for _, K, N in DECODE_SHAPES),
+            "layers": L, "M": M_DECODE}
+
+
 def run_reference_arm(args, world, rank):
     if rank != 0:
         return
@@ -249,13 +258,10 @@ def run_reference_arm(args, world, rank):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic",
-        "config": {"workload": "BASELINE config 1 at M=8: q 2048x2048, kv 2048x512, o 2048x2048, "
-                               "gate_up 2048x16384, down 8192x2048 (KxN), int4 q4g group 64 f16 "
-                               f"scales, {args.layers} distinct layer copies, 4 preps + 5 GEMMs per "
-                               "layer (the GPU arm's step), reference CPU kernels",
-                   "weight_bytes_per_step": args.layers * sum(sum(q4g_bytes(K, N))
-                                                              for _, K, N in DECODE_SHAPES),
-                   "l2": f"{args.layers} layer copies (381 MB) > host last-level cache"},
+        "config": step_config(args.layers),
+        "execution": {"kernels": "the reference's own CPU kernels (oracle/_ref, built from "
+                                 "its sources), every layer of the step once per step",
+                      "l2": "the step's weights exceed the host's last-level cache"},
         "cpu_baseline": dict(info, value=gbs, unit="GB/s"),
         "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -435,14 +441,11 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (seeded uniform int4 codes, f16 scales U(0.005,0.02), X~N(0,1))",
-            "config": {
-                "workload": "BASELINE config 1 at M=8: q 2048x2048, kv 2048x512, o 2048x2048, "
-                            "gate_up 2048x16384, down 8192x2048 (KxN), int4 q4g group 64 f16 "
-                            f"scales, {L} distinct layer copies, 4 preps + 5 GEMMs per layer",
-                "weight_bytes_per_step": wbytes_step, "l2": "inputs larger than L2 "
-                f"({wbytes_step / 1e6:.0f} MB of weights per step > 2 x 126 MB)",
-                "launch": "one work-list kernel launch per step (fgm_cuda_worklist_run)",
-                "parallelism": f"replicas x{world}"},
+            "config": step_config(L),
+            "execution": {"launch": "one work-list kernel launch per step (fgm_cuda_worklist_run)",
+                          "parallelism": f"replicas x{world}",
+                          "l2": "inputs larger than L2 "
+                                f"({wbytes_step / 1e6:.0f} MB of weights per step > 2 x 126 MB)"},
             "roofline": roofline,
             "config1_per_call": per_call,
             "gpu_launches": int(launches_per_step * args.steps),
