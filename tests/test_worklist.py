@@ -210,3 +210,39 @@ def test_worklist_matches_the_per_call_kernels_at_full_config1_width(orc):
     assert _lib.lib().fgm_cuda_device_status() == 0
     wl.close()
     del rng
+
+
+@pytest.mark.gpu
+def test_many_long_dependency_free_preps(orc):
+    """24 preps of K = 16384 that depend on nothing (192 rows over the CTAs:
+    some CTAs prepare two rows, more chunks per warp than one held batch, so
+    the second pass reloads), a third of them with the FWHT, each feeding an
+    int4 GEMM.  Outputs, packed rows [0, M) and scales against the oracle,
+    bit for bit."""
+    _gpu()
+    M, K, N, P = 8, 16384, 64, 24
+    rng = np.random.default_rng(41)
+    xs = [rng.standard_normal((M, K), dtype=np.float32) * (1 + i) for i in range(P)]
+    b, s = F.synth_q4g(N, K, 64, 9, structured=False)
+    bd, sd = Dv(b), Dv(s.view(np.uint16))
+    wl = D.WorkList()
+    outs = []
+    for i, x in enumerate(xs):
+        pa, qs = D.packed_a(M, K), torch.empty(M, device="cuda")
+        ip = wl.prep(Dv(x), K, K, pa, qs, hsz=128 if i % 3 == 0 else 0)
+        c = torch.empty((M, N), device="cuda")
+        wl.gemm_q4g(N, K, pa, qs, bd, sd, 64, c, deps=(ip,))
+        outs.append((pa, qs, c))
+    wl.build(M)
+    for _ in range(2):
+        wl.run()
+    torch.cuda.synchronize()
+    assert _lib.lib().fgm_cuda_device_status() == 0
+    for i, (x, (pa, qs, c)) in enumerate(zip(xs, outs)):
+        hsz = 128 if i % 3 == 0 else 0
+        _, _, qs_r, pa_r = orc.prep_rows(x, M, K, hsz)
+        assert np.array_equal(_rows(pa.cpu().numpy(), K, M), _rows(pa_r, K, M)), i
+        assert np.array_equal(qs.cpu().numpy().view(np.uint32), qs_r.view(np.uint32)), i
+        want = orc.gemm_q4g(M, N, K, pa_r, qs_r, b, s, 64)[:M]
+        assert bits_equal(c.cpu().numpy(), want)[0], i
+    wl.close()
