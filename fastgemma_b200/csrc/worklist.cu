@@ -23,30 +23,34 @@
 // Items are levelled by their dependencies (an item's level is one more than
 // its deepest dependency).  Levels run in order; inside a level the items'
 // units -- 16-column n-blocks of a GEMM over all of K, or single rows of a
-// prep -- are spread over all CTAs: GEMM units as contiguous ranges of equal
-// weight bytes (independent items of a level run side by side on different
-// SMs), prep rows round-robin.  A CTA's share is a list of segments (item,
-// unit range); inside a CTA the units of its segments go round-robin to the
-// consumer warps.  Every warp walks its units in list order, so the lowest
-// unfinished item can always progress: the kernel cannot deadlock while all
-// CTAs are resident (grid = one CTA per SM).
+// prep -- are spread over all CTAs: an item whose units cost more than twice
+// the level's cheapest gets CTAs of its own (about half of each one's
+// share), the other GEMM units fill every CTA's remaining share in
+// contiguous ranges (biggest item first), prep rows go round-robin.  A
+// CTA's share is a list of segments (item, unit range), its large units
+// first.  The preps that depend on nothing are prepared at the start of the
+// run by the CTAs their rows are dealt to (all consumer warps of a CTA
+// together).  Consumer warps take a CTA's units from a shared counter in
+// list order, so the lowest unfinished item can always progress: the kernel
+// cannot deadlock while all CTAs are resident (grid = one CTA per SM).
 //
 // CTA roles
 // ---------
 // Warp 0 (producer) stages each GEMM segment's activations: it waits for the
 // item's dependencies (counters in global memory, acquire loads), then one
-// 3-D TMA box brings the segment's packed rows [tiles][rows][64 B] into one
-// of two shared buffers with the 64-byte swizzle, so the consumers' B-fragment
-// loads (k-quads t, 4+t, 8+t, 12+t of row g) hit 32 distinct banks.  Warps
-// 1..8 (consumers) each own a ring of 4 KB stages (8 int4 or 4 int8 tiles),
-// filled by cp.async.bulk and refilled as soon as a stage is consumed, across
-// unit and item boundaries; the weight issue runs ahead of everything else,
-// before griddepcontrol.wait.  The arithmetic per stage is the decode
-// kernel's (gemv.cu): mma.sync m16n8k32 s8 with the weights as the A operand
-// read straight from the tile layout, int32 group sums, and the fold
-// C = fmaf((float)acc_g, s_g, C) over ascending groups, then * a_scale
-// (amx_gemm.c:103-113, :365-371); int8: (float)acc * (b_scale * a_scale)
-// (amx_gemm.c:399).  Bit-identical to the per-call kernels.
+// 3-D TMA box brings the segment's packed rows [tiles][rows][64 B] into a
+// region of the activation ring (first fit) with the 64-byte swizzle, so the
+// consumers' B-fragment loads (k-quads t, 4+t, 8+t, 12+t of row g) hit 32
+// distinct banks.  Warps 1..W (consumers, W <= 15) each own a ring of
+// 4352-byte stages (4 KB of weights: 8 int4 or 4 int8 tiles by one bulk
+// copy, plus the int4 scale rows of its groups by one 2-D TMA box), refilled
+// as soon as a stage is consumed, across unit and item boundaries.  The
+// arithmetic per stage is the decode kernel's (gemv.cu): mma.sync m16n8k32
+// s8 with the weights as the A operand read straight from the tile layout,
+// int32 group sums, and the fold C = fmaf((float)acc_g, s_g, C) over
+// ascending groups, then * a_scale (amx_gemm.c:103-113, :365-371); int8:
+// (float)acc * (b_scale * a_scale) (amx_gemm.c:399).  Bit-identical to the
+// per-call kernels.
 //
 // Waits and failures
 // ------------------
@@ -1003,11 +1007,10 @@ const char *worklist_plan(WlPlan &pl, std::vector<WlItem> &items, int M, int num
       if (d >= 0) level[i] = std::max(level[i], level[d] + 1);
     nlev = std::max(nlev, level[i] + 1);
   }
-  // Cost of one unit in 4 KB weight stages (a prep row: two passes over its
-  // f32 source, which one warp reads at a fraction of the weight rate).
   // Cost of one unit in 4 KB weight stages: its stages plus a fixed cost per
   // unit (taking it, its epilogue) measured at about one and a half stages;
-  // a prep row: two passes over its f32 source.
+  // a prep row: two passes over its f32 source, which one warp reads at a
+  // fraction of the weight rate.
   auto unit_cost = [&](const WlItem &it, int u) -> double {
     if (it.kind == kWlQ4) return it.K / 512 + 1.5;
     if (it.kind == kWlQ8) return it.K / 256 + 1.5;
