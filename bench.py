@@ -825,8 +825,10 @@ def bench_config4(args, dev, world, rank):
     bit against a whole-width GEMM of the same inputs on its own GPU."""
     import torch
     import torch.distributed as dist
+    from fastgemma_b200 import _lib
     from fastgemma_b200 import device as D
     from fastgemma_b200 import shard as S
+    lib = _lib.lib()
     N, K = LM_HEAD_N, 2048
     g = torch.Generator(device=dev)
     g.manual_seed(31337)  # same weight on every rank
@@ -856,8 +858,34 @@ def bench_config4(args, dev, world, rank):
             if world > 1:
                 dist.all_gather_into_tensor(gathered, local)
 
+        # the token choice without the logits gather (engine.rs:297-302): each
+        # rank reduces its columns to per-row (value, index) pairs, only the
+        # pairs cross NVLink, and every rank merges them
+        parts = lib.fgm_cuda_argmax_parts(cols)
+        vals = torch.empty((M, parts), device=dev)
+        idx = torch.empty((M, parts), dtype=torch.int32, device=dev)
+        gv = torch.empty((world, M, parts), device=dev)
+        gi = torch.empty((world, M, parts), dtype=torch.int32, device=dev)
+        tok = torch.empty(M, dtype=torch.int32, device=dev)
+
+        def gemm_argmax():
+            gemm()
+            st_ = torch.cuda.current_stream().cuda_stream
+            _lib.call("fgm_cuda_argmax_partials", local.data_ptr(), M, cols, cols, nb0 * 16,
+                      vals.data_ptr(), idx.data_ptr(), st_)
+            if world > 1:
+                dist.all_gather_into_tensor(gv, vals)
+                dist.all_gather_into_tensor(gi, idx)
+                av = gv.permute(1, 0, 2).reshape(M, world * parts).contiguous()
+                ai = gi.permute(1, 0, 2).reshape(M, world * parts).contiguous()
+            else:
+                av, ai = vals, idx
+            _lib.call("fgm_cuda_argmax_merge", av.data_ptr(), ai.data_ptr(), M, av.shape[1],
+                      tok.data_ptr(), st_)
+
         ms_gemm = _timed(gemm, steps, world, dev)
         ms_all = _timed(gemm_gather, steps, world, dev)
+        ms_tok = _timed(gemm_argmax, steps, world, dev)
         # parity: whole-width GEMM of the same inputs on this GPU
         D.q8c_prepare(w_full, N, K)
         whole = torch.empty((M, N), device=dev)
@@ -870,6 +898,19 @@ def bench_config4(args, dev, world, rank):
             src = gathered[r] if world > 1 else local
             ok &= bool(torch.equal(src.view(torch.int32),
                                    whole[:, a * 16:b * 16].contiguous().view(torch.int32)))
+        # tokens: the whole logits' row argmax on this GPU
+        gemm_argmax()
+        wparts = lib.fgm_cuda_argmax_parts(N)
+        wv = torch.empty((M, wparts), device=dev)
+        wi = torch.empty((M, wparts), dtype=torch.int32, device=dev)
+        wt = torch.empty(M, dtype=torch.int32, device=dev)
+        st_ = torch.cuda.current_stream().cuda_stream
+        _lib.call("fgm_cuda_argmax_partials", whole.data_ptr(), M, N, N, 0, wv.data_ptr(),
+                  wi.data_ptr(), st_)
+        _lib.call("fgm_cuda_argmax_merge", wv.data_ptr(), wi.data_ptr(), M, wparts,
+                  wt.data_ptr(), st_)
+        torch.cuda.synchronize()
+        ok_tok = bool(torch.equal(tok, wt))
         del whole
         torch.cuda.empty_cache()
         ops = 2.0 * M * N * K
@@ -878,8 +919,10 @@ def bench_config4(args, dev, world, rank):
             "gemm_ms": ms_gemm, "gemm_gather_ms": ms_all,
             "gemm_tops": ops / (ms_gemm * 1e-3) / 1e12,
             "gemm_gather_tops": ops / (ms_all * 1e-3) / 1e12,
+            "gemm_token_ms": ms_tok, "gemm_token_tops": ops / (ms_tok * 1e-3) / 1e12,
             "roofline_gemm": tc_roofline(ops, bytes_, ms_gemm * 1e-3, world),
-            "parity": _all_ranks(ok, world, dev)}
+            "parity": _all_ranks(ok, world, dev),
+            "token_parity": _all_ranks(ok_tok, world, dev)}
         del local, gathered
     D.q8c_release(w)
     return {"unit": "TOPS (whole job)", "results": res, "n_gpus": world,
@@ -887,8 +930,11 @@ def bench_config4(args, dev, world, rank):
             "workload": f"BASELINE config 4: prep of X~N(0,1) then W8A8 GEMM M x K={K} x N={N}, "
                         f"{world}-way output-column shards (one prepared int8 shard per rank), "
                         f"gather = NCCL all_gather_into_tensor of the [M, N/{world}] blocks "
-                        f"(rank-major); roofline per GPU; parity: gathered blocks == a "
-                        f"whole-width GEMM on each rank's own GPU, bit for bit"}
+                        f"(rank-major); gemm_token: the GEMM then the rows' token choice "
+                        f"with only (value, index) pairs exchanged (argmax partials per rank, "
+                        f"all-gather of the pairs, merge); roofline per GPU; parity: gathered "
+                        f"blocks == a whole-width GEMM on each rank's own GPU, bit for bit; "
+                        f"token_parity: tokens == the whole logits' row argmax"}
 
 
 def build_decode_chain(dev, gen, T, L=30, world=1, rank=0):
