@@ -107,12 +107,15 @@ __device__ __forceinline__ void wl_fail(const WlParams &p, int code) {
 }
 
 // mbarrier phase wait, bounded in time and abandoned when the list aborts.
+// The abort word (a global load, an L2 round trip) is read only once a wait
+// has lasted 20 us: a normal wait then reacts as soon as the phase completes.
 __device__ __forceinline__ bool wl_wait(uint64_t *bar, uint32_t parity, const WlParams &p) {
   if (tc::mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = tc::globaltimer_ns();
   while (!tc::mbar_try_wait(bar, parity)) {
-    if (ld_volatile(p.abort)) return false;
-    if (tc::globaltimer_ns() - t0 > kWlLimitNs) return false;
+    const uint64_t dt = tc::globaltimer_ns() - t0;
+    if (dt > 20000 && ld_volatile(p.abort)) return false;  // another warp gave up
+    if (dt > kWlLimitNs) return false;
   }
   return true;
 }
