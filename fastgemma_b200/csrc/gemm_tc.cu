@@ -205,6 +205,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const bool ok = __all_sync(0xffffffffu, tc::mbar_wait(accum, 0));  // warp-uniform
   if (!ok) s_fail = 1;
   tc::fence_after_sync();
+  if constexpr (NB == 128) {
+    // split K: this CTA's int32 partial goes into its send buffer before the
+    // cluster barrier -- its ring is idle once its own MMAs are done, and the
+    // peers write only into its receive slots, only after the barrier -- so
+    // the drain overlaps the wait for the slowest CTA of the cluster
+    if (splits > 1 && ok) {
+      const int q = warp & 3, ch = warp >> 2;
+#pragma unroll 1
+      for (int h = 0; h < H; h++) {
+        const int ml = h * 128 + q * 32 + lane;
+        uint32_t v[64];
+        const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + h * NB + ch * (NB / 2);
+        tc::tmem_ld_x32(ta, v);
+        tc::tmem_ld_x32(ta + 32, v + 32);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int c4 = 0; c4 < 16; c4++)
+          *reinterpret_cast<uint4 *>(smem + row_off(ml, ch * 16 + c4)) =
+              make_uint4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
+      }
+    }
+  }
   asm volatile("griddepcontrol.wait;" ::: "memory");  // a_scale comes from earlier kernels
   if (threadIdx.x < BM) {
     const int m = m0 + threadIdx.x;
@@ -233,7 +255,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   const int q = warp & 3, ch = warp >> 2;
   const bool tma_out = p.tma_store != 0;  // launcher: no raw output, no split, aligned
-  if (ok && !s_fail) {
+  if (ok && !s_fail && splits == 1) {  // (a split CTA drained its partial above)
 #pragma unroll 1
     for (int h = 0; h < H; h++) {
       const int ml = h * 128 + q * 32 + lane;
@@ -247,15 +269,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc::tmem_ld_x32(ta, v);
       tc::tmem_ld_x32(ta + 32, v + 32);
       tc::tmem_wait_ld();
-      if constexpr (NB == 128) {
-        if (splits > 1) {  // int32 partial row into the send buffer
-#pragma unroll
-          for (int c4 = 0; c4 < 16; c4++)
-            *reinterpret_cast<uint4 *>(smem + row_off(ml, ch * 16 + c4)) =
-                make_uint4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
-          continue;
-        }
-      }
 #pragma unroll
       for (int cc = 0; cc < 4; cc++) {
         const int c = ch * (NB / 32) + cb * 4 + cc;  // 16-column chunk of the tile
