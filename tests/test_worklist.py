@@ -246,3 +246,37 @@ def test_many_long_dependency_free_preps(orc):
         want = orc.gemm_q4g(M, N, K, pa_r, qs_r, b, s, 64)[:M]
         assert bits_equal(c.cpu().numpy(), want)[0], i
     wl.close()
+
+
+@pytest.mark.gpu
+def test_host_inputs_and_outputs(orc):
+    """Prep sources and GEMM outputs in page-locked host memory (the kernel
+    reads and writes them through their device mapping): bit for bit the
+    oracle's results, on two runs; a pageable host buffer is rejected."""
+    _gpu()
+    M, K, N = 8, 2048, 512
+    rng = np.random.default_rng(23)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    b, s = F.synth_q4g(N, K, 64, 4, structured=False)
+    xh = torch.from_numpy(x).pin_memory()
+    ch = torch.zeros((M, N), dtype=torch.float32).pin_memory()
+    pa, qs = D.packed_a(M, K), torch.empty(M, device="cuda")
+    wl = D.WorkList()
+    ip = wl.prep(xh, K, K, pa, qs)
+    wl.gemm_q4g(N, K, pa, qs, Dv(b), Dv(s.view(np.uint16)), 64, ch, deps=(ip,))
+    wl.build(M)
+    _, _, qs_r, pa_r = orc.prep_rows(x, M, K, 0)
+    want = orc.gemm_q4g(M, N, K, pa_r, qs_r, b, s, 64)[:M]
+    for _ in range(2):
+        ch.zero_()
+        wl.run()
+        torch.cuda.synchronize()
+        assert _lib.lib().fgm_cuda_device_status() == 0
+        assert bits_equal(ch.numpy(), want)[0]
+    wl.close()
+    # pageable host memory cannot be reached by the kernel: rejected at creation
+    cp = torch.zeros((M, N), dtype=torch.float32)
+    bad = D.WorkList()
+    bad.gemm_q4g(N, K, pa, qs, Dv(b), Dv(s.view(np.uint16)), 64, cp)
+    with pytest.raises(_lib.FgmCudaError):
+        bad.build(M)
